@@ -1,0 +1,169 @@
+/*
+ * qa_b200 — C ABI of the B200 (sm_100a) backend for the Qwen3-ForcedAligner
+ * single-forward alignment path.
+ *
+ * This is the drop-in boundary.  In the reference crate the towers sit behind
+ * a private enum (src/align_inference.rs:82-181, `enum Backend { Gpu, Cpu }`)
+ * with four methods; a `Backend::Cuda { ctx }` arm binds the functions below
+ * one for one (see INTEGRATION.md for the Rust `extern "C"` block):
+ *
+ *   Backend::half()                 -> qa_half
+ *   Backend::audio_embeds(mel, v)   -> qa_audio_embeds
+ *   Backend::ensure_capacity(need)  -> qa_ensure_capacity
+ *   Backend::text_hidden(bytes, s)  -> qa_text_hidden
+ *
+ * plus the stages the reference runs on the host that this backend moves onto
+ * the GPU: the log-mel (src/mel.rs:15-242 -> qa_mel) and the final norm +
+ * timestamp head + argmax (src/align_inference.rs:737-805 -> qa_head), and a
+ * batched, device-resident whole-path call (qa_align_batch) that runs
+ * samples -> raw_ms for many clips with one upload and one readback.
+ *
+ * Conventions (mirroring the reference's anyhow::Result contract):
+ *  - every function returns an int status, QA_OK (0) on success; nothing
+ *    aborts; qa_last_error(ctx) gives the message of the last failure;
+ *  - the context owns all device memory; the caller owns every host buffer
+ *    (inputs are borrowed for the call, outputs are caller-allocated);
+ *  - one context is single-threaded (the reference's `align` takes &mut self);
+ *    distinct contexts on distinct devices may run concurrently;
+ *  - 16-bit element buffers are little-endian f16 or bf16 per the context's
+ *    storage format (qa_half).
+ */
+#ifndef QA_B200_H
+#define QA_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define QA_OK 0
+#define QA_ERR_SHAPE 1   /* a size or shape does not match (reference: ensure!/bail!) */
+#define QA_ERR_CAP 2     /* seq > max_seq (8192) or audio tokens > 16384 */
+#define QA_ERR_CUDA 3    /* a CUDA runtime call failed */
+#define QA_ERR_OOM 4     /* device allocation failed */
+#define QA_ERR_TIMEOUT 5 /* a bounded device wait ran out */
+#define QA_ERR_STATE 6   /* call out of order, or a conflicting storage format */
+#define QA_ERR_WEIGHTS 7 /* a weight is missing or mis-shaped */
+#define QA_ERR_ARG 8     /* a NULL or otherwise invalid argument */
+
+/* 16-bit storage formats (src/shaders.rs:108-160, `Half`). */
+#define QA_HALF_F16 0
+#define QA_HALF_BF16 1
+
+/* Tensor element types for qa_load (safetensors dtypes). */
+#define QA_DTYPE_F32 0
+#define QA_DTYPE_F16 1
+#define QA_DTYPE_BF16 2
+
+typedef struct qa_ctx qa_ctx;
+
+/* One host tensor, borrowed for the duration of qa_load (e.g. a pointer into
+ * an mmap'd safetensors shard).  Names are the checkpoint's own, in either
+ * layout: the `-hf` names (model.audio_tower.*, model.language_model.*,
+ * model.multi_modal_projector.linear_{1,2}.*, score.weight) are remapped the
+ * way src/weights.rs:231-265 does. */
+typedef struct {
+  const char* name;
+  int dtype;
+  int ndim;
+  int64_t shape[4];
+  const void* data;
+} qa_tensor;
+
+/* Model geometry, as parsed from config.json (src/config.rs:81-137,186-236). */
+typedef struct {
+  /* audio tower */
+  int d_model, encoder_layers, encoder_heads, encoder_ffn_dim, num_mel_bins;
+  int downsample_hidden, max_source_positions, n_window, n_window_infer, output_dim;
+  /* text decoder */
+  int vocab_size, hidden_size, intermediate_size, num_layers, num_heads, num_kv_heads, head_dim;
+  double rms_norm_eps, rope_theta;
+  /* forced-aligner head */
+  int num_labels, timestamp_token_id, audio_token_id;
+  double timestamp_segment_time_ms;
+  int max_seq; /* 8192 (src/align_inference.rs:70) */
+} qa_cfg;
+
+/* Per-phase device times of the last qa_align_batch / stage call, in ms
+ * (CUDA events on the context's stream; src/align_inference.rs:230-251). */
+typedef struct {
+  double h2d_ms, mel_ms, enc_ms, gather_ms, prefill_ms, head_ms, d2h_ms, total_ms;
+  int64_t gpu_launches; /* kernels this library launched in the call */
+} qa_timings;
+
+/* ---------------------------------------------------------------- lifetime */
+
+/* Open a context on CUDA device `device` storing 16-bit values in `half`
+ * (Aligner::load_backend_with_dtype, src/align_inference.rs:287-292). */
+int qa_open(int device, int half, qa_ctx** out);
+/* Upload the weights (src/align_inference.rs:294-453). */
+int qa_load(qa_ctx* ctx, const qa_tensor* tensors, int n, const qa_cfg* cfg);
+int qa_close(qa_ctx* ctx);
+const char* qa_last_error(const qa_ctx* ctx);
+/* Bound on every host-side wait for the device (default 60000 ms). */
+int qa_set_timeout_ms(qa_ctx* ctx, int ms);
+/* Backend::half (src/align_inference.rs:103-108). */
+int qa_half(const qa_ctx* ctx);
+int qa_get_timings(const qa_ctx* ctx, qa_timings* out);
+
+/* ---------------------------------------------------------------- stages */
+
+/* Log-mel of 16 kHz mono samples (mel::mel_features, src/mel.rs:15-242):
+ * out is [num_mel_bins, n_frames] row-major f32 with n_frames = n / 160.
+ * *n_frames receives the frame count; out_len is out's capacity in floats. */
+int qa_mel(qa_ctx* ctx, const float* samples, int64_t n, float* out, int64_t out_len,
+           int* n_frames);
+
+/* Backend::audio_embeds (src/align_inference.rs:118-133): mel [n_mels,
+ * valid_frames] row-major f32 -> [n_audio_tokens, output_dim] 16-bit.
+ * out_len is out's capacity in elements; the produced count must equal
+ * n_audio_tokens * output_dim. */
+int qa_audio_embeds(qa_ctx* ctx, const float* mel, int n_mels, int valid_frames, uint16_t* out,
+                    int64_t out_len);
+
+/* Backend::ensure_capacity (src/align_inference.rs:137-142): make the K/V
+ * cache hold `need` positions (grow-only, capped at max_seq). */
+int qa_ensure_capacity(qa_ctx* ctx, int need, int* cap);
+
+/* Backend::text_hidden (src/align_inference.rs:150-173): [seq, hidden] 16-bit
+ * input embeddings -> [seq, hidden] f32 hidden states after the last layer. */
+int qa_text_hidden(qa_ctx* ctx, const uint16_t* emb, int seq, float* out);
+
+/* Final RMSNorm + timestamp head + argmax on the given rows of `hidden`
+ * (src/align_inference.rs:737-805).  hidden [seq, hidden_size] f32; rows the
+ * timestamp positions.  raw_ms [n_rows] receives (argmax * segment_ms) as
+ * i64.  logits [n_rows, num_labels] and normed [n_rows, hidden_size] (the
+ * unfolded norm the Local Head reads) are optional (NULL to skip). */
+int qa_head(qa_ctx* ctx, const float* hidden, int seq, const int* rows, int n_rows,
+            int64_t* raw_ms, float* logits, float* normed);
+
+/* ---------------------------------------------------------------- batched path */
+
+typedef struct {
+  const float* samples; /* 16 kHz mono */
+  int64_t n_samples;
+  const uint32_t* input_ids; /* InputBuilder::build output (src/align_input.rs:190-262) */
+  int seq_len;
+} qa_clip;
+
+typedef struct {
+  int64_t* raw_ms; /* [n_ts] caller-allocated: one value per <timestamp> token */
+  int n_ts;        /* number of <timestamp> tokens in the clip's input_ids */
+  float* logits;   /* optional [n_ts, num_labels] */
+  float* normed;   /* optional [n_ts, hidden_size] unfolded-norm rows */
+} qa_result;
+
+/* Align a batch of independent clips in one device-resident pass:
+ * samples -> mel -> audio tower -> embedding gather + audio scatter -> causal
+ * prefill over a paged K/V cache -> timestamp head -> argmax -> raw_ms.
+ * Equivalent, clip by clip, to Aligner::align_raw_rows
+ * (src/align_inference.rs:656-834) fed by mel::mel_features. */
+int qa_align_batch(qa_ctx* ctx, const qa_clip* clips, int n, qa_result* results);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QA_B200_H */

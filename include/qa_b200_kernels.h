@@ -1,0 +1,49 @@
+/*
+ * Kernel-level entry points of the B200 alignment backend.
+ *
+ * These take DEVICE pointers (already resident in HBM) and a CUDA stream, and
+ * run one hot-path kernel each.  They exist so that each kernel can be
+ * parity-tested and timed on its own; the reference has no counterpart at this
+ * granularity (its kernels are WGSL dispatches inside src/decoder.rs and
+ * src/audio_encoder_gpu.rs), so each declaration names the reference stage it
+ * computes instead.
+ *
+ * All functions return 0 on success or a QA_ERR_* code (see qa_b200.h).
+ * 16-bit element buffers are f16 when `bf16 == 0`, bf16 otherwise.
+ */
+#ifndef QA_B200_KERNELS_H
+#define QA_B200_KERNELS_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Epilogue selectors for qa_k_gemm (values match the library's EpiMode). */
+#define QA_EPI_STORE16 0
+#define QA_EPI_RESID16 1
+#define QA_EPI_RESID32 2
+#define QA_EPI_SWIGLU16 3
+#define QA_EPI_STORE32 4
+#define QA_EPI_ARGMAX 5
+
+/*
+ * D = A · Bᵀ on the tcgen05 tensor cores (TMEM accumulator, TMA-fed).
+ * A [M, K] (row stride lda), B [N, K] (row stride ldb), 16-bit.
+ * `mode`/`act`/`bias`/`out`/`ldo`/`row_map`/`pe`/`keys` select the fused
+ * epilogue.  Stands in for every `prefill_gemm*` dispatch of the reference
+ * (src/shaders.rs:1817-2077; src/decoder.rs:1321-1657) and for the host
+ * projections of src/audio_encoder.rs and src/align_inference.rs:789-790.
+ * `status` (device, may be NULL) receives timeout bits.
+ */
+int qa_k_gemm(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
+              int bf16, int mode, int act, void* out, long long ldo, const float* bias,
+              const int* row_map, const float* pe, int pe_period, unsigned long long* keys,
+              unsigned* status, int force_bn, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QA_B200_KERNELS_H */

@@ -1,0 +1,7 @@
+"""B200 (sm_100a) backend for the Qwen3-ForcedAligner alignment path.
+
+The compute lives in libqa_b200.so (CUDA kernels + a C++ host runtime behind
+the C ABI of include/qa_b200.h); this package is the Python mirror of the
+reference crate's `Aligner` API on top of that ABI.
+"""
+from . import _lib  # noqa: F401

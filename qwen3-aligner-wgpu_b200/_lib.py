@@ -1,0 +1,148 @@
+"""ctypes binding of libqa_b200.so (the C ABI in include/qa_b200.h and
+include/qa_b200_kernels.h).
+
+The library is built in-tree by ``make`` in this directory (see
+``__graft_entry__.build``).  There is no fallback: if the shared object is
+missing, :func:`lib` raises, so a product path can never silently run on the
+CPU.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libqa_b200.so")
+
+QA_OK = 0
+QA_ERR_SHAPE = 1
+QA_ERR_CAP = 2
+QA_ERR_CUDA = 3
+QA_ERR_OOM = 4
+QA_ERR_TIMEOUT = 5
+QA_ERR_STATE = 6
+QA_ERR_WEIGHTS = 7
+QA_ERR_ARG = 8
+
+ERR_NAMES = {
+    QA_ERR_SHAPE: "QA_ERR_SHAPE",
+    QA_ERR_CAP: "QA_ERR_CAP",
+    QA_ERR_CUDA: "QA_ERR_CUDA",
+    QA_ERR_OOM: "QA_ERR_OOM",
+    QA_ERR_TIMEOUT: "QA_ERR_TIMEOUT",
+    QA_ERR_STATE: "QA_ERR_STATE",
+    QA_ERR_WEIGHTS: "QA_ERR_WEIGHTS",
+    QA_ERR_ARG: "QA_ERR_ARG",
+}
+
+QA_HALF_F16 = 0
+QA_HALF_BF16 = 1
+QA_DTYPE_F32 = 0
+QA_DTYPE_F16 = 1
+QA_DTYPE_BF16 = 2
+
+EPI_STORE16 = 0
+EPI_RESID16 = 1
+EPI_RESID32 = 2
+EPI_SWIGLU16 = 3
+EPI_STORE32 = 4
+EPI_ARGMAX = 5
+ACT_NONE = 0
+ACT_GELU = 1
+
+# Every symbol the two public headers declare; tests check each is exported.
+EXPORTED = [
+    "qa_open", "qa_load", "qa_close", "qa_last_error", "qa_set_timeout_ms", "qa_half",
+    "qa_get_timings", "qa_mel", "qa_audio_embeds", "qa_ensure_capacity", "qa_text_hidden",
+    "qa_head", "qa_align_batch",
+    "qa_k_gemm",
+]
+
+c_void_p = ctypes.c_void_p
+c_int = ctypes.c_int
+c_ll = ctypes.c_longlong
+
+
+class QaError(RuntimeError):
+    """A non-zero status from the C ABI."""
+
+    def __init__(self, code: int, msg: str = ""):
+        self.code = code
+        super().__init__(f"{ERR_NAMES.get(code, code)}: {msg}")
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def lib_exists() -> bool:
+    return os.path.exists(LIB_PATH)
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the shared library; raise if it was not built."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"{LIB_PATH} is missing: build it with `make` in {_HERE} "
+                    "(or __graft_entry__.build()); there is no CPU fallback")
+            L = ctypes.CDLL(LIB_PATH)
+            _declare(L)
+            _lib = L
+        return _lib
+
+
+def _declare(L: ctypes.CDLL) -> None:
+    L.qa_k_gemm.argtypes = [c_void_p, c_ll, c_void_p, c_ll, c_int, c_int, c_int, c_int, c_int,
+                            c_int, c_void_p, c_ll, c_void_p, c_void_p, c_void_p, c_int, c_void_p,
+                            c_void_p, c_int, c_void_p]
+    L.qa_k_gemm.restype = c_int
+    if hasattr(L, "qa_open"):
+        L.qa_open.argtypes = [c_int, c_int, ctypes.POINTER(c_void_p)]
+        L.qa_load.argtypes = [c_void_p, c_void_p, c_int, c_void_p]
+        L.qa_close.argtypes = [c_void_p]
+        L.qa_last_error.argtypes = [c_void_p]
+        L.qa_last_error.restype = ctypes.c_char_p
+        L.qa_set_timeout_ms.argtypes = [c_void_p, c_int]
+        L.qa_half.argtypes = [c_void_p]
+        L.qa_get_timings.argtypes = [c_void_p, c_void_p]
+        L.qa_mel.argtypes = [c_void_p, c_void_p, ctypes.c_int64, c_void_p, ctypes.c_int64,
+                             ctypes.POINTER(c_int)]
+        L.qa_audio_embeds.argtypes = [c_void_p, c_void_p, c_int, c_int, c_void_p, ctypes.c_int64]
+        L.qa_ensure_capacity.argtypes = [c_void_p, c_int, ctypes.POINTER(c_int)]
+        L.qa_text_hidden.argtypes = [c_void_p, c_void_p, c_int, c_void_p]
+        L.qa_head.argtypes = [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
+                              c_void_p]
+        L.qa_align_batch.argtypes = [c_void_p, c_void_p, c_int, c_void_p]
+
+
+def check(rc: int, ctx=None) -> None:
+    if rc != QA_OK:
+        msg = ""
+        if ctx is not None:
+            m = lib().qa_last_error(ctx)
+            msg = m.decode() if m else ""
+        raise QaError(rc, msg)
+
+
+def ptr(t) -> int:
+    """Device/host address of a torch tensor (0 for None)."""
+    return 0 if t is None else int(t.data_ptr())
+
+
+def gemm(A, B, out, mode=EPI_STORE16, act=ACT_NONE, bias=None, row_map=None, pe=None,
+         pe_period=1, keys=None, status=None, force_bn=0, stream=None):
+    """Run the tcgen05 GEMM on torch CUDA tensors: A [M, K], B [N, K]."""
+    import torch
+    M, K = A.shape
+    N = B.shape[0]
+    assert B.shape[1] == K and A.dtype == B.dtype
+    bf16 = 1 if A.dtype == torch.bfloat16 else 0
+    s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
+    rc = lib().qa_k_gemm(ptr(A), A.stride(0), ptr(B), B.stride(0), M, N, K, bf16, mode, act,
+                         ptr(out), out.stride(0) if out is not None else 0, ptr(bias),
+                         ptr(row_map), ptr(pe), pe_period, ptr(keys), ptr(status), force_bn, s)
+    check(rc)

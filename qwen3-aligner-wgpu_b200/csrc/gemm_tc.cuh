@@ -1,0 +1,55 @@
+// Tensor-core GEMM for sm_100a: D = A · Bᵀ with A [M, K] and B [N, K], both
+// K-major 16-bit (f16 or bf16), f32 accumulation in TMEM, and a fused
+// epilogue.  This is the one GEMM core behind every dense projection of the
+// aligner: the decoder's QKV / O / gate-up / down, the audio tower's conv
+// stem, QKV, out_proj, fc1/fc2, conv_out and projector, and the timestamp head.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace qa {
+
+// Epilogue modes (what happens to each f32 accumulator element acc[r, c]).
+enum EpiMode : int {
+  // out16[r, c] = h16(act(acc + bias[c]))
+  EPI_STORE16 = 0,
+  // out16[r, c] = h16(f32(out16[r, c]) + acc)            (decoder residual)
+  EPI_RESID16 = 1,
+  // out32[r, c] += acc + bias[c]                          (audio-tower residual)
+  EPI_RESID32 = 2,
+  // columns [0, BN/2) of a tile are gate, [BN/2, BN) up, for the same outputs:
+  // out16[r, j] = h16(silu(h16(g)) * h16(u))             (SwiGLU, out width N/2)
+  EPI_SWIGLU16 = 3,
+  // out32[map(r), c] = acc + bias[c] + pe[(r % pe_period), c]
+  EPI_STORE32 = 4,
+  // optional out32[r, c] = acc; keys[r] = max over c of (ordered(acc), ~c)
+  EPI_ARGMAX = 5,
+};
+
+enum EpiAct : int { ACT_NONE = 0, ACT_GELU = 1 };
+
+struct EpiParams {
+  int mode = EPI_STORE16;
+  int act = ACT_NONE;
+  void* out = nullptr;          // output base (16-bit or f32 per mode)
+  long long ldo = 0;            // output row stride in elements
+  const float* bias = nullptr;  // [N] f32, optional
+  const int* row_map = nullptr; // optional output row per A row; < 0 skips the row
+  const float* pe = nullptr;    // optional [pe_period, N] f32 added by row % pe_period
+  int pe_period = 1;
+  unsigned long long* keys = nullptr;  // EPI_ARGMAX: [M] packed (value, index) keys
+  unsigned* status = nullptr;   // device status word (timeouts)
+};
+
+// Launch D = A·Bᵀ.  A: [M, K] rows lda elements apart; B: [N, K] rows ldb
+// apart.  Both pointers 16-byte aligned, lda/ldb multiples of 8.  K tails and
+// M/N tails are zero-filled by TMA and masked in the epilogue.
+// Returns 0 or a cudaError_t value.
+int gemm_tc(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
+            bool bf16, const EpiParams& ep, cudaStream_t stream, int force_bn = 0);
+
+// Tile width the launcher picks for N (exposed for SwiGLU weight packing).
+int gemm_pick_bn(int N);
+
+}  // namespace qa

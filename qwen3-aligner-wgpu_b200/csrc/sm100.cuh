@@ -1,0 +1,222 @@
+// Blackwell (sm_100a) primitives used by the tensor-core kernels: mbarriers
+// with bounded waits, TMA tile loads, tcgen05 MMA / TMEM management and the
+// shared-memory matrix descriptors that tcgen05.mma consumes.
+//
+// Every wait in this file is bounded by a wall-clock limit read from
+// %globaltimer.  A wait that runs out returns false; the caller records an
+// error in the kernel's status word and leaves its loop, so a descriptor or
+// pipeline bug surfaces as QA_ERR_TIMEOUT on the host instead of a hung GPU.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+
+namespace qa {
+
+// Bound on any single spin-wait inside a kernel (nanoseconds).
+constexpr unsigned long long kSpinLimitNs = 2000000000ull;  // 2 s
+
+// Status bits a kernel may raise in its device status word.
+constexpr unsigned kStatusTimeout = 1u;
+constexpr unsigned kStatusBadShape = 2u;
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- mbarrier
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait until the barrier's phase with the given parity has completed.
+// Returns false when the wall-clock limit ran out first.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = smem_u32(bar);
+  if (mbar_try_wait(addr, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try_wait(addr, parity)) return true;
+    if ((it & 255u) == 255u && global_ns() - t0 > kSpinLimitNs) return false;
+  }
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// ---------------------------------------------------------------- TMA
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// 2-D tiled load global -> shared, completion signalled on `bar` (tx bytes).
+// x is the innermost (contiguous) coordinate in elements, y the row.
+__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst,
+                                            int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// ---------------------------------------------------------------- tcgen05
+
+// Allocate `ncols` TMEM columns (power of two, >= 32); the base address is
+// written to *slot.  Must be executed by one whole warp.
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(slot)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor for a K-major operand tile written by TMA
+// with 128-byte swizzling: rows of 64 16-bit elements (128 B), 8-row groups
+// 1024 B apart.  Fields: start address >> 4 (bits 0-13), leading byte offset
+// >> 4 (16-29, unused for swizzled K-major, set to 1), stride byte offset >> 4
+// (32-45) = 1024 B, descriptor version 1 (bit 46), layout 2 = 128B swizzle
+// (bits 61-63).  The tile base must be 1024-byte aligned.
+__device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
+// Instruction descriptor for kind::f16 with f32 accumulation, both operands
+// K-major.  a/b format: 0 = f16, 1 = bf16 (the two operands share a type).
+__host__ __device__ constexpr uint32_t f16_instr_desc(int M, int N, bool bf16) {
+  return (1u << 4)                                 // D format f32
+         | ((bf16 ? 1u : 0u) << 7)                 // A format
+         | ((bf16 ? 1u : 0u) << 10)                // B format
+         | (static_cast<uint32_t>(N >> 3) << 17)   // N / 8
+         | (static_cast<uint32_t>(M >> 4) << 24);  // M / 16
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, issued by a single thread.
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` once every tcgen05.mma previously issued by this thread has
+// completed (their shared-memory operands may then be overwritten).
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// Load 32 consecutive f32 columns of this warp's 32 TMEM lanes (one lane per
+// thread).  taddr = base | (lane0 << 16) | column.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// ---------------------------------------------------------------- 16-bit helpers
+
+template <typename T>
+struct H16Traits;
+template <>
+struct H16Traits<__half> {
+  static constexpr bool kBf16 = false;
+  __device__ static __forceinline__ __half from(float x) { return __float2half_rn(x); }
+  __device__ static __forceinline__ float to(__half x) { return __half2float(x); }
+};
+template <>
+struct H16Traits<__nv_bfloat16> {
+  static constexpr bool kBf16 = true;
+  __device__ static __forceinline__ __nv_bfloat16 from(float x) { return __float2bfloat16_rn(x); }
+  __device__ static __forceinline__ float to(__nv_bfloat16 x) { return __bfloat162float(x); }
+};
+
+template <typename T>
+__device__ __forceinline__ float h2f(T x) {
+  return H16Traits<T>::to(x);
+}
+template <typename T>
+__device__ __forceinline__ T f2h(float x) {
+  return H16Traits<T>::from(x);
+}
+
+// Round an f32 through the 16-bit format and back.
+template <typename T>
+__device__ __forceinline__ float round16(float x) {
+  return h2f<T>(f2h<T>(x));
+}
+
+}  // namespace qa

@@ -1,0 +1,150 @@
+"""tcgen05 GEMM (qa_k_gemm) against a plain PyTorch fp32 reference of the same op.
+
+Tolerances: the kernel accumulates in f32 like the reference and rounds once
+to the 16-bit output, so the error is the output rounding: max |Δ| / max |ref|
+below 2e-3 for f16 and 1e-2 for bf16 outputs; f32 outputs below 1e-4.
+"""
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from conftest import cuda_ok, pkg  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+TOL16 = {torch.float16: 2e-3, torch.bfloat16: 1e-2}
+
+
+def _lib():
+    return pkg()._lib
+
+
+def _rel(a, b):
+    a = a.float()
+    b = b.float()
+    return ((a - b).abs().max() / b.abs().max().clamp_min(1e-12)).item()
+
+
+def _mk(M, N, K, dtype, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    A = (torch.randn(M, K, device="cuda", generator=g) * 0.5).to(dtype)
+    B = (torch.randn(N, K, device="cuda", generator=g) * 0.05).to(dtype)
+    return A, B
+
+
+@pytest.fixture(autouse=True)
+def _need_cuda():
+    if not cuda_ok():
+        pytest.skip("no CUDA device")
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 1024, 1024), (1000, 4096, 1024),
+                                   (77, 896, 896), (513, 480, 4320), (129, 1024, 3072),
+                                   (1, 256, 128), (250, 2688, 896)])
+def test_store16(dtype, M, N, K):
+    L = _lib()
+    A, B = _mk(M, N, K, dtype)
+    out = torch.full((M, N), float("nan"), device="cuda", dtype=dtype)
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    L.gemm(A, B, out, status=st)
+    torch.cuda.synchronize()
+    assert st.item() == 0
+    ref = A.float() @ B.float().t()
+    assert torch.isfinite(out.float()).all()
+    assert _rel(out, ref) < TOL16[dtype]
+
+
+@pytest.mark.parametrize("bn", [128, 224, 240, 256])
+def test_tile_widths(bn):
+    L = _lib()
+    A, B = _mk(200, 960, 512, torch.float16, seed=bn)
+    out = torch.zeros(200, 960, device="cuda", dtype=torch.float16)
+    L.gemm(A, B, out, force_bn=bn)
+    torch.cuda.synchronize()
+    assert _rel(out, A.float() @ B.float().t()) < 2e-3
+
+
+def test_bias_gelu():
+    L = _lib()
+    A, B = _mk(333, 3584, 896, torch.float16, seed=3)
+    bias = torch.randn(3584, device="cuda") * 0.1
+    out = torch.zeros(333, 3584, device="cuda", dtype=torch.float16)
+    L.gemm(A, B, out, act=L.ACT_GELU, bias=bias)
+    torch.cuda.synchronize()
+    ref = torch.nn.functional.gelu(A.float() @ B.float().t() + bias)
+    assert _rel(out, ref) < 2e-3
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_resid16(dtype):
+    L = _lib()
+    A, B = _mk(300, 1024, 2048, dtype, seed=4)
+    h = (torch.randn(300, 1024, device="cuda") * 2).to(dtype)
+    ref = (h.float() + A.float() @ B.float().t())
+    L.gemm(A, B, h, mode=L.EPI_RESID16)
+    torch.cuda.synchronize()
+    assert _rel(h, ref) < TOL16[dtype]
+
+
+def test_resid32_bias():
+    L = _lib()
+    A, B = _mk(250, 896, 3584, torch.float16, seed=5)
+    bias = torch.randn(896, device="cuda") * 0.1
+    h = torch.randn(250, 896, device="cuda")
+    ref = h + A.float() @ B.float().t() + bias
+    L.gemm(A, B, h, mode=L.EPI_RESID32, bias=bias)
+    torch.cuda.synchronize()
+    assert _rel(h, ref) < 1e-4
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_swiglu(dtype):
+    """Gate/up rows interleaved in blocks of 128 (half a 256-wide tile)."""
+    L = _lib()
+    M, I, K = 300, 3072, 1024
+    A, _ = _mk(M, 1, K, dtype, seed=6)
+    g = torch.Generator(device="cuda").manual_seed(7)
+    Wg = (torch.randn(I, K, device="cuda", generator=g) * 0.05).to(dtype)
+    Wu = (torch.randn(I, K, device="cuda", generator=g) * 0.05).to(dtype)
+    Wp = torch.stack([Wg.view(I // 128, 128, K), Wu.view(I // 128, 128, K)], 1).reshape(2 * I, K)
+    out = torch.zeros(M, I, device="cuda", dtype=dtype)
+    L.gemm(A, Wp.contiguous(), out, mode=L.EPI_SWIGLU16)
+    torch.cuda.synchronize()
+    gg = (A.float() @ Wg.float().t()).to(dtype).float()
+    uu = (A.float() @ Wu.float().t()).to(dtype).float()
+    ref = gg / (1 + torch.exp(-gg)) * uu
+    assert _rel(out, ref) < TOL16[dtype]
+
+
+def test_store32_rowmap_pe():
+    L = _lib()
+    M, N, K = 260, 896, 7680
+    A, B = _mk(M, N, K, torch.float16, seed=8)
+    bias = torch.randn(N, device="cuda") * 0.1
+    pe = torch.randn(13, N, device="cuda")
+    rmap = torch.arange(M, device="cuda", dtype=torch.int32)
+    rmap[5::13] = -1
+    dst = torch.arange(M, device="cuda")[rmap >= 0]
+    rmap[rmap >= 0] = torch.arange(dst.numel(), device="cuda", dtype=torch.int32)
+    out = torch.zeros(dst.numel(), N, device="cuda")
+    L.gemm(A, B, out, mode=L.EPI_STORE32, bias=bias, row_map=rmap, pe=pe, pe_period=13)
+    torch.cuda.synchronize()
+    full = A.float() @ B.float().t() + bias + pe[torch.arange(M, device="cuda") % 13]
+    ref = full[dst]
+    assert _rel(out, ref) < 1e-4
+
+
+def test_argmax():
+    L = _lib()
+    M, N, K = 333, 5000, 2048
+    A, B = _mk(M, N, K, torch.bfloat16, seed=9)
+    logits = torch.zeros(M, N, device="cuda")
+    keys = torch.zeros(M, dtype=torch.int64, device="cuda")
+    L.gemm(A, B, logits, mode=L.EPI_ARGMAX, keys=keys)
+    torch.cuda.synchronize()
+    ref = A.float() @ B.float().t()
+    assert _rel(logits, ref) < 1e-4
+    idx = (0xFFFFFFFF - (keys & 0xFFFFFFFF)).cpu()
+    got_from_logits = logits.argmax(1).cpu()
+    assert torch.equal(idx, got_from_logits)
