@@ -2,6 +2,11 @@
 
 The compute lives in libqa_b200.so (CUDA kernels + a C++ host runtime behind
 the C ABI of include/qa_b200.h); this package is the Python mirror of the
-reference crate's `Aligner` API on top of that ABI.
+reference crate's `Aligner` API on top of that ABI, plus the host glue the
+reference also keeps on the CPU (word splitting, input building, timestamp
+repair) and the seeded synthetic assets the tests and benchmark run on.
 """
 from . import _lib  # noqa: F401
+from . import postprocess  # noqa: F401
+from . import rope  # noqa: F401
+from . import synth  # noqa: F401

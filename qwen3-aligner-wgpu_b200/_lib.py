@@ -64,6 +64,71 @@ c_int = ctypes.c_int
 c_ll = ctypes.c_longlong
 
 
+class QaTensor(ctypes.Structure):
+    """qa_tensor (include/qa_b200.h)."""
+    _fields_ = [("name", ctypes.c_char_p), ("dtype", c_int), ("ndim", c_int),
+                ("shape", ctypes.c_int64 * 4), ("data", c_void_p)]
+
+
+class QaCfg(ctypes.Structure):
+    """qa_cfg (include/qa_b200.h)."""
+    _fields_ = [(n, c_int) for n in (
+        "d_model", "encoder_layers", "encoder_heads", "encoder_ffn_dim", "num_mel_bins",
+        "downsample_hidden", "max_source_positions", "n_window", "n_window_infer", "output_dim",
+        "vocab_size", "hidden_size", "intermediate_size", "num_layers", "num_heads",
+        "num_kv_heads", "head_dim")] + [("rms_norm_eps", ctypes.c_double),
+                                       ("rope_theta", ctypes.c_double)] + [
+        (n, c_int) for n in ("num_labels", "timestamp_token_id", "audio_token_id")] + [
+        ("timestamp_segment_time_ms", ctypes.c_double), ("max_seq", c_int)]
+
+
+class QaTimings(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_double) for n in (
+        "h2d_ms", "mel_ms", "enc_ms", "gather_ms", "prefill_ms", "head_ms", "d2h_ms",
+        "total_ms")] + [("gpu_launches", ctypes.c_int64)]
+
+
+class QaClip(ctypes.Structure):
+    _fields_ = [("samples", c_void_p), ("n_samples", ctypes.c_int64), ("input_ids", c_void_p),
+                ("seq_len", c_int)]
+
+
+class QaResult(ctypes.Structure):
+    _fields_ = [("raw_ms", c_void_p), ("n_ts", c_int), ("logits", c_void_p),
+                ("normed", c_void_p)]
+
+
+def make_cfg(mc) -> QaCfg:
+    """QaCfg from a synth.ModelConfig-like object."""
+    c = QaCfg()
+    for name, _ in QaCfg._fields_:
+        setattr(c, name, getattr(mc, name))
+    return c
+
+
+def make_tensors(weights: dict):
+    """(QaTensor array, keepalive) from name -> (dtype, np array) or bf16 bits."""
+    import numpy as np
+    items = []
+    for name, v in weights.items():
+        if isinstance(v, tuple):
+            dt, arr = v
+        else:
+            dt, arr = "BF16", v
+        code = {"BF16": QA_DTYPE_BF16, "F16": QA_DTYPE_F16, "F32": QA_DTYPE_F32}[dt]
+        arr = np.ascontiguousarray(arr)
+        items.append((name.encode(), code, arr))
+    arr_t = (QaTensor * len(items))()
+    for i, (nm, code, a) in enumerate(items):
+        arr_t[i].name = nm
+        arr_t[i].dtype = code
+        arr_t[i].ndim = a.ndim
+        for d in range(a.ndim):
+            arr_t[i].shape[d] = a.shape[d]
+        arr_t[i].data = a.ctypes.data
+    return arr_t, items
+
+
 class QaError(RuntimeError):
     """A non-zero status from the C ABI."""
 

@@ -1,0 +1,527 @@
+"""Seeded synthetic assets for the aligner: a random-init checkpoint in the
+reference's `-hf` safetensors layout, a tokenizer with the reference's marker
+ids, and synthetic audio + transcripts for each benchmark configuration.
+
+No checkpoint, tokenizer or audio fixture of the reference exists in this
+environment, so every parity test and benchmark runs on these stand-ins:
+
+* weights: N(0, 0.02) for every matrix, embedding and bias, RMSNorm and
+  LayerNorm gains 1, LayerNorm biases 0, stored bf16 (the checkpoint's dtype);
+  each tensor has its own generator seeded from (seed, name) so a model with
+  fewer layers shares its tensors with the full one;
+* audio: 16 kHz Gaussian noise, low-passed (4th-order Butterworth at 3.4 kHz,
+  zero phase), shaped by Hann bursts of 150-400 ms separated by 40-200 ms gaps,
+  scaled to RMS 0.1;
+* transcripts: English pseudo-words of 3-8 lowercase letters, Chinese words of
+  one CJK ideograph in U+4E00..U+62FF;
+* tokenizer: the markers of src/align_input.rs:33-44 are atomic tokens with
+  the checkpoint's ids (151669, 151670, 151676, 151705); a CJK character is one
+  token; a Latin word is split into 3-letter pieces, each one token.
+"""
+from __future__ import annotations
+
+import hashlib
+import json
+import os
+import struct
+from dataclasses import dataclass, field, asdict
+
+import numpy as np
+
+AUDIO_START_ID = 151669
+AUDIO_END_ID = 151670
+AUDIO_PAD_ID = 151676
+TIMESTAMP_ID = 151705
+AUDIO_START = "<|audio_start|>"
+AUDIO_END = "<|audio_end|>"
+AUDIO_PAD = "<|audio_pad|>"
+TIMESTAMP = "<timestamp>"
+SAMPLE_RATE = 16000
+HOP = 160
+
+
+@dataclass
+class ModelConfig:
+    """Geometry of the Qwen3-ForcedAligner-0.6B checkpoint (src/config.rs:81-137)."""
+    # audio tower
+    d_model: int = 896
+    encoder_layers: int = 18
+    encoder_heads: int = 14
+    encoder_ffn_dim: int = 3584
+    num_mel_bins: int = 128
+    downsample_hidden: int = 480
+    max_source_positions: int = 1500
+    n_window: int = 50
+    n_window_infer: int = 800
+    output_dim: int = 1024
+    # text decoder
+    vocab_size: int = 151936
+    hidden_size: int = 1024
+    intermediate_size: int = 3072
+    num_layers: int = 28
+    num_heads: int = 16
+    num_kv_heads: int = 8
+    head_dim: int = 128
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 1e6
+    # head
+    num_labels: int = 5000
+    timestamp_token_id: int = TIMESTAMP_ID
+    audio_token_id: int = AUDIO_PAD_ID
+    timestamp_segment_time_ms: float = 80.0
+    max_seq: int = 8192
+
+    def config_json(self) -> dict:
+        """config.json in the `-hf` layout the reference parses (src/config.rs:153-236)."""
+        return {
+            "audio_config": {
+                "d_model": self.d_model, "encoder_layers": self.encoder_layers,
+                "encoder_attention_heads": self.encoder_heads,
+                "encoder_ffn_dim": self.encoder_ffn_dim, "num_mel_bins": self.num_mel_bins,
+                "downsample_hidden_size": self.downsample_hidden,
+                "max_source_positions": self.max_source_positions, "n_window": self.n_window,
+                "n_window_infer": self.n_window_infer, "output_dim": self.output_dim,
+            },
+            "text_config": {
+                "vocab_size": self.vocab_size, "hidden_size": self.hidden_size,
+                "intermediate_size": self.intermediate_size,
+                "num_hidden_layers": self.num_layers, "num_attention_heads": self.num_heads,
+                "num_key_value_heads": self.num_kv_heads, "head_dim": self.head_dim,
+                "rms_norm_eps": self.rms_norm_eps, "rope_theta": self.rope_theta,
+            },
+            "audio_token_id": self.audio_token_id,
+            "audio_start_token_id": AUDIO_START_ID,
+            "audio_end_token_id": AUDIO_END_ID,
+            "timestamp_token_id": self.timestamp_token_id,
+            "timestamp_segment_time": self.timestamp_segment_time_ms,
+            "id2label": {str(i): f"LABEL_{i}" for i in range(self.num_labels)},
+        }
+
+    @staticmethod
+    def from_config_json(d: dict) -> "ModelConfig":
+        a = d.get("audio_config") or d["thinker_config"]["audio_config"]
+        t = d.get("text_config") or d["thinker_config"]["text_config"]
+        c = ModelConfig()
+        c.d_model = a.get("d_model", c.d_model)
+        c.encoder_layers = a.get("encoder_layers", c.encoder_layers)
+        c.encoder_heads = a.get("encoder_attention_heads", c.encoder_heads)
+        c.encoder_ffn_dim = a.get("encoder_ffn_dim", c.encoder_ffn_dim)
+        c.num_mel_bins = a.get("num_mel_bins", c.num_mel_bins)
+        c.downsample_hidden = a.get("downsample_hidden_size", c.downsample_hidden)
+        c.max_source_positions = a.get("max_source_positions", c.max_source_positions)
+        c.n_window = a.get("n_window", c.n_window)
+        c.n_window_infer = a.get("n_window_infer", c.n_window_infer)
+        c.output_dim = a.get("output_dim", c.output_dim)
+        c.vocab_size = t.get("vocab_size", c.vocab_size)
+        c.hidden_size = t.get("hidden_size", c.hidden_size)
+        c.intermediate_size = t.get("intermediate_size", c.intermediate_size)
+        c.num_layers = t.get("num_hidden_layers", c.num_layers)
+        c.num_heads = t.get("num_attention_heads", c.num_heads)
+        c.num_kv_heads = t.get("num_key_value_heads", c.num_kv_heads)
+        c.head_dim = t.get("head_dim", c.head_dim)
+        c.rms_norm_eps = t.get("rms_norm_eps", c.rms_norm_eps)
+        rp = t.get("rope_parameters") or {}
+        c.rope_theta = rp.get("rope_theta", t.get("rope_theta", c.rope_theta))
+        c.audio_token_id = d.get("audio_token_id", c.audio_token_id)
+        c.timestamp_token_id = d.get("timestamp_token_id", c.timestamp_token_id)
+        c.timestamp_segment_time_ms = d.get("timestamp_segment_time", 80.0)
+        c.num_labels = len(d.get("id2label") or {}) or c.num_labels
+        return c
+
+
+# ---------------------------------------------------------------- weights
+
+def _bf16_bits(x: np.ndarray) -> np.ndarray:
+    """f32 -> bf16 bits, round to nearest even (src/shaders.rs:74-80)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    return ((u + np.uint32(0x7FFF) + ((u >> 16) & np.uint32(1))) >> 16).astype(np.uint16)
+
+
+def bf16_to_f32(bits: np.ndarray) -> np.ndarray:
+    return (bits.astype(np.uint32) << 16).view(np.float32)
+
+
+def _rng(seed: int, name: str) -> np.random.Generator:
+    h = hashlib.sha256(f"{seed}:{name}".encode()).digest()
+    return np.random.default_rng(int.from_bytes(h[:8], "little"))
+
+
+def weight_specs(cfg: ModelConfig) -> list:
+    """(name, shape, kind) of every checkpoint tensor, `-hf` names
+    (src/weights.rs:231-249).  kind: 'normal' | 'ones' | 'zeros'."""
+    s = []
+    A = "model.audio_tower."
+    ds, dm = cfg.downsample_hidden, cfg.d_model
+    f3 = cfg.num_mel_bins
+    for _ in range(3):
+        f3 = (f3 - 1) // 2 + 1
+    s += [(A + "conv2d1.weight", (ds, 1, 3, 3), "normal"), (A + "conv2d1.bias", (ds,), "normal"),
+          (A + "conv2d2.weight", (ds, ds, 3, 3), "normal"), (A + "conv2d2.bias", (ds,), "normal"),
+          (A + "conv2d3.weight", (ds, ds, 3, 3), "normal"), (A + "conv2d3.bias", (ds,), "normal"),
+          (A + "conv_out.weight", (dm, ds * f3), "normal")]
+    for i in range(cfg.encoder_layers):
+        p = f"{A}layers.{i}."
+        for ln in ("self_attn_layer_norm", "final_layer_norm"):
+            s += [(p + ln + ".weight", (dm,), "ones"), (p + ln + ".bias", (dm,), "zeros")]
+        for pr in ("q_proj", "k_proj", "v_proj", "out_proj"):
+            s += [(p + f"self_attn.{pr}.weight", (dm, dm), "normal")]
+            if pr != "k_proj":
+                s += [(p + f"self_attn.{pr}.bias", (dm,), "normal")]
+        s += [(p + "fc1.weight", (cfg.encoder_ffn_dim, dm), "normal"),
+              (p + "fc1.bias", (cfg.encoder_ffn_dim,), "normal"),
+              (p + "fc2.weight", (dm, cfg.encoder_ffn_dim), "normal"),
+              (p + "fc2.bias", (dm,), "normal")]
+    s += [(A + "ln_post.weight", (dm,), "ones"), (A + "ln_post.bias", (dm,), "zeros"),
+          ("model.multi_modal_projector.linear_1.weight", (dm, dm), "normal"),
+          ("model.multi_modal_projector.linear_1.bias", (dm,), "normal"),
+          ("model.multi_modal_projector.linear_2.weight", (cfg.output_dim, dm), "normal"),
+          ("model.multi_modal_projector.linear_2.bias", (cfg.output_dim,), "normal")]
+    T = "model.language_model."
+    H, hd = cfg.hidden_size, cfg.head_dim
+    s += [(T + "embed_tokens.weight", (cfg.vocab_size, H), "normal")]
+    for i in range(cfg.num_layers):
+        p = f"{T}layers.{i}."
+        s += [(p + "input_layernorm.weight", (H,), "ones"),
+              (p + "post_attention_layernorm.weight", (H,), "ones"),
+              (p + "self_attn.q_norm.weight", (hd,), "ones"),
+              (p + "self_attn.k_norm.weight", (hd,), "ones"),
+              (p + "self_attn.q_proj.weight", (cfg.num_heads * hd, H), "normal"),
+              (p + "self_attn.k_proj.weight", (cfg.num_kv_heads * hd, H), "normal"),
+              (p + "self_attn.v_proj.weight", (cfg.num_kv_heads * hd, H), "normal"),
+              (p + "self_attn.o_proj.weight", (H, cfg.num_heads * hd), "normal"),
+              (p + "mlp.gate_proj.weight", (cfg.intermediate_size, H), "normal"),
+              (p + "mlp.up_proj.weight", (cfg.intermediate_size, H), "normal"),
+              (p + "mlp.down_proj.weight", (H, cfg.intermediate_size), "normal")]
+    s += [(T + "norm.weight", (H,), "ones"), ("score.weight", (cfg.num_labels, H), "normal")]
+    return s
+
+
+def random_weights(cfg: ModelConfig, seed: int = 0, std: float = 0.02) -> dict:
+    """name -> bf16 bits (np.uint16) in the tensor's shape."""
+    out = {}
+    for name, shape, kind in weight_specs(cfg):
+        n = int(np.prod(shape))
+        if kind == "ones":
+            v = np.ones(n, np.float32)
+        elif kind == "zeros":
+            v = np.zeros(n, np.float32)
+        else:
+            v = _rng(seed, name).standard_normal(n, dtype=np.float32) * np.float32(std)
+        out[name] = _bf16_bits(v).reshape(shape)
+    return out
+
+
+def save_safetensors(path: str, tensors: dict) -> None:
+    """Write bf16 tensors (uint16 bits) as a safetensors file."""
+    header, off = {}, 0
+    for name, arr in tensors.items():
+        nb = arr.size * 2
+        header[name] = {"dtype": "BF16", "shape": list(arr.shape), "data_offsets": [off, off + nb]}
+        off += nb
+    hb = json.dumps(header, separators=(",", ":")).encode()
+    hb += b" " * ((8 - len(hb) % 8) % 8)
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(hb)))
+        f.write(hb)
+        for arr in tensors.values():
+            f.write(np.ascontiguousarray(arr, dtype=np.uint16).tobytes())
+
+
+def load_safetensors(path: str) -> dict:
+    """mmap a safetensors file: name -> (dtype str, np array view)."""
+    mm = np.memmap(path, dtype=np.uint8, mode="r")
+    hl = int(np.frombuffer(mm[:8].tobytes(), "<u8")[0])
+    header = json.loads(bytes(mm[8:8 + hl]).decode())
+    base = 8 + hl
+    out = {}
+    np_t = {"BF16": np.uint16, "F16": np.float16, "F32": np.float32}
+    for name, meta in header.items():
+        if name == "__metadata__":
+            continue
+        a, b = meta["data_offsets"]
+        arr = mm[base + a:base + b].view(np_t[meta["dtype"]]).reshape(meta["shape"])
+        out[name] = (meta["dtype"], arr)
+    return out
+
+
+def write_model_dir(path: str, cfg: ModelConfig, seed: int = 0) -> None:
+    """A complete `-hf` model directory: config.json, model.safetensors and the
+    tokenizer files (tokenizer.json carries the synthetic vocabulary's markers)."""
+    os.makedirs(path, exist_ok=True)
+    with open(os.path.join(path, "config.json"), "w") as f:
+        json.dump(cfg.config_json(), f)
+    save_safetensors(os.path.join(path, "model.safetensors"), random_weights(cfg, seed))
+    with open(os.path.join(path, "tokenizer_config.json"), "w") as f:
+        json.dump({"audio_token": AUDIO_PAD, "audio_bos_token": AUDIO_START,
+                   "audio_eos_token": AUDIO_END}, f)
+    with open(os.path.join(path, "tokenizer.json"), "w") as f:
+        json.dump({"synthetic": True, "added_tokens": [
+            {"id": AUDIO_START_ID, "content": AUDIO_START}, {"id": AUDIO_END_ID, "content": AUDIO_END},
+            {"id": AUDIO_PAD_ID, "content": AUDIO_PAD}, {"id": TIMESTAMP_ID, "content": TIMESTAMP}]}, f)
+
+
+# ---------------------------------------------------------------- tokenizer
+
+class SyntheticTokenizer:
+    """Deterministic stand-in for the checkpoint's BPE (`tokenizers` 0.22.2).
+
+    Contract kept from the reference's use of it (src/align_input.rs:183-262):
+    the four markers are atomic with the checkpoint ids; encoding adds no
+    special tokens; every other character sequence maps to ordinary ids below
+    151643.  A CJK ideograph is one token; Latin letters are grouped in 3s."""
+
+    MARKERS = {AUDIO_START: AUDIO_START_ID, AUDIO_END: AUDIO_END_ID, AUDIO_PAD: AUDIO_PAD_ID,
+               TIMESTAMP: TIMESTAMP_ID}
+    ORDINARY = 151643
+
+    def token_to_id(self, s: str):
+        return self.MARKERS.get(s)
+
+    def _piece_id(self, piece: str) -> int:
+        h = hashlib.blake2b(piece.encode(), digest_size=8).digest()
+        return int.from_bytes(h, "little") % self.ORDINARY
+
+    def encode(self, text: str) -> list:
+        ids, i, n = [], 0, len(text)
+        buf = ""
+        while i < n:
+            m = None
+            if text[i] == "<":
+                for k, v in self.MARKERS.items():
+                    if text.startswith(k, i):
+                        m = (k, v)
+                        break
+            if m:
+                if buf:
+                    ids += self._word(buf)
+                    buf = ""
+                ids.append(m[1])
+                i += len(m[0])
+                continue
+            ch = text[i]
+            if 0x3400 <= ord(ch) <= 0x9FFF or 0xF900 <= ord(ch) <= 0xFAFF:
+                if buf:
+                    ids += self._word(buf)
+                    buf = ""
+                ids.append(self._piece_id(ch))
+            else:
+                buf += ch
+            i += 1
+        if buf:
+            ids += self._word(buf)
+        return ids
+
+    def _word(self, w: str) -> list:
+        return [self._piece_id(w[j:j + 3]) for j in range(0, len(w), 3)]
+
+
+# ---------------------------------------------------------------- words / inputs
+
+def is_cjk_char(c: str) -> bool:
+    """src/words.rs:30-40."""
+    k = ord(c)
+    return (0x4E00 <= k <= 0x9FFF or 0x3400 <= k <= 0x4DBF or 0x20000 <= k <= 0x2A6DF
+            or 0x2A700 <= k <= 0x2B73F or 0x2B740 <= k <= 0x2B81F or 0x2B820 <= k <= 0x2CEAF
+            or 0xF900 <= k <= 0xFAFF or 0x2F800 <= k <= 0x2FA1F)
+
+
+def is_hangul_char(c: str) -> bool:
+    """src/words.rs:44-51."""
+    k = ord(c)
+    return (0x1100 <= k <= 0x11FF or 0x3130 <= k <= 0x318F or 0xA960 <= k <= 0xA97F
+            or 0xAC00 <= k <= 0xD7A3 or 0xD7B0 <= k <= 0xD7FF)
+
+
+def is_kept_char(c: str) -> bool:
+    """src/words.rs:59-74: apostrophe, or general category L* / N*, or CJK."""
+    import unicodedata
+    return c == "'" or unicodedata.category(c)[0] in "LN" or is_cjk_char(c)
+
+
+def split_words(text: str, language=None) -> list:
+    """src/words.rs:107-118 + split_default (:190-232) for every language but
+    Japanese (which needs the reference's nagisa tagger and is out of scope)."""
+    import unicodedata
+    text = text.strip()
+    lang = (language or "").lower()
+    if lang in ("japanese", "ja"):
+        raise ValueError("Japanese word splitting requires the nagisa tagger (not available)")
+    tokens, buf, buf_hangul = [], "", None
+    for c in text:
+        if is_cjk_char(c):
+            if buf:
+                tokens.append(buf)
+                buf, buf_hangul = "", None
+            tokens.append(c)
+        elif c.isspace():
+            if buf:
+                tokens.append(buf)
+                buf, buf_hangul = "", None
+        elif is_kept_char(c):
+            script_letter = c != "'" and unicodedata.category(c) not in ("Nd", "Nl", "No")
+            if script_letter:
+                hangul = is_hangul_char(c)
+                if buf_hangul is not None and buf_hangul != hangul:
+                    tokens.append(buf)
+                    buf = ""
+                buf_hangul = hangul
+            buf += c
+    if buf:
+        tokens.append(buf)
+    return tokens
+
+
+def conv3_length(n: int) -> int:
+    """src/align_input.rs:49-57."""
+    for _ in range(3):
+        n = (n - 1) // 2 + 1 if n > 0 else 0
+    return n
+
+
+def audio_token_count(valid_mel_frames: int, n_window: int = 50) -> int:
+    """src/align_input.rs:63-67."""
+    cl = n_window * 2
+    return (valid_mel_frames // cl) * 13 + conv3_length(valid_mel_frames % cl)
+
+
+def padded_mel_frames(valid: int, n_window: int = 50) -> int:
+    """src/align_input.rs:71-79."""
+    m = n_window * 2
+    r = valid % m
+    return valid if r == 0 else valid + (m - r)
+
+
+def valid_mel_frames(n_samples: int) -> int:
+    """src/align_input.rs:85-87."""
+    return n_samples // HOP
+
+
+@dataclass
+class AlignerInput:
+    """src/align_input.rs:91-111."""
+    input_ids: list
+    words: list
+    n_audio_tokens: int
+    valid_mel_frames: int
+    padded_mel_frames: int
+    timestamp_positions: list = field(default_factory=list)
+
+    def seq_len(self) -> int:
+        return len(self.input_ids)
+
+
+class InputBuilder:
+    """InputBuilder::build (src/align_input.rs:190-262), same structural checks."""
+
+    def __init__(self, tokenizer=None, n_window: int = 50):
+        self.tok = tokenizer or SyntheticTokenizer()
+        self.n_window = n_window
+
+    def build(self, words: list, valid_mel: int) -> AlignerInput:
+        n_audio = audio_token_count(valid_mel, self.n_window)
+        if n_audio <= 0:
+            raise ValueError(f"audio produced 0 tokens ({valid_mel} mel frames)")
+        text = AUDIO_START + AUDIO_PAD * n_audio + AUDIO_END
+        for i, w in enumerate(words):
+            if i > 0:
+                text += TIMESTAMP + TIMESTAMP
+            text += w
+        text += TIMESTAMP + TIMESTAMP
+        ids = self.tok.encode(text)
+        if sum(1 for t in ids if t == AUDIO_PAD_ID) != n_audio:
+            raise ValueError("audio token count mismatch")
+        if ids[0] != AUDIO_START_ID or ids[n_audio + 1] != AUDIO_END_ID:
+            raise ValueError("sequence must be <|audio_start|> pads <|audio_end|> ...")
+        ts = [i for i, t in enumerate(ids) if t == TIMESTAMP_ID]
+        if len(ts) != 2 * len(words):
+            raise ValueError(f"expected {2 * len(words)} timestamp tokens, got {len(ts)}")
+        return AlignerInput(ids, list(words), n_audio, valid_mel,
+                            padded_mel_frames(valid_mel, self.n_window), ts)
+
+
+# ---------------------------------------------------------------- audio / text
+
+def synth_audio(seconds: float, seed: int) -> np.ndarray:
+    """Syllable-like bursts of low-passed noise at RMS 0.1, 16 kHz f32."""
+    from scipy.signal import butter, sosfiltfilt
+    rng = np.random.default_rng(seed)
+    n = int(round(seconds * SAMPLE_RATE))
+    noise = rng.standard_normal(n)
+    sos = butter(4, 3400, btype="low", fs=SAMPLE_RATE, output="sos")
+    x = sosfiltfilt(sos, noise)
+    env = np.zeros(n)
+    t = int(rng.uniform(0.04, 0.2) * SAMPLE_RATE)
+    while t < n:
+        d = int(rng.uniform(0.15, 0.40) * SAMPLE_RATE)
+        e = min(n, t + d)
+        env[t:e] = np.hanning(d)[: e - t]
+        t = e + int(rng.uniform(0.04, 0.2) * SAMPLE_RATE)
+    y = x * env
+    rms = np.sqrt(np.mean(y * y)) if n else 1.0
+    y = y * (0.1 / max(rms, 1e-12))
+    return y.astype(np.float32)
+
+
+def english_words(count: int, rng: np.random.Generator) -> list:
+    letters = np.array(list("abcdefghijklmnopqrstuvwxyz"))
+    return ["".join(rng.choice(letters, size=int(rng.integers(3, 9)))) for _ in range(count)]
+
+
+def chinese_words(count: int, rng: np.random.Generator) -> list:
+    return [chr(int(rng.integers(0x4E00, 0x62FF + 1))) for _ in range(count)]
+
+
+@dataclass
+class Clip:
+    samples: np.ndarray
+    text: str
+    language: str
+    seconds: float
+
+
+def workload(config: int, seed_base: int = None, n_clips: int = None) -> list:
+    """The clips of a BASELINE configuration (0-4), seeded 1000 * config + i."""
+    clips = []
+
+    def one(i, seconds, n_words, mix_cjk=False):
+        seed = 1000 * config + i if seed_base is None else seed_base + i
+        rng = np.random.default_rng(seed + 7)
+        if mix_cjk:
+            words, left, en = [], n_words, True
+            while left > 0:
+                run = min(left, int(rng.integers(2, 7)))
+                words += english_words(run, rng) if en else chinese_words(run, rng)
+                left -= run
+                en = not en
+            text, lang = "".join(w if is_cjk_char(w[0]) else f" {w} " for w in words), "Chinese"
+        else:
+            words = english_words(n_words, rng)
+            text, lang = " ".join(words), "English"
+        return Clip(synth_audio(seconds, seed), " ".join(text.split()), lang, seconds)
+
+    if config == 0:
+        clips.append(one(0, 10.0, 25))
+    elif config == 1:
+        clips.append(one(0, 60.0, 180))
+    elif config == 2:
+        rng = np.random.default_rng(2000)
+        n = 64 if n_clips is None else n_clips
+        for i in range(n):
+            sec = float(rng.uniform(5, 30))
+            rate = float(rng.uniform(2.5, 3.5))
+            clips.append(one(i, sec, max(1, int(round(sec * rate))), mix_cjk=True))
+    elif config == 3:
+        clips.append(one(0, 300.0, 900))
+    elif config == 4:
+        rng = np.random.default_rng(4000)
+        n = 4096 if n_clips is None else n_clips
+        for i in range(n):
+            sec = float(rng.uniform(5, 60))
+            clips.append(one(i, sec, max(1, int(round(sec * 3.0)))))
+    else:
+        raise ValueError(config)
+    return clips
+
+
+def asdict_cfg(cfg: ModelConfig) -> dict:
+    return asdict(cfg)
