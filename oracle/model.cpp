@@ -51,6 +51,7 @@ struct Loader {
   std::vector<float> f32(const std::string& name) const {
     const View& v = get(name);
     std::vector<float> o(v.numel());
+#pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < v.numel(); ++i) o[i] = elem_f32(v, i);
     return o;
   }
@@ -59,6 +60,7 @@ struct Loader {
   std::vector<float> f16w(const std::string& name) const {
     const View& v = get(name);
     std::vector<float> o(v.numel());
+#pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < v.numel(); ++i) o[i] = orc::r16(elem_f32(v, i));
     return o;
   }
@@ -165,6 +167,7 @@ extern "C" or_model* or_load(const qa_tensor* tensors, int n, const qa_cfg* cfg,
     {
       const View& e = L.get(T + "embed_tokens.weight");
       m->embed.resize(e.numel());
+#pragma omp parallel for schedule(static)
       for (int64_t i = 0; i < e.numel(); ++i) m->embed[i] = orc::f32_to_f16(elem_f32(e, i));
     }
     m->final_norm = L.f32(T + "norm.weight");

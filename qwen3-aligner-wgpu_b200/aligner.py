@@ -1,0 +1,223 @@
+"""Python mirror of the reference crate's `Aligner` (src/align_inference.rs)
+on top of the C ABI of libqa_b200.so.
+
+Same names, argument meaning and error behaviour as the Rust API where it
+applies:
+
+* ``Aligner.load_backend_with_dtype(model, half)`` — load weights onto one
+  CUDA device in the given 16-bit storage format (``"f16"`` default, ``"bf16"``);
+* ``align_samples(samples, text, language)`` -> ``(raw_ms, items)`` — one clip
+  of 16 kHz mono f32 audio (src/align_inference.rs:521-569, Local Head off);
+* ``align_batch([(samples, text, language), ...])`` — many independent clips
+  in one device-resident pass (new: the reference aligns one clip per call);
+* the tower-boundary stages ``mel``, ``audio_embeds``, ``text_hidden`` and
+  ``head`` (src/align_inference.rs:103-181, 737-805) for callers that drive
+  the phases themselves.
+
+Every failure of the C ABI raises ``QaError`` carrying the status code
+(QA_ERR_SHAPE, QA_ERR_CAP, ...) and the library's message; nothing falls back
+to a CPU path.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+from . import _lib
+from . import postprocess
+from . import synth
+
+
+FORCED_ALIGNER_LANGUAGES = ["Chinese", "Cantonese", "English", "French", "German", "Italian",
+                            "Japanese", "Korean", "Portuguese", "Russian", "Spanish"]
+
+
+class Aligner:
+    def __init__(self, ctx, cfg: synth.ModelConfig, half: str, builder: synth.InputBuilder):
+        self._ctx = ctx
+        self.cfg = cfg
+        self._half = half
+        self.input_builder = builder
+        self.timings = None
+
+    # ------------------------------------------------------------ load / close
+
+    @classmethod
+    def load_backend_with_dtype(cls, model, half: str = "f16", device: int = 0,
+                                cfg: synth.ModelConfig = None, tokenizer=None) -> "Aligner":
+        """``model``: a model directory (config.json + model.safetensors, `-hf`
+        layout) or a dict of name -> bf16 bits / (dtype, array) with ``cfg``."""
+        half = half.lower()
+        if half in ("f16", "fp16", "half"):
+            code = _lib.QA_HALF_F16
+        elif half in ("bf16", "bfloat16"):
+            code = _lib.QA_HALF_BF16
+        else:
+            raise ValueError(f"unknown 16-bit format {half!r}")
+        if isinstance(model, (str, os.PathLike)):
+            import json
+            with open(os.path.join(model, "config.json")) as f:
+                cfg = synth.ModelConfig.from_config_json(json.load(f))
+            weights = synth.load_safetensors(os.path.join(model, "model.safetensors"))
+        else:
+            if cfg is None:
+                raise ValueError("a weights dict needs its ModelConfig")
+            weights = model
+        L = _lib.lib()
+        ctx = ctypes.c_void_p()
+        _lib.check(L.qa_open(device, code, ctypes.byref(ctx)))
+        tens, keep = _lib.make_tensors(weights)
+        qcfg = _lib.make_cfg(cfg)
+        rc = L.qa_load(ctx, ctypes.addressof(tens), len(tens), ctypes.addressof(qcfg))
+        del keep
+        if rc != _lib.QA_OK:
+            msg = L.qa_last_error(ctx)
+            L.qa_close(ctx)
+            raise _lib.QaError(rc, msg.decode() if msg else "")
+        return cls(ctx, cfg, "bf16" if code else "f16",
+                   synth.InputBuilder(tokenizer, n_window=cfg.n_window))
+
+    @classmethod
+    def load_with_dtype(cls, model, half: str = "f16", **kw) -> "Aligner":
+        return cls.load_backend_with_dtype(model, half, **kw)
+
+    @classmethod
+    def load(cls, model, **kw) -> "Aligner":
+        return cls.load_backend_with_dtype(model, "f16", **kw)
+
+    def close(self) -> None:
+        if self._ctx:
+            _lib.lib().qa_close(self._ctx)
+            self._ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def half(self) -> str:
+        return self._half
+
+    def backend_name(self) -> str:
+        return "cuda"
+
+    def set_timeout_ms(self, ms: int) -> None:
+        self._check(_lib.lib().qa_set_timeout_ms(self._ctx, int(ms)))
+
+    def _check(self, rc: int) -> None:
+        _lib.check(rc, self._ctx)
+
+    # ------------------------------------------------------------ language
+
+    def supported_languages(self) -> list:
+        return sorted({s.lower() for s in FORCED_ALIGNER_LANGUAGES})
+
+    def check_language(self, language) -> None:
+        if language is None:
+            return
+        if language.lower() not in self.supported_languages():
+            raise ValueError(f"language {language.lower()!r} is not supported by the forced "
+                             f"aligner; supported: {self.supported_languages()}")
+
+    # ------------------------------------------------------------ whole path
+
+    def build_input(self, samples: np.ndarray, text: str, language=None):
+        self.check_language(language)
+        words = synth.split_words(text, language)
+        return self.input_builder.build(words, synth.valid_mel_frames(len(samples)))
+
+    def align_samples(self, samples: np.ndarray, text: str, language=None):
+        """(raw_ms, items) for one clip (src/align_inference.rs:521-569)."""
+        return self.align_batch([(samples, text, language)])[0]
+
+    def align_batch(self, clips, want_logits: bool = False, want_normed: bool = False):
+        """[(samples, text, language)] -> [(raw_ms, items)]; raw_ms is the
+        unrepaired argmax stream, items the repaired word times."""
+        inputs = [self.build_input(s, t, l) for s, t, l in clips]
+        raws = self.align_inputs([c[0] for c in clips], inputs, want_logits, want_normed)
+        out = []
+        for (r, extra), inp in zip(raws, inputs):
+            items = postprocess.decode_timestamps(inp.words, r.tolist())
+            out.append((r, items) if not (want_logits or want_normed) else (r, items, extra))
+        return out
+
+    def align_inputs(self, samples_list, inputs, want_logits=False, want_normed=False):
+        """The device-resident batched call on prebuilt inputs: [(raw_ms, extra)]."""
+        n = len(inputs)
+        L = _lib.lib()
+        clips = (_lib.QaClip * n)()
+        res = (_lib.QaResult * n)()
+        keep, outs = [], []
+        for i, (s, inp) in enumerate(zip(samples_list, inputs)):
+            s = np.ascontiguousarray(s, np.float32)
+            ids = np.ascontiguousarray(inp.input_ids, np.uint32)
+            n_ts = len(inp.timestamp_positions)
+            raw = np.zeros(n_ts, np.int64)
+            lg = np.zeros((n_ts, self.cfg.num_labels), np.float32) if want_logits else None
+            nm = np.zeros((n_ts, self.cfg.hidden_size), np.float32) if want_normed else None
+            keep += [s, ids]
+            clips[i].samples = s.ctypes.data
+            clips[i].n_samples = len(s)
+            clips[i].input_ids = ids.ctypes.data
+            clips[i].seq_len = len(ids)
+            res[i].raw_ms = raw.ctypes.data
+            res[i].n_ts = n_ts
+            res[i].logits = lg.ctypes.data if lg is not None else None
+            res[i].normed = nm.ctypes.data if nm is not None else None
+            outs.append((raw, {"logits": lg, "normed": nm}))
+        self._check(L.qa_align_batch(self._ctx, ctypes.addressof(clips), n, ctypes.addressof(res)))
+        t = _lib.QaTimings()
+        L.qa_get_timings(self._ctx, ctypes.byref(t))
+        self.timings = {k: getattr(t, k) for k, _ in _lib.QaTimings._fields_}
+        return outs
+
+    # ------------------------------------------------------------ stages
+
+    def mel(self, samples: np.ndarray) -> np.ndarray:
+        """mel::mel_features: [128, n/160] f32."""
+        s = np.ascontiguousarray(samples, np.float32)
+        frames = len(s) // 160
+        out = np.zeros((128, max(frames, 1)), np.float32)
+        nf = ctypes.c_int(0)
+        self._check(_lib.lib().qa_mel(self._ctx, s.ctypes.data, len(s), out.ctypes.data,
+                                      out.size, ctypes.byref(nf)))
+        return out[:, :nf.value] if nf.value != out.shape[1] else out
+
+    def audio_embeds(self, mel: np.ndarray) -> np.ndarray:
+        """Backend::audio_embeds: [128, valid] -> [n_audio, 1024] 16-bit bits (uint16)."""
+        mel = np.ascontiguousarray(mel, np.float32)
+        valid = mel.shape[1]
+        na = synth.audio_token_count(valid, self.cfg.n_window)
+        out = np.zeros((na, self.cfg.output_dim), np.uint16)
+        self._check(_lib.lib().qa_audio_embeds(self._ctx, mel.ctypes.data, mel.shape[0], valid,
+                                               out.ctypes.data, out.size))
+        return out
+
+    def ensure_capacity(self, need: int) -> int:
+        cap = ctypes.c_int(0)
+        self._check(_lib.lib().qa_ensure_capacity(self._ctx, int(need), ctypes.byref(cap)))
+        return cap.value
+
+    def text_hidden(self, emb_bits: np.ndarray) -> np.ndarray:
+        """Backend::text_hidden: [seq, 1024] 16-bit bits -> [seq, 1024] f32."""
+        e = np.ascontiguousarray(emb_bits, np.uint16)
+        out = np.zeros((e.shape[0], self.cfg.hidden_size), np.float32)
+        self._check(_lib.lib().qa_text_hidden(self._ctx, e.ctypes.data, e.shape[0],
+                                              out.ctypes.data))
+        return out
+
+    def head(self, hidden: np.ndarray, rows, want_logits=True, want_normed=False):
+        """Final norm + timestamp head + argmax on `rows` of f32 `hidden`."""
+        h = np.ascontiguousarray(hidden, np.float32)
+        r = np.ascontiguousarray(rows, np.int32)
+        raw = np.zeros(len(r), np.int64)
+        lg = np.zeros((len(r), self.cfg.num_labels), np.float32) if want_logits else None
+        nm = np.zeros((len(r), self.cfg.hidden_size), np.float32) if want_normed else None
+        self._check(_lib.lib().qa_head(self._ctx, h.ctypes.data, h.shape[0], r.ctypes.data,
+                                       len(r), raw.ctypes.data,
+                                       lg.ctypes.data if lg is not None else None,
+                                       nm.ctypes.data if nm is not None else None))
+        return raw, lg, nm

@@ -1,0 +1,117 @@
+// Launchers of the non-GEMM kernels on the alignment path.  Every launcher
+// returns 0 or a cudaError_t value; `bf16` selects the 16-bit storage type
+// (f16 when false).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace qa {
+
+// ---------------------------------------------------------------- (a) mel
+// Per-clip geometry of a batched mel pass.
+struct MelClip {
+  long long sample_off;  // first sample of the clip in the sample buffer
+  int n_samples;
+  int frame_off;         // first frame of the clip in the frame-major scratch
+  int n_frames;          // n_samples / 160
+  int chunk_off;         // first 100-frame chunk of the clip in the chunked output
+};
+
+// Filterbank in compact form: for mel m, weights w[start[m] .. start[m]+len[m]).
+struct MelBank {
+  const int* start;
+  const int* len;
+  const int* woff;  // offset of mel m's weights in w
+  const float* w;
+};
+
+// Pass 1: log10 mel power of every frame -> scratch [total_frames][128] and
+// per-clip running max (ordered-uint encoding) in maxkey[clip].
+int mel_logpower(const float* samples, const MelClip* clips, int n_clips, int max_frames,
+                 const float* window, const float2* twiddle, MelBank bank, float log10_factor,
+                 float* scratch, unsigned* maxkey, cudaStream_t s);
+// Pass 2a: clamp at max - 8 and (x + 4) / 4 into the chunked encoder input
+// [chunk][128][chunk_frames] (tail zero padded).
+int mel_finalize_chunked(const float* scratch, const MelClip* clips, const int* chunk_clip,
+                         int total_chunks, int chunk_frames, const unsigned* maxkey, float* chunked,
+                         cudaStream_t s);
+// Pass 2b: the same values in the reference's [128][frames] layout (one clip).
+int mel_finalize_rows(const float* scratch, int n_frames, const unsigned* maxkey, float* out,
+                      cudaStream_t s);
+
+// ---------------------------------------------------------------- (b) audio tower
+// conv1: chunked mel [n][h][w] f32 (c_in = 1) -> NHWC [n][ho][wo][c_out] 16-bit,
+// gelu(w·x + b).  w [c_out][9] f32 (k = kh*3 + kw).
+int conv1_direct(const float* mel, int n, int h, int w, const float* wt, const float* bias,
+                 int c_out, void* out, bool bf16, cudaStream_t s);
+// im2col for a 3x3 / stride 2 / pad 1 conv over NHWC [n][h][w][c] 16-bit:
+// cols [n*ho*wo][9*c] with k = (kh*3 + kw)*c + ic.  Positions are ordered
+// (oh, ow) when !time_major, (ow, oh) when time_major.
+int im2col_3x3s2(const void* x, int n, int h, int w, int c, void* cols, bool time_major,
+                 cudaStream_t s);
+// LayerNorm (eps) over rows of f32 x [rows][d] -> 16-bit out.
+int layernorm_rows(const float* x, int rows, int d, const float* g, const float* b, float eps,
+                   void* out, bool bf16, cudaStream_t s);
+// Windowed self-attention over packed audio tokens.  qkv [T][3*dm] 16-bit
+// (q | k | v, head h at columns h*hd), out [T][dm].  Windows are given as
+// (start, len) pairs, len <= 128.
+int window_attention(const void* qkv, int dm, int nh, int hd, const int2* windows, int n_windows,
+                     void* out, bool bf16, cudaStream_t s);
+
+// ---------------------------------------------------------------- decoder
+// RMSNorm over rows of 16-bit x [rows][d] -> 16-bit out, f16(x*inv*w).
+int rmsnorm_rows(const void* x, int rows, int d, const float* w, float eps, void* out, bool bf16,
+                 cudaStream_t s);
+
+// Geometry of the paged K/V cache of one layer: [pages][nkv][page][hd].
+struct PagedKV {
+  void* k;
+  void* v;
+  int page_size;  // tokens per page (64)
+};
+
+// Per-token position bookkeeping for packed variable-length clips.
+struct TokenMap {
+  const int* clip_of;   // [T] clip index
+  const int* pos_of;    // [T] position within the clip
+  const int* block_tab; // [clips][max_pages] page ids
+  int max_pages;
+};
+
+// (d) q/k RMSNorm + rotate-half RoPE, Q written in place into qkv's q part,
+// K (normed+roped) and V appended into the paged cache.
+int qk_norm_rope_append(void* qkv, int T, int nqh, int nkvh, int hd, const float* qn,
+                        const float* kn, float eps, const float* cos_t, const float* sin_t,
+                        TokenMap tm, PagedKV kv, bool bf16, cudaStream_t s);
+
+// (e) causal GQA flash attention.  Q rows in qkv (row stride ldq, head h at
+// column h*hd), K/V from the paged cache, out [T][nqh*hd].  Work items are
+// (clip, q0) tiles of 64 queries.
+struct AttnTile {
+  int clip;
+  int q0;       // first query position of the tile within the clip
+  int tok0;     // packed token index of position 0 of the clip
+  int len;      // clip length
+};
+int causal_attention(const void* qkv, long long ldq, int nqh, int nkvh, int hd,
+                     const AttnTile* tiles, int n_tiles, const int* block_tab, int max_pages,
+                     PagedKV kv, void* out, bool bf16, cudaStream_t s);
+
+// Embedding gather: rows of the device table for every non-audio token.
+int embed_gather(const uint32_t* ids, int T, const void* table, int vocab, int d, int audio_id,
+                 void* out, int* bad, cudaStream_t s);
+
+// (f) timestamp rows: folded final RMSNorm -> [hi | lo] bf16 split (A operand
+// of the head GEMM); optional unfolded norm rows (f32).
+// hidden_kind: 0 = f16, 1 = bf16, 2 = f32 rows.
+int head_gather_norm(const void* hidden, int hidden_kind, const int* rows, int n_rows, int d,
+                     const float* w, float eps, void* a_hilo, float* unfolded, cudaStream_t s);
+// keys -> raw_ms = (int64)(argmax * segment_ms)
+int argmax_finalize(const unsigned long long* keys, int n, double segment_ms, long long* raw_ms,
+                    cudaStream_t s);
+
+// 16-bit [rows][d] -> f32 widening (text_hidden readback).
+int widen16(const void* x, long long n, float* out, bool bf16, cudaStream_t s);
+
+}  // namespace qa

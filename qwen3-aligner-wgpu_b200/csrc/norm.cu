@@ -1,0 +1,325 @@
+// HBM-bound row kernels of the alignment path: the audio tower's LayerNorm,
+// the decoder's RMSNorm, (d) q/k RMSNorm + RoPE + paged K/V append, the
+// embedding gather, and (f) the timestamp-row gather + final norm.
+//
+// One warp per row (or per (token, head)); 16-bit rows are read as 16-byte
+// vectors.  Arithmetic follows the reference's CPU order where it decides a
+// rounding: products and sums that the reference writes as separate f32
+// operations use __fmul_rn/__fadd_rn so nvcc cannot contract them into FMAs.
+#include "kernels.cuh"
+#include "sm100.cuh"
+
+namespace qa {
+
+namespace {
+
+__device__ __forceinline__ float to_f32(float x) { return x; }
+__device__ __forceinline__ float to_f32(__half x) { return __half2float(x); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+
+// ---------------------------------------------------------------- LayerNorm
+// CpuAudioLayerNorm::forward (src/audio_encoder.rs:170-191), eps 1e-5.
+template <typename T>
+__global__ void layernorm_kernel(const float* __restrict__ x, int rows, int d,
+                                 const float* __restrict__ g, const float* __restrict__ b,
+                                 float eps, T* __restrict__ out) {
+  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* xr = x + static_cast<long long>(row) * d;
+  float v[32];
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < 32; ++k) {
+    const int i = lane + 32 * k;
+    v[k] = i < d ? xr[i] : 0.f;
+    s += v[k];
+  }
+  const float mean = warp_sum(s) / static_cast<float>(d);
+  float q = 0.f;
+#pragma unroll
+  for (int k = 0; k < 32; ++k) {
+    const int i = lane + 32 * k;
+    if (i < d) {
+      const float t = v[k] - mean;
+      q = fmaf(t, t, q);
+    }
+  }
+  const float var = warp_sum(q) / static_cast<float>(d);
+  const float inv = 1.0f / sqrtf(var + eps);
+  T* o = out + static_cast<long long>(row) * d;
+#pragma unroll
+  for (int k = 0; k < 32; ++k) {
+    const int i = lane + 32 * k;
+    if (i < d) o[i] = f2h<T>(__fadd_rn(__fmul_rn(__fmul_rn(v[k] - mean, inv), g[i]), b[i]));
+  }
+}
+
+// ---------------------------------------------------------------- RMSNorm
+// rms_norm_row (src/cpu_decoder.rs:289-300): f16(x * inv * w), d % 256 == 0.
+template <typename T>
+__global__ void rmsnorm_kernel(const T* __restrict__ x, int rows, int d,
+                               const float* __restrict__ w, float eps, T* __restrict__ out) {
+  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<long long>(row) * d);
+  const int nv = d / 8;  // 16-byte vectors per row
+  float v[32];
+  float s2 = 0.f;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int vi = lane + 32 * k;
+    if (vi < nv) {
+      uint4 u = xr[vi];
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[k * 8 + j] = h2f<T>(e[j]);
+        s2 = fmaf(v[k * 8 + j], v[k * 8 + j], s2);
+      }
+    }
+  }
+  const float inv = 1.0f / sqrtf(warp_sum(s2) / static_cast<float>(d) + eps);
+  uint4* orow = reinterpret_cast<uint4*>(out + static_cast<long long>(row) * d);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int vi = lane + 32 * k;
+    if (vi < nv) {
+      alignas(16) T e[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) e[j] = f2h<T>(__fmul_rn(__fmul_rn(v[k * 8 + j], inv), w[vi * 8 + j]));
+      orow[vi] = *reinterpret_cast<const uint4*>(e);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- (d) q/k norm + rope + append
+// norm_rope_head (src/cpu_decoder.rs:305-321) for every q and k head of every
+// token, hd == 128: lane l holds dims 4l..4l+3, whose rotate-half partners
+// (j +- 64) sit in lane l ^ 16.  V rows are copied into the cache unchanged.
+template <typename T>
+__global__ void qk_norm_rope_kernel(T* __restrict__ qkv, int T_, int nqh, int nkvh,
+                                    const float* __restrict__ qn, const float* __restrict__ kn,
+                                    float eps, const float* __restrict__ cos_t,
+                                    const float* __restrict__ sin_t, TokenMap tm, PagedKV kv) {
+  constexpr int HD = 128;
+  const int nh = nqh + nkvh;
+  const long long item = blockIdx.x * static_cast<long long>(blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (item >= static_cast<long long>(T_) * nh) return;
+  const int t = static_cast<int>(item / nh);
+  const int hh = static_cast<int>(item % nh);
+  const long long ldq = static_cast<long long>(nqh + 2 * nkvh) * HD;
+  const int pos = tm.pos_of[t];
+  const bool is_q = hh < nqh;
+  T* src = qkv + t * ldq + static_cast<long long>(hh) * HD;  // k heads follow q heads
+  const float* nw = is_q ? qn : kn;
+
+  // 4 raw values
+  uint2 u = *reinterpret_cast<const uint2*>(src + 4 * lane);
+  const T* e = reinterpret_cast<const T*>(&u);
+  float r[4];
+  float s2 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    r[j] = h2f<T>(e[j]);
+    s2 = fmaf(r[j], r[j], s2);
+  }
+  const float inv = 1.0f / sqrtf(warp_sum(s2) / static_cast<float>(HD) + eps);
+  const bool lo = lane < 16;  // dims < 64: partner is j + 64, sign -1
+  alignas(8) T o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int dim = 4 * lane + j;
+    const int pdim = lo ? dim + 64 : dim - 64;
+    const float rp = __shfl_xor_sync(0xFFFFFFFFu, r[j], 16);
+    const float xj = __fmul_rn(__fmul_rn(r[j], inv), nw[dim]);
+    const float xp = __fmul_rn(__fmul_rn(rp, inv), nw[pdim]);
+    const float c = cos_t[pos * 64 + (dim & 63)];
+    const float sn = sin_t[pos * 64 + (dim & 63)];
+    const float sxp = lo ? -xp : xp;
+    o[j] = f2h<T>(__fadd_rn(__fmul_rn(xj, c), __fmul_rn(sxp, sn)));
+  }
+  if (is_q) {
+    *reinterpret_cast<uint2*>(src + 4 * lane) = *reinterpret_cast<const uint2*>(o);
+    return;
+  }
+  const int kh = hh - nqh;
+  const int clip = tm.clip_of[t];
+  const int page = tm.block_tab[clip * tm.max_pages + pos / kv.page_size];
+  const long long off =
+      ((static_cast<long long>(page) * nkvh + kh) * kv.page_size + pos % kv.page_size) * HD;
+  *reinterpret_cast<uint2*>(static_cast<T*>(kv.k) + off + 4 * lane) =
+      *reinterpret_cast<const uint2*>(o);
+  const T* vsrc = qkv + t * ldq + static_cast<long long>(nqh + nkvh + kh) * HD;
+  *reinterpret_cast<uint2*>(static_cast<T*>(kv.v) + off + 4 * lane) =
+      *reinterpret_cast<const uint2*>(vsrc + 4 * lane);
+}
+
+// ---------------------------------------------------------------- embedding gather
+// src/align_inference.rs:690-715, on the device: one thread per 16 bytes.
+__global__ void embed_gather_kernel(const uint32_t* __restrict__ ids, int T_,
+                                    const uint4* __restrict__ table, int vocab, int dv,
+                                    int audio_id, uint4* __restrict__ out, int* bad) {
+  const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (i >= static_cast<long long>(T_) * dv) return;
+  const int t = static_cast<int>(i / dv);
+  const int v = static_cast<int>(i % dv);
+  const uint32_t id = ids[t];
+  if (static_cast<int>(id) == audio_id) return;  // filled by the projector's scatter
+  if (id >= static_cast<uint32_t>(vocab)) {
+    if (v == 0) atomicExch(bad, 1);
+    return;
+  }
+  out[i] = table[static_cast<long long>(id) * dv + v];
+}
+
+// ---------------------------------------------------------------- (f) head rows
+// src/align_inference.rs:766-783 (folded) and :748-765 (unfolded): one warp per row.
+template <typename T>
+__global__ void head_norm_kernel(const T* __restrict__ hidden, const int* __restrict__ rows,
+                                 int n_rows, int d, const float* __restrict__ w, float eps,
+                                 __nv_bfloat16* __restrict__ a, float* __restrict__ unfolded) {
+  const int r = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (r >= n_rows) return;
+  const T* x = hidden + static_cast<long long>(rows[r]) * d;
+  float v[32];
+  float acc = 0.f, a2 = 0.f;
+#pragma unroll
+  for (int k = 0; k < 32; ++k) {
+    const int i = lane + 32 * k;
+    v[k] = i < d ? to_f32(x[i]) : 0.f;
+    const float xf = i < d ? __fmul_rn(v[k], w[i]) : 0.f;
+    acc = fmaf(xf, xf, acc);
+    a2 = fmaf(v[k], v[k], a2);
+  }
+  const float inv = 1.0f / sqrtf(warp_sum(acc) / static_cast<float>(d) + eps);
+  const float inv2 = 1.0f / sqrtf(warp_sum(a2) / static_cast<float>(d) + eps);
+  __nv_bfloat16* ar = a + static_cast<long long>(r) * 2 * d;
+#pragma unroll
+  for (int k = 0; k < 32; ++k) {
+    const int i = lane + 32 * k;
+    if (i < d) {
+      const float nrm = __fmul_rn(__fmul_rn(v[k], w[i]), inv);
+      const __nv_bfloat16 hi = __float2bfloat16_rn(nrm);
+      ar[i] = hi;
+      ar[d + i] = __float2bfloat16_rn(nrm - __bfloat162float(hi));
+      if (unfolded) unfolded[static_cast<long long>(r) * d + i] = __fmul_rn(__fmul_rn(v[k], inv2), w[i]);
+    }
+  }
+}
+
+__global__ void argmax_finalize_kernel(const unsigned long long* __restrict__ keys, int n,
+                                       double seg_ms, long long* __restrict__ raw) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const unsigned long long k = keys[i];
+  const long long idx = k == 0ull ? 0 : static_cast<long long>(0xFFFFFFFFull - (k & 0xFFFFFFFFull));
+  raw[i] = static_cast<long long>(static_cast<double>(idx) * seg_ms);
+}
+
+template <typename T>
+__global__ void widen_kernel(const T* __restrict__ x, long long n, float* __restrict__ out) {
+  const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (i < n) out[i] = h2f<T>(x[i]);
+}
+
+}  // namespace
+
+int layernorm_rows(const float* x, int rows, int d, const float* g, const float* b, float eps,
+                   void* out, bool bf16, cudaStream_t s) {
+  if (rows <= 0) return 0;
+  if (d > 1024) return (int)cudaErrorInvalidValue;
+  const unsigned blocks = (rows + 7) / 8;
+  if (bf16)
+    layernorm_kernel<<<blocks, 256, 0, s>>>(x, rows, d, g, b, eps, static_cast<__nv_bfloat16*>(out));
+  else
+    layernorm_kernel<<<blocks, 256, 0, s>>>(x, rows, d, g, b, eps, static_cast<__half*>(out));
+  return (int)cudaGetLastError();
+}
+
+int rmsnorm_rows(const void* x, int rows, int d, const float* w, float eps, void* out, bool bf16,
+                 cudaStream_t s) {
+  if (rows <= 0) return 0;
+  if (d % 8 || d > 1024) return (int)cudaErrorInvalidValue;
+  const unsigned blocks = (rows + 7) / 8;
+  if (bf16)
+    rmsnorm_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), rows, d, w, eps,
+                                          static_cast<__nv_bfloat16*>(out));
+  else
+    rmsnorm_kernel<<<blocks, 256, 0, s>>>(static_cast<const __half*>(x), rows, d, w, eps,
+                                          static_cast<__half*>(out));
+  return (int)cudaGetLastError();
+}
+
+int qk_norm_rope_append(void* qkv, int T_, int nqh, int nkvh, int hd, const float* qn,
+                        const float* kn, float eps, const float* cos_t, const float* sin_t,
+                        TokenMap tm, PagedKV kv, bool bf16, cudaStream_t s) {
+  if (T_ <= 0) return 0;
+  if (hd != 128) return (int)cudaErrorInvalidValue;
+  const long long items = static_cast<long long>(T_) * (nqh + nkvh);
+  const unsigned blocks = (unsigned)((items + 7) / 8);
+  if (bf16)
+    qk_norm_rope_kernel<<<blocks, 256, 0, s>>>(static_cast<__nv_bfloat16*>(qkv), T_, nqh, nkvh, qn,
+                                               kn, eps, cos_t, sin_t, tm, kv);
+  else
+    qk_norm_rope_kernel<<<blocks, 256, 0, s>>>(static_cast<__half*>(qkv), T_, nqh, nkvh, qn, kn,
+                                               eps, cos_t, sin_t, tm, kv);
+  return (int)cudaGetLastError();
+}
+
+int embed_gather(const uint32_t* ids, int T_, const void* table, int vocab, int d, int audio_id,
+                 void* out, int* bad, cudaStream_t s) {
+  if (T_ <= 0) return 0;
+  if (d % 8) return (int)cudaErrorInvalidValue;
+  const int dv = d / 8;
+  const long long total = static_cast<long long>(T_) * dv;
+  embed_gather_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(
+      ids, T_, static_cast<const uint4*>(table), vocab, dv, audio_id, static_cast<uint4*>(out), bad);
+  return (int)cudaGetLastError();
+}
+
+int head_gather_norm(const void* hidden, int hidden_kind, const int* rows, int n_rows, int d,
+                     const float* w, float eps, void* a_hilo, float* unfolded, cudaStream_t s) {
+  if (n_rows <= 0) return 0;
+  if (d > 1024) return (int)cudaErrorInvalidValue;
+  const unsigned blocks = (n_rows + 7) / 8;
+  auto* a = static_cast<__nv_bfloat16*>(a_hilo);
+  if (hidden_kind == 1)
+    head_norm_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(hidden), rows, n_rows,
+                                            d, w, eps, a, unfolded);
+  else if (hidden_kind == 2)
+    head_norm_kernel<<<blocks, 256, 0, s>>>(static_cast<const float*>(hidden), rows, n_rows, d, w,
+                                            eps, a, unfolded);
+  else
+    head_norm_kernel<<<blocks, 256, 0, s>>>(static_cast<const __half*>(hidden), rows, n_rows, d, w,
+                                            eps, a, unfolded);
+  return (int)cudaGetLastError();
+}
+
+int argmax_finalize(const unsigned long long* keys, int n, double segment_ms, long long* raw_ms,
+                    cudaStream_t s) {
+  if (n <= 0) return 0;
+  argmax_finalize_kernel<<<(n + 255) / 256, 256, 0, s>>>(keys, n, segment_ms, raw_ms);
+  return (int)cudaGetLastError();
+}
+
+int widen16(const void* x, long long n, float* out, bool bf16, cudaStream_t s) {
+  if (n <= 0) return 0;
+  const unsigned blocks = (unsigned)((n + 255) / 256);
+  if (bf16)
+    widen_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), n, out);
+  else
+    widen_kernel<<<blocks, 256, 0, s>>>(static_cast<const __half*>(x), n, out);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace qa

@@ -1,0 +1,1300 @@
+// Host runtime behind include/qa_b200.h: context lifetime, weight upload
+// (with the layout transforms the kernels want), grow-only workspaces, the
+// single-clip stage calls that mirror the reference's tower boundary, and the
+// batched device-resident alignment path.
+#include "runtime.h"
+#include "sm100.cuh"
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <numeric>
+#include <thread>
+
+using namespace qa;
+
+namespace {
+
+// ------------------------------------------------------------ errors
+
+int fail(qa_ctx* ctx, int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  std::vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  if (ctx) ctx->err = buf;
+  return code;
+}
+
+#define CK(expr)                                                                              \
+  do {                                                                                        \
+    cudaError_t e_ = (expr);                                                                  \
+    if (e_ != cudaSuccess)                                                                    \
+      return fail(ctx, e_ == cudaErrorMemoryAllocation ? QA_ERR_OOM : QA_ERR_CUDA,            \
+                  "%s: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__, __LINE__);       \
+  } while (0)
+
+#define KL(expr)                                                                              \
+  do {                                                                                        \
+    int e_ = (expr);                                                                          \
+    ++ctx->launches;                                                                          \
+    if (e_)                                                                                   \
+      return fail(ctx, QA_ERR_CUDA, "%s: %s (%s:%d)", #expr,                                  \
+                  cudaGetErrorString(static_cast<cudaError_t>(e_)), __FILE__, __LINE__);      \
+  } while (0)
+
+#define TRY(expr)            \
+  do {                       \
+    int r_ = (expr);         \
+    if (r_) return r_;       \
+  } while (0)
+
+// Run f(i) for i in [0, n) on all host cores (weight conversion at load).
+template <typename F>
+void parallel_for(int64_t n, F f) {
+  const int64_t nt = std::max<int64_t>(1, std::min<int64_t>(std::thread::hardware_concurrency(), n / 65536));
+  if (nt <= 1) {
+    for (int64_t i = 0; i < n; ++i) f(i);
+    return;
+  }
+  std::vector<std::thread> th;
+  for (int64_t t = 0; t < nt; ++t)
+    th.emplace_back([=, &f] {
+      const int64_t a = n * t / nt, b = n * (t + 1) / nt;
+      for (int64_t i = a; i < b; ++i) f(i);
+    });
+  for (auto& x : th) x.join();
+}
+
+// ------------------------------------------------------------ 16-bit host conversions
+
+uint16_t f32_to_f16(float x) {
+  uint32_t u;
+  std::memcpy(&u, &x, 4);
+  const uint32_t sign = (u >> 16) & 0x8000u;
+  const uint32_t a = u & 0x7FFFFFFFu;
+  if (a >= 0x7F800000u) return static_cast<uint16_t>(sign | (a == 0x7F800000u ? 0x7C00u : 0x7E00u));
+  if (a >= 0x477FF000u) return static_cast<uint16_t>(sign | 0x7C00u);
+  if (a < 0x38800000u) {
+    if (a < 0x33000000u) return static_cast<uint16_t>(sign);
+    const uint32_t e = a >> 23, m = (a & 0x7FFFFFu) | 0x800000u, sh = 126 - e;
+    uint32_t r = m >> sh;
+    const uint32_t rem = m & ((1u << sh) - 1u), hf = 1u << (sh - 1);
+    if (rem > hf || (rem == hf && (r & 1u))) ++r;
+    return static_cast<uint16_t>(sign | r);
+  }
+  uint32_t r = (a >> 13) - ((127u - 15u) << 10);
+  const uint32_t rem = a & 0x1FFFu;
+  if (rem > 0x1000u || (rem == 0x1000u && (r & 1u))) ++r;
+  return static_cast<uint16_t>(sign | r);
+}
+
+float f16_to_f32(uint16_t h) {
+  const uint32_t sign = static_cast<uint32_t>(h & 0x8000u) << 16;
+  const uint32_t e = (h >> 10) & 0x1Fu;
+  uint32_t m = h & 0x3FFu, u;
+  if (e == 0) {
+    if (m == 0) {
+      u = sign;
+    } else {
+      int ee = -1;
+      do {
+        ++ee;
+        m <<= 1;
+      } while (!(m & 0x400u));
+      u = sign | ((127u - 15u - ee) << 23) | ((m & 0x3FFu) << 13);
+    }
+  } else if (e == 31) {
+    u = sign | 0x7F800000u | (m << 13);
+  } else {
+    u = sign | ((e + 112u) << 23) | (m << 13);
+  }
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+
+uint16_t f32_to_bf16(float x) {
+  uint32_t u;
+  std::memcpy(&u, &x, 4);
+  if ((u & 0x7FFFFFFFu) > 0x7F800000u) return static_cast<uint16_t>((u >> 16) | 0x40u);
+  return static_cast<uint16_t>((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+}
+
+float bf16_to_f32(uint16_t h) {
+  const uint32_t u = static_cast<uint32_t>(h) << 16;
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+
+uint16_t to_half_bits(float x, bool bf16) { return bf16 ? f32_to_bf16(x) : f32_to_f16(x); }
+float round_half(float x, bool bf16) {
+  return bf16 ? bf16_to_f32(f32_to_bf16(x)) : f16_to_f32(f32_to_f16(x));
+}
+
+// ------------------------------------------------------------ workspace
+
+int ensure(qa_ctx* ctx, DevBuf& b, size_t bytes) {
+  if (bytes <= b.cap) return QA_OK;
+  if (b.p) cudaFree(b.p);
+  b.p = nullptr;
+  b.cap = 0;
+  const size_t want = std::max<size_t>(bytes + bytes / 8, 256);
+  CK(cudaMalloc(&b.p, want));
+  b.cap = want;
+  return QA_OK;
+}
+
+int ensure_pin(qa_ctx* ctx, PinBuf& b, size_t bytes) {
+  if (bytes <= b.cap) return QA_OK;
+  if (b.p) cudaFreeHost(b.p);
+  b.p = nullptr;
+  b.cap = 0;
+  const size_t want = std::max<size_t>(bytes + bytes / 8, 4096);
+  CK(cudaMallocHost(&b.p, want));
+  b.cap = want;
+  return QA_OK;
+}
+
+// Bounded wait for everything queued on the context's stream.
+int wait_stream(qa_ctx* ctx) {
+  cudaEvent_t e = ctx->ev[9];
+  CK(cudaEventRecord(e, ctx->stream));
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t q = cudaEventQuery(e);
+    if (q == cudaSuccess) break;
+    if (q != cudaErrorNotReady)
+      return fail(ctx, QA_ERR_CUDA, "device error: %s", cudaGetErrorString(q));
+    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                        std::chrono::steady_clock::now() - t0)
+                        .count();
+    if (ms > ctx->timeout_ms)
+      return fail(ctx, QA_ERR_TIMEOUT, "device did not finish within %d ms", ctx->timeout_ms);
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+  return QA_OK;
+}
+
+int check_status(qa_ctx* ctx) {
+  unsigned st = 0;
+  int bad = 0;
+  CK(cudaMemcpy(&st, ctx->status.p, sizeof st, cudaMemcpyDeviceToHost));
+  CK(cudaMemcpy(&bad, ctx->badflag.p, sizeof bad, cudaMemcpyDeviceToHost));
+  if (st & kStatusTimeout)
+    return fail(ctx, QA_ERR_TIMEOUT, "a tensor-core pipeline wait ran out (status %u)", st);
+  if (bad) return fail(ctx, QA_ERR_SHAPE, "a token id is outside the vocabulary");
+  return QA_OK;
+}
+
+// ------------------------------------------------------------ weights
+
+struct HostT {
+  int dtype = 0;
+  std::vector<int64_t> shape;
+  const void* data = nullptr;
+  int64_t numel() const {
+    int64_t n = 1;
+    for (auto s : shape) n *= s;
+    return n;
+  }
+};
+
+// src/weights.rs:231-265
+std::string remap(const std::string& n) {
+  auto starts = [&](const char* p) { return n.rfind(p, 0) == 0; };
+  if (starts("model.multi_modal_projector.linear_1"))
+    return "thinker.audio_tower.proj1" + n.substr(std::strlen("model.multi_modal_projector.linear_1"));
+  if (starts("model.multi_modal_projector.linear_2"))
+    return "thinker.audio_tower.proj2" + n.substr(std::strlen("model.multi_modal_projector.linear_2"));
+  if (starts("model.audio_tower.")) return "thinker.audio_tower." + n.substr(18);
+  if (starts("model.language_model.")) return "thinker.model." + n.substr(21);
+  if (starts("thinker.lm_head.")) return "score." + n.substr(16);
+  return n;
+}
+
+struct Loader {
+  qa_ctx* ctx;
+  std::map<std::string, HostT> t;
+  std::string missing;
+
+  const HostT* get(const std::string& name, std::vector<int64_t> shape) {
+    auto it = t.find(name);
+    if (it == t.end()) {
+      if (missing.empty()) missing = "weight not found: " + name;
+      return nullptr;
+    }
+    if (!shape.empty() && it->second.shape != shape) {
+      if (missing.empty()) {
+        missing = "weight " + name + " has shape [";
+        for (auto s : it->second.shape) missing += std::to_string(s) + ",";
+        missing += "], expected [";
+        for (auto s : shape) missing += std::to_string(s) + ",";
+        missing += "]";
+      }
+      return nullptr;
+    }
+    return &it->second;
+  }
+  bool has(const std::string& name) const { return t.count(name) != 0; }
+  static float elem(const HostT& v, int64_t i) {
+    switch (v.dtype) {
+      case QA_DTYPE_F32: return static_cast<const float*>(v.data)[i];
+      case QA_DTYPE_F16: return f16_to_f32(static_cast<const uint16_t*>(v.data)[i]);
+      default: return bf16_to_f32(static_cast<const uint16_t*>(v.data)[i]);
+    }
+  }
+  std::vector<float> f32(const std::string& name, std::vector<int64_t> shape) {
+    const HostT* v = get(name, shape);
+    if (!v) return {};
+    std::vector<float> o(v->numel());
+    parallel_for(v->numel(), [&](int64_t i) { o[i] = elem(*v, i); });
+    return o;
+  }
+  std::vector<float> f32_or_zero(const std::string& name, int64_t n) {
+    if (!has(name)) return std::vector<float>(n, 0.0f);
+    return f32(name, {n});
+  }
+};
+
+template <typename T>
+T* upload(qa_ctx* ctx, const void* host, size_t bytes, int* rc) {
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, std::max<size_t>(bytes, 16));
+  if (e != cudaSuccess) {
+    *rc = fail(ctx, QA_ERR_OOM, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+    return nullptr;
+  }
+  ctx->allocations.push_back(p);
+  e = cudaMemcpy(p, host, bytes, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    *rc = fail(ctx, QA_ERR_CUDA, "cudaMemcpy: %s", cudaGetErrorString(e));
+    return nullptr;
+  }
+  return static_cast<T*>(p);
+}
+
+float* up_f32(qa_ctx* ctx, const std::vector<float>& v, int* rc) {
+  return upload<float>(ctx, v.data(), v.size() * 4, rc);
+}
+
+void* up_h16(qa_ctx* ctx, const std::vector<float>& v, int* rc) {
+  std::vector<uint16_t> b(v.size());
+  const bool bf = ctx->bf16;
+  parallel_for(static_cast<int64_t>(v.size()), [&](int64_t i) { b[i] = to_half_bits(v[i], bf); });
+  return upload<void>(ctx, b.data(), b.size() * 2, rc);
+}
+
+std::vector<float> rounded(std::vector<float> v, bool bf16) {
+  for (auto& x : v) x = round_half(x, bf16);
+  return v;
+}
+
+// src/mel.rs:101-164 filterbank (f64 build, f32 weights) in compact form.
+void mel_bank(std::vector<int>& start, std::vector<int>& len, std::vector<int>& woff,
+              std::vector<float>& w) {
+  const int num_mels = 128, n_fft = 400, n_freqs = 201;
+  const double sr = 16000.0, f_sp = 200.0 / 3.0, min_log_hz = 1000.0;
+  const double min_log_mel = min_log_hz / f_sp, logstep = std::log(6.4) / 27.0;
+  auto hz_to_mel = [&](double f) {
+    return f < min_log_hz ? f / f_sp : min_log_mel + std::log(f / min_log_hz) / logstep;
+  };
+  auto mel_to_hz = [&](double m) {
+    return m < min_log_mel ? f_sp * m : min_log_hz * std::exp(logstep * (m - min_log_mel));
+  };
+  const double mmin = hz_to_mel(0.0), mmax = hz_to_mel(sr / 2.0);
+  std::vector<double> ff(num_mels + 2), fd(num_mels + 1);
+  for (int i = 0; i < num_mels + 2; ++i)
+    ff[i] = mel_to_hz(mmin + (mmax - mmin) * i / static_cast<double>(num_mels + 1));
+  for (int i = 0; i < num_mels + 1; ++i) fd[i] = ff[i + 1] - ff[i];
+  start.assign(num_mels, 0);
+  len.assign(num_mels, 0);
+  woff.assign(num_mels, 0);
+  w.clear();
+  for (int i = 0; i < num_mels; ++i) {
+    const double enorm = 2.0 / (ff[i + 2] - ff[i]);
+    std::vector<float> row(n_freqs);
+    for (int j = 0; j < n_freqs; ++j) {
+      const double f = j * sr / n_fft;
+      const double down = (f - ff[i]) / fd[i], up = (ff[i + 2] - f) / fd[i + 1];
+      row[j] = static_cast<float>(std::max(std::min(down, up), 0.0));
+      row[j] *= static_cast<float>(enorm);
+    }
+    int a = 0, b = n_freqs - 1;
+    while (a < n_freqs && row[a] == 0.0f) ++a;
+    while (b >= a && row[b] == 0.0f) --b;
+    start[i] = a < n_freqs ? a : 0;
+    len[i] = a < n_freqs ? b - a + 1 : 0;
+    woff[i] = static_cast<int>(w.size());
+    for (int j = a; j <= b && a < n_freqs; ++j) w.push_back(row[j]);
+  }
+}
+
+int64_t feo(int64_t l) {
+  auto f = [](int64_t x) { return (x - 1) / 2 + 1; };
+  return f(f(f(l)));
+}
+int64_t conv3_length(int64_t len) {
+  int64_t l = len;
+  for (int i = 0; i < 3; ++i) l = l > 0 ? (l - 1) / 2 + 1 : 0;
+  return l;
+}
+int64_t audio_token_count(int64_t valid, int64_t n_window) {
+  return (valid / (2 * n_window)) * 13 + conv3_length(valid % (2 * n_window));
+}
+
+int load_weights(qa_ctx* ctx, const qa_tensor* tensors, int n, const qa_cfg& c) {
+  Loader L{ctx, {}, {}};
+  bool hf = false;
+  for (int i = 0; i < n; ++i) {
+    if (!tensors[i].name || !tensors[i].data || tensors[i].ndim < 1 || tensors[i].ndim > 4)
+      return fail(ctx, QA_ERR_ARG, "tensor %d: null name/data or bad rank", i);
+    std::string nm = tensors[i].name;
+    if (nm.rfind("model.audio_tower.", 0) == 0 || nm.rfind("model.language_model.", 0) == 0 ||
+        nm.rfind("thinker.lm_head.", 0) == 0)
+      hf = true;
+  }
+  for (int i = 0; i < n; ++i) {
+    HostT h;
+    h.dtype = tensors[i].dtype;
+    if (h.dtype < 0 || h.dtype > 2) return fail(ctx, QA_ERR_ARG, "tensor %s: bad dtype", tensors[i].name);
+    h.data = tensors[i].data;
+    for (int d = 0; d < tensors[i].ndim; ++d) h.shape.push_back(tensors[i].shape[d]);
+    L.t[hf ? remap(tensors[i].name) : std::string(tensors[i].name)] = h;
+  }
+  const bool bf = ctx->bf16;
+  int rc = QA_OK;
+  Weights& W = ctx->w;
+  const std::string A = "thinker.audio_tower.";
+  const int dm = c.d_model, ds = c.downsample_hidden;
+  int f3 = c.num_mel_bins;
+  for (int i = 0; i < 3; ++i) f3 = (f3 - 1) / 2 + 1;
+  ctx->f3 = f3;
+  if (dm % 64 || dm != c.encoder_heads * 64 || ds % 8 || c.hidden_size != c.output_dim ||
+      c.head_dim != 128 || c.num_heads != 2 * c.num_kv_heads || c.hidden_size % 256 ||
+      c.intermediate_size % 128 || c.num_mel_bins != 128 || c.n_window <= 0)
+    return fail(ctx, QA_ERR_SHAPE, "unsupported model geometry");
+
+  // ---- mel constants (src/mel.rs:19-27, 101-164)
+  {
+    std::vector<float> win(400);
+    for (int i = 0; i < 400; ++i) {
+      const float x = 2.0f * static_cast<float>(M_PI) * static_cast<float>(i) / 400.0f;
+      win[i] = 0.5f * (1.0f - std::cos(x));
+    }
+    std::vector<float2> tw(400);
+    for (int k = 0; k < 400; ++k)
+      tw[k] = make_float2(static_cast<float>(std::cos(2.0 * M_PI * k / 400.0)),
+                          static_cast<float>(std::sin(2.0 * M_PI * k / 400.0)));
+    std::vector<int> st, ln, wo;
+    std::vector<float> fw;
+    mel_bank(st, ln, wo, fw);
+    W.window = up_f32(ctx, win, &rc);
+    W.twiddle = upload<float2>(ctx, tw.data(), tw.size() * sizeof(float2), &rc);
+    W.fb_start = upload<int>(ctx, st.data(), st.size() * 4, &rc);
+    W.fb_len = upload<int>(ctx, ln.data(), ln.size() * 4, &rc);
+    W.fb_woff = upload<int>(ctx, wo.data(), wo.size() * 4, &rc);
+    W.fb_w = up_f32(ctx, fw, &rc);
+    if (rc) return rc;
+  }
+
+  // ---- conv stem: weights in the run's format; conv2/conv3 permuted to
+  // k = (kh*3 + kw)*c_in + ic; conv_out columns to f*c + ch (NHWC order)
+  {
+    auto w1 = L.f32(A + "conv2d1.weight", {ds, 1, 3, 3});
+    auto w2 = L.f32(A + "conv2d2.weight", {ds, ds, 3, 3});
+    auto w3 = L.f32(A + "conv2d3.weight", {ds, ds, 3, 3});
+    auto co = L.f32(A + "conv_out.weight", {dm, (int64_t)ds * f3});
+    auto b1 = L.f32(A + "conv2d1.bias", {ds});
+    auto b2 = L.f32(A + "conv2d2.bias", {ds});
+    auto b3 = L.f32(A + "conv2d3.bias", {ds});
+    if (!L.missing.empty()) return fail(ctx, QA_ERR_WEIGHTS, "%s", L.missing.c_str());
+    auto perm = [&](const std::vector<float>& w) {
+      std::vector<float> o(w.size());
+      for (int oc = 0; oc < ds; ++oc)
+        for (int ic = 0; ic < ds; ++ic)
+          for (int k = 0; k < 9; ++k)
+            o[(static_cast<size_t>(oc) * 9 + k) * ds + ic] = w[(static_cast<size_t>(oc) * ds + ic) * 9 + k];
+      return o;
+    };
+    std::vector<float> cop(co.size());
+    for (int o = 0; o < dm; ++o)
+      for (int ch = 0; ch < ds; ++ch)
+        for (int f = 0; f < f3; ++f)
+          cop[static_cast<size_t>(o) * ds * f3 + f * ds + ch] = co[static_cast<size_t>(o) * ds * f3 + ch * f3 + f];
+    W.c1_w = up_f32(ctx, rounded(w1, bf), &rc);
+    W.c1_b = up_f32(ctx, b1, &rc);
+    W.c2_w = up_h16(ctx, perm(w2), &rc);
+    W.c2_b = up_f32(ctx, b2, &rc);
+    W.c3_w = up_h16(ctx, perm(w3), &rc);
+    W.c3_b = up_f32(ctx, b3, &rc);
+    W.co_w = up_h16(ctx, cop, &rc);
+    W.co_b = up_f32(ctx, L.f32_or_zero(A + "conv_out.bias", dm), &rc);
+    // sinusoidal PE rows 0..12 (src/audio_encoder.rs:263-275)
+    const int tpc = static_cast<int>(feo(2 * c.n_window));
+    std::vector<float> pe(static_cast<size_t>(tpc) * dm);
+    const int half = dm / 2;
+    const double lt = std::log(10000.0) / (half - 1.0);
+    for (int p = 0; p < tpc; ++p)
+      for (int i = 0; i < half; ++i) {
+        const double a = p * std::exp(-i * lt);
+        pe[static_cast<size_t>(p) * dm + i] = static_cast<float>(std::sin(a));
+        pe[static_cast<size_t>(p) * dm + half + i] = static_cast<float>(std::cos(a));
+      }
+    W.pe = up_f32(ctx, pe, &rc);
+    if (rc) return rc;
+  }
+  // ---- encoder layers
+  W.enc.clear();
+  for (int l = 0; l < c.encoder_layers; ++l) {
+    const std::string p = A + "layers." + std::to_string(l) + ".";
+    EncLayerW e{};
+    auto q = L.f32(p + "self_attn.q_proj.weight", {dm, dm});
+    auto k = L.f32(p + "self_attn.k_proj.weight", {dm, dm});
+    auto v = L.f32(p + "self_attn.v_proj.weight", {dm, dm});
+    std::vector<float> qkv(q);
+    qkv.insert(qkv.end(), k.begin(), k.end());
+    qkv.insert(qkv.end(), v.begin(), v.end());
+    auto qb = L.f32_or_zero(p + "self_attn.q_proj.bias", dm);
+    auto kb = L.f32_or_zero(p + "self_attn.k_proj.bias", dm);
+    auto vb = L.f32_or_zero(p + "self_attn.v_proj.bias", dm);
+    std::vector<float> qkvb(qb);
+    qkvb.insert(qkvb.end(), kb.begin(), kb.end());
+    qkvb.insert(qkvb.end(), vb.begin(), vb.end());
+    auto ow = L.f32(p + "self_attn.out_proj.weight", {dm, dm});
+    auto f1 = L.f32(p + "fc1.weight", {c.encoder_ffn_dim, dm});
+    auto f2 = L.f32(p + "fc2.weight", {dm, c.encoder_ffn_dim});
+    auto g1 = L.f32(p + "self_attn_layer_norm.weight", {dm});
+    auto be1 = L.f32(p + "self_attn_layer_norm.bias", {dm});
+    auto g2 = L.f32(p + "final_layer_norm.weight", {dm});
+    auto be2 = L.f32(p + "final_layer_norm.bias", {dm});
+    if (!L.missing.empty()) return fail(ctx, QA_ERR_WEIGHTS, "%s", L.missing.c_str());
+    e.qkv_w = up_h16(ctx, qkv, &rc);
+    e.qkv_b = up_f32(ctx, qkvb, &rc);
+    e.o_w = up_h16(ctx, ow, &rc);
+    e.o_b = up_f32(ctx, L.f32_or_zero(p + "self_attn.out_proj.bias", dm), &rc);
+    e.fc1_w = up_h16(ctx, f1, &rc);
+    e.fc1_b = up_f32(ctx, L.f32_or_zero(p + "fc1.bias", c.encoder_ffn_dim), &rc);
+    e.fc2_w = up_h16(ctx, f2, &rc);
+    e.fc2_b = up_f32(ctx, L.f32_or_zero(p + "fc2.bias", dm), &rc);
+    e.ln1_g = up_f32(ctx, g1, &rc);
+    e.ln1_b = up_f32(ctx, be1, &rc);
+    e.ln2_g = up_f32(ctx, g2, &rc);
+    e.ln2_b = up_f32(ctx, be2, &rc);
+    if (rc) return rc;
+    W.enc.push_back(e);
+  }
+  {
+    auto g = L.f32(A + "ln_post.weight", {dm});
+    auto b = L.f32(A + "ln_post.bias", {dm});
+    auto p1 = L.f32(A + "proj1.weight", {dm, dm});
+    auto p2 = L.f32(A + "proj2.weight", {c.output_dim, dm});
+    if (!L.missing.empty()) return fail(ctx, QA_ERR_WEIGHTS, "%s", L.missing.c_str());
+    W.lnp_g = up_f32(ctx, g, &rc);
+    W.lnp_b = up_f32(ctx, b, &rc);
+    W.p1_w = up_h16(ctx, p1, &rc);
+    W.p1_b = up_f32(ctx, L.f32_or_zero(A + "proj1.bias", dm), &rc);
+    W.p2_w = up_h16(ctx, p2, &rc);
+    W.p2_b = up_f32(ctx, L.f32_or_zero(A + "proj2.bias", c.output_dim), &rc);
+    if (rc) return rc;
+  }
+  // ---- decoder
+  const std::string T = "thinker.model.";
+  const int H = c.hidden_size, hd = c.head_dim, nq = c.num_heads, nkv = c.num_kv_heads;
+  const int I = c.intermediate_size;
+  {
+    const HostT* e = L.get(T + "embed_tokens.weight", {c.vocab_size, H});
+    if (!e) return fail(ctx, QA_ERR_WEIGHTS, "%s", L.missing.c_str());
+    std::vector<uint16_t> b(e->numel());
+    parallel_for(e->numel(), [&](int64_t i) { b[i] = to_half_bits(Loader::elem(*e, i), bf); });
+    W.embed = upload<void>(ctx, b.data(), b.size() * 2, &rc);
+    if (rc) return rc;
+  }
+  W.dec.clear();
+  for (int l = 0; l < c.num_layers; ++l) {
+    const std::string p = T + "layers." + std::to_string(l) + ".";
+    DecLayerW d{};
+    auto q = L.f32(p + "self_attn.q_proj.weight", {(int64_t)nq * hd, H});
+    auto k = L.f32(p + "self_attn.k_proj.weight", {(int64_t)nkv * hd, H});
+    auto v = L.f32(p + "self_attn.v_proj.weight", {(int64_t)nkv * hd, H});
+    auto o = L.f32(p + "self_attn.o_proj.weight", {H, (int64_t)nq * hd});
+    auto gt = L.f32(p + "mlp.gate_proj.weight", {I, H});
+    auto up = L.f32(p + "mlp.up_proj.weight", {I, H});
+    auto dn = L.f32(p + "mlp.down_proj.weight", {H, I});
+    auto iln = L.f32(p + "input_layernorm.weight", {H});
+    auto pln = L.f32(p + "post_attention_layernorm.weight", {H});
+    auto qn = L.f32(p + "self_attn.q_norm.weight", {hd});
+    auto kn = L.f32(p + "self_attn.k_norm.weight", {hd});
+    if (!L.missing.empty()) return fail(ctx, QA_ERR_WEIGHTS, "%s", L.missing.c_str());
+    std::vector<float> qkv(q);
+    qkv.insert(qkv.end(), k.begin(), k.end());
+    qkv.insert(qkv.end(), v.begin(), v.end());
+    // gate/up interleaved in blocks of 128 rows: a 256-wide GEMM tile holds
+    // the gate and up rows of the same 128 outputs (SwiGLU epilogue).
+    std::vector<float> gu(static_cast<size_t>(2) * I * H);
+    for (int b = 0; b < I / 128; ++b)
+      for (int r = 0; r < 128; ++r) {
+        std::memcpy(&gu[(static_cast<size_t>(b) * 256 + r) * H], &gt[(static_cast<size_t>(b) * 128 + r) * H], H * 4);
+        std::memcpy(&gu[(static_cast<size_t>(b) * 256 + 128 + r) * H], &up[(static_cast<size_t>(b) * 128 + r) * H], H * 4);
+      }
+    d.qkv_w = up_h16(ctx, qkv, &rc);
+    d.o_w = up_h16(ctx, o, &rc);
+    d.gu_w = up_h16(ctx, gu, &rc);
+    d.down_w = up_h16(ctx, dn, &rc);
+    d.iln = up_f32(ctx, rounded(iln, bf), &rc);
+    d.pln = up_f32(ctx, rounded(pln, bf), &rc);
+    d.qn = up_f32(ctx, rounded(qn, bf), &rc);
+    d.kn = up_f32(ctx, rounded(kn, bf), &rc);
+    if (rc) return rc;
+    W.dec.push_back(d);
+  }
+  {
+    auto fn = L.f32(T + "norm.weight", {H});
+    auto sc = L.f32("score.weight", {c.num_labels, H});
+    if (!L.missing.empty()) return fail(ctx, QA_ERR_WEIGHTS, "%s", L.missing.c_str());
+    W.final_norm = up_f32(ctx, fn, &rc);
+    // [score | score] in bf16: the head multiplies a hi/lo bf16 split of the
+    // f32 normed rows by the checkpoint's exact bf16 weights.
+    std::vector<uint16_t> w2(static_cast<size_t>(c.num_labels) * 2 * H);
+    for (int r = 0; r < c.num_labels; ++r)
+      for (int j = 0; j < H; ++j) {
+        const uint16_t b = f32_to_bf16(sc[static_cast<size_t>(r) * H + j]);
+        w2[static_cast<size_t>(r) * 2 * H + j] = b;
+        w2[static_cast<size_t>(r) * 2 * H + H + j] = b;
+      }
+    W.head_w2 = upload<void>(ctx, w2.data(), w2.size() * 2, &rc);
+    // RoPE (src/align_inference.rs:320-328, 371-373): theta 1e6, plain, f32
+    // then rounded to the run's format; halves duplicate, keep one.
+    const int half = hd / 2;
+    std::vector<float> cs(static_cast<size_t>(c.max_seq) * half), sn(cs.size());
+    for (int t = 0; t < c.max_seq; ++t)
+      for (int j = 0; j < half; ++j) {
+        const double inv = 1.0 / std::pow(1000000.0, 2.0 * j / hd);
+        const double a = static_cast<double>(t) * inv;
+        cs[static_cast<size_t>(t) * half + j] = round_half(static_cast<float>(std::cos(a)), bf);
+        sn[static_cast<size_t>(t) * half + j] = round_half(static_cast<float>(std::sin(a)), bf);
+      }
+    W.rope_cos = up_f32(ctx, cs, &rc);
+    W.rope_sin = up_f32(ctx, sn, &rc);
+    if (rc) return rc;
+  }
+  return QA_OK;
+}
+
+// ------------------------------------------------------------ batched-path plan
+
+// Host-side bookkeeping for one batch of clips (all indices into packed
+// device buffers).  Built once per call, uploaded as one int buffer.
+struct Plan {
+  int n = 0;
+  // mel
+  std::vector<MelClip> mel;
+  std::vector<int> chunk_clip;
+  int total_frames = 0, total_chunks = 0, max_frames = 0;
+  // audio tower
+  std::vector<int> atok0, n_audio;
+  int T_a = 0;
+  std::vector<int> co_map;     // [total_chunks*13] -> packed audio row or -1
+  std::vector<int2> windows;   // encoder windows
+  // decoder
+  std::vector<int> tok0, seq;
+  int T_d = 0;
+  std::vector<int> p2_map;     // [T_a] -> packed decoder row
+  std::vector<int> clip_of, pos_of;
+  std::vector<int> block_tab;  // [n][max_pages]
+  int max_pages = 0, total_pages = 0;
+  std::vector<AttnTile> tiles;
+  // head
+  std::vector<int> ts_rows;    // packed decoder rows of <timestamp> tokens
+  std::vector<int> ts_off;     // per clip offset into ts_rows
+};
+
+// Device copies of the plan's arrays inside ctx->idx_dev.
+struct PlanDev {
+  MelClip* mel;
+  int* chunk_clip;
+  int* co_map;
+  int2* windows;
+  int* p2_map;
+  int* clip_of;
+  int* pos_of;
+  int* block_tab;
+  AttnTile* tiles;
+  int* ts_rows;
+  uint32_t* ids;
+};
+
+void plan_tiles(Plan& P) {
+  P.tiles.clear();
+  for (int c = 0; c < P.n; ++c)
+    for (int q0 = 0; q0 < P.seq[c]; q0 += 64) P.tiles.push_back({c, q0, P.tok0[c], P.seq[c]});
+  // longest causal work first for load balance
+  std::stable_sort(P.tiles.begin(), P.tiles.end(),
+                   [](const AttnTile& a, const AttnTile& b) { return a.q0 > b.q0; });
+}
+
+void plan_decoder(Plan& P) {
+  P.clip_of.assign(P.T_d, 0);
+  P.pos_of.assign(P.T_d, 0);
+  P.max_pages = 0;
+  P.total_pages = 0;
+  for (int c = 0; c < P.n; ++c) {
+    for (int p = 0; p < P.seq[c]; ++p) {
+      P.clip_of[P.tok0[c] + p] = c;
+      P.pos_of[P.tok0[c] + p] = p;
+    }
+    P.max_pages = std::max(P.max_pages, (P.seq[c] + 63) / 64);
+  }
+  P.block_tab.assign(static_cast<size_t>(P.n) * std::max(P.max_pages, 1), 0);
+  for (int c = 0; c < P.n; ++c) {
+    const int np = (P.seq[c] + 63) / 64;
+    for (int j = 0; j < np; ++j) P.block_tab[static_cast<size_t>(c) * P.max_pages + j] = P.total_pages++;
+  }
+  plan_tiles(P);
+}
+
+template <typename T>
+size_t pad16(size_t n) {
+  return (n * sizeof(T) + 15) / 16 * 16;
+}
+
+int upload_plan(qa_ctx* ctx, const Plan& P, const std::vector<uint32_t>& ids, PlanDev& D) {
+  const size_t sz_mel = pad16<MelClip>(P.mel.size()), sz_cc = pad16<int>(P.chunk_clip.size()),
+               sz_co = pad16<int>(P.co_map.size()), sz_w = pad16<int2>(P.windows.size()),
+               sz_p2 = pad16<int>(P.p2_map.size()), sz_clip = pad16<int>(P.clip_of.size()),
+               sz_pos = pad16<int>(P.pos_of.size()), sz_bt = pad16<int>(P.block_tab.size()),
+               sz_t = pad16<AttnTile>(P.tiles.size()), sz_ts = pad16<int>(P.ts_rows.size()),
+               sz_ids = pad16<uint32_t>(ids.size());
+  const size_t total = sz_mel + sz_cc + sz_co + sz_w + sz_p2 + sz_clip + sz_pos + sz_bt + sz_t +
+                       sz_ts + sz_ids;
+  TRY(ensure(ctx, ctx->idx_dev, total));
+  TRY(ensure_pin(ctx, ctx->pin_in, total));
+  uint8_t* h = static_cast<uint8_t*>(ctx->pin_in.p);
+  uint8_t* d = ctx->idx_dev.as<uint8_t>();
+  size_t off = 0;
+  auto put = [&](const void* src, size_t bytes, size_t padded) {
+    if (bytes) std::memcpy(h + off, src, bytes);
+    void* dp = d + off;
+    off += padded;
+    return dp;
+  };
+  D.mel = static_cast<MelClip*>(put(P.mel.data(), P.mel.size() * sizeof(MelClip), sz_mel));
+  D.chunk_clip = static_cast<int*>(put(P.chunk_clip.data(), P.chunk_clip.size() * 4, sz_cc));
+  D.co_map = static_cast<int*>(put(P.co_map.data(), P.co_map.size() * 4, sz_co));
+  D.windows = static_cast<int2*>(put(P.windows.data(), P.windows.size() * sizeof(int2), sz_w));
+  D.p2_map = static_cast<int*>(put(P.p2_map.data(), P.p2_map.size() * 4, sz_p2));
+  D.clip_of = static_cast<int*>(put(P.clip_of.data(), P.clip_of.size() * 4, sz_clip));
+  D.pos_of = static_cast<int*>(put(P.pos_of.data(), P.pos_of.size() * 4, sz_pos));
+  D.block_tab = static_cast<int*>(put(P.block_tab.data(), P.block_tab.size() * 4, sz_bt));
+  D.tiles = static_cast<AttnTile*>(put(P.tiles.data(), P.tiles.size() * sizeof(AttnTile), sz_t));
+  D.ts_rows = static_cast<int*>(put(P.ts_rows.data(), P.ts_rows.size() * 4, sz_ts));
+  D.ids = static_cast<uint32_t*>(put(ids.data(), ids.size() * 4, sz_ids));
+  CK(cudaMemcpyAsync(d, h, total, cudaMemcpyHostToDevice, ctx->stream));
+  return QA_OK;
+}
+
+// Audio-tower bookkeeping for a set of clips whose mel is already chunked:
+// conv_out row map, packed audio offsets and attention windows.
+void plan_audio(Plan& P, const qa_cfg& c, const std::vector<int>& frames) {
+  const int cs = 2 * c.n_window;
+  const int tpc = static_cast<int>(feo(cs));
+  const int ws = tpc * (c.n_window_infer / cs);
+  P.atok0.assign(P.n, 0);
+  P.n_audio.assign(P.n, 0);
+  P.T_a = 0;
+  P.co_map.assign(static_cast<size_t>(P.total_chunks) * tpc, -1);
+  P.windows.clear();
+  for (int ci = 0; ci < P.n; ++ci) {
+    const int nfull = frames[ci] / cs, tail = frames[ci] % cs;
+    const int nch = nfull + (tail > 0);
+    const int na = static_cast<int>(audio_token_count(frames[ci], c.n_window));
+    P.atok0[ci] = P.T_a;
+    P.n_audio[ci] = na;
+    for (int i = 0; i < nch; ++i) {
+      const int valid = i < nfull ? tpc : static_cast<int>(feo(tail));
+      const int ch = P.mel[ci].chunk_off + i;
+      for (int t = 0; t < valid; ++t) P.co_map[static_cast<size_t>(ch) * tpc + t] = P.T_a + i * tpc + t;
+    }
+    const int window = (ws > 0 && ws < na) ? ws : na;
+    for (int st = 0; st < na; st += window) P.windows.push_back(make_int2(P.T_a + st, std::min(window, na - st)));
+    P.T_a += na;
+  }
+}
+
+// ------------------------------------------------------------ stages on device buffers
+
+// Conv stem + transformer + projector over `chunks` mel chunks (already in
+// ctx->mel_chunked).  Writes the projected audio rows through `p2_map`
+// (row i -> out row map[i]; identity when null) into `out16` [.., out_dim].
+int run_encoder(qa_ctx* ctx, const Plan& P, const PlanDev& D, void* out16, const int* p2_map) {
+  const qa_cfg& c = ctx->cfg;
+  const bool bf = ctx->bf16;
+  cudaStream_t s = ctx->stream;
+  const Weights& W = ctx->w;
+  const int ds = c.downsample_hidden, dm = c.d_model, cs = 2 * c.n_window;
+  const int h1 = (c.num_mel_bins - 1) / 2 + 1, w1 = (cs - 1) / 2 + 1;
+  const int h2 = (h1 - 1) / 2 + 1, w2 = (w1 - 1) / 2 + 1;
+  const int h3 = (h2 - 1) / 2 + 1, w3 = (w2 - 1) / 2 + 1;
+  const int tpc = w3;
+  const int G = std::max(1, std::min(P.total_chunks, 256));  // chunks per conv group
+  TRY(ensure(ctx, ctx->act1, static_cast<size_t>(G) * h1 * w1 * ds * 2));
+  TRY(ensure(ctx, ctx->cols, static_cast<size_t>(G) * h2 * w2 * 9 * ds * 2));
+  TRY(ensure(ctx, ctx->act2, static_cast<size_t>(G) * h2 * w2 * ds * 2));
+  TRY(ensure(ctx, ctx->act3, static_cast<size_t>(G) * h3 * w3 * ds * 2));
+  TRY(ensure(ctx, ctx->xenc, static_cast<size_t>(std::max(P.T_a, 1)) * dm * 4));
+  EpiParams ep;
+  ep.status = ctx->status.as<unsigned>();
+  for (int g0 = 0; g0 < P.total_chunks; g0 += G) {
+    const int g = std::min(G, P.total_chunks - g0);
+    const float* mel = ctx->mel_chunked.as<float>() + static_cast<size_t>(g0) * c.num_mel_bins * cs;
+    KL(conv1_direct(mel, g, c.num_mel_bins, cs, W.c1_w, W.c1_b, ds, ctx->act1.p, bf, s));
+    KL(im2col_3x3s2(ctx->act1.p, g, h1, w1, ds, ctx->cols.p, false, s));
+    ep.mode = EPI_STORE16;
+    ep.act = ACT_GELU;
+    ep.bias = W.c2_b;
+    ep.out = ctx->act2.p;
+    ep.ldo = ds;
+    ep.row_map = nullptr;
+    KL(gemm_tc(ctx->cols.p, 9LL * ds, W.c2_w, 9LL * ds, g * h2 * w2, ds, 9 * ds, bf, ep, s));
+    KL(im2col_3x3s2(ctx->act2.p, g, h2, w2, ds, ctx->cols.p, true, s));
+    ep.bias = W.c3_b;
+    ep.out = ctx->act3.p;
+    KL(gemm_tc(ctx->cols.p, 9LL * ds, W.c3_w, 9LL * ds, g * h3 * w3, ds, 9 * ds, bf, ep, s));
+    // conv_out + bias + PE[t], scattered into the packed token rows
+    EpiParams eo;
+    eo.status = ep.status;
+    eo.mode = EPI_STORE32;
+    eo.bias = W.co_b;
+    eo.pe = W.pe;
+    eo.pe_period = tpc;
+    eo.out = ctx->xenc.p;
+    eo.ldo = dm;
+    eo.row_map = D.co_map + static_cast<size_t>(g0) * tpc;
+    KL(gemm_tc(ctx->act3.p, (long long)h3 * ds, W.co_w, (long long)h3 * ds, g * tpc, dm, h3 * ds, bf,
+               eo, s));
+  }
+  const int Ta = P.T_a;
+  TRY(ensure(ctx, ctx->h16a, static_cast<size_t>(Ta) * dm * 2));
+  TRY(ensure(ctx, ctx->qkv_enc, static_cast<size_t>(Ta) * 3 * dm * 2));
+  TRY(ensure(ctx, ctx->attn_enc, static_cast<size_t>(Ta) * dm * 2));
+  TRY(ensure(ctx, ctx->ffn_enc, static_cast<size_t>(Ta) * c.encoder_ffn_dim * 2));
+  for (const EncLayerW& L : W.enc) {
+    KL(layernorm_rows(ctx->xenc.as<float>(), Ta, dm, L.ln1_g, L.ln1_b, 1e-5f, ctx->h16a.p, bf, s));
+    ep.mode = EPI_STORE16;
+    ep.act = ACT_NONE;
+    ep.bias = L.qkv_b;
+    ep.out = ctx->qkv_enc.p;
+    ep.ldo = 3 * dm;
+    KL(gemm_tc(ctx->h16a.p, dm, L.qkv_w, dm, Ta, 3 * dm, dm, bf, ep, s));
+    KL(window_attention(ctx->qkv_enc.p, dm, c.encoder_heads, 64, D.windows,
+                        static_cast<int>(P.windows.size()), ctx->attn_enc.p, bf, s));
+    ep.mode = EPI_RESID32;
+    ep.bias = L.o_b;
+    ep.out = ctx->xenc.p;
+    ep.ldo = dm;
+    KL(gemm_tc(ctx->attn_enc.p, dm, L.o_w, dm, Ta, dm, dm, bf, ep, s));
+    KL(layernorm_rows(ctx->xenc.as<float>(), Ta, dm, L.ln2_g, L.ln2_b, 1e-5f, ctx->h16a.p, bf, s));
+    ep.mode = EPI_STORE16;
+    ep.act = ACT_GELU;
+    ep.bias = L.fc1_b;
+    ep.out = ctx->ffn_enc.p;
+    ep.ldo = c.encoder_ffn_dim;
+    KL(gemm_tc(ctx->h16a.p, dm, L.fc1_w, dm, Ta, c.encoder_ffn_dim, dm, bf, ep, s));
+    ep.mode = EPI_RESID32;
+    ep.act = ACT_NONE;
+    ep.bias = L.fc2_b;
+    ep.out = ctx->xenc.p;
+    ep.ldo = dm;
+    KL(gemm_tc(ctx->ffn_enc.p, c.encoder_ffn_dim, L.fc2_w, c.encoder_ffn_dim, Ta, dm,
+               c.encoder_ffn_dim, bf, ep, s));
+  }
+  // ln_post -> proj1 + GELU -> proj2 (src/audio_encoder.rs:816-821)
+  TRY(ensure(ctx, ctx->proj1, static_cast<size_t>(Ta) * dm * 2));
+  KL(layernorm_rows(ctx->xenc.as<float>(), Ta, dm, W.lnp_g, W.lnp_b, 1e-5f, ctx->h16a.p, bf, s));
+  ep.mode = EPI_STORE16;
+  ep.act = ACT_GELU;
+  ep.bias = W.p1_b;
+  ep.out = ctx->proj1.p;
+  ep.ldo = dm;
+  KL(gemm_tc(ctx->h16a.p, dm, W.p1_w, dm, Ta, dm, dm, bf, ep, s));
+  ep.act = ACT_NONE;
+  ep.bias = W.p2_b;
+  ep.out = out16;
+  ep.ldo = c.output_dim;
+  ep.row_map = p2_map;
+  KL(gemm_tc(ctx->proj1.p, dm, W.p2_w, dm, Ta, c.output_dim, dm, bf, ep, s));
+  return QA_OK;
+}
+
+int ensure_kv(qa_ctx* ctx, int pages) {
+  const qa_cfg& c = ctx->cfg;
+  if (pages <= ctx->kv_pages) return QA_OK;
+  const size_t bytes = static_cast<size_t>(c.num_layers) * pages * c.num_kv_heads * 64 * c.head_dim * 2;
+  TRY(ensure(ctx, ctx->kcache, bytes));
+  TRY(ensure(ctx, ctx->vcache, bytes));
+  ctx->kv_pages = pages;
+  ctx->kv_cap_tokens = std::min(pages * 64, c.max_seq);
+  return QA_OK;
+}
+
+// 28 decoder layers over ctx->hid [T_d][H] (16-bit), in place.
+int run_decoder(qa_ctx* ctx, const Plan& P, const PlanDev& D) {
+  const qa_cfg& c = ctx->cfg;
+  const bool bf = ctx->bf16;
+  cudaStream_t s = ctx->stream;
+  const int T = P.T_d, H = c.hidden_size, hd = c.head_dim, nq = c.num_heads, nkv = c.num_kv_heads;
+  const int I = c.intermediate_size, qd = nq * hd, ldq = (nq + 2 * nkv) * hd;
+  TRY(ensure(ctx, ctx->xn, static_cast<size_t>(T) * H * 2));
+  TRY(ensure(ctx, ctx->qkv, static_cast<size_t>(T) * ldq * 2));
+  TRY(ensure(ctx, ctx->attn, static_cast<size_t>(T) * qd * 2));
+  TRY(ensure(ctx, ctx->mlp, static_cast<size_t>(T) * I * 2));
+  TRY(ensure_kv(ctx, P.total_pages));
+  const size_t layer_kv = static_cast<size_t>(ctx->kv_pages) * nkv * 64 * hd;  // elements
+  TokenMap tm{D.clip_of, D.pos_of, D.block_tab, P.max_pages};
+  const float eps = static_cast<float>(c.rms_norm_eps);
+  EpiParams ep;
+  ep.status = ctx->status.as<unsigned>();
+  for (int l = 0; l < c.num_layers; ++l) {
+    const DecLayerW& L = ctx->w.dec[l];
+    PagedKV kv{ctx->kcache.as<uint16_t>() + l * layer_kv, ctx->vcache.as<uint16_t>() + l * layer_kv, 64};
+    KL(rmsnorm_rows(ctx->hid.p, T, H, L.iln, eps, ctx->xn.p, bf, s));
+    ep.mode = EPI_STORE16;
+    ep.act = ACT_NONE;
+    ep.bias = nullptr;
+    ep.out = ctx->qkv.p;
+    ep.ldo = ldq;
+    KL(gemm_tc(ctx->xn.p, H, L.qkv_w, H, T, ldq, H, bf, ep, s));
+    KL(qk_norm_rope_append(ctx->qkv.p, T, nq, nkv, hd, L.qn, L.kn, eps, ctx->w.rope_cos,
+                           ctx->w.rope_sin, tm, kv, bf, s));
+    KL(causal_attention(ctx->qkv.p, ldq, nq, nkv, hd, D.tiles, static_cast<int>(P.tiles.size()),
+                        D.block_tab, P.max_pages, kv, ctx->attn.p, bf, s));
+    ep.mode = EPI_RESID16;
+    ep.out = ctx->hid.p;
+    ep.ldo = H;
+    KL(gemm_tc(ctx->attn.p, qd, L.o_w, qd, T, H, qd, bf, ep, s));
+    KL(rmsnorm_rows(ctx->hid.p, T, H, L.pln, eps, ctx->xn.p, bf, s));
+    ep.mode = EPI_SWIGLU16;
+    ep.out = ctx->mlp.p;
+    ep.ldo = I;
+    KL(gemm_tc(ctx->xn.p, H, L.gu_w, H, T, 2 * I, H, bf, ep, s, 256));
+    ep.mode = EPI_RESID16;
+    ep.out = ctx->hid.p;
+    ep.ldo = H;
+    KL(gemm_tc(ctx->mlp.p, I, L.down_w, I, T, H, I, bf, ep, s));
+  }
+  return QA_OK;
+}
+
+// Timestamp head over `rows` of a hidden buffer (kind 0 f16, 1 bf16, 2 f32).
+int run_head(qa_ctx* ctx, const void* hidden, int kind, const int* rows_dev, int R, bool want_logits,
+             bool want_normed) {
+  const qa_cfg& c = ctx->cfg;
+  cudaStream_t s = ctx->stream;
+  const int H = c.hidden_size;
+  TRY(ensure(ctx, ctx->head_a, static_cast<size_t>(R) * 2 * H * 2));
+  TRY(ensure(ctx, ctx->head_keys, static_cast<size_t>(R) * 8));
+  TRY(ensure(ctx, ctx->head_raw, static_cast<size_t>(R) * 8));
+  if (want_logits) TRY(ensure(ctx, ctx->head_logits, static_cast<size_t>(R) * c.num_labels * 4));
+  if (want_normed) TRY(ensure(ctx, ctx->head_normed, static_cast<size_t>(R) * H * 4));
+  KL(head_gather_norm(hidden, kind, rows_dev, R, H, ctx->w.final_norm,
+                      static_cast<float>(c.rms_norm_eps), ctx->head_a.p,
+                      want_normed ? ctx->head_normed.as<float>() : nullptr, s));
+  CK(cudaMemsetAsync(ctx->head_keys.p, 0, static_cast<size_t>(R) * 8, s));
+  EpiParams ep;
+  ep.status = ctx->status.as<unsigned>();
+  ep.mode = EPI_ARGMAX;
+  ep.out = want_logits ? ctx->head_logits.p : nullptr;
+  ep.ldo = c.num_labels;
+  ep.keys = ctx->head_keys.as<unsigned long long>();
+  KL(gemm_tc(ctx->head_a.p, 2 * H, ctx->w.head_w2, 2 * H, R, c.num_labels, 2 * H, true, ep, s));
+  KL(argmax_finalize(ctx->head_keys.as<unsigned long long>(), R, c.timestamp_segment_time_ms,
+                     ctx->head_raw.as<long long>(), s));
+  return QA_OK;
+}
+
+int reset_flags(qa_ctx* ctx) {
+  CK(cudaMemsetAsync(ctx->status.p, 0, 4, ctx->stream));
+  CK(cudaMemsetAsync(ctx->badflag.p, 0, 4, ctx->stream));
+  return QA_OK;
+}
+
+int need_loaded(qa_ctx* ctx) {
+  if (!ctx) return QA_ERR_ARG;
+  if (!ctx->loaded) return fail(ctx, QA_ERR_STATE, "qa_load has not succeeded on this context");
+  CK(cudaSetDevice(ctx->device));
+  ctx->err.clear();
+  ctx->launches = 0;
+  return QA_OK;
+}
+
+float elapsed(qa_ctx* ctx, int a, int b) {
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, ctx->ev[a], ctx->ev[b]);
+  return ms;
+}
+
+}  // namespace
+
+// ====================================================================== C ABI
+
+extern "C" {
+
+int qa_open(int device, int half, qa_ctx** out) {
+  if (!out) return QA_ERR_ARG;
+  *out = nullptr;
+  if (half != QA_HALF_F16 && half != QA_HALF_BF16) return QA_ERR_ARG;
+  auto* ctx = new qa_ctx();
+  ctx->device = device;
+  ctx->half = half;
+  ctx->bf16 = half == QA_HALF_BF16;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+    delete ctx;
+    return QA_ERR_CUDA;
+  }
+  if (cudaSetDevice(device) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    delete ctx;
+    return QA_ERR_CUDA;
+  }
+  for (auto& e : ctx->ev) cudaEventCreate(&e);
+  if (ensure(ctx, ctx->status, 16) || ensure(ctx, ctx->badflag, 16)) {
+    qa_close(ctx);
+    return QA_ERR_OOM;
+  }
+  cudaMemset(ctx->status.p, 0, 16);
+  cudaMemset(ctx->badflag.p, 0, 16);
+  *out = ctx;
+  return QA_OK;
+}
+
+int qa_load(qa_ctx* ctx, const qa_tensor* tensors, int n, const qa_cfg* cfg) {
+  if (!ctx || !tensors || !cfg || n <= 0) return QA_ERR_ARG;
+  if (ctx->loaded) return fail(ctx, QA_ERR_STATE, "weights are already loaded on this context");
+  CK(cudaSetDevice(ctx->device));
+  ctx->cfg = *cfg;
+  if (ctx->cfg.max_seq <= 0) ctx->cfg.max_seq = 8192;
+  const int rc = load_weights(ctx, tensors, n, ctx->cfg);
+  if (rc) {
+    for (void* p : ctx->allocations) cudaFree(p);
+    ctx->allocations.clear();
+    return rc;
+  }
+  ctx->loaded = true;
+  return QA_OK;
+}
+
+int qa_close(qa_ctx* ctx) {
+  if (!ctx) return QA_ERR_ARG;
+  cudaSetDevice(ctx->device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  for (void* p : ctx->allocations) cudaFree(p);
+  DevBuf* bufs[] = {&ctx->samples, &ctx->mel_scratch, &ctx->mel_chunked, &ctx->maxkey,
+                    &ctx->clips_dev, &ctx->idx_dev, &ctx->act1, &ctx->cols, &ctx->act2,
+                    &ctx->act3, &ctx->xenc, &ctx->h16a, &ctx->qkv_enc, &ctx->attn_enc,
+                    &ctx->ffn_enc, &ctx->proj1, &ctx->emb_out, &ctx->hid, &ctx->xn, &ctx->qkv,
+                    &ctx->attn, &ctx->mlp, &ctx->kcache, &ctx->vcache, &ctx->head_a,
+                    &ctx->head_keys, &ctx->head_raw, &ctx->head_logits, &ctx->head_normed,
+                    &ctx->hidden_f32, &ctx->status, &ctx->badflag};
+  for (DevBuf* b : bufs)
+    if (b->p) cudaFree(b->p);
+  if (ctx->pin_in.p) cudaFreeHost(ctx->pin_in.p);
+  if (ctx->pin_out.p) cudaFreeHost(ctx->pin_out.p);
+  if (ctx->pin_res.p) cudaFreeHost(ctx->pin_res.p);
+  for (auto& e : ctx->ev)
+    if (e) cudaEventDestroy(e);
+  if (ctx->stream) cudaStreamDestroy(ctx->stream);
+  delete ctx;
+  return QA_OK;
+}
+
+const char* qa_last_error(const qa_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+int qa_set_timeout_ms(qa_ctx* ctx, int ms) {
+  if (!ctx || ms <= 0) return QA_ERR_ARG;
+  ctx->timeout_ms = ms;
+  return QA_OK;
+}
+
+int qa_half(const qa_ctx* ctx) { return ctx ? ctx->half : -1; }
+
+int qa_get_timings(const qa_ctx* ctx, qa_timings* out) {
+  if (!ctx || !out) return QA_ERR_ARG;
+  *out = ctx->timings;
+  return QA_OK;
+}
+
+int qa_mel(qa_ctx* ctx, const float* samples, int64_t n, float* out, int64_t out_len,
+           int* n_frames) {
+  TRY(need_loaded(ctx));
+  if (!samples || !out) return fail(ctx, QA_ERR_ARG, "null buffer");
+  if (n <= 0) return fail(ctx, QA_ERR_SHAPE, "empty audio");
+  const int frames = static_cast<int>(n / 160);
+  if (out_len < static_cast<int64_t>(frames) * 128)
+    return fail(ctx, QA_ERR_SHAPE, "out holds %lld floats, needs %d", (long long)out_len, frames * 128);
+  if (n_frames) *n_frames = frames;
+  if (frames == 0) return QA_OK;
+  cudaStream_t s = ctx->stream;
+  TRY(ensure(ctx, ctx->samples, n * 4));
+  TRY(ensure(ctx, ctx->mel_scratch, static_cast<size_t>(frames) * 128 * 4));
+  TRY(ensure(ctx, ctx->mel_chunked, static_cast<size_t>(frames) * 128 * 4));
+  TRY(ensure(ctx, ctx->maxkey, 16));
+  TRY(ensure(ctx, ctx->clips_dev, sizeof(MelClip)));
+  MelClip mc{0, static_cast<int>(n), 0, frames, 0};
+  CK(cudaMemcpyAsync(ctx->clips_dev.p, &mc, sizeof mc, cudaMemcpyHostToDevice, s));
+  CK(cudaMemcpyAsync(ctx->samples.p, samples, n * 4, cudaMemcpyHostToDevice, s));
+  CK(cudaMemsetAsync(ctx->maxkey.p, 0, 4, s));
+  const Weights& W = ctx->w;
+  MelBank bank{W.fb_start, W.fb_len, W.fb_woff, W.fb_w};
+  KL(mel_logpower(ctx->samples.as<float>(), ctx->clips_dev.as<MelClip>(), 1, frames, W.window,
+                  W.twiddle, bank, 1.0f / std::log(10.0f), ctx->mel_scratch.as<float>(),
+                  ctx->maxkey.as<unsigned>(), s));
+  KL(mel_finalize_rows(ctx->mel_scratch.as<float>(), frames, ctx->maxkey.as<unsigned>(),
+                       ctx->mel_chunked.as<float>(), s));
+  CK(cudaMemcpyAsync(out, ctx->mel_chunked.p, static_cast<size_t>(frames) * 128 * 4,
+                     cudaMemcpyDeviceToHost, s));
+  return wait_stream(ctx);
+}
+
+int qa_audio_embeds(qa_ctx* ctx, const float* mel, int n_mels, int valid_frames, uint16_t* out,
+                    int64_t out_len) {
+  TRY(need_loaded(ctx));
+  const qa_cfg& c = ctx->cfg;
+  if (!mel || !out) return fail(ctx, QA_ERR_ARG, "null buffer");
+  if (n_mels != c.num_mel_bins) return fail(ctx, QA_ERR_SHAPE, "mel has %d bins, expected %d", n_mels, c.num_mel_bins);
+  const int cs = 2 * c.n_window;
+  const int na = static_cast<int>(audio_token_count(valid_frames, c.n_window));
+  if (valid_frames <= 0 || na <= 0) return fail(ctx, QA_ERR_SHAPE, "audio produced 0 tokens (%d mel frames)", valid_frames);
+  if (na > 16384) return fail(ctx, QA_ERR_CAP, "%d audio tokens exceed the tower's 16384", na);
+  if (out_len < static_cast<int64_t>(na) * c.output_dim)
+    return fail(ctx, QA_ERR_SHAPE, "audio tower returns %d x %d values, out holds %lld", na, c.output_dim, (long long)out_len);
+  TRY(reset_flags(ctx));
+  Plan P;
+  P.n = 1;
+  const int nch = (valid_frames + cs - 1) / cs;
+  P.mel.push_back({0, 0, 0, valid_frames, 0});
+  P.total_chunks = nch;
+  P.chunk_clip.assign(nch, 0);
+  plan_audio(P, c, {valid_frames});
+  // chunk the mel on the host (src/audio_encoder.rs:763-790), zero padded
+  const size_t chunk_elems = static_cast<size_t>(nch) * n_mels * cs;
+  TRY(ensure_pin(ctx, ctx->pin_out, chunk_elems * 4));
+  float* ch = static_cast<float*>(ctx->pin_out.p);
+  std::memset(ch, 0, chunk_elems * 4);
+  for (int i = 0; i < nch; ++i) {
+    const int len = std::min(cs, valid_frames - i * cs);
+    for (int m = 0; m < n_mels; ++m)
+      std::memcpy(ch + (static_cast<size_t>(i) * n_mels + m) * cs,
+                  mel + static_cast<size_t>(m) * valid_frames + static_cast<size_t>(i) * cs, len * 4);
+  }
+  TRY(ensure(ctx, ctx->mel_chunked, chunk_elems * 4));
+  CK(cudaMemcpyAsync(ctx->mel_chunked.p, ch, chunk_elems * 4, cudaMemcpyHostToDevice, ctx->stream));
+  PlanDev D{};
+  TRY(upload_plan(ctx, P, {}, D));
+  TRY(ensure(ctx, ctx->emb_out, static_cast<size_t>(na) * c.output_dim * 2));
+  TRY(run_encoder(ctx, P, D, ctx->emb_out.p, nullptr));
+  CK(cudaMemcpyAsync(out, ctx->emb_out.p, static_cast<size_t>(na) * c.output_dim * 2,
+                     cudaMemcpyDeviceToHost, ctx->stream));
+  TRY(wait_stream(ctx));
+  return check_status(ctx);
+}
+
+int qa_ensure_capacity(qa_ctx* ctx, int need, int* cap) {
+  TRY(need_loaded(ctx));
+  const int target = std::min(((std::max(need, 1) + 255) / 256) * 256, ctx->cfg.max_seq);
+  TRY(ensure_kv(ctx, (target + 63) / 64));
+  if (cap) *cap = ctx->kv_cap_tokens;
+  return QA_OK;
+}
+
+int qa_text_hidden(qa_ctx* ctx, const uint16_t* emb, int seq, float* out) {
+  TRY(need_loaded(ctx));
+  const qa_cfg& c = ctx->cfg;
+  if (!emb || !out) return fail(ctx, QA_ERR_ARG, "null buffer");
+  if (seq <= 0) return fail(ctx, QA_ERR_SHAPE, "empty sequence");
+  if (seq > c.max_seq) return fail(ctx, QA_ERR_CAP, "prefill needs %d positions, max_seq is %d", seq, c.max_seq);
+  TRY(qa_ensure_capacity(ctx, seq, nullptr));
+  TRY(reset_flags(ctx));
+  Plan P;
+  P.n = 1;
+  P.tok0 = {0};
+  P.seq = {seq};
+  P.T_d = seq;
+  plan_decoder(P);
+  PlanDev D{};
+  TRY(upload_plan(ctx, P, {}, D));
+  const int H = c.hidden_size;
+  TRY(ensure(ctx, ctx->hid, static_cast<size_t>(seq) * H * 2));
+  TRY(ensure(ctx, ctx->hidden_f32, static_cast<size_t>(seq) * H * 4));
+  CK(cudaMemcpyAsync(ctx->hid.p, emb, static_cast<size_t>(seq) * H * 2, cudaMemcpyHostToDevice, ctx->stream));
+  TRY(run_decoder(ctx, P, D));
+  KL(widen16(ctx->hid.p, static_cast<long long>(seq) * H, ctx->hidden_f32.as<float>(), ctx->bf16, ctx->stream));
+  CK(cudaMemcpyAsync(out, ctx->hidden_f32.p, static_cast<size_t>(seq) * H * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  TRY(wait_stream(ctx));
+  return check_status(ctx);
+}
+
+int qa_head(qa_ctx* ctx, const float* hidden, int seq, const int* rows, int n_rows,
+            int64_t* raw_ms, float* logits, float* normed) {
+  TRY(need_loaded(ctx));
+  const qa_cfg& c = ctx->cfg;
+  if (!hidden || !rows || !raw_ms) return fail(ctx, QA_ERR_ARG, "null buffer");
+  if (n_rows <= 0) return QA_OK;
+  for (int i = 0; i < n_rows; ++i)
+    if (rows[i] < 0 || rows[i] >= seq) return fail(ctx, QA_ERR_SHAPE, "row %d out of range", rows[i]);
+  TRY(reset_flags(ctx));
+  const int H = c.hidden_size;
+  TRY(ensure(ctx, ctx->hidden_f32, static_cast<size_t>(seq) * H * 4));
+  TRY(ensure(ctx, ctx->idx_dev, static_cast<size_t>(n_rows) * 4));
+  CK(cudaMemcpyAsync(ctx->hidden_f32.p, hidden, static_cast<size_t>(seq) * H * 4, cudaMemcpyHostToDevice, ctx->stream));
+  CK(cudaMemcpyAsync(ctx->idx_dev.p, rows, static_cast<size_t>(n_rows) * 4, cudaMemcpyHostToDevice, ctx->stream));
+  TRY(run_head(ctx, ctx->hidden_f32.p, 2, ctx->idx_dev.as<int>(), n_rows, logits != nullptr, normed != nullptr));
+  CK(cudaMemcpyAsync(raw_ms, ctx->head_raw.p, static_cast<size_t>(n_rows) * 8, cudaMemcpyDeviceToHost, ctx->stream));
+  if (logits)
+    CK(cudaMemcpyAsync(logits, ctx->head_logits.p, static_cast<size_t>(n_rows) * c.num_labels * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  if (normed)
+    CK(cudaMemcpyAsync(normed, ctx->head_normed.p, static_cast<size_t>(n_rows) * H * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  TRY(wait_stream(ctx));
+  return check_status(ctx);
+}
+
+int qa_align_batch(qa_ctx* ctx, const qa_clip* clips, int n, qa_result* results) {
+  TRY(need_loaded(ctx));
+  const qa_cfg& c = ctx->cfg;
+  if (!clips || !results || n <= 0) return fail(ctx, QA_ERR_ARG, "empty batch");
+  cudaStream_t s = ctx->stream;
+  const int cs = 2 * c.n_window;
+  Plan P;
+  P.n = n;
+  std::vector<int> frames(n);
+  std::vector<uint32_t> ids;
+  long long total_samples = 0;
+  bool want_logits = false, want_normed = false;
+  // ---- validate and plan (host)
+  for (int i = 0; i < n; ++i) {
+    const qa_clip& cl = clips[i];
+    if (!cl.samples || !cl.input_ids || cl.n_samples <= 0 || cl.seq_len <= 0)
+      return fail(ctx, QA_ERR_ARG, "clip %d: empty audio or input", i);
+    if (cl.seq_len > c.max_seq)
+      return fail(ctx, QA_ERR_CAP, "clip %d: prefill needs %d positions, max_seq is %d", i, cl.seq_len, c.max_seq);
+    frames[i] = static_cast<int>(cl.n_samples / 160);
+    const int na = static_cast<int>(audio_token_count(frames[i], c.n_window));
+    if (na <= 0) return fail(ctx, QA_ERR_SHAPE, "clip %d: audio produced 0 tokens (%d mel frames)", i, frames[i]);
+    if (na > 16384) return fail(ctx, QA_ERR_CAP, "clip %d: %d audio tokens exceed 16384", i, na);
+    int pads = 0, ts = 0;
+    for (int p = 0; p < cl.seq_len; ++p) {
+      pads += static_cast<int>(cl.input_ids[p]) == c.audio_token_id;
+      ts += static_cast<int>(cl.input_ids[p]) == c.timestamp_token_id;
+    }
+    if (pads != na)
+      return fail(ctx, QA_ERR_SHAPE, "clip %d: %d audio tokens in the input, the audio gives %d", i, pads, na);
+    if (ts != results[i].n_ts || !results[i].raw_ms)
+      return fail(ctx, QA_ERR_SHAPE, "clip %d: %d timestamp tokens, result holds %d", i, ts, results[i].n_ts);
+    want_logits |= results[i].logits != nullptr;
+    want_normed |= results[i].normed != nullptr;
+    P.mel.push_back({total_samples, static_cast<int>(cl.n_samples), P.total_frames, frames[i], P.total_chunks});
+    const int nch = (frames[i] + cs - 1) / cs;
+    for (int k = 0; k < nch; ++k) P.chunk_clip.push_back(i);
+    P.total_frames += frames[i];
+    P.total_chunks += nch;
+    P.max_frames = std::max(P.max_frames, frames[i]);
+    total_samples += cl.n_samples;
+    P.tok0.push_back(P.T_d);
+    P.seq.push_back(cl.seq_len);
+    P.T_d += cl.seq_len;
+  }
+  plan_audio(P, c, frames);
+  P.p2_map.assign(P.T_a, 0);
+  P.ts_off.assign(n + 1, 0);
+  ids.reserve(P.T_d);
+  for (int i = 0; i < n; ++i) {
+    int k = 0;
+    for (int p = 0; p < clips[i].seq_len; ++p) {
+      const uint32_t id = clips[i].input_ids[p];
+      ids.push_back(id);
+      if (static_cast<int>(id) == c.audio_token_id) P.p2_map[P.atok0[i] + k++] = P.tok0[i] + p;
+      if (static_cast<int>(id) == c.timestamp_token_id) P.ts_rows.push_back(P.tok0[i] + p);
+    }
+    P.ts_off[i + 1] = static_cast<int>(P.ts_rows.size());
+  }
+  plan_decoder(P);
+  const int R = static_cast<int>(P.ts_rows.size());
+
+  // ---- device pass
+  CK(cudaEventRecord(ctx->ev[0], s));
+  TRY(reset_flags(ctx));
+  TRY(ensure(ctx, ctx->samples, total_samples * 4));
+  TRY(ensure_pin(ctx, ctx->pin_out, total_samples * 4));
+  {
+    float* st = static_cast<float*>(ctx->pin_out.p);
+    for (int i = 0; i < n; ++i) std::memcpy(st + P.mel[i].sample_off, clips[i].samples, clips[i].n_samples * 4);
+    CK(cudaMemcpyAsync(ctx->samples.p, st, total_samples * 4, cudaMemcpyHostToDevice, s));
+  }
+  PlanDev D{};
+  TRY(upload_plan(ctx, P, ids, D));
+  CK(cudaEventRecord(ctx->ev[1], s));
+  // (a) mel
+  TRY(ensure(ctx, ctx->mel_scratch, static_cast<size_t>(P.total_frames) * 128 * 4));
+  TRY(ensure(ctx, ctx->mel_chunked, static_cast<size_t>(P.total_chunks) * 128 * cs * 4));
+  TRY(ensure(ctx, ctx->maxkey, static_cast<size_t>(n) * 4));
+  CK(cudaMemsetAsync(ctx->maxkey.p, 0, static_cast<size_t>(n) * 4, s));
+  const Weights& W = ctx->w;
+  MelBank bank{W.fb_start, W.fb_len, W.fb_woff, W.fb_w};
+  KL(mel_logpower(ctx->samples.as<float>(), D.mel, n, P.max_frames, W.window, W.twiddle, bank,
+                  1.0f / std::log(10.0f), ctx->mel_scratch.as<float>(), ctx->maxkey.as<unsigned>(), s));
+  KL(mel_finalize_chunked(ctx->mel_scratch.as<float>(), D.mel, D.chunk_clip, P.total_chunks, cs,
+                          ctx->maxkey.as<unsigned>(), ctx->mel_chunked.as<float>(), s));
+  CK(cudaEventRecord(ctx->ev[2], s));
+  // (b) audio tower, projected rows scattered straight into the decoder input
+  const int H = c.hidden_size;
+  TRY(ensure(ctx, ctx->hid, static_cast<size_t>(P.T_d) * H * 2));
+  TRY(run_encoder(ctx, P, D, ctx->hid.p, D.p2_map));
+  CK(cudaEventRecord(ctx->ev[3], s));
+  // embedding gather for the text rows
+  KL(embed_gather(D.ids, P.T_d, W.embed, c.vocab_size, H, c.audio_token_id, ctx->hid.p,
+                  ctx->badflag.as<int>(), s));
+  CK(cudaEventRecord(ctx->ev[4], s));
+  // (c)(d)(e) decoder prefill
+  TRY(run_decoder(ctx, P, D));
+  CK(cudaEventRecord(ctx->ev[5], s));
+  // (f) head
+  TRY(run_head(ctx, ctx->hid.p, ctx->bf16 ? 1 : 0, D.ts_rows, R, want_logits, want_normed));
+  CK(cudaEventRecord(ctx->ev[6], s));
+  // readback
+  const size_t out_bytes = static_cast<size_t>(R) * 8;
+  TRY(ensure_pin(ctx, ctx->pin_res, out_bytes));
+  CK(cudaMemcpyAsync(ctx->pin_res.p, ctx->head_raw.p, out_bytes, cudaMemcpyDeviceToHost, s));
+  CK(cudaEventRecord(ctx->ev[7], s));
+  TRY(wait_stream(ctx));
+  TRY(check_status(ctx));
+  const int64_t* raw = static_cast<const int64_t*>(ctx->pin_res.p);
+  for (int i = 0; i < n; ++i) {
+    const int o = P.ts_off[i], k = P.ts_off[i + 1] - o;
+    std::memcpy(results[i].raw_ms, raw + o, static_cast<size_t>(k) * 8);
+    if (results[i].logits)
+      CK(cudaMemcpy(results[i].logits, ctx->head_logits.as<float>() + static_cast<size_t>(o) * c.num_labels,
+                    static_cast<size_t>(k) * c.num_labels * 4, cudaMemcpyDeviceToHost));
+    if (results[i].normed)
+      CK(cudaMemcpy(results[i].normed, ctx->head_normed.as<float>() + static_cast<size_t>(o) * H,
+                    static_cast<size_t>(k) * H * 4, cudaMemcpyDeviceToHost));
+  }
+  qa_timings& t = ctx->timings;
+  t.h2d_ms = elapsed(ctx, 0, 1);
+  t.mel_ms = elapsed(ctx, 1, 2);
+  t.enc_ms = elapsed(ctx, 2, 3);
+  t.gather_ms = elapsed(ctx, 3, 4);
+  t.prefill_ms = elapsed(ctx, 4, 5);
+  t.head_ms = elapsed(ctx, 5, 6);
+  t.d2h_ms = elapsed(ctx, 6, 7);
+  t.total_ms = elapsed(ctx, 0, 7);
+  t.gpu_launches = ctx->launches;
+  return QA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,107 @@
+// Host runtime of the B200 alignment backend: the qa_ctx behind the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "gemm_tc.cuh"
+#include "kernels.cuh"
+#include "qa_b200.h"
+
+namespace qa {
+
+// Grow-only device buffer (the reference's capacities are grow-only too,
+// src/decoder.rs:657-688).
+struct DevBuf {
+  void* p = nullptr;
+  size_t cap = 0;
+  template <typename T = void>
+  T* as() const {
+    return static_cast<T*>(p);
+  }
+};
+
+struct PinBuf {
+  void* p = nullptr;
+  size_t cap = 0;
+};
+
+struct EncLayerW {
+  float *ln1_g, *ln1_b, *ln2_g, *ln2_b;
+  void* qkv_w;  // [3*dm][dm]
+  float* qkv_b; // [3*dm]
+  void* o_w;
+  float* o_b;
+  void* fc1_w;
+  float* fc1_b;
+  void* fc2_w;
+  float* fc2_b;
+};
+
+struct DecLayerW {
+  float *iln, *pln, *qn, *kn;  // rounded to the run's 16-bit format, held as f32
+  void* qkv_w;                 // [(nqh + 2 nkv) hd][H]
+  void* o_w;                   // [H][nqh hd]
+  void* gu_w;                  // [2I][H], gate/up interleaved in blocks of 128 rows
+  void* down_w;                // [H][I]
+};
+
+struct Weights {
+  // mel constants
+  float* window;     // [400]
+  float2* twiddle;   // [400]
+  int *fb_start, *fb_len, *fb_woff;
+  float* fb_w;
+  // conv stem
+  float* c1_w;  // [c1][9]
+  float* c1_b;
+  void* c2_w;   // [c][9c] permuted
+  float* c2_b;
+  void* c3_w;
+  float* c3_b;
+  void* co_w;   // [dm][f3*c] permuted
+  float* co_b;
+  float* pe;    // [13][dm]
+  std::vector<EncLayerW> enc;
+  float *lnp_g, *lnp_b;
+  void* p1_w;
+  float* p1_b;
+  void* p2_w;
+  float* p2_b;
+  // decoder
+  void* embed;  // [vocab][H]
+  std::vector<DecLayerW> dec;
+  float* final_norm;
+  void* head_w2;  // [labels][2H] bf16: [score | score]
+  float *rope_cos, *rope_sin;  // [max_seq][hd/2]
+};
+
+}  // namespace qa
+
+struct qa_ctx {
+  int device = 0;
+  int half = QA_HALF_F16;
+  bool bf16 = false;
+  cudaStream_t stream = nullptr;
+  int timeout_ms = 60000;
+  std::string err;
+  bool loaded = false;
+  qa_cfg cfg{};
+  int f3 = 0;  // conv3 frequency rows (16)
+  qa::Weights w{};
+  std::vector<void*> allocations;  // weights, freed at close
+  // workspace (grow-only)
+  qa::DevBuf samples, mel_scratch, mel_chunked, maxkey, clips_dev, idx_dev;
+  qa::DevBuf act1, cols, act2, act3, xenc, h16a, qkv_enc, attn_enc, ffn_enc, proj1;
+  qa::DevBuf emb_out, hid, xn, qkv, attn, mlp, kcache, vcache;
+  qa::DevBuf head_a, head_keys, head_raw, head_logits, head_normed, hidden_f32, status, badflag;
+  qa::PinBuf pin_in, pin_out, pin_res;  // plan staging, sample staging, results
+  int kv_pages = 0;     // pages per layer the cache holds
+  int kv_cap_tokens = 0;
+  cudaEvent_t ev[10] = {};
+  qa_timings timings{};
+  long long launches = 0;
+};
