@@ -1,0 +1,358 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 alignment path: aligned audio-seconds per second.
+
+Workload (per GPU): 64 independent clips, durations
+U(5, 30) s, 2.5-3.5 words/s, English pseudo-words mixed with CJK characters,
+f16 storage, on the seeded random-init Qwen3-ForcedAligner-0.6B architecture.
+One step = one pass of the whole path over the batch: samples -> log-mel ->
+audio tower -> embedding gather / audio scatter -> 28-layer causal prefill
+over the paged K/V cache -> timestamp head -> argmax.
+
+* value   — device time of the batched pass with its inputs already in HBM
+            (qa_batch_stage once, then qa_batch_run per step on this stream),
+            L2 flushed between steps; whole job = audio seconds of all ranks /
+            the slowest rank's time (weak scaling: every GPU runs its own shard
+            of clips; no data-path collective).
+* e2e     — the same metric through the public API (Aligner.align_batch:
+            word split + tokenize + host->device copy from pinned staging +
+            device pass + device->host read of raw_ms + timestamp repair).
+* roofline — the tcgen05 GEMM kernel (the dominant kernel) timed live with CUDA
+            events around every launch on its stream during the timed region.
+* cpu_baseline — the CPU restatement of the reference's --device cpu path
+            (oracle/) on a bounded sample, rank 0 at N=1 only.
+
+`--impl reference` times that CPU path alone on the same workload (the
+reference crate is Rust and cannot be built here; the oracle restates it).
+"""
+import argparse
+import datetime
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "aligned audio-sec/sec per B200 at 1/2/4/8 GPUs; prefill tok/s; % TC/HBM peak"
+UNIT = "audio-s/s"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--clips", type=int, default=64, help="clips per GPU per step")
+    ap.add_argument("--half", default="f16")
+    ap.add_argument("--cpu-sample-clips", type=int, default=4)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], d["bf16_tflops_sustained"], "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in self.lines:
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def build_inputs(qa, clips, builder):
+    inps = []
+    for c in clips:
+        words = qa.synth.split_words(c.text, c.language)
+        inps.append(builder.build(words, qa.synth.valid_mel_frames(len(c.samples))))
+    return inps
+
+
+def cpu_reference(qa, orc, cfg, weights, clips, inps, threads):
+    """The oracle (CPU restatement of the reference's --device cpu path) over
+    `clips`: audio-seconds per wall second, whole path per clip."""
+    orc.set_threads(threads)
+    om = orc.Model(weights, cfg)
+    t0 = time.perf_counter()
+    audio = 0.0
+    for c, inp in zip(clips, inps):
+        om.align_raw(c.samples, inp.input_ids, inp.timestamp_positions)
+        audio += len(c.samples) / 16000.0
+    dt = time.perf_counter() - t0
+    return audio / dt, audio, dt
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    qa = importlib.import_module("qwen3-aligner-wgpu_b200")
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    orc.build()
+    cfg = qa.synth.ModelConfig()
+    weights = qa.synth.random_weights(cfg)
+    clips = qa.synth.workload(2, n_clips=args.clips)
+    inps = build_inputs(qa, clips, qa.synth.InputBuilder())
+    threads = os.cpu_count() or 1
+    orc.set_threads(threads)
+    om = orc.Model(weights, cfg)
+    per_step = 2
+    audio = 0.0
+    total = 0.0
+    for step in range(args.warmup + args.steps):
+        idx = [(step * per_step + k) % len(clips) for k in range(per_step)]
+        t0 = time.perf_counter()
+        a = 0.0
+        for i in idx:
+            om.align_raw(clips[i].samples, inps[i].input_ids, inps[i].timestamp_positions)
+            a += len(clips[i].samples) / 16000.0
+        dt = time.perf_counter() - t0
+        if step >= args.warmup:
+            audio += a
+            total += dt
+    value = audio / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded audio/transcripts, random-init weights)",
+        "config": {"workload": "BASELINE config 2 (64 clips U(5,30) s, English+CJK)",
+                   "sample_per_step": f"{per_step} clips of the workload, cycled"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} steps x {per_step} clips ({audio:.1f} audio-s); "
+                                   "C++/OpenMP restatement of the reference's --device cpu path"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+
+    qa = importlib.import_module("qwen3-aligner-wgpu_b200")
+    cfg = qa.synth.ModelConfig()
+    weights = qa.synth.random_weights(cfg)
+    al = qa.Aligner.load_backend_with_dtype(weights, args.half, device=local, cfg=cfg)
+    clips = qa.synth.workload(2, n_clips=args.clips, start=rank * args.clips)
+    inps = build_inputs(qa, clips, al.input_builder)
+    samples = [c.samples for c in clips]
+    audio_s = sum(len(s) for s in samples) / 16000.0
+    T_d = sum(i.seq_len() for i in inps)
+    T_a = sum(i.n_audio_tokens for i in inps)
+
+    stream = torch.cuda.current_stream(dev)
+    al.set_stream(stream.cuda_stream)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    # ---- value: device pass on HBM-resident inputs
+    staged = al.stage(samples, inps)
+    for _ in range(args.warmup):
+        al.run()
+    barrier()
+    al.set_profile(True)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    launches = 0
+    with ClockSampler(local) as clk:
+        barrier()
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record(stream)
+            al.run()
+            e1.record(stream)
+            launches += al_launches(al, qa)
+        barrier()
+    dev_ms = sum(e0.elapsed_time(e1) for e0, e1 in evs)
+    prof = al.profile()
+    al.set_profile(False)
+    raw_check = al.fetch(staged)
+    assert all(len(r) == len(i.timestamp_positions) for (r, _), i in zip(raw_check, inps))
+    ms_max = max_over_ranks(dev_ms)
+    audio_all = sum_over_ranks(audio_s)
+    value = audio_all * args.steps / (ms_max / 1e3)
+
+    # ---- e2e through the public API (host buffers, copies inside)
+    texts = [(c.samples, c.text, c.language) for c in clips]
+    al.align_batch(texts)  # warm the staging buffers
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        al.align_batch(texts)
+    e1.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    e2e_value = audio_all * args.steps / (e2e_ms / 1e3)
+    t = al.timings
+
+    # ---- roofline of the dominant kernel (tcgen05 GEMM), from live events
+    hbm, tf_burst, tf_sus, src = peaks()
+    g = prof.get("gemm", {"launches": 0, "total_ms": 0.0, "flops": 0.0})
+    gemm_tflops = g["flops"] / (g["total_ms"] / 1e3) / 1e12 if g["total_ms"] else 0.0
+    total_prof_ms = sum(v["total_ms"] for v in prof.values()) or 1.0
+    kernels = {k: {"launches": v["launches"], "ms_per_step": v["total_ms"] / args.steps,
+                   "share": v["total_ms"] / total_prof_ms,
+                   **({"tflops": v["flops"] / (v["total_ms"] / 1e3) / 1e12} if v["flops"] else {}),
+                   **({"gbs": v["bytes"] / (v["total_ms"] / 1e3) / 1e9} if v["bytes"] and not v["flops"] else {})}
+               for k, v in sorted(prof.items(), key=lambda kv: -kv[1]["total_ms"])}
+    traffic = None
+    tr = os.path.join(ROOT, "profiles", "gemm_traffic.json")
+    if os.path.exists(tr):
+        traffic = json.load(open(tr)).get("bytes_per_launch")
+
+    out = None
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": args.half,
+            "data": "synthetic (seeded audio/transcripts, random-init weights)",
+            "config": {"workload": "BASELINE config 2: 64 clips/GPU, U(5,30) s, 2.5-3.5 words/s, "
+                                   "English + CJK, f16, one device pass per step",
+                       "clips_per_gpu": args.clips, "audio_s_per_gpu_step": audio_s,
+                       "decoder_tokens_per_gpu_step": T_d, "audio_tokens_per_gpu_step": T_a,
+                       "l2": "flushed between timed steps (256 MiB write, outside the events)",
+                       "parallelism": f"clip-sharded x{world}, no collectives"},
+            "realtime_factor_per_gpu": value / world,
+            "prefill_tok_s": T_d * world * args.steps / (ms_max / 1e3),
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(t["h2d_bytes"]) * world,
+                    "d2h_bytes_per_step": int(t["d2h_bytes"]) * world,
+                    "includes": "split_words + tokenize + pinned staging + H2D + device pass + "
+                                "D2H raw_ms + LIS repair"},
+            "gpu_launches": launches,
+            "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (tcgen05, all launches)",
+                         "achieved": gemm_tflops, "peak": tf_sus, "unit": "TFLOP/s",
+                         "frac": gemm_tflops / tf_sus, "peak_kind": f"{src} sustained bf16",
+                         "traffic": traffic,
+                         "launches_per_step": g["launches"] / args.steps,
+                         "flops_per_launch": g["flops"] / max(g["launches"], 1)},
+            "kernels": kernels,
+            "phases_ms": {k: t[k] for k in ("mel_ms", "enc_ms", "gather_ms", "prefill_ms", "head_ms")},
+            "clocks": clk.summary(),
+        }
+    # ---- CPU baseline (rank 0 at N=1 only; after the GPU phase)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as orc
+        orc.build()
+        k = min(args.cpu_sample_clips, len(clips))
+        threads = os.cpu_count() or 1
+        v, a, dt = cpu_reference(qa, orc, cfg, weights, clips[:k], inps[:k], threads)
+        out["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+                               "sample": f"first {k} clips of the workload ({a:.1f} audio-s in "
+                                         f"{dt:.1f} s), whole path per clip"}
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    al.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def al_launches(al, qa):
+    """Kernels the library launched in the last qa_batch_run."""
+    import ctypes
+    t = qa._lib.QaTimings()
+    qa._lib.lib().qa_get_timings(al._ctx, ctypes.byref(t))
+    return int(t.gpu_launches)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -86,12 +86,24 @@ typedef struct {
   int max_seq; /* 8192 (src/align_inference.rs:70) */
 } qa_cfg;
 
-/* Per-phase device times of the last qa_align_batch / stage call, in ms
- * (CUDA events on the context's stream; src/align_inference.rs:230-251). */
+/* Per-phase device times of the last batched call, in ms (CUDA events on the
+ * context's stream; the phases of src/align_inference.rs:230-251). */
 typedef struct {
   double h2d_ms, mel_ms, enc_ms, gather_ms, prefill_ms, head_ms, d2h_ms, total_ms;
   int64_t gpu_launches; /* kernels this library launched in the call */
+  int64_t h2d_bytes;    /* host->device bytes the call copied */
+  int64_t d2h_bytes;    /* device->host bytes the call copied */
 } qa_timings;
+
+/* Live per-kernel statistics (qa_set_profile): CUDA-event time of every launch
+ * of a kernel class on the launching stream, and the class's algorithmic work. */
+typedef struct {
+  char name[32];
+  int64_t launches;
+  double total_ms;
+  double flops; /* algorithmic FLOPs of all launches (0 for memory-bound kernels) */
+  double bytes; /* algorithmic HBM bytes of all launches */
+} qa_kernel_stat;
 
 /* ---------------------------------------------------------------- lifetime */
 
@@ -107,6 +119,14 @@ int qa_set_timeout_ms(qa_ctx* ctx, int ms);
 /* Backend::half (src/align_inference.rs:103-108). */
 int qa_half(const qa_ctx* ctx);
 int qa_get_timings(const qa_ctx* ctx, qa_timings* out);
+/* Launch on the caller's CUDA stream (a cudaStream_t; NULL restores the
+ * context's own stream).  No reference counterpart: wgpu owns its queue. */
+int qa_set_stream(qa_ctx* ctx, void* stream);
+/* Record CUDA events around every kernel launch (on = 1) and accumulate them
+ * per kernel class; qa_get_profile returns up to `max` classes.  No reference
+ * counterpart (the reference profiles with host timers, src/load_trace.rs). */
+int qa_set_profile(qa_ctx* ctx, int on);
+int qa_get_profile(qa_ctx* ctx, qa_kernel_stat* stats, int max, int* n);
 
 /* ---------------------------------------------------------------- stages */
 
@@ -161,6 +181,20 @@ typedef struct {
  * Equivalent, clip by clip, to Aligner::align_raw_rows
  * (src/align_inference.rs:656-834) fed by mel::mel_features. */
 int qa_align_batch(qa_ctx* ctx, const qa_clip* clips, int n, qa_result* results);
+
+/* qa_align_batch in three parts, for callers that keep inputs resident or
+ * overlap phases (no reference counterpart; the reference is one blocking
+ * call per clip):
+ *   qa_batch_stage  validates and plans the batch and copies its inputs to
+ *                   the device (results give the n_ts per clip and which
+ *                   optional outputs to produce);
+ *   qa_batch_run    enqueues the device pass over the staged inputs on the
+ *                   context's stream and returns without waiting; it may be
+ *                   called repeatedly on the same staged batch;
+ *   qa_batch_fetch  copies the results back (bounded wait) into `results`. */
+int qa_batch_stage(qa_ctx* ctx, const qa_clip* clips, int n, const qa_result* results);
+int qa_batch_run(qa_ctx* ctx);
+int qa_batch_fetch(qa_ctx* ctx, qa_result* results);
 
 #ifdef __cplusplus
 }

@@ -55,7 +55,8 @@ ACT_GELU = 1
 EXPORTED = [
     "qa_open", "qa_load", "qa_close", "qa_last_error", "qa_set_timeout_ms", "qa_half",
     "qa_get_timings", "qa_mel", "qa_audio_embeds", "qa_ensure_capacity", "qa_text_hidden",
-    "qa_head", "qa_align_batch",
+    "qa_head", "qa_align_batch", "qa_batch_stage", "qa_batch_run", "qa_batch_fetch",
+    "qa_set_stream", "qa_set_profile", "qa_get_profile",
     "qa_k_gemm",
 ]
 
@@ -85,7 +86,14 @@ class QaCfg(ctypes.Structure):
 class QaTimings(ctypes.Structure):
     _fields_ = [(n, ctypes.c_double) for n in (
         "h2d_ms", "mel_ms", "enc_ms", "gather_ms", "prefill_ms", "head_ms", "d2h_ms",
-        "total_ms")] + [("gpu_launches", ctypes.c_int64)]
+        "total_ms")] + [("gpu_launches", ctypes.c_int64), ("h2d_bytes", ctypes.c_int64),
+                        ("d2h_bytes", ctypes.c_int64)]
+
+
+class QaKernelStat(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 32), ("launches", ctypes.c_int64),
+                ("total_ms", ctypes.c_double), ("flops", ctypes.c_double),
+                ("bytes", ctypes.c_double)]
 
 
 class QaClip(ctypes.Structure):
@@ -182,6 +190,12 @@ def _declare(L: ctypes.CDLL) -> None:
         L.qa_head.argtypes = [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
                               c_void_p]
         L.qa_align_batch.argtypes = [c_void_p, c_void_p, c_int, c_void_p]
+        L.qa_batch_stage.argtypes = [c_void_p, c_void_p, c_int, c_void_p]
+        L.qa_batch_run.argtypes = [c_void_p]
+        L.qa_batch_fetch.argtypes = [c_void_p, c_void_p]
+        L.qa_set_stream.argtypes = [c_void_p, c_void_p]
+        L.qa_set_profile.argtypes = [c_void_p, c_int]
+        L.qa_get_profile.argtypes = [c_void_p, c_void_p, c_int, ctypes.POINTER(c_int)]
 
 
 def check(rc: int, ctx=None) -> None:

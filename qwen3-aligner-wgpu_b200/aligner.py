@@ -146,6 +146,12 @@ class Aligner:
 
     def align_inputs(self, samples_list, inputs, want_logits=False, want_normed=False):
         """The device-resident batched call on prebuilt inputs: [(raw_ms, extra)]."""
+        b = self.stage(samples_list, inputs, want_logits, want_normed)
+        self.run()
+        return self.fetch(b)
+
+    def stage(self, samples_list, inputs, want_logits=False, want_normed=False):
+        """qa_batch_stage: plan the batch and copy its inputs to the device."""
         n = len(inputs)
         L = _lib.lib()
         clips = (_lib.QaClip * n)()
@@ -168,11 +174,41 @@ class Aligner:
             res[i].logits = lg.ctypes.data if lg is not None else None
             res[i].normed = nm.ctypes.data if nm is not None else None
             outs.append((raw, {"logits": lg, "normed": nm}))
-        self._check(L.qa_align_batch(self._ctx, ctypes.addressof(clips), n, ctypes.addressof(res)))
+        self._check(L.qa_batch_stage(self._ctx, ctypes.addressof(clips), n,
+                                     ctypes.addressof(res)))
+        return (clips, res, keep, outs)
+
+    def run(self) -> None:
+        """qa_batch_run: enqueue the device pass over the staged batch (no wait)."""
+        self._check(_lib.lib().qa_batch_run(self._ctx))
+
+    def fetch(self, staged):
+        """qa_batch_fetch: copy the staged batch's results back: [(raw_ms, extra)]."""
+        clips, res, keep, outs = staged
+        L = _lib.lib()
+        self._check(L.qa_batch_fetch(self._ctx, ctypes.addressof(res)))
         t = _lib.QaTimings()
         L.qa_get_timings(self._ctx, ctypes.byref(t))
         self.timings = {k: getattr(t, k) for k, _ in _lib.QaTimings._fields_}
         return outs
+
+    def set_stream(self, stream) -> None:
+        """Launch on a caller's cudaStream_t (an int handle; None = own stream)."""
+        self._check(_lib.lib().qa_set_stream(self._ctx, stream))
+
+    def set_profile(self, on: bool) -> None:
+        self._check(_lib.lib().qa_set_profile(self._ctx, 1 if on else 0))
+
+    def profile(self) -> dict:
+        """Per kernel class: launches, total_ms, flops, bytes (qa_get_profile)."""
+        L = _lib.lib()
+        n = ctypes.c_int(0)
+        self._check(L.qa_get_profile(self._ctx, None, 0, ctypes.byref(n)))
+        arr = (_lib.QaKernelStat * max(n.value, 1))()
+        self._check(L.qa_get_profile(self._ctx, ctypes.addressof(arr), n.value, ctypes.byref(n)))
+        return {arr[i].name.decode(): {"launches": arr[i].launches, "total_ms": arr[i].total_ms,
+                                       "flops": arr[i].flops, "bytes": arr[i].bytes}
+                for i in range(n.value)}
 
     # ------------------------------------------------------------ stages
 

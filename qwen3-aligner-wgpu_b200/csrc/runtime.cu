@@ -39,14 +39,76 @@ int fail(qa_ctx* ctx, int code, const char* fmt, ...) {
                   "%s: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__, __LINE__);       \
   } while (0)
 
-#define KL(expr)                                                                              \
+// Launch a kernel (expr returns a cudaError_t value), count it, and when
+// profiling is on bracket it with CUDA events tagged with its kernel class and
+// algorithmic FLOPs / HBM bytes.
+#define KL(tag, flops, bytes, expr)                                                           \
   do {                                                                                        \
+    ProfScope ps_(ctx, tag, static_cast<double>(flops), static_cast<double>(bytes));          \
     int e_ = (expr);                                                                          \
     ++ctx->launches;                                                                          \
     if (e_)                                                                                   \
       return fail(ctx, QA_ERR_CUDA, "%s: %s (%s:%d)", #expr,                                  \
                   cudaGetErrorString(static_cast<cudaError_t>(e_)), __FILE__, __LINE__);      \
   } while (0)
+
+int prof_class(qa_ctx* ctx, const char* name) {
+  for (size_t i = 0; i < ctx->prof_names.size(); ++i)
+    if (ctx->prof_names[i] == name) return static_cast<int>(i);
+  ctx->prof_names.push_back(name);
+  qa_kernel_stat st{};
+  std::snprintf(st.name, sizeof st.name, "%s", name);
+  ctx->prof_stats.push_back(st);
+  return static_cast<int>(ctx->prof_names.size() - 1);
+}
+
+cudaEvent_t prof_event(qa_ctx* ctx, int* idx) {
+  if (ctx->prof_next >= static_cast<int>(ctx->prof_pool.size())) {
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    ctx->prof_pool.push_back(e);
+  }
+  *idx = ctx->prof_next++;
+  return ctx->prof_pool[*idx];
+}
+
+struct ProfScope {
+  qa_ctx* ctx;
+  int rec = -1;
+  ProfScope(qa_ctx* c, const char* name, double fl, double by) : ctx(c) {
+    if (!ctx->profile) return;
+    ProfRec r{prof_class(ctx, name), 0, -1, fl, by};
+    cudaEventRecord(prof_event(ctx, &r.ev0), ctx->stream);
+    ctx->prof_recs.push_back(r);
+    rec = static_cast<int>(ctx->prof_recs.size()) - 1;
+  }
+  ~ProfScope() {
+    if (rec < 0) return;
+    int i1 = -1;
+    cudaEventRecord(prof_event(ctx, &i1), ctx->stream);
+    ctx->prof_recs[rec].ev1 = i1;
+  }
+};
+
+// Fold completed profile records into the per-class statistics (call after
+// the stream has drained).
+void prof_resolve(qa_ctx* ctx) {
+  for (const ProfRec& r : ctx->prof_recs) {
+    if (r.ev1 < 0) continue;
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, ctx->prof_pool[r.ev0], ctx->prof_pool[r.ev1]) != cudaSuccess) continue;
+    qa_kernel_stat& st = ctx->prof_stats[r.cls];
+    st.launches += 1;
+    st.total_ms += ms;
+    st.flops += r.flops;
+    st.bytes += r.bytes;
+  }
+  ctx->prof_recs.clear();
+  ctx->prof_next = 0;
+}
+
+double gemm_flops(double M, double N, double K) { return 2.0 * M * N * K; }
+double gemm_bytes(double M, double N, double K, double ob) { return (M * K + N * K) * 2.0 + M * N * ob; }
 
 #define TRY(expr)            \
   do {                       \
@@ -164,7 +226,7 @@ int ensure_pin(qa_ctx* ctx, PinBuf& b, size_t bytes) {
 
 // Bounded wait for everything queued on the context's stream.
 int wait_stream(qa_ctx* ctx) {
-  cudaEvent_t e = ctx->ev[9];
+  cudaEvent_t e = ctx->ev[11];
   CK(cudaEventRecord(e, ctx->stream));
   const auto t0 = std::chrono::steady_clock::now();
   for (;;) {
@@ -179,6 +241,7 @@ int wait_stream(qa_ctx* ctx) {
       return fail(ctx, QA_ERR_TIMEOUT, "device did not finish within %d ms", ctx->timeout_ms);
     std::this_thread::sleep_for(std::chrono::microseconds(50));
   }
+  if (!ctx->prof_recs.empty()) prof_resolve(ctx);
   return QA_OK;
 }
 
@@ -589,47 +652,6 @@ int load_weights(qa_ctx* ctx, const qa_tensor* tensors, int n, const qa_cfg& c) 
 
 // ------------------------------------------------------------ batched-path plan
 
-// Host-side bookkeeping for one batch of clips (all indices into packed
-// device buffers).  Built once per call, uploaded as one int buffer.
-struct Plan {
-  int n = 0;
-  // mel
-  std::vector<MelClip> mel;
-  std::vector<int> chunk_clip;
-  int total_frames = 0, total_chunks = 0, max_frames = 0;
-  // audio tower
-  std::vector<int> atok0, n_audio;
-  int T_a = 0;
-  std::vector<int> co_map;     // [total_chunks*13] -> packed audio row or -1
-  std::vector<int2> windows;   // encoder windows
-  // decoder
-  std::vector<int> tok0, seq;
-  int T_d = 0;
-  std::vector<int> p2_map;     // [T_a] -> packed decoder row
-  std::vector<int> clip_of, pos_of;
-  std::vector<int> block_tab;  // [n][max_pages]
-  int max_pages = 0, total_pages = 0;
-  std::vector<AttnTile> tiles;
-  // head
-  std::vector<int> ts_rows;    // packed decoder rows of <timestamp> tokens
-  std::vector<int> ts_off;     // per clip offset into ts_rows
-};
-
-// Device copies of the plan's arrays inside ctx->idx_dev.
-struct PlanDev {
-  MelClip* mel;
-  int* chunk_clip;
-  int* co_map;
-  int2* windows;
-  int* p2_map;
-  int* clip_of;
-  int* pos_of;
-  int* block_tab;
-  AttnTile* tiles;
-  int* ts_rows;
-  uint32_t* ids;
-};
-
 void plan_tiles(Plan& P) {
   P.tiles.clear();
   for (int c = 0; c < P.n; ++c)
@@ -753,19 +775,24 @@ int run_encoder(qa_ctx* ctx, const Plan& P, const PlanDev& D, void* out16, const
   for (int g0 = 0; g0 < P.total_chunks; g0 += G) {
     const int g = std::min(G, P.total_chunks - g0);
     const float* mel = ctx->mel_chunked.as<float>() + static_cast<size_t>(g0) * c.num_mel_bins * cs;
-    KL(conv1_direct(mel, g, c.num_mel_bins, cs, W.c1_w, W.c1_b, ds, ctx->act1.p, bf, s));
-    KL(im2col_3x3s2(ctx->act1.p, g, h1, w1, ds, ctx->cols.p, false, s));
+    KL("conv1", 18.0 * g * h1 * w1 * ds, 4.0 * g * c.num_mel_bins * cs + 2.0 * g * h1 * w1 * ds,
+       conv1_direct(mel, g, c.num_mel_bins, cs, W.c1_w, W.c1_b, ds, ctx->act1.p, bf, s));
+    KL("im2col", 0, 2.0 * g * h2 * w2 * 9.0 * ds * 2.0,
+       im2col_3x3s2(ctx->act1.p, g, h1, w1, ds, ctx->cols.p, false, s));
     ep.mode = EPI_STORE16;
     ep.act = ACT_GELU;
     ep.bias = W.c2_b;
     ep.out = ctx->act2.p;
     ep.ldo = ds;
     ep.row_map = nullptr;
-    KL(gemm_tc(ctx->cols.p, 9LL * ds, W.c2_w, 9LL * ds, g * h2 * w2, ds, 9 * ds, bf, ep, s));
-    KL(im2col_3x3s2(ctx->act2.p, g, h2, w2, ds, ctx->cols.p, true, s));
+    KL("gemm", gemm_flops(g * h2 * w2, ds, 9 * ds), gemm_bytes(g * h2 * w2, ds, 9 * ds, 2),
+       gemm_tc(ctx->cols.p, 9LL * ds, W.c2_w, 9LL * ds, g * h2 * w2, ds, 9 * ds, bf, ep, s));
+    KL("im2col", 0, 2.0 * g * h3 * w3 * 9.0 * ds * 2.0,
+       im2col_3x3s2(ctx->act2.p, g, h2, w2, ds, ctx->cols.p, true, s));
     ep.bias = W.c3_b;
     ep.out = ctx->act3.p;
-    KL(gemm_tc(ctx->cols.p, 9LL * ds, W.c3_w, 9LL * ds, g * h3 * w3, ds, 9 * ds, bf, ep, s));
+    KL("gemm", gemm_flops(g * h3 * w3, ds, 9 * ds), gemm_bytes(g * h3 * w3, ds, 9 * ds, 2),
+       gemm_tc(ctx->cols.p, 9LL * ds, W.c3_w, 9LL * ds, g * h3 * w3, ds, 9 * ds, bf, ep, s));
     // conv_out + bias + PE[t], scattered into the packed token rows
     EpiParams eo;
     eo.status = ep.status;
@@ -776,59 +803,69 @@ int run_encoder(qa_ctx* ctx, const Plan& P, const PlanDev& D, void* out16, const
     eo.out = ctx->xenc.p;
     eo.ldo = dm;
     eo.row_map = D.co_map + static_cast<size_t>(g0) * tpc;
-    KL(gemm_tc(ctx->act3.p, (long long)h3 * ds, W.co_w, (long long)h3 * ds, g * tpc, dm, h3 * ds, bf,
-               eo, s));
+    KL("gemm", gemm_flops(g * tpc, dm, h3 * ds), gemm_bytes(g * tpc, dm, h3 * ds, 4),
+       gemm_tc(ctx->act3.p, (long long)h3 * ds, W.co_w, (long long)h3 * ds, g * tpc, dm, h3 * ds,
+               bf, eo, s));
   }
   const int Ta = P.T_a;
+  double win_flops = 0;  // 4 * len^2 * dm per window (QKᵀ and PV)
+  for (const int2& wv : P.windows) win_flops += 4.0 * wv.y * wv.y * dm;
   TRY(ensure(ctx, ctx->h16a, static_cast<size_t>(Ta) * dm * 2));
   TRY(ensure(ctx, ctx->qkv_enc, static_cast<size_t>(Ta) * 3 * dm * 2));
   TRY(ensure(ctx, ctx->attn_enc, static_cast<size_t>(Ta) * dm * 2));
   TRY(ensure(ctx, ctx->ffn_enc, static_cast<size_t>(Ta) * c.encoder_ffn_dim * 2));
   for (const EncLayerW& L : W.enc) {
-    KL(layernorm_rows(ctx->xenc.as<float>(), Ta, dm, L.ln1_g, L.ln1_b, 1e-5f, ctx->h16a.p, bf, s));
+    KL("layernorm", 0, 6.0 * Ta * dm, layernorm_rows(ctx->xenc.as<float>(), Ta, dm, L.ln1_g, L.ln1_b, 1e-5f, ctx->h16a.p, bf, s));
     ep.mode = EPI_STORE16;
     ep.act = ACT_NONE;
     ep.bias = L.qkv_b;
     ep.out = ctx->qkv_enc.p;
     ep.ldo = 3 * dm;
-    KL(gemm_tc(ctx->h16a.p, dm, L.qkv_w, dm, Ta, 3 * dm, dm, bf, ep, s));
-    KL(window_attention(ctx->qkv_enc.p, dm, c.encoder_heads, 64, D.windows,
+    KL("gemm", gemm_flops(Ta, 3 * dm, dm), gemm_bytes(Ta, 3 * dm, dm, 2),
+       gemm_tc(ctx->h16a.p, dm, L.qkv_w, dm, Ta, 3 * dm, dm, bf, ep, s));
+    KL("window_attn", win_flops, 2.0 * Ta * 4 * dm,
+       window_attention(ctx->qkv_enc.p, dm, c.encoder_heads, 64, D.windows,
                         static_cast<int>(P.windows.size()), ctx->attn_enc.p, bf, s));
     ep.mode = EPI_RESID32;
     ep.bias = L.o_b;
     ep.out = ctx->xenc.p;
     ep.ldo = dm;
-    KL(gemm_tc(ctx->attn_enc.p, dm, L.o_w, dm, Ta, dm, dm, bf, ep, s));
-    KL(layernorm_rows(ctx->xenc.as<float>(), Ta, dm, L.ln2_g, L.ln2_b, 1e-5f, ctx->h16a.p, bf, s));
+    KL("gemm", gemm_flops(Ta, dm, dm), gemm_bytes(Ta, dm, dm, 8),
+       gemm_tc(ctx->attn_enc.p, dm, L.o_w, dm, Ta, dm, dm, bf, ep, s));
+    KL("layernorm", 0, 6.0 * Ta * dm, layernorm_rows(ctx->xenc.as<float>(), Ta, dm, L.ln2_g, L.ln2_b, 1e-5f, ctx->h16a.p, bf, s));
     ep.mode = EPI_STORE16;
     ep.act = ACT_GELU;
     ep.bias = L.fc1_b;
     ep.out = ctx->ffn_enc.p;
     ep.ldo = c.encoder_ffn_dim;
-    KL(gemm_tc(ctx->h16a.p, dm, L.fc1_w, dm, Ta, c.encoder_ffn_dim, dm, bf, ep, s));
+    KL("gemm", gemm_flops(Ta, c.encoder_ffn_dim, dm), gemm_bytes(Ta, c.encoder_ffn_dim, dm, 2),
+       gemm_tc(ctx->h16a.p, dm, L.fc1_w, dm, Ta, c.encoder_ffn_dim, dm, bf, ep, s));
     ep.mode = EPI_RESID32;
     ep.act = ACT_NONE;
     ep.bias = L.fc2_b;
     ep.out = ctx->xenc.p;
     ep.ldo = dm;
-    KL(gemm_tc(ctx->ffn_enc.p, c.encoder_ffn_dim, L.fc2_w, c.encoder_ffn_dim, Ta, dm,
+    KL("gemm", gemm_flops(Ta, dm, c.encoder_ffn_dim), gemm_bytes(Ta, dm, c.encoder_ffn_dim, 8),
+       gemm_tc(ctx->ffn_enc.p, c.encoder_ffn_dim, L.fc2_w, c.encoder_ffn_dim, Ta, dm,
                c.encoder_ffn_dim, bf, ep, s));
   }
   // ln_post -> proj1 + GELU -> proj2 (src/audio_encoder.rs:816-821)
   TRY(ensure(ctx, ctx->proj1, static_cast<size_t>(Ta) * dm * 2));
-  KL(layernorm_rows(ctx->xenc.as<float>(), Ta, dm, W.lnp_g, W.lnp_b, 1e-5f, ctx->h16a.p, bf, s));
+  KL("layernorm", 0, 6.0 * Ta * dm, layernorm_rows(ctx->xenc.as<float>(), Ta, dm, W.lnp_g, W.lnp_b, 1e-5f, ctx->h16a.p, bf, s));
   ep.mode = EPI_STORE16;
   ep.act = ACT_GELU;
   ep.bias = W.p1_b;
   ep.out = ctx->proj1.p;
   ep.ldo = dm;
-  KL(gemm_tc(ctx->h16a.p, dm, W.p1_w, dm, Ta, dm, dm, bf, ep, s));
+  KL("gemm", gemm_flops(Ta, dm, dm), gemm_bytes(Ta, dm, dm, 2),
+     gemm_tc(ctx->h16a.p, dm, W.p1_w, dm, Ta, dm, dm, bf, ep, s));
   ep.act = ACT_NONE;
   ep.bias = W.p2_b;
   ep.out = out16;
   ep.ldo = c.output_dim;
   ep.row_map = p2_map;
-  KL(gemm_tc(ctx->proj1.p, dm, W.p2_w, dm, Ta, c.output_dim, dm, bf, ep, s));
+  KL("gemm", gemm_flops(Ta, c.output_dim, dm), gemm_bytes(Ta, c.output_dim, dm, 2),
+     gemm_tc(ctx->proj1.p, dm, W.p2_w, dm, Ta, c.output_dim, dm, bf, ep, s));
   return QA_OK;
 }
 
@@ -857,36 +894,44 @@ int run_decoder(qa_ctx* ctx, const Plan& P, const PlanDev& D) {
   TRY(ensure_kv(ctx, P.total_pages));
   const size_t layer_kv = static_cast<size_t>(ctx->kv_pages) * nkv * 64 * hd;  // elements
   TokenMap tm{D.clip_of, D.pos_of, D.block_tab, P.max_pages};
+  double attn_flops = 0;  // exact causal: 4 * hd * nq per (query, key <= query) pair
+  for (int cl = 0; cl < P.n; ++cl) attn_flops += 4.0 * hd * nq * 0.5 * P.seq[cl] * (P.seq[cl] + 1.0);
   const float eps = static_cast<float>(c.rms_norm_eps);
   EpiParams ep;
   ep.status = ctx->status.as<unsigned>();
   for (int l = 0; l < c.num_layers; ++l) {
     const DecLayerW& L = ctx->w.dec[l];
     PagedKV kv{ctx->kcache.as<uint16_t>() + l * layer_kv, ctx->vcache.as<uint16_t>() + l * layer_kv, 64};
-    KL(rmsnorm_rows(ctx->hid.p, T, H, L.iln, eps, ctx->xn.p, bf, s));
+    KL("rmsnorm", 0, 4.0 * T * H, rmsnorm_rows(ctx->hid.p, T, H, L.iln, eps, ctx->xn.p, bf, s));
     ep.mode = EPI_STORE16;
     ep.act = ACT_NONE;
     ep.bias = nullptr;
     ep.out = ctx->qkv.p;
     ep.ldo = ldq;
-    KL(gemm_tc(ctx->xn.p, H, L.qkv_w, H, T, ldq, H, bf, ep, s));
-    KL(qk_norm_rope_append(ctx->qkv.p, T, nq, nkv, hd, L.qn, L.kn, eps, ctx->w.rope_cos,
+    KL("gemm", gemm_flops(T, ldq, H), gemm_bytes(T, ldq, H, 2),
+       gemm_tc(ctx->xn.p, H, L.qkv_w, H, T, ldq, H, bf, ep, s));
+    KL("qk_rope_kv", 0, T * (4.0 * ldq + 2.0 * hd * 4.0),
+       qk_norm_rope_append(ctx->qkv.p, T, nq, nkv, hd, L.qn, L.kn, eps, ctx->w.rope_cos,
                            ctx->w.rope_sin, tm, kv, bf, s));
-    KL(causal_attention(ctx->qkv.p, ldq, nq, nkv, hd, D.tiles, static_cast<int>(P.tiles.size()),
+    KL("causal_attn", attn_flops, T * (2.0 * qd * 2 + 2.0 * nkv * hd * 2),
+       causal_attention(ctx->qkv.p, ldq, nq, nkv, hd, D.tiles, static_cast<int>(P.tiles.size()),
                         D.block_tab, P.max_pages, kv, ctx->attn.p, bf, s));
     ep.mode = EPI_RESID16;
     ep.out = ctx->hid.p;
     ep.ldo = H;
-    KL(gemm_tc(ctx->attn.p, qd, L.o_w, qd, T, H, qd, bf, ep, s));
-    KL(rmsnorm_rows(ctx->hid.p, T, H, L.pln, eps, ctx->xn.p, bf, s));
+    KL("gemm", gemm_flops(T, H, qd), gemm_bytes(T, H, qd, 4),
+       gemm_tc(ctx->attn.p, qd, L.o_w, qd, T, H, qd, bf, ep, s));
+    KL("rmsnorm", 0, 4.0 * T * H, rmsnorm_rows(ctx->hid.p, T, H, L.pln, eps, ctx->xn.p, bf, s));
     ep.mode = EPI_SWIGLU16;
     ep.out = ctx->mlp.p;
     ep.ldo = I;
-    KL(gemm_tc(ctx->xn.p, H, L.gu_w, H, T, 2 * I, H, bf, ep, s, 256));
+    KL("gemm", gemm_flops(T, 2 * I, H), gemm_bytes(T, I, H, 2) + 2.0 * I * H,
+       gemm_tc(ctx->xn.p, H, L.gu_w, H, T, 2 * I, H, bf, ep, s, 256));
     ep.mode = EPI_RESID16;
     ep.out = ctx->hid.p;
     ep.ldo = H;
-    KL(gemm_tc(ctx->mlp.p, I, L.down_w, I, T, H, I, bf, ep, s));
+    KL("gemm", gemm_flops(T, H, I), gemm_bytes(T, H, I, 4),
+       gemm_tc(ctx->mlp.p, I, L.down_w, I, T, H, I, bf, ep, s));
   }
   return QA_OK;
 }
@@ -902,7 +947,8 @@ int run_head(qa_ctx* ctx, const void* hidden, int kind, const int* rows_dev, int
   TRY(ensure(ctx, ctx->head_raw, static_cast<size_t>(R) * 8));
   if (want_logits) TRY(ensure(ctx, ctx->head_logits, static_cast<size_t>(R) * c.num_labels * 4));
   if (want_normed) TRY(ensure(ctx, ctx->head_normed, static_cast<size_t>(R) * H * 4));
-  KL(head_gather_norm(hidden, kind, rows_dev, R, H, ctx->w.final_norm,
+  KL("head_norm", 0, R * (H * (kind == 2 ? 4.0 : 2.0) + 4.0 * H),
+     head_gather_norm(hidden, kind, rows_dev, R, H, ctx->w.final_norm,
                       static_cast<float>(c.rms_norm_eps), ctx->head_a.p,
                       want_normed ? ctx->head_normed.as<float>() : nullptr, s));
   CK(cudaMemsetAsync(ctx->head_keys.p, 0, static_cast<size_t>(R) * 8, s));
@@ -912,8 +958,9 @@ int run_head(qa_ctx* ctx, const void* hidden, int kind, const int* rows_dev, int
   ep.out = want_logits ? ctx->head_logits.p : nullptr;
   ep.ldo = c.num_labels;
   ep.keys = ctx->head_keys.as<unsigned long long>();
-  KL(gemm_tc(ctx->head_a.p, 2 * H, ctx->w.head_w2, 2 * H, R, c.num_labels, 2 * H, true, ep, s));
-  KL(argmax_finalize(ctx->head_keys.as<unsigned long long>(), R, c.timestamp_segment_time_ms,
+  KL("gemm", gemm_flops(R, c.num_labels, 2 * H), gemm_bytes(R, c.num_labels, 2 * H, want_logits ? 4 : 0),
+     gemm_tc(ctx->head_a.p, 2 * H, ctx->w.head_w2, 2 * H, R, c.num_labels, 2 * H, true, ep, s));
+  KL("argmax", 0, 16.0 * R, argmax_finalize(ctx->head_keys.as<unsigned long long>(), R, c.timestamp_segment_time_ms,
                      ctx->head_raw.as<long long>(), s));
   return QA_OK;
 }
@@ -959,10 +1006,11 @@ int qa_open(int device, int half, qa_ctx** out) {
     return QA_ERR_CUDA;
   }
   if (cudaSetDevice(device) != cudaSuccess ||
-      cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess) {
+      cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
     delete ctx;
     return QA_ERR_CUDA;
   }
+  ctx->stream = ctx->own_stream;
   for (auto& e : ctx->ev) cudaEventCreate(&e);
   if (ensure(ctx, ctx->status, 16) || ensure(ctx, ctx->badflag, 16)) {
     qa_close(ctx);
@@ -1009,7 +1057,9 @@ int qa_close(qa_ctx* ctx) {
   if (ctx->pin_res.p) cudaFreeHost(ctx->pin_res.p);
   for (auto& e : ctx->ev)
     if (e) cudaEventDestroy(e);
-  if (ctx->stream) cudaStreamDestroy(ctx->stream);
+  for (auto& e : ctx->prof_pool)
+    if (e) cudaEventDestroy(e);
+  if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
   delete ctx;
   return QA_OK;
 }
@@ -1052,10 +1102,10 @@ int qa_mel(qa_ctx* ctx, const float* samples, int64_t n, float* out, int64_t out
   CK(cudaMemsetAsync(ctx->maxkey.p, 0, 4, s));
   const Weights& W = ctx->w;
   MelBank bank{W.fb_start, W.fb_len, W.fb_woff, W.fb_w};
-  KL(mel_logpower(ctx->samples.as<float>(), ctx->clips_dev.as<MelClip>(), 1, frames, W.window,
+  KL("mel", 0, 4.0 * n + 512.0 * frames, mel_logpower(ctx->samples.as<float>(), ctx->clips_dev.as<MelClip>(), 1, frames, W.window,
                   W.twiddle, bank, 1.0f / std::log(10.0f), ctx->mel_scratch.as<float>(),
                   ctx->maxkey.as<unsigned>(), s));
-  KL(mel_finalize_rows(ctx->mel_scratch.as<float>(), frames, ctx->maxkey.as<unsigned>(),
+  KL("mel_finalize", 0, 1024.0 * frames, mel_finalize_rows(ctx->mel_scratch.as<float>(), frames, ctx->maxkey.as<unsigned>(),
                        ctx->mel_chunked.as<float>(), s));
   CK(cudaMemcpyAsync(out, ctx->mel_chunked.p, static_cast<size_t>(frames) * 128 * 4,
                      cudaMemcpyDeviceToHost, s));
@@ -1134,7 +1184,7 @@ int qa_text_hidden(qa_ctx* ctx, const uint16_t* emb, int seq, float* out) {
   TRY(ensure(ctx, ctx->hidden_f32, static_cast<size_t>(seq) * H * 4));
   CK(cudaMemcpyAsync(ctx->hid.p, emb, static_cast<size_t>(seq) * H * 2, cudaMemcpyHostToDevice, ctx->stream));
   TRY(run_decoder(ctx, P, D));
-  KL(widen16(ctx->hid.p, static_cast<long long>(seq) * H, ctx->hidden_f32.as<float>(), ctx->bf16, ctx->stream));
+  KL("widen", 0, 6.0 * seq * H, widen16(ctx->hid.p, static_cast<long long>(seq) * H, ctx->hidden_f32.as<float>(), ctx->bf16, ctx->stream));
   CK(cudaMemcpyAsync(out, ctx->hidden_f32.p, static_cast<size_t>(seq) * H * 4, cudaMemcpyDeviceToHost, ctx->stream));
   TRY(wait_stream(ctx));
   return check_status(ctx);
@@ -1164,18 +1214,23 @@ int qa_head(qa_ctx* ctx, const float* hidden, int seq, const int* rows, int n_ro
   return check_status(ctx);
 }
 
-int qa_align_batch(qa_ctx* ctx, const qa_clip* clips, int n, qa_result* results) {
+int qa_batch_stage(qa_ctx* ctx, const qa_clip* clips, int n, const qa_result* results) {
   TRY(need_loaded(ctx));
   const qa_cfg& c = ctx->cfg;
   if (!clips || !results || n <= 0) return fail(ctx, QA_ERR_ARG, "empty batch");
+  if (!ctx->staged) ctx->staged.reset(new Staged());
+  Staged& S = *ctx->staged;
+  S.valid = false;
   cudaStream_t s = ctx->stream;
   const int cs = 2 * c.n_window;
-  Plan P;
+  Plan& P = S.P;
+  P = Plan();
   P.n = n;
   std::vector<int> frames(n);
   std::vector<uint32_t> ids;
   long long total_samples = 0;
-  bool want_logits = false, want_normed = false;
+  S.want_logits = S.want_normed = false;
+  S.n_ts.assign(n, 0);
   // ---- validate and plan (host)
   for (int i = 0; i < n; ++i) {
     const qa_clip& cl = clips[i];
@@ -1194,10 +1249,11 @@ int qa_align_batch(qa_ctx* ctx, const qa_clip* clips, int n, qa_result* results)
     }
     if (pads != na)
       return fail(ctx, QA_ERR_SHAPE, "clip %d: %d audio tokens in the input, the audio gives %d", i, pads, na);
-    if (ts != results[i].n_ts || !results[i].raw_ms)
+    if (ts != results[i].n_ts)
       return fail(ctx, QA_ERR_SHAPE, "clip %d: %d timestamp tokens, result holds %d", i, ts, results[i].n_ts);
-    want_logits |= results[i].logits != nullptr;
-    want_normed |= results[i].normed != nullptr;
+    S.n_ts[i] = ts;
+    S.want_logits |= results[i].logits != nullptr;
+    S.want_normed |= results[i].normed != nullptr;
     P.mel.push_back({total_samples, static_cast<int>(cl.n_samples), P.total_frames, frames[i], P.total_chunks});
     const int nch = (frames[i] + cs - 1) / cs;
     for (int k = 0; k < nch; ++k) P.chunk_clip.push_back(i);
@@ -1224,76 +1280,155 @@ int qa_align_batch(qa_ctx* ctx, const qa_clip* clips, int n, qa_result* results)
     P.ts_off[i + 1] = static_cast<int>(P.ts_rows.size());
   }
   plan_decoder(P);
-  const int R = static_cast<int>(P.ts_rows.size());
-
-  // ---- device pass
+  S.R = static_cast<int>(P.ts_rows.size());
+  // ---- inputs to the device (sample staging is pinned; one copy each)
   CK(cudaEventRecord(ctx->ev[0], s));
   TRY(reset_flags(ctx));
   TRY(ensure(ctx, ctx->samples, total_samples * 4));
   TRY(ensure_pin(ctx, ctx->pin_out, total_samples * 4));
-  {
-    float* st = static_cast<float*>(ctx->pin_out.p);
-    for (int i = 0; i < n; ++i) std::memcpy(st + P.mel[i].sample_off, clips[i].samples, clips[i].n_samples * 4);
-    CK(cudaMemcpyAsync(ctx->samples.p, st, total_samples * 4, cudaMemcpyHostToDevice, s));
-  }
-  PlanDev D{};
-  TRY(upload_plan(ctx, P, ids, D));
+  float* st = static_cast<float*>(ctx->pin_out.p);
+  for (int i = 0; i < n; ++i) std::memcpy(st + P.mel[i].sample_off, clips[i].samples, clips[i].n_samples * 4);
+  CK(cudaMemcpyAsync(ctx->samples.p, st, total_samples * 4, cudaMemcpyHostToDevice, s));
+  TRY(upload_plan(ctx, P, ids, S.D));
   CK(cudaEventRecord(ctx->ev[1], s));
-  // (a) mel
+  S.h2d_bytes = total_samples * 4 + static_cast<long long>(ids.size()) * 4 +
+                 static_cast<long long>(P.mel.size() * sizeof(MelClip) + P.chunk_clip.size() * 4 +
+                                        P.co_map.size() * 4 + P.windows.size() * 8 +
+                                        P.p2_map.size() * 4 + P.clip_of.size() * 8 +
+                                        P.block_tab.size() * 4 + P.tiles.size() * sizeof(AttnTile) +
+                                        P.ts_rows.size() * 4);
+  // workspaces sized here so that qa_batch_run allocates nothing
+  const int H = c.hidden_size;
   TRY(ensure(ctx, ctx->mel_scratch, static_cast<size_t>(P.total_frames) * 128 * 4));
   TRY(ensure(ctx, ctx->mel_chunked, static_cast<size_t>(P.total_chunks) * 128 * cs * 4));
   TRY(ensure(ctx, ctx->maxkey, static_cast<size_t>(n) * 4));
+  TRY(ensure(ctx, ctx->hid, static_cast<size_t>(P.T_d) * H * 2));
+  S.valid = true;
+  return QA_OK;
+}
+
+int qa_batch_run(qa_ctx* ctx) {
+  if (!ctx) return QA_ERR_ARG;
+  if (!ctx->loaded || !ctx->staged || !ctx->staged->valid)
+    return fail(ctx, QA_ERR_STATE, "qa_batch_run needs a staged batch (qa_batch_stage)");
+  CK(cudaSetDevice(ctx->device));
+  ctx->launches = 0;
+  Staged& S = *ctx->staged;
+  const Plan& P = S.P;
+  const PlanDev& D = S.D;
+  const qa_cfg& c = ctx->cfg;
+  cudaStream_t s = ctx->stream;
+  const int cs = 2 * c.n_window, n = P.n, H = c.hidden_size;
+  CK(cudaEventRecord(ctx->ev[2], s));
+  TRY(reset_flags(ctx));
+  // (a) mel
   CK(cudaMemsetAsync(ctx->maxkey.p, 0, static_cast<size_t>(n) * 4, s));
   const Weights& W = ctx->w;
   MelBank bank{W.fb_start, W.fb_len, W.fb_woff, W.fb_w};
-  KL(mel_logpower(ctx->samples.as<float>(), D.mel, n, P.max_frames, W.window, W.twiddle, bank,
+  KL("mel", 0, 4.0 * P.mel.back().sample_off + 4.0 * P.mel.back().n_samples + 512.0 * P.total_frames,
+     mel_logpower(ctx->samples.as<float>(), D.mel, n, P.max_frames, W.window, W.twiddle, bank,
                   1.0f / std::log(10.0f), ctx->mel_scratch.as<float>(), ctx->maxkey.as<unsigned>(), s));
-  KL(mel_finalize_chunked(ctx->mel_scratch.as<float>(), D.mel, D.chunk_clip, P.total_chunks, cs,
+  KL("mel_finalize", 0, 512.0 * P.total_frames + 512.0 * P.total_chunks * cs,
+     mel_finalize_chunked(ctx->mel_scratch.as<float>(), D.mel, D.chunk_clip, P.total_chunks, cs,
                           ctx->maxkey.as<unsigned>(), ctx->mel_chunked.as<float>(), s));
-  CK(cudaEventRecord(ctx->ev[2], s));
-  // (b) audio tower, projected rows scattered straight into the decoder input
-  const int H = c.hidden_size;
-  TRY(ensure(ctx, ctx->hid, static_cast<size_t>(P.T_d) * H * 2));
-  TRY(run_encoder(ctx, P, D, ctx->hid.p, D.p2_map));
   CK(cudaEventRecord(ctx->ev[3], s));
-  // embedding gather for the text rows
-  KL(embed_gather(D.ids, P.T_d, W.embed, c.vocab_size, H, c.audio_token_id, ctx->hid.p,
-                  ctx->badflag.as<int>(), s));
+  // (b) audio tower, projected rows scattered straight into the decoder input
+  TRY(run_encoder(ctx, P, D, ctx->hid.p, D.p2_map));
   CK(cudaEventRecord(ctx->ev[4], s));
+  // embedding gather for the text rows
+  KL("embed", 0, 4.0 * (P.T_d - P.T_a) * H,
+     embed_gather(D.ids, P.T_d, W.embed, c.vocab_size, H, c.audio_token_id, ctx->hid.p,
+                  ctx->badflag.as<int>(), s));
+  CK(cudaEventRecord(ctx->ev[5], s));
   // (c)(d)(e) decoder prefill
   TRY(run_decoder(ctx, P, D));
-  CK(cudaEventRecord(ctx->ev[5], s));
-  // (f) head
-  TRY(run_head(ctx, ctx->hid.p, ctx->bf16 ? 1 : 0, D.ts_rows, R, want_logits, want_normed));
   CK(cudaEventRecord(ctx->ev[6], s));
-  // readback
-  const size_t out_bytes = static_cast<size_t>(R) * 8;
-  TRY(ensure_pin(ctx, ctx->pin_res, out_bytes));
-  CK(cudaMemcpyAsync(ctx->pin_res.p, ctx->head_raw.p, out_bytes, cudaMemcpyDeviceToHost, s));
+  // (f) head
+  TRY(run_head(ctx, ctx->hid.p, ctx->bf16 ? 1 : 0, D.ts_rows, S.R, S.want_logits, S.want_normed));
   CK(cudaEventRecord(ctx->ev[7], s));
+  ctx->timings.gpu_launches = ctx->launches;
+  return QA_OK;
+}
+
+int qa_batch_fetch(qa_ctx* ctx, qa_result* results) {
+  if (!ctx || !results) return QA_ERR_ARG;
+  if (!ctx->staged || !ctx->staged->valid) return fail(ctx, QA_ERR_STATE, "no staged batch");
+  CK(cudaSetDevice(ctx->device));
+  Staged& S = *ctx->staged;
+  const Plan& P = S.P;
+  const qa_cfg& c = ctx->cfg;
+  const int H = c.hidden_size;
+  cudaStream_t s = ctx->stream;
+  for (int i = 0; i < P.n; ++i)
+    if (results[i].n_ts != S.n_ts[i] || (S.n_ts[i] > 0 && !results[i].raw_ms))
+      return fail(ctx, QA_ERR_SHAPE, "clip %d: result holds %d timestamps, the batch has %d", i,
+                  results[i].n_ts, S.n_ts[i]);
+  CK(cudaEventRecord(ctx->ev[8], s));
+  const size_t raw_bytes = static_cast<size_t>(S.R) * 8;
+  const size_t lg_bytes = S.want_logits ? static_cast<size_t>(S.R) * c.num_labels * 4 : 0;
+  const size_t nm_bytes = S.want_normed ? static_cast<size_t>(S.R) * H * 4 : 0;
+  TRY(ensure_pin(ctx, ctx->pin_res, raw_bytes + lg_bytes + nm_bytes + 16));
+  uint8_t* pr = static_cast<uint8_t*>(ctx->pin_res.p);
+  CK(cudaMemcpyAsync(pr, ctx->head_raw.p, raw_bytes, cudaMemcpyDeviceToHost, s));
+  if (lg_bytes) CK(cudaMemcpyAsync(pr + raw_bytes, ctx->head_logits.p, lg_bytes, cudaMemcpyDeviceToHost, s));
+  if (nm_bytes) CK(cudaMemcpyAsync(pr + raw_bytes + lg_bytes, ctx->head_normed.p, nm_bytes, cudaMemcpyDeviceToHost, s));
+  CK(cudaEventRecord(ctx->ev[9], s));
   TRY(wait_stream(ctx));
   TRY(check_status(ctx));
-  const int64_t* raw = static_cast<const int64_t*>(ctx->pin_res.p);
-  for (int i = 0; i < n; ++i) {
+  const int64_t* raw = reinterpret_cast<const int64_t*>(pr);
+  const float* lg = reinterpret_cast<const float*>(pr + raw_bytes);
+  const float* nm = reinterpret_cast<const float*>(pr + raw_bytes + lg_bytes);
+  for (int i = 0; i < P.n; ++i) {
     const int o = P.ts_off[i], k = P.ts_off[i + 1] - o;
-    std::memcpy(results[i].raw_ms, raw + o, static_cast<size_t>(k) * 8);
-    if (results[i].logits)
-      CK(cudaMemcpy(results[i].logits, ctx->head_logits.as<float>() + static_cast<size_t>(o) * c.num_labels,
-                    static_cast<size_t>(k) * c.num_labels * 4, cudaMemcpyDeviceToHost));
-    if (results[i].normed)
-      CK(cudaMemcpy(results[i].normed, ctx->head_normed.as<float>() + static_cast<size_t>(o) * H,
-                    static_cast<size_t>(k) * H * 4, cudaMemcpyDeviceToHost));
+    if (k) std::memcpy(results[i].raw_ms, raw + o, static_cast<size_t>(k) * 8);
+    if (results[i].logits && lg_bytes)
+      std::memcpy(results[i].logits, lg + static_cast<size_t>(o) * c.num_labels, static_cast<size_t>(k) * c.num_labels * 4);
+    if (results[i].normed && nm_bytes)
+      std::memcpy(results[i].normed, nm + static_cast<size_t>(o) * H, static_cast<size_t>(k) * H * 4);
   }
   qa_timings& t = ctx->timings;
   t.h2d_ms = elapsed(ctx, 0, 1);
-  t.mel_ms = elapsed(ctx, 1, 2);
-  t.enc_ms = elapsed(ctx, 2, 3);
-  t.gather_ms = elapsed(ctx, 3, 4);
-  t.prefill_ms = elapsed(ctx, 4, 5);
-  t.head_ms = elapsed(ctx, 5, 6);
-  t.d2h_ms = elapsed(ctx, 6, 7);
-  t.total_ms = elapsed(ctx, 0, 7);
-  t.gpu_launches = ctx->launches;
+  t.mel_ms = elapsed(ctx, 2, 3);
+  t.enc_ms = elapsed(ctx, 3, 4);
+  t.gather_ms = elapsed(ctx, 4, 5);
+  t.prefill_ms = elapsed(ctx, 5, 6);
+  t.head_ms = elapsed(ctx, 6, 7);
+  t.d2h_ms = elapsed(ctx, 8, 9);
+  t.total_ms = t.h2d_ms + elapsed(ctx, 2, 7) + t.d2h_ms;
+  t.h2d_bytes = S.h2d_bytes;
+  t.d2h_bytes = static_cast<long long>(raw_bytes + lg_bytes + nm_bytes);
+  return QA_OK;
+}
+
+int qa_align_batch(qa_ctx* ctx, const qa_clip* clips, int n, qa_result* results) {
+  TRY(qa_batch_stage(ctx, clips, n, results));
+  TRY(qa_batch_run(ctx));
+  return qa_batch_fetch(ctx, results);
+}
+
+int qa_set_stream(qa_ctx* ctx, void* stream) {
+  if (!ctx) return QA_ERR_ARG;
+  ctx->stream = stream ? static_cast<cudaStream_t>(stream) : ctx->own_stream;
+  return QA_OK;
+}
+
+int qa_set_profile(qa_ctx* ctx, int on) {
+  if (!ctx) return QA_ERR_ARG;
+  ctx->profile = on != 0;
+  ctx->prof_recs.clear();
+  ctx->prof_next = 0;
+  ctx->prof_names.clear();
+  ctx->prof_stats.clear();
+  return QA_OK;
+}
+
+int qa_get_profile(qa_ctx* ctx, qa_kernel_stat* stats, int max, int* n) {
+  if (!ctx || !n) return QA_ERR_ARG;
+  CK(cudaSetDevice(ctx->device));
+  TRY(wait_stream(ctx));  // resolves pending records
+  const int k = static_cast<int>(ctx->prof_stats.size());
+  *n = k;
+  for (int i = 0; i < k && i < max && stats; ++i) stats[i] = ctx->prof_stats[i];
   return QA_OK;
 }
 

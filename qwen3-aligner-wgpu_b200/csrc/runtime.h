@@ -5,6 +5,8 @@
 
 #include <cstdint>
 #include <string>
+#include <map>
+#include <memory>
 #include <vector>
 
 #include "gemm_tc.cuh"
@@ -79,6 +81,66 @@ struct Weights {
   float *rope_cos, *rope_sin;  // [max_seq][hd/2]
 };
 
+// Host-side bookkeeping for one batch of clips (all indices into packed
+// device buffers).  Built once per call, uploaded as one int buffer.
+struct Plan {
+  int n = 0;
+  // mel
+  std::vector<MelClip> mel;
+  std::vector<int> chunk_clip;
+  int total_frames = 0, total_chunks = 0, max_frames = 0;
+  // audio tower
+  std::vector<int> atok0, n_audio;
+  int T_a = 0;
+  std::vector<int> co_map;     // [total_chunks*13] -> packed audio row or -1
+  std::vector<int2> windows;   // encoder windows
+  // decoder
+  std::vector<int> tok0, seq;
+  int T_d = 0;
+  std::vector<int> p2_map;     // [T_a] -> packed decoder row
+  std::vector<int> clip_of, pos_of;
+  std::vector<int> block_tab;  // [n][max_pages]
+  int max_pages = 0, total_pages = 0;
+  std::vector<AttnTile> tiles;
+  // head
+  std::vector<int> ts_rows;    // packed decoder rows of <timestamp> tokens
+  std::vector<int> ts_off;     // per clip offset into ts_rows
+};
+
+// Device copies of the plan's arrays inside ctx->idx_dev.
+struct PlanDev {
+  MelClip* mel;
+  int* chunk_clip;
+  int* co_map;
+  int2* windows;
+  int* p2_map;
+  int* clip_of;
+  int* pos_of;
+  int* block_tab;
+  AttnTile* tiles;
+  int* ts_rows;
+  uint32_t* ids;
+};
+
+
+// A batch staged by qa_batch_stage, kept until the next stage call.
+struct Staged {
+  Plan P;
+  PlanDev D;
+  std::vector<int> n_ts;
+  int R = 0;
+  bool want_logits = false, want_normed = false;
+  long long h2d_bytes = 0;
+  bool valid = false;
+};
+
+// One profiled launch: CUDA events around it on the launching stream.
+struct ProfRec {
+  int cls;
+  int ev0, ev1;
+  double flops, bytes;
+};
+
 }  // namespace qa
 
 struct qa_ctx {
@@ -101,7 +163,16 @@ struct qa_ctx {
   qa::PinBuf pin_in, pin_out, pin_res;  // plan staging, sample staging, results
   int kv_pages = 0;     // pages per layer the cache holds
   int kv_cap_tokens = 0;
-  cudaEvent_t ev[10] = {};
+  cudaEvent_t ev[12] = {};
+  cudaStream_t own_stream = nullptr;  // the context's stream (stream may be the caller's)
+  std::unique_ptr<qa::Staged> staged;
+  // live profile (qa_set_profile)
+  bool profile = false;
+  std::vector<cudaEvent_t> prof_pool;
+  int prof_next = 0;
+  std::vector<qa::ProfRec> prof_recs;
+  std::vector<std::string> prof_names;
+  std::vector<qa_kernel_stat> prof_stats;
   qa_timings timings{};
   long long launches = 0;
 };

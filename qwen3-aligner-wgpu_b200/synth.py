@@ -479,8 +479,12 @@ class Clip:
     seconds: float
 
 
-def workload(config: int, seed_base: int = None, n_clips: int = None) -> list:
-    """The clips of a BASELINE configuration (0-4), seeded 1000 * config + i."""
+def workload(config: int, seed_base: int = None, n_clips: int = None, start: int = 0) -> list:
+    """The clips of a BASELINE configuration (0-4), clip i seeded 1000 * config + i.
+
+    ``n_clips`` overrides the configuration's clip count (configs 2 and 4) and
+    ``start`` skips the first clips, so shards of a long stream (one per GPU)
+    can be generated without synthesising the others."""
     clips = []
 
     def one(i, seconds, n_words, mix_cjk=False):
@@ -504,20 +508,20 @@ def workload(config: int, seed_base: int = None, n_clips: int = None) -> list:
     elif config == 1:
         clips.append(one(0, 60.0, 180))
     elif config == 2:
-        rng = np.random.default_rng(2000)
         n = 64 if n_clips is None else n_clips
-        for i in range(n):
-            sec = float(rng.uniform(5, 30))
-            rate = float(rng.uniform(2.5, 3.5))
+        rng = np.random.default_rng(2000)
+        spec = [(float(rng.uniform(5, 30)), float(rng.uniform(2.5, 3.5))) for _ in range(start + n)]
+        for i in range(start, start + n):
+            sec, rate = spec[i]
             clips.append(one(i, sec, max(1, int(round(sec * rate))), mix_cjk=True))
     elif config == 3:
         clips.append(one(0, 300.0, 900))
     elif config == 4:
-        rng = np.random.default_rng(4000)
         n = 4096 if n_clips is None else n_clips
-        for i in range(n):
-            sec = float(rng.uniform(5, 60))
-            clips.append(one(i, sec, max(1, int(round(sec * 3.0)))))
+        rng = np.random.default_rng(4000)
+        spec = [float(rng.uniform(5, 60)) for _ in range(start + n)]
+        for i in range(start, start + n):
+            clips.append(one(i, spec[i], max(1, int(round(spec[i] * 3.0)))))
     else:
         raise ValueError(config)
     return clips
