@@ -159,6 +159,12 @@ int qa_text_hidden(qa_ctx* ctx, const uint16_t* emb, int seq, float* out);
 int qa_head(qa_ctx* ctx, const float* hidden, int seq, const int* rows, int n_rows,
             int64_t* raw_ms, float* logits, float* normed);
 
+/* Timestamp repair (src/postprocess.rs:33-113, `fix_timestamps`): longest
+ * non-decreasing subsequence by O(n^2) DP with earliest-index ties; runs of
+ * <= 2 outliers snap to the nearer neighbour by index distance, longer runs
+ * are interpolated in f64 and truncated toward zero.  out may alias data. */
+int qa_fix_timestamps(const int64_t* data, int n, int64_t* out);
+
 /* ---------------------------------------------------------------- batched path */
 
 typedef struct {

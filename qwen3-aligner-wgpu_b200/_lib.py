@@ -56,7 +56,7 @@ EXPORTED = [
     "qa_open", "qa_load", "qa_close", "qa_last_error", "qa_set_timeout_ms", "qa_half",
     "qa_get_timings", "qa_mel", "qa_audio_embeds", "qa_ensure_capacity", "qa_text_hidden",
     "qa_head", "qa_align_batch", "qa_batch_stage", "qa_batch_run", "qa_batch_fetch",
-    "qa_set_stream", "qa_set_profile", "qa_get_profile",
+    "qa_set_stream", "qa_set_profile", "qa_get_profile", "qa_fix_timestamps",
     "qa_k_gemm",
 ]
 
@@ -191,6 +191,7 @@ def _declare(L: ctypes.CDLL) -> None:
                               c_void_p]
         L.qa_align_batch.argtypes = [c_void_p, c_void_p, c_int, c_void_p]
         L.qa_batch_stage.argtypes = [c_void_p, c_void_p, c_int, c_void_p]
+        L.qa_fix_timestamps.argtypes = [c_void_p, c_int, c_void_p]
         L.qa_batch_run.argtypes = [c_void_p]
         L.qa_batch_fetch.argtypes = [c_void_p, c_void_p]
         L.qa_set_stream.argtypes = [c_void_p, c_void_p]
@@ -205,6 +206,16 @@ def check(rc: int, ctx=None) -> None:
             m = lib().qa_last_error(ctx)
             msg = m.decode() if m else ""
         raise QaError(rc, msg)
+
+
+def fix_timestamps(raw) -> list:
+    """qa_fix_timestamps over an int64 sequence (the compiled LIS repair)."""
+    import numpy as np
+    a = np.ascontiguousarray(raw, np.int64)
+    out = np.empty_like(a)
+    if len(a):
+        check(lib().qa_fix_timestamps(a.ctypes.data, len(a), out.ctypes.data))
+    return out.tolist()
 
 
 def ptr(t) -> int:

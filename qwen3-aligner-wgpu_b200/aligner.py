@@ -140,7 +140,7 @@ class Aligner:
         raws = self.align_inputs([c[0] for c in clips], inputs, want_logits, want_normed)
         out = []
         for (r, extra), inp in zip(raws, inputs):
-            items = postprocess.decode_timestamps(inp.words, r.tolist())
+            items = postprocess.pair_words(inp.words, _lib.fix_timestamps(r))
             out.append((r, items) if not (want_logits or want_normed) else (r, items, extra))
         return out
 

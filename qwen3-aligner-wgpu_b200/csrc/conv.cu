@@ -17,41 +17,51 @@ __device__ __forceinline__ float gelu_erf(float x) {
   return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
 }
 
-// One CTA per (chunk, output row oh): stage the three input rows and the
-// weights in shared memory, write [wo][c_out] contiguously.
+// One CTA per (chunk, output row oh).  The three input rows are staged in
+// shared memory; thread j owns output channels 2j and 2j+1, keeps their 18
+// weights and 2 biases in registers and walks the row's output positions, so
+// each input tap is a shared-memory broadcast and each store is a coalesced
+// 2 x 16-bit word.
 template <typename T>
 __global__ void __launch_bounds__(256) conv1_kernel(const float* __restrict__ mel, int h, int w,
                                                     const float* __restrict__ wt,
                                                     const float* __restrict__ bias, int c_out,
                                                     T* __restrict__ out) {
-  extern __shared__ float sm[];
+  extern __shared__ float s_in[];  // [3][w]
   const int ho = (h + 2 - 3) / 2 + 1, wo = (w + 2 - 3) / 2 + 1;
   const int chunk = blockIdx.y, oh = blockIdx.x;
-  float* s_in = sm;              // [3][w]
-  float* s_w = sm + 3 * w;       // [c_out][9]
-  float* s_b = s_w + c_out * 9;  // [c_out]
   const float* src = mel + static_cast<long long>(chunk) * h * w;
   for (int i = threadIdx.x; i < 3 * w; i += blockDim.x) {
     const int r = i / w, col = i % w;
     const int ih = 2 * oh + r - 1;
     s_in[i] = (ih >= 0 && ih < h) ? src[ih * w + col] : 0.0f;
   }
-  for (int i = threadIdx.x; i < c_out * 9; i += blockDim.x) s_w[i] = wt[i];
-  for (int i = threadIdx.x; i < c_out; i += blockDim.x) s_b[i] = bias[i];
   __syncthreads();
   T* dst = out + (static_cast<long long>(chunk) * ho + oh) * wo * c_out;
-  for (int i = threadIdx.x; i < wo * c_out; i += blockDim.x) {
-    const int oc = i % c_out, ow = i / c_out;
-    float acc = 0.0f;
+  for (int pair = threadIdx.x; pair < c_out / 2; pair += blockDim.x) {
+    const int oc = 2 * pair;
+    float w0[9], w1[9];
 #pragma unroll
-    for (int kh = 0; kh < 3; ++kh)
+    for (int k = 0; k < 9; ++k) {
+      w0[k] = wt[oc * 9 + k];
+      w1[k] = wt[(oc + 1) * 9 + k];
+    }
+    const float b0 = bias[oc], b1 = bias[oc + 1];
+    for (int ow = 0; ow < wo; ++ow) {
+      float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll
-      for (int kw = 0; kw < 3; ++kw) {
-        const int iw = 2 * ow + kw - 1;
-        const float v = (iw >= 0 && iw < w) ? s_in[kh * w + iw] : 0.0f;
-        acc = fmaf(s_w[oc * 9 + kh * 3 + kw], v, acc);
-      }
-    dst[i] = f2h<T>(gelu_erf(acc + s_b[oc]));
+      for (int kh = 0; kh < 3; ++kh)
+#pragma unroll
+        for (int kw = 0; kw < 3; ++kw) {
+          const int iw = 2 * ow + kw - 1;
+          const float v = (iw >= 0 && iw < w) ? s_in[kh * w + iw] : 0.0f;
+          a0 = fmaf(w0[kh * 3 + kw], v, a0);
+          a1 = fmaf(w1[kh * 3 + kw], v, a1);
+        }
+      T pr[2] = {f2h<T>(gelu_erf(a0 + b0)), f2h<T>(gelu_erf(a1 + b1))};
+      *reinterpret_cast<uint32_t*>(dst + static_cast<long long>(ow) * c_out + oc) =
+          *reinterpret_cast<const uint32_t*>(pr);
+    }
   }
 }
 
@@ -87,20 +97,16 @@ __global__ void im2col_kernel(const uint4* __restrict__ x, int n, int h, int w, 
 int conv1_direct(const float* mel, int n, int h, int w, const float* wt, const float* bias,
                  int c_out, void* out, bool bf16, cudaStream_t s) {
   if (n <= 0) return 0;
+  if (c_out % 2 || 3 * w * sizeof(float) > 48 * 1024) return (int)cudaErrorInvalidValue;
   const int ho = (h + 2 - 3) / 2 + 1;
-  const size_t smem = (3 * w + c_out * 10) * sizeof(float);
+  const size_t smem = 3 * w * sizeof(float);
   dim3 grid(ho, n);
-  if (bf16) {
-    cudaFuncSetAttribute(conv1_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
+  if (bf16)
     conv1_kernel<__nv_bfloat16><<<grid, 256, smem, s>>>(mel, h, w, wt, bias, c_out,
                                                         static_cast<__nv_bfloat16*>(out));
-  } else {
-    cudaFuncSetAttribute(conv1_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
+  else
     conv1_kernel<__half><<<grid, 256, smem, s>>>(mel, h, w, wt, bias, c_out,
                                                  static_cast<__half*>(out));
-  }
   return (int)cudaGetLastError();
 }
 

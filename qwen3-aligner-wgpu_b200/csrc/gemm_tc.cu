@@ -76,6 +76,12 @@ __device__ __forceinline__ void load16_row(const T* src, float (&v)[32], int nco
   }
 }
 
+// 32 consecutive f32 of one row: 16-byte vector accesses when the row
+// segment is whole and aligned.
+__device__ __forceinline__ bool vec_ok(const void* p, int ncols) {
+  return ncols == 32 && (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
 template <int BN, typename T>
 __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row, int row, int M,
                                          int n0, int N) {
@@ -93,7 +99,7 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
         for (int i = 0; i < 32; ++i) {
           const float gh = round16<T>(g[i]);
           const float uh = round16<T>(u[i]);
-          const float silu = gh / (1.0f + expf(-gh));
+          const float silu = __fdividef(gh, 1.0f + __expf(-gh));
           g[i] = silu * uh;
         }
         const int oc = n0 / 2 + c0;
@@ -113,11 +119,19 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
       tmem_ld32(tmem_row + c0, v);
       if (row < M) {
         const int nc = min(min(32, BN - c0), N - (n0 + c0));
+        float* orow = out ? out + (long long)row * ep.ldo + n0 + c0 : nullptr;
+        if (orow && vec_ok(orow, nc)) {
+          float4* d4 = reinterpret_cast<float4*>(orow);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          orow = nullptr;
+        }
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          if (i >= nc) break;
+          if (i >= nc) continue;
           const float x = v[i];
-          if (out) out[(long long)row * ep.ldo + n0 + c0 + i] = x;
+          if (orow) orow[i] = x;
           if (x == x) {  // NaN never wins, as in a strict `>` scan
             const unsigned long long k = argmax_key(x, n0 + c0 + i);
             best = k > best ? k : best;
@@ -138,9 +152,22 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
     const int nc = min(min(32, BN - c0), N - col);  // BN need not be a multiple of 32
     if (nc <= 0) continue;
     if (ep.bias) {
+      const float* bp = ep.bias + col;
+      if (vec_ok(bp, nc)) {
+        const float4* b4 = reinterpret_cast<const float4*>(bp);
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (i < nc) v[i] += ep.bias[col + i];
+        for (int i = 0; i < 8; ++i) {
+          const float4 t = b4[i];
+          v[4 * i] += t.x;
+          v[4 * i + 1] += t.y;
+          v[4 * i + 2] += t.z;
+          v[4 * i + 3] += t.w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < nc) v[i] += bp[i];
+      }
     }
     switch (ep.mode) {
       case EPI_STORE16: {
@@ -164,9 +191,20 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
       }
       case EPI_RESID32: {
         float* dst = static_cast<float*>(ep.out) + (long long)row * ep.ldo + col;
+        if (vec_ok(dst, nc)) {
+          float4* d4 = reinterpret_cast<float4*>(dst);
+          float4 h[8];
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (i < nc) dst[i] += v[i];
+          for (int i = 0; i < 8; ++i) h[i] = d4[i];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            d4[i] = make_float4(h[i].x + v[4 * i], h[i].y + v[4 * i + 1], h[i].z + v[4 * i + 2],
+                                h[i].w + v[4 * i + 3]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (i < nc) dst[i] += v[i];
+        }
         break;
       }
       case EPI_STORE32: {
@@ -180,9 +218,16 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
             if (i < nc) v[i] += pe[i];
         }
         float* dst = static_cast<float*>(ep.out) + (long long)orow * ep.ldo + col;
+        if (vec_ok(dst, nc)) {
+          float4* d4 = reinterpret_cast<float4*>(dst);
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (i < nc) dst[i] = v[i];
+          for (int i = 0; i < 8; ++i)
+            d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (i < nc) dst[i] = v[i];
+        }
         break;
       }
       default:
@@ -191,12 +236,19 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
   }
 }
 
+// Persistent kernel: gridDim.x CTAs (at most one per SM) walk the tile list
+// t = blockIdx.x, blockIdx.x + gridDim.x, ... with tiles numbered N-fastest so
+// that the CTAs in flight share A row-blocks and the whole B operand stays in
+// L2.  The accumulator is double-buffered in TMEM (2 x BN columns): the MMA
+// warp starts tile i+1 while the epilogue warps drain tile i.
 template <int BN, typename T>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    int M, int N, int K, EpiParams ep) {
   using Cfg = GemmCfg<BN>;
   constexpr int S = Cfg::kStages;
+  constexpr uint32_t kAccCols = Cfg::kTmemCols;      // columns per accumulator buffer
+  constexpr uint32_t kAllocCols = 2 * Cfg::kTmemCols;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -204,21 +256,27 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sB = smem + S * Cfg::kABytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBBytes);
   uint64_t* empty = full + S;
-  uint64_t* accb = empty + S;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(accb + 1);
+  uint64_t* tfull = empty + S;   // [2] accumulator ready for the epilogue
+  uint64_t* tempty = tfull + 2;  // [2] accumulator drained by the epilogue
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * kBM;
-  const int n0 = blockIdx.x * BN;
   const int nkb = (K + kBK - 1) / kBK;
+  const int n_tiles_n = (N + BN - 1) / BN;
+  const int n_tiles = n_tiles_n * ((M + kBM - 1) / kBM);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
-    mbar_init(accb, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 128);
+    }
+    *abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
   }
@@ -226,61 +284,88 @@ __global__ void __launch_bounds__(192, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
   }
-  if (warp == 1) tmem_alloc(tslot, Cfg::kTmemCols);
+  if (warp == 1) tmem_alloc(tslot, kAllocCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tslot;
 
+  auto timed_out = [&]() {
+    *abort_flag = 1;
+    if (ep.status) atomicOr(ep.status, kStatusTimeout);
+  };
+
   if (warp == 0) {
     if (lane == 0) {
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % S;
-        const uint32_t ph = (kb / S) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1u)) {
-          if (ep.status) atomicOr(ep.status, kStatusTimeout);
-          break;
+      uint32_t c = 0;  // k-blocks issued so far (ring position)
+      for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
+        const int m0 = (t / n_tiles_n) * kBM, n0 = (t % n_tiles_n) * BN;
+        for (int kb = 0; kb < nkb; ++kb, ++c) {
+          const int s = c % S;
+          const uint32_t ph = (c / S) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1u)) {
+            timed_out();
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], Cfg::kABytes + Cfg::kBBytes);
+          tma_load_2d(&tmA, &full[s], sA + s * Cfg::kABytes, kb * kBK, m0);
+          tma_load_2d(&tmB, &full[s], sB + s * Cfg::kBBytes, kb * kBK, n0);
         }
-        mbar_arrive_expect_tx(&full[s], Cfg::kABytes + Cfg::kBBytes);
-        tma_load_2d(&tmA, &full[s], sA + s * Cfg::kABytes, kb * kBK, m0);
-        tma_load_2d(&tmB, &full[s], sB + s * Cfg::kBBytes, kb * kBK, n0);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = f16_instr_desc(kBM, BN, H16Traits<T>::kBf16);
-      bool ok = true;
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % S;
-        const uint32_t ph = (kb / S) & 1;
-        if (!mbar_wait(&full[s], ph)) {
-          if (ep.status) atomicOr(ep.status, kStatusTimeout);
-          ok = false;
+      uint32_t c = 0;
+      int lt = 0;  // tiles done by this CTA
+      for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x, ++lt) {
+        const int buf = lt & 1;
+        if (!mbar_wait(&tempty[buf], ((lt >> 1) & 1) ^ 1u)) {
+          timed_out();
           break;
         }
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(sA + s * Cfg::kABytes);
-        const uint32_t b_addr = smem_u32(sB + s * Cfg::kBBytes);
+        const uint32_t acc = tbase + buf * kAccCols;
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb, ++c) {
+          const int s = c % S;
+          const uint32_t ph = (c / S) & 1;
+          if (!mbar_wait(&full[s], ph)) {
+            timed_out();
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + s * Cfg::kABytes);
+          const uint32_t b_addr = smem_u32(sB + s * Cfg::kBBytes);
 #pragma unroll
-        for (int k = 0; k < kBK / 16; ++k) {
-          const uint64_t da = sw128_kmajor_desc(a_addr + k * 32);
-          const uint64_t db = sw128_kmajor_desc(b_addr + k * 32);
-          mma_f16(tbase, da, db, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t da = sw128_kmajor_desc(a_addr + k * 32);
+            const uint64_t db = sw128_kmajor_desc(b_addr + k * 32);
+            mma_f16(acc, da, db, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[s]);
         }
-        mma_commit(&empty[s]);
+        if (!ok) break;
+        mma_commit(&tfull[buf]);
       }
-      if (ok) mma_commit(accb);
     }
   } else {
     const int q = warp & 3;
-    const bool ok = mbar_wait(accb, 0);
-    tc_fence_after();
-    if (ok) {
+    int lt = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++lt) {
+      const int buf = lt & 1;
+      if (*abort_flag || !mbar_wait(&tfull[buf], (lt >> 1) & 1)) {
+        if (lane == 0) timed_out();
+        break;
+      }
+      tc_fence_after();
+      const int m0 = (t / n_tiles_n) * kBM, n0 = (t % n_tiles_n) * BN;
       const int row = m0 + q * 32 + lane;
-      const uint32_t trow = tbase + (static_cast<uint32_t>(q * 32) << 16);
+      const uint32_t trow = tbase + buf * kAccCols + (static_cast<uint32_t>(q * 32) << 16);
       epilogue<BN, T>(ep, trow, row, M, n0, N);
-    } else if (lane == 0 && ep.status) {
-      atomicOr(ep.status, kStatusTimeout);
+      tc_fence_before();
+      mbar_arrive(&tempty[buf]);
     }
   }
 
@@ -288,8 +373,21 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tbase, Cfg::kTmemCols);
+    tmem_dealloc(tbase, kAllocCols);
   }
+}
+
+int num_sms() {
+  static int sms[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!sms[dev]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    sms[dev] = v > 0 ? v : 148;
+  }
+  return sms[dev];
 }
 
 template <int BN, typename T>
@@ -305,7 +403,8 @@ int launch(const void* A, long long lda, const void* B, long long ldb, int M, in
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmem);
   if (e != cudaSuccess) return (int)e;
-  dim3 grid((N + BN - 1) / BN, (M + kBM - 1) / kBM);
+  const int tiles = ((N + BN - 1) / BN) * ((M + kBM - 1) / kBM);
+  const int grid = tiles < num_sms() ? tiles : num_sms();
   kern<<<grid, 192, Cfg::kSmem, stream>>>(ta, tb, M, N, K, ep);
   return (int)cudaGetLastError();
 }

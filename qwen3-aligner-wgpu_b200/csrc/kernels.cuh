@@ -81,8 +81,9 @@ struct TokenMap {
 
 // (d) q/k RMSNorm + rotate-half RoPE, Q written in place into qkv's q part,
 // K (normed+roped) and V appended into the paged cache.
+// cos_t / sin_t: [max_seq][hd/2] in the storage format.
 int qk_norm_rope_append(void* qkv, int T, int nqh, int nkvh, int hd, const float* qn,
-                        const float* kn, float eps, const float* cos_t, const float* sin_t,
+                        const float* kn, float eps, const void* cos_t, const void* sin_t,
                         TokenMap tm, PagedKV kv, bool bf16, cudaStream_t s);
 
 // (e) causal GQA flash attention.  Q rows in qkv (row stride ldq, head h at

@@ -6,6 +6,7 @@
 #include "sm100.cuh"
 
 #include <algorithm>
+#include <atomic>
 #include <chrono>
 #include <cmath>
 #include <cstdarg>
@@ -643,8 +644,8 @@ int load_weights(qa_ctx* ctx, const qa_tensor* tensors, int n, const qa_cfg& c) 
         cs[static_cast<size_t>(t) * half + j] = round_half(static_cast<float>(std::cos(a)), bf);
         sn[static_cast<size_t>(t) * half + j] = round_half(static_cast<float>(std::sin(a)), bf);
       }
-    W.rope_cos = up_f32(ctx, cs, &rc);
-    W.rope_sin = up_f32(ctx, sn, &rc);
+    W.rope_cos = up_h16(ctx, cs, &rc);  // exact: the values are already rounded to the format
+    W.rope_sin = up_h16(ctx, sn, &rc);
     if (rc) return rc;
   }
   return QA_OK;
@@ -1287,7 +1288,19 @@ int qa_batch_stage(qa_ctx* ctx, const qa_clip* clips, int n, const qa_result* re
   TRY(ensure(ctx, ctx->samples, total_samples * 4));
   TRY(ensure_pin(ctx, ctx->pin_out, total_samples * 4));
   float* st = static_cast<float*>(ctx->pin_out.p);
-  for (int i = 0; i < n; ++i) std::memcpy(st + P.mel[i].sample_off, clips[i].samples, clips[i].n_samples * 4);
+  // clips spread over the host cores: one pass, pageable -> pinned
+  {
+    std::atomic<int> next{0};
+    auto worker = [&] {
+      for (int i = next++; i < n; i = next++)
+        std::memcpy(st + P.mel[i].sample_off, clips[i].samples, clips[i].n_samples * 4);
+    };
+    const int nt = std::max(1, std::min<int>(n, std::min<int>(8, std::thread::hardware_concurrency())));
+    std::vector<std::thread> th;
+    for (int k = 1; k < nt; ++k) th.emplace_back(worker);
+    worker();
+    for (auto& x : th) x.join();
+  }
   CK(cudaMemcpyAsync(ctx->samples.p, st, total_samples * 4, cudaMemcpyHostToDevice, s));
   TRY(upload_plan(ctx, P, ids, S.D));
   CK(cudaEventRecord(ctx->ev[1], s));

@@ -78,7 +78,7 @@ struct Weights {
   std::vector<DecLayerW> dec;
   float* final_norm;
   void* head_w2;  // [labels][2H] bf16: [score | score]
-  float *rope_cos, *rope_sin;  // [max_seq][hd/2]
+  void *rope_cos, *rope_sin;  // [max_seq][hd/2] in the storage format
 };
 
 // Host-side bookkeeping for one batch of clips (all indices into packed

@@ -281,34 +281,32 @@ class SyntheticTokenizer:
         h = hashlib.blake2b(piece.encode(), digest_size=8).digest()
         return int.from_bytes(h, "little") % self.ORDINARY
 
+    _SPLIT = None
+
     def encode(self, text: str) -> list:
-        ids, i, n = [], 0, len(text)
-        buf = ""
-        while i < n:
-            m = None
-            if text[i] == "<":
-                for k, v in self.MARKERS.items():
-                    if text.startswith(k, i):
-                        m = (k, v)
-                        break
-            if m:
-                if buf:
-                    ids += self._word(buf)
-                    buf = ""
-                ids.append(m[1])
-                i += len(m[0])
+        import re
+        if SyntheticTokenizer._SPLIT is None:
+            SyntheticTokenizer._SPLIT = re.compile(
+                "(" + "|".join(re.escape(k) for k in self.MARKERS) + ")")
+        ids = []
+        for part in self._SPLIT.split(text):
+            if not part:
                 continue
-            ch = text[i]
-            if 0x3400 <= ord(ch) <= 0x9FFF or 0xF900 <= ord(ch) <= 0xFAFF:
-                if buf:
-                    ids += self._word(buf)
-                    buf = ""
-                ids.append(self._piece_id(ch))
-            else:
-                buf += ch
-            i += 1
-        if buf:
-            ids += self._word(buf)
+            m = self.MARKERS.get(part)
+            if m is not None:
+                ids.append(m)
+                continue
+            buf = ""
+            for ch in part:
+                if 0x3400 <= ord(ch) <= 0x9FFF or 0xF900 <= ord(ch) <= 0xFAFF:
+                    if buf:
+                        ids += self._word(buf)
+                        buf = ""
+                    ids.append(self._piece_id(ch))
+                else:
+                    buf += ch
+            if buf:
+                ids += self._word(buf)
         return ids
 
     def _word(self, w: str) -> list:

@@ -53,6 +53,25 @@ def test_fix_timestamps_kats(orc):
     assert orc.fix_timestamps([]) == [] and post.fix_timestamps([]) == []
 
 
+def test_library_fix_timestamps_kats():
+    """The compiled repair in libqa_b200.so (the Aligner's host path) against
+    the reference's own cases and the Python restatement on random streams."""
+    import random
+    lib = pkg()._lib
+    post = pkg().postprocess
+    for case in KAT["fix_timestamps"]:
+        got = lib.fix_timestamps(case["data"])
+        if "want" in case:
+            assert got == case["want"], (case, got)
+        else:
+            assert all(a <= b for a, b in zip(got, got[1:]))
+    rnd = random.Random(3)
+    for _ in range(300):
+        n = rnd.randint(0, 40)
+        data = [rnd.choice([rnd.randint(0, 30) * 80, rnd.randint(0, 4000)]) for _ in range(n)]
+        assert lib.fix_timestamps(data) == post.fix_timestamps(data)
+
+
 def test_pairing_kat():
     post = pkg().postprocess
     k = KAT["pair_words"]
