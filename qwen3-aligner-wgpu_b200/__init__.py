@@ -9,6 +9,7 @@ repair) and the seeded synthetic assets the tests and benchmark run on.
 from . import _lib  # noqa: F401
 from . import postprocess  # noqa: F401
 from . import rope  # noqa: F401
+from . import shard  # noqa: F401
 from . import synth  # noqa: F401
 from .aligner import Aligner, FORCED_ALIGNER_LANGUAGES  # noqa: F401
 from ._lib import QaError  # noqa: F401
