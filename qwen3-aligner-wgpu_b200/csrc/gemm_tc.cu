@@ -82,9 +82,82 @@ __device__ __forceinline__ bool vec_ok(const void* p, int ncols) {
   return ncols == 32 && (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }
 
+// EPI_QKV_ROPE for one 128-column head of one row (this thread's row).
+template <typename T>
+__device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem_col0, int row,
+                                              int M, int head) {
+  constexpr int HD = 128;
+  float r[HD];
+#pragma unroll
+  for (int c = 0; c < HD / 32; ++c) {
+    float v[32];
+    tmem_ld32(tmem_col0 + c * 32, v);  // warp-collective: every lane loads
+#pragma unroll
+    for (int i = 0; i < 32; ++i) r[c * 32 + i] = round16<T>(v[i]);  // the GEMM's f16 rounding
+  }
+  if (row >= M) return;
+  const RopeKV& rk = ep.rk;
+  const int pos = rk.pos_of[row];
+  T* dst;
+  if (head < rk.nq) {
+    dst = static_cast<T*>(ep.out) + (long long)row * ep.ldo + head * HD;
+  } else {
+    const int clip = rk.clip_of[row];
+    const int page = rk.block_tab[clip * rk.max_pages + pos / rk.page_size];
+    const int kvh = head < rk.nq + rk.nkv ? head - rk.nq : head - rk.nq - rk.nkv;
+    const long long off =
+        ((static_cast<long long>(page) * rk.nkv + kvh) * rk.page_size + pos % rk.page_size) * HD;
+    dst = static_cast<T*>(head < rk.nq + rk.nkv ? rk.kc : rk.vc) + off;
+  }
+  alignas(16) T o[8];
+  if (head >= rk.nq + rk.nkv) {  // v: appended as rounded
+#pragma unroll
+    for (int j0 = 0; j0 < HD; j0 += 8) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = f2h<T>(r[j0 + j]);
+      *reinterpret_cast<uint4*>(dst + j0) = *reinterpret_cast<const uint4*>(o);
+    }
+    return;
+  }
+  // RMSNorm over the head's raw values (sequential sum, no FMA, as the
+  // reference's loop), per-element gain, then rotate-half RoPE at `pos`.
+  const float* nw = head < rk.nq ? rk.qn : rk.kn;
+  float s2 = 0.0f;
+#pragma unroll
+  for (int j = 0; j < HD; ++j) s2 = __fadd_rn(s2, __fmul_rn(r[j], r[j]));
+  const float inv = 1.0f / sqrtf(s2 / static_cast<float>(HD) + rk.eps);
+  const T* ct = static_cast<const T*>(rk.cos_t) + pos * (HD / 2);
+  const T* st = static_cast<const T*>(rk.sin_t) + pos * (HD / 2);
+#pragma unroll
+  for (int j0 = 0; j0 < HD; j0 += 8) {
+    const uint4 cu = *reinterpret_cast<const uint4*>(ct + (j0 & 63));
+    const uint4 su = *reinterpret_cast<const uint4*>(st + (j0 & 63));
+    const T* cv = reinterpret_cast<const T*>(&cu);
+    const T* sv = reinterpret_cast<const T*>(&su);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int d = j0 + j;
+      const int pd = d < 64 ? d + 64 : d - 64;
+      const float xj = __fmul_rn(__fmul_rn(r[d], inv), nw[d]);
+      const float xp = __fmul_rn(__fmul_rn(r[pd], inv), nw[pd]);
+      const float sxp = d < 64 ? -xp : xp;
+      o[j] = f2h<T>(__fadd_rn(__fmul_rn(xj, h2f<T>(cv[j])), __fmul_rn(sxp, h2f<T>(sv[j]))));
+    }
+    *reinterpret_cast<uint4*>(dst + j0) = *reinterpret_cast<const uint4*>(o);
+  }
+}
+
 template <int BN, typename T>
 __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row, int row, int M,
                                          int n0, int N) {
+  if constexpr (BN % 128 == 0) {
+    if (ep.mode == EPI_QKV_ROPE) {
+#pragma unroll 1
+      for (int hb = 0; hb < BN / 128; ++hb)
+        if (n0 + hb * 128 < N) qkv_rope_head<T>(ep, tmem_row + hb * 128, row, M, (n0 + hb * 128) / 128);
+      return;
+    }
+  }
   if (ep.mode == EPI_SWIGLU16) {
     // gate in columns [0, BN/2), up in [BN/2, BN) of this tile
     constexpr int H = BN / 2;
@@ -427,6 +500,7 @@ int gemm_tc(const void* A, long long lda, const void* B, long long ldb, int M, i
     return (int)cudaErrorInvalidValue;
   const int bn = force_bn ? force_bn : gemm_pick_bn(N);
   if (ep.mode == EPI_SWIGLU16 && ((N % bn) || (bn % 64))) return (int)cudaErrorInvalidValue;
+  if (ep.mode == EPI_QKV_ROPE && ((N % 128) || (bn % 128))) return (int)cudaErrorInvalidValue;
 #define QA_GEMM_CASE(BNV)                                                               \
   case BNV:                                                                             \
     return bf16 ? launch<BNV, __nv_bfloat16>(A, lda, B, ldb, M, N, K, ep, stream)       \

@@ -25,6 +25,28 @@ enum EpiMode : int {
   EPI_STORE32 = 4,
   // optional out32[r, c] = acc; keys[r] = max over c of (ordered(acc), ~c)
   EPI_ARGMAX = 5,
+  // decoder QKV projection with (d) fused: every 128-column head of the row is
+  // rounded to 16 bits, q/k heads get RMSNorm + rotate-half RoPE (Q written to
+  // out at the head's columns, K appended to the paged cache), v heads are
+  // appended as they are.  Tiles must be 256 wide (two heads).
+  EPI_QKV_ROPE = 6,
+};
+
+// Operands of EPI_QKV_ROPE (norm_rope_head, src/cpu_decoder.rs:305-321).
+struct RopeKV {
+  const int* pos_of = nullptr;     // [M] position of the row within its clip
+  const int* clip_of = nullptr;    // [M] clip of the row
+  const int* block_tab = nullptr;  // [clips][max_pages] page ids
+  int max_pages = 0;
+  int page_size = 64;
+  void* kc = nullptr;              // this layer's K pages [page][nkv][page_size][128]
+  void* vc = nullptr;
+  const void* cos_t = nullptr;     // [max_seq][64] in the storage format
+  const void* sin_t = nullptr;
+  const float* qn = nullptr;       // [128] q_norm gain (rounded to the storage format)
+  const float* kn = nullptr;
+  float eps = 1e-6f;
+  int nq = 16, nkv = 8;
 };
 
 enum EpiAct : int { ACT_NONE = 0, ACT_GELU = 1 };
@@ -40,6 +62,7 @@ struct EpiParams {
   int pe_period = 1;
   unsigned long long* keys = nullptr;  // EPI_ARGMAX: [M] packed (value, index) keys
   unsigned* status = nullptr;   // device status word (timeouts)
+  RopeKV rk;                    // EPI_QKV_ROPE only
 };
 
 // Launch D = A·Bᵀ.  A: [M, K] rows lda elements apart; B: [N, K] rows ldb

@@ -79,13 +79,6 @@ struct TokenMap {
   int max_pages;
 };
 
-// (d) q/k RMSNorm + rotate-half RoPE, Q written in place into qkv's q part,
-// K (normed+roped) and V appended into the paged cache.
-// cos_t / sin_t: [max_seq][hd/2] in the storage format.
-int qk_norm_rope_append(void* qkv, int T, int nqh, int nkvh, int hd, const float* qn,
-                        const float* kn, float eps, const void* cos_t, const void* sin_t,
-                        TokenMap tm, PagedKV kv, bool bf16, cudaStream_t s);
-
 // (e) causal GQA flash attention.  Q rows in qkv (row stride ldq, head h at
 // column h*hd), K/V from the paged cache, out [T][nqh*hd].  Work items are
 // (clip, q0) tiles of 64 queries.

@@ -1,6 +1,7 @@
 // HBM-bound row kernels of the alignment path: the audio tower's LayerNorm,
-// the decoder's RMSNorm, (d) q/k RMSNorm + RoPE + paged K/V append, the
-// embedding gather, and (f) the timestamp-row gather + final norm.
+// the decoder's RMSNorm, the embedding gather, and (f) the timestamp-row
+// gather + final norm.  (d), the q/k RMSNorm + RoPE + paged K/V append, runs
+// in the decoder QKV GEMM's epilogue (gemm_tc.cu, EPI_QKV_ROPE).
 //
 // One warp per row (or per (token, head)); 16-bit rows are read as 16-byte
 // vectors.  Arithmetic follows the reference's CPU order where it decides a
@@ -100,78 +101,6 @@ __global__ void rmsnorm_kernel(const T* __restrict__ x, int rows, int d,
   }
 }
 
-// ---------------------------------------------------------------- (d) q/k norm + rope + append
-// norm_rope_head (src/cpu_decoder.rs:305-321) for every q and k head of every
-// token, hd == 128.  One half-warp per head (two heads per warp): lane l of
-// the half holds dims 8l..8l+7 as one 16-byte vector; the rotate-half
-// partners (j +- 64) sit in lane l ^ 8.  The cos/sin tables are [pos][64] in
-// the storage format (the reference rounds them to it, src/align_inference.rs
-// :371-373, 394-396).  V rows are copied into the cache unchanged.
-template <typename T>
-__global__ void qk_norm_rope_kernel(T* __restrict__ qkv, int T_, int nqh, int nkvh,
-                                    const float* __restrict__ qn, const float* __restrict__ kn,
-                                    float eps, const T* __restrict__ cos_t,
-                                    const T* __restrict__ sin_t, TokenMap tm, PagedKV kv) {
-  constexpr int HD = 128;
-  const int nh = nqh + nkvh;  // even
-  const int pairs = nh / 2;
-  const long long item = blockIdx.x * static_cast<long long>(blockDim.x / 32) + threadIdx.x / 32;
-  const int lane = threadIdx.x & 31;
-  if (item >= static_cast<long long>(T_) * pairs) return;
-  const int t = static_cast<int>(item / pairs);
-  const int hh = 2 * static_cast<int>(item % pairs) + (lane >> 4);
-  const int l16 = lane & 15;
-  const long long ldq = static_cast<long long>(nqh + 2 * nkvh) * HD;
-  const int pos = tm.pos_of[t];
-  const bool is_q = hh < nqh;
-  T* src = qkv + t * ldq + static_cast<long long>(hh) * HD;  // k heads follow q heads
-  const float* nw = is_q ? qn : kn;
-
-  uint4 u = *reinterpret_cast<const uint4*>(src + 8 * l16);
-  const T* e = reinterpret_cast<const T*>(&u);
-  float r[8];
-  float s2 = 0.f;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    r[j] = h2f<T>(e[j]);
-    s2 = fmaf(r[j], r[j], s2);
-  }
-#pragma unroll
-  for (int o = 8; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xFFFFFFFFu, s2, o);
-  const float inv = 1.0f / sqrtf(s2 / static_cast<float>(HD) + eps);
-  const bool lo = l16 < 8;  // dims < 64: partner is j + 64, sign -1
-  const int tb = pos * 64 + ((8 * l16) & 63);
-  uint4 cu = *reinterpret_cast<const uint4*>(cos_t + tb);
-  uint4 su = *reinterpret_cast<const uint4*>(sin_t + tb);
-  const T* cv = reinterpret_cast<const T*>(&cu);
-  const T* sv = reinterpret_cast<const T*>(&su);
-  alignas(16) T o[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int dim = 8 * l16 + j;
-    const int pdim = lo ? dim + 64 : dim - 64;
-    const float rp = __shfl_xor_sync(0xFFFFFFFFu, r[j], 8);
-    const float xj = __fmul_rn(__fmul_rn(r[j], inv), nw[dim]);
-    const float xp = __fmul_rn(__fmul_rn(rp, inv), nw[pdim]);
-    const float sxp = lo ? -xp : xp;
-    o[j] = f2h<T>(__fadd_rn(__fmul_rn(xj, h2f<T>(cv[j])), __fmul_rn(sxp, h2f<T>(sv[j]))));
-  }
-  if (is_q) {
-    *reinterpret_cast<uint4*>(src + 8 * l16) = *reinterpret_cast<const uint4*>(o);
-    return;
-  }
-  const int kh = hh - nqh;
-  const int clip = tm.clip_of[t];
-  const int page = tm.block_tab[clip * tm.max_pages + pos / kv.page_size];
-  const long long off =
-      ((static_cast<long long>(page) * nkvh + kh) * kv.page_size + pos % kv.page_size) * HD;
-  *reinterpret_cast<uint4*>(static_cast<T*>(kv.k) + off + 8 * l16) =
-      *reinterpret_cast<const uint4*>(o);
-  const T* vsrc = qkv + t * ldq + static_cast<long long>(nqh + nkvh + kh) * HD;
-  *reinterpret_cast<uint4*>(static_cast<T*>(kv.v) + off + 8 * l16) =
-      *reinterpret_cast<const uint4*>(vsrc + 8 * l16);
-}
-
 // ---------------------------------------------------------------- embedding gather
 // src/align_inference.rs:690-715, on the device: one thread per 16 bytes.
 __global__ void embed_gather_kernel(const uint32_t* __restrict__ ids, int T_,
@@ -266,24 +195,6 @@ int rmsnorm_rows(const void* x, int rows, int d, const float* w, float eps, void
   else
     rmsnorm_kernel<<<blocks, 256, 0, s>>>(static_cast<const __half*>(x), rows, d, w, eps,
                                           static_cast<__half*>(out));
-  return (int)cudaGetLastError();
-}
-
-int qk_norm_rope_append(void* qkv, int T_, int nqh, int nkvh, int hd, const float* qn,
-                        const float* kn, float eps, const void* cos_t, const void* sin_t,
-                        TokenMap tm, PagedKV kv, bool bf16, cudaStream_t s) {
-  if (T_ <= 0) return 0;
-  if (hd != 128 || (nqh + nkvh) % 2) return (int)cudaErrorInvalidValue;
-  const long long items = static_cast<long long>(T_) * ((nqh + nkvh) / 2);
-  const unsigned blocks = (unsigned)((items + 7) / 8);
-  if (bf16)
-    qk_norm_rope_kernel<<<blocks, 256, 0, s>>>(
-        static_cast<__nv_bfloat16*>(qkv), T_, nqh, nkvh, qn, kn, eps,
-        static_cast<const __nv_bfloat16*>(cos_t), static_cast<const __nv_bfloat16*>(sin_t), tm, kv);
-  else
-    qk_norm_rope_kernel<<<blocks, 256, 0, s>>>(static_cast<__half*>(qkv), T_, nqh, nkvh, qn, kn,
-                                               eps, static_cast<const __half*>(cos_t),
-                                               static_cast<const __half*>(sin_t), tm, kv);
   return (int)cudaGetLastError();
 }
 

@@ -904,16 +904,29 @@ int run_decoder(qa_ctx* ctx, const Plan& P, const PlanDev& D) {
     const DecLayerW& L = ctx->w.dec[l];
     PagedKV kv{ctx->kcache.as<uint16_t>() + l * layer_kv, ctx->vcache.as<uint16_t>() + l * layer_kv, 64};
     KL("rmsnorm", 0, 4.0 * T * H, rmsnorm_rows(ctx->hid.p, T, H, L.iln, eps, ctx->xn.p, bf, s));
-    ep.mode = EPI_STORE16;
+    // QKV projection with (d) fused into its epilogue: Q (normed + roped)
+    // lands in the q columns of ctx->qkv, K and V in this layer's pages.
+    ep.mode = EPI_QKV_ROPE;
     ep.act = ACT_NONE;
     ep.bias = nullptr;
     ep.out = ctx->qkv.p;
     ep.ldo = ldq;
+    ep.rk.pos_of = D.pos_of;
+    ep.rk.clip_of = D.clip_of;
+    ep.rk.block_tab = D.block_tab;
+    ep.rk.max_pages = P.max_pages;
+    ep.rk.page_size = 64;
+    ep.rk.kc = kv.k;
+    ep.rk.vc = kv.v;
+    ep.rk.cos_t = ctx->w.rope_cos;
+    ep.rk.sin_t = ctx->w.rope_sin;
+    ep.rk.qn = L.qn;
+    ep.rk.kn = L.kn;
+    ep.rk.eps = eps;
+    ep.rk.nq = nq;
+    ep.rk.nkv = nkv;
     KL("gemm", gemm_flops(T, ldq, H), gemm_bytes(T, ldq, H, 2),
-       gemm_tc(ctx->xn.p, H, L.qkv_w, H, T, ldq, H, bf, ep, s));
-    KL("qk_rope_kv", 0, T * (4.0 * ldq + 2.0 * hd * 4.0),
-       qk_norm_rope_append(ctx->qkv.p, T, nq, nkv, hd, L.qn, L.kn, eps, ctx->w.rope_cos,
-                           ctx->w.rope_sin, tm, kv, bf, s));
+       gemm_tc(ctx->xn.p, H, L.qkv_w, H, T, ldq, H, bf, ep, s, 256));
     KL("causal_attn", attn_flops, T * (2.0 * qd * 2 + 2.0 * nkv * hd * 2),
        causal_attention(ctx->qkv.p, ldq, nq, nkv, hd, D.tiles, static_cast<int>(P.tiles.size()),
                         D.block_tab, P.max_pages, kv, ctx->attn.p, bf, s));
