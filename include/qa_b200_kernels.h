@@ -42,6 +42,18 @@ int qa_k_gemm(const void* A, long long lda, const void* B, long long ldb, int M,
               const int* row_map, const float* pe, int pe_period, unsigned long long* keys,
               unsigned* status, int force_bn, void* stream);
 
+/*
+ * Implicit-GEMM conv2d, 3x3 / stride 2 / pad 1, on the tcgen05 tensor cores:
+ * x NHWC [n][h][w][c] 16-bit, wt [c_out][9c] (k = (kh*3 + kw)*c + ic),
+ * output [n*ho*wo][c_out] through the same epilogues as qa_k_gemm (rows in
+ * (oh, ow) order, or (ow, oh) when time_major).  Stands in for the conv2 /
+ * conv3 levels of CpuConvStem::conv_block_stages (src/audio_encoder.rs:361-447)
+ * and the GPU tower's im2col + GEMM (src/audio_encoder_gpu.rs:1714-1795).
+ */
+int qa_k_conv3x3s2(const void* x, int n, int h, int w, int c, const void* wt, int c_out,
+                   int time_major, int bf16, int mode, int act, void* out, long long ldo,
+                   const float* bias, unsigned* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -57,7 +57,7 @@ EXPORTED = [
     "qa_get_timings", "qa_mel", "qa_audio_embeds", "qa_ensure_capacity", "qa_text_hidden",
     "qa_head", "qa_align_batch", "qa_batch_stage", "qa_batch_run", "qa_batch_fetch",
     "qa_set_stream", "qa_set_profile", "qa_get_profile", "qa_fix_timestamps",
-    "qa_k_gemm",
+    "qa_k_gemm", "qa_k_conv3x3s2",
 ]
 
 c_void_p = ctypes.c_void_p
@@ -173,6 +173,8 @@ def _declare(L: ctypes.CDLL) -> None:
                             c_int, c_void_p, c_ll, c_void_p, c_void_p, c_void_p, c_int, c_void_p,
                             c_void_p, c_int, c_void_p]
     L.qa_k_gemm.restype = c_int
+    L.qa_k_conv3x3s2.argtypes = [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_int,
+                                 c_int, c_int, c_int, c_void_p, c_ll, c_void_p, c_void_p, c_void_p]
     if hasattr(L, "qa_open"):
         L.qa_open.argtypes = [c_int, c_int, ctypes.POINTER(c_void_p)]
         L.qa_load.argtypes = [c_void_p, c_void_p, c_int, c_void_p]
@@ -235,4 +237,16 @@ def gemm(A, B, out, mode=EPI_STORE16, act=ACT_NONE, bias=None, row_map=None, pe=
     rc = lib().qa_k_gemm(ptr(A), A.stride(0), ptr(B), B.stride(0), M, N, K, bf16, mode, act,
                          ptr(out), out.stride(0) if out is not None else 0, ptr(bias),
                          ptr(row_map), ptr(pe), pe_period, ptr(keys), ptr(status), force_bn, s)
+    check(rc)
+
+
+def conv3x3s2(x, wt, out, time_major=False, mode=EPI_STORE16, act=ACT_NONE, bias=None,
+              status=None, stream=None):
+    """Implicit-GEMM conv on torch CUDA tensors: x [n, h, w, c] NHWC, wt [c_out, 9c]."""
+    import torch
+    n, h, w, c = x.shape
+    bf16 = 1 if x.dtype == torch.bfloat16 else 0
+    s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
+    rc = lib().qa_k_conv3x3s2(ptr(x), n, h, w, c, ptr(wt), wt.shape[0], 1 if time_major else 0,
+                              bf16, mode, act, ptr(out), out.stride(0), ptr(bias), ptr(status), s)
     check(rc)

@@ -1,14 +1,15 @@
 // tcgen05 / TMEM / TMA GEMM with fused epilogues (see gemm_tc.cuh).
 //
-// One CTA computes a 128 x BN tile.  Warp roles (192 threads):
+// One CTA computes 128 x BN tiles.  Warp roles (320 threads):
 //   warp 0      TMA producer: streams 128x64 A and BNx64 B tiles (128B swizzle)
 //               into a STAGES-deep shared-memory ring, one mbarrier per slot;
 //   warp 1      allocates the TMEM accumulator and issues tcgen05.mma
 //               (M=128, N=BN, K=16) from one thread; tcgen05.commit frees a
 //               ring slot when the MMAs reading it retire;
-//   warps 2..5  epilogue: tcgen05.ld 32x32b pulls one accumulator row per
-//               thread (warp w reads TMEM lanes 32*(w%4) .. +31), applies the
-//               fused epilogue and stores to global memory.
+//   warps 2..9  epilogue, two warpgroups that split each tile's columns:
+//               tcgen05.ld 32x32b pulls one accumulator row per thread (warp
+//               w reads TMEM lanes 32*(w%4) .. +31), applies the fused
+//               epilogue and stores to global memory.
 // Nothing here uses cluster multicast: each CTA loads its own tiles.
 #include "gemm_tc.cuh"
 #include "sm100.cuh"
@@ -82,18 +83,36 @@ __device__ __forceinline__ bool vec_ok(const void* p, int ncols) {
   return ncols == 32 && (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }
 
-// EPI_QKV_ROPE for one 128-column head of one row (this thread's row).
+__device__ __forceinline__ uint32_t pack_bits(uint16_t lo, uint16_t hi) {
+  return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+}
+
+template <typename T>
+__device__ __forceinline__ uint16_t bits_of(T x) {
+  return *reinterpret_cast<const uint16_t*>(&x);
+}
+
+template <typename T>
+__device__ __forceinline__ float word_half(uint32_t w, int hi) {
+  const uint16_t b = hi ? static_cast<uint16_t>(w >> 16) : static_cast<uint16_t>(w & 0xFFFFu);
+  return h2f<T>(*reinterpret_cast<const T*>(&b));
+}
+
+// EPI_QKV_ROPE for one 128-column head of this thread's row.  The head's
+// values are rounded to the storage type (the GEMM output's rounding point)
+// and kept packed, two per register.
 template <typename T>
 __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem_col0, int row,
                                               int M, int head) {
   constexpr int HD = 128;
-  float r[HD];
+  uint32_t hv[HD / 2];
 #pragma unroll
   for (int c = 0; c < HD / 32; ++c) {
     float v[32];
     tmem_ld32(tmem_col0 + c * 32, v);  // warp-collective: every lane loads
 #pragma unroll
-    for (int i = 0; i < 32; ++i) r[c * 32 + i] = round16<T>(v[i]);  // the GEMM's f16 rounding
+    for (int i = 0; i < 16; ++i)
+      hv[c * 16 + i] = pack_bits(bits_of(f2h<T>(v[2 * i])), bits_of(f2h<T>(v[2 * i + 1])));
   }
   if (row >= M) return;
   const RopeKV& rk = ep.rk;
@@ -109,51 +128,58 @@ __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem
         ((static_cast<long long>(page) * rk.nkv + kvh) * rk.page_size + pos % rk.page_size) * HD;
     dst = static_cast<T*>(head < rk.nq + rk.nkv ? rk.kc : rk.vc) + off;
   }
-  alignas(16) T o[8];
   if (head >= rk.nq + rk.nkv) {  // v: appended as rounded
 #pragma unroll
-    for (int j0 = 0; j0 < HD; j0 += 8) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = f2h<T>(r[j0 + j]);
-      *reinterpret_cast<uint4*>(dst + j0) = *reinterpret_cast<const uint4*>(o);
-    }
+    for (int j = 0; j < HD / 8; ++j)
+      reinterpret_cast<uint4*>(dst)[j] =
+          make_uint4(hv[4 * j], hv[4 * j + 1], hv[4 * j + 2], hv[4 * j + 3]);
     return;
   }
   // RMSNorm over the head's raw values (sequential sum, no FMA, as the
-  // reference's loop), per-element gain, then rotate-half RoPE at `pos`.
+  // reference's loop), per-element gain, then rotate-half RoPE at `pos`:
+  // out[d] = x_d c_d - x_{d+64} s_d and out[d+64] = x_{d+64} c_d + x_d s_d.
   const float* nw = head < rk.nq ? rk.qn : rk.kn;
   float s2 = 0.0f;
 #pragma unroll
-  for (int j = 0; j < HD; ++j) s2 = __fadd_rn(s2, __fmul_rn(r[j], r[j]));
+  for (int j = 0; j < HD; ++j) {
+    const float x = word_half<T>(hv[j / 2], j & 1);
+    s2 = __fadd_rn(s2, __fmul_rn(x, x));
+  }
   const float inv = 1.0f / sqrtf(s2 / static_cast<float>(HD) + rk.eps);
   const T* ct = static_cast<const T*>(rk.cos_t) + pos * (HD / 2);
   const T* st = static_cast<const T*>(rk.sin_t) + pos * (HD / 2);
 #pragma unroll
-  for (int j0 = 0; j0 < HD; j0 += 8) {
-    const uint4 cu = *reinterpret_cast<const uint4*>(ct + (j0 & 63));
-    const uint4 su = *reinterpret_cast<const uint4*>(st + (j0 & 63));
+  for (int j0 = 0; j0 < HD / 2; j0 += 8) {
+    const uint4 cu = *reinterpret_cast<const uint4*>(ct + j0);
+    const uint4 su = *reinterpret_cast<const uint4*>(st + j0);
     const T* cv = reinterpret_cast<const T*>(&cu);
     const T* sv = reinterpret_cast<const T*>(&su);
+    alignas(16) T lo[8], hi[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int d = j0 + j;
-      const int pd = d < 64 ? d + 64 : d - 64;
-      const float xj = __fmul_rn(__fmul_rn(r[d], inv), nw[d]);
-      const float xp = __fmul_rn(__fmul_rn(r[pd], inv), nw[pd]);
-      const float sxp = d < 64 ? -xp : xp;
-      o[j] = f2h<T>(__fadd_rn(__fmul_rn(xj, h2f<T>(cv[j])), __fmul_rn(sxp, h2f<T>(sv[j]))));
+      const float xa = __fmul_rn(__fmul_rn(word_half<T>(hv[d / 2], d & 1), inv), nw[d]);
+      const float xb =
+          __fmul_rn(__fmul_rn(word_half<T>(hv[(d + 64) / 2], d & 1), inv), nw[d + 64]);
+      const float c = h2f<T>(cv[j]), sn = h2f<T>(sv[j]);
+      lo[j] = f2h<T>(__fadd_rn(__fmul_rn(xa, c), __fmul_rn(-xb, sn)));
+      hi[j] = f2h<T>(__fadd_rn(__fmul_rn(xb, c), __fmul_rn(xa, sn)));
     }
-    *reinterpret_cast<uint4*>(dst + j0) = *reinterpret_cast<const uint4*>(o);
+    *reinterpret_cast<uint4*>(dst + j0) = *reinterpret_cast<const uint4*>(lo);
+    *reinterpret_cast<uint4*>(dst + j0 + 64) = *reinterpret_cast<const uint4*>(hi);
   }
 }
 
+// The fused epilogue over columns [cb, ce) of this thread's tile row (cb, ce
+// multiples of 32; two epilogue warpgroups split a tile between them).  For
+// SwiGLU the range is over the output columns [0, BN/2).
 template <int BN, typename T>
 __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row, int row, int M,
-                                         int n0, int N) {
+                                         int n0, int N, int cb, int ce) {
   if constexpr (BN % 128 == 0) {
     if (ep.mode == EPI_QKV_ROPE) {
 #pragma unroll 1
-      for (int hb = 0; hb < BN / 128; ++hb)
+      for (int hb = cb / 128; hb < ce / 128; ++hb)
         if (n0 + hb * 128 < N) qkv_rope_head<T>(ep, tmem_row + hb * 128, row, M, (n0 + hb * 128) / 128);
       return;
     }
@@ -163,7 +189,7 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
     constexpr int H = BN / 2;
     T* out = static_cast<T*>(ep.out);
 #pragma unroll 1
-    for (int c0 = 0; c0 < H; c0 += 32) {
+    for (int c0 = cb; c0 < ce; c0 += 32) {
       float g[32], u[32];
       tmem_ld32(tmem_row + c0, g);
       tmem_ld32(tmem_row + H + c0, u);
@@ -187,7 +213,7 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
     unsigned long long best = 0ull;
     float* out = static_cast<float*>(ep.out);
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
+    for (int c0 = cb; c0 < ce; c0 += 32) {
       float v[32];
       tmem_ld32(tmem_row + c0, v);
       if (row < M) {
@@ -217,7 +243,7 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
   }
 
 #pragma unroll 1
-  for (int c0 = 0; c0 < BN; c0 += 32) {
+  for (int c0 = cb; c0 < ce; c0 += 32) {
     float v[32];
     tmem_ld32(tmem_row + c0, v);
     if (row >= M) continue;
@@ -309,13 +335,31 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
   }
 }
 
+// Column range of epilogue warpgroup `wg` out of `nwg` for a BN-wide tile.
+template <int BN>
+__device__ __forceinline__ void epi_range(int mode, int wg, int nwg, int& cb, int& ce) {
+  const int span = mode == EPI_SWIGLU16 ? BN / 2 : BN;
+  if (nwg == 1) {
+    cb = 0;
+    ce = span;
+    return;
+  }
+  const int chunks = (span + 31) / 32;
+  const int split = ((chunks + 1) / 2) * 32;
+  cb = wg == 0 ? 0 : split;
+  ce = wg == 0 ? split : chunks * 32;
+}
+
 // Persistent kernel: gridDim.x CTAs (at most one per SM) walk the tile list
 // t = blockIdx.x, blockIdx.x + gridDim.x, ... with tiles numbered N-fastest so
 // that the CTAs in flight share A row-blocks and the whole B operand stays in
 // L2.  The accumulator is double-buffered in TMEM (2 x BN columns): the MMA
 // warp starts tile i+1 while the epilogue warps drain tile i.
+constexpr int kGemmEpiWarps = 8;                          // two warpgroups
+constexpr int kGemmThreads = (2 + kGemmEpiWarps) * 32;     // TMA, MMA, epilogue
+
 template <int BN, typename T>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    int M, int N, int K, EpiParams ep) {
   using Cfg = GemmCfg<BN>;
@@ -347,7 +391,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 128);
+      mbar_init(&tempty[i], 32 * kGemmEpiWarps);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -424,7 +468,10 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    const int q = warp & 3;
+    const int q = warp & 3;              // TMEM lane quarter this warp may read
+    const int wg = (warp - 2) / 4;       // column half of the tile
+    int cb, ce;
+    epi_range<BN>(ep.mode, wg, kGemmEpiWarps / 4, cb, ce);
     int lt = 0;
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++lt) {
       const int buf = lt & 1;
@@ -436,7 +483,7 @@ __global__ void __launch_bounds__(192, 1)
       const int m0 = (t / n_tiles_n) * kBM, n0 = (t % n_tiles_n) * BN;
       const int row = m0 + q * 32 + lane;
       const uint32_t trow = tbase + buf * kAccCols + (static_cast<uint32_t>(q * 32) << 16);
-      epilogue<BN, T>(ep, trow, row, M, n0, N);
+      epilogue<BN, T>(ep, trow, row, M, n0, N, cb, ce);
       tc_fence_before();
       mbar_arrive(&tempty[buf]);
     }
@@ -463,6 +510,224 @@ int num_sms() {
   return sms[dev];
 }
 
+// ---------------------------------------------------------------------------
+// Implicit-GEMM 3x3 / stride 2 / pad 1 convolution over NHWC activations.
+// Same MMA warp and epilogue as gemm_tc_kernel; the A operand is not a matrix
+// in memory but gathered per k-block by four producer warps: row r of the tile
+// is output position m0 + r, 16-byte chunk c of the 64-wide k-block is
+// channels [ic, ic + 8) of tap (kh, kw), read from input pixel
+// (2*oh + kh - 1, 2*ow + kw - 1) with cp.async (zero-filled off the image) and
+// written at the 128B-swizzled place TMA would have used.  Each producer
+// thread keeps two k-blocks in flight: after issuing block i it waits for
+// block i-1, fences the async proxy and arrives on that stage's barrier.
+// Warp roles (288 threads): 0-3 gather A (thread 0 also TMA-loads B),
+// 4 MMA + TMEM, 5-8 epilogue.
+struct ConvGeom {
+  int h, w, c;       // input NHWC geometry (per image)
+  int ho, wo;        // output geometry
+  int time_major;    // output positions ordered (ow, oh) instead of (oh, ow)
+};
+
+__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+
+template <int BN, typename T>
+__global__ void __launch_bounds__(288, 1)
+    conv_gemm_kernel(const T* __restrict__ x, ConvGeom g, const __grid_constant__ CUtensorMap tmB,
+                     int M, int N, int K, EpiParams ep) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  constexpr uint32_t kAccCols = Cfg::kTmemCols;
+  constexpr uint32_t kAllocCols = 2 * Cfg::kTmemCols;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * Cfg::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBBytes);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nkb = (K + kBK - 1) / kBK;
+  const int n_tiles_n = (N + BN - 1) / BN;
+  const int n_tiles = n_tiles_n * ((M + kBM - 1) / kBM);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 128 + 1);  // 128 gather threads + the B expect_tx arrive
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 128);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (threadIdx.x == 0) tma_prefetch_desc(&tmB);
+  if (warp == 4) tmem_alloc(tslot, kAllocCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+  auto timed_out = [&]() {
+    *abort_flag = 1;
+    if (ep.status) atomicOr(ep.status, kStatusTimeout);
+  };
+
+  if (warp < 4) {
+    // ---- A gather (+ B TMA from thread 0)
+    const int r = threadIdx.x;  // tile row of this thread
+    uint32_t c = 0;
+    int pending = -1;  // stage whose copies this thread still has to publish
+    bool ok = true;
+    for (int t = blockIdx.x; t < n_tiles && ok && !*abort_flag; t += gridDim.x) {
+      const int m0 = (t / n_tiles_n) * kBM, n0 = (t % n_tiles_n) * BN;
+      const int p = m0 + r;
+      const bool row_ok = p < M;
+      int img = 0, oh = 0, ow = 0;
+      if (row_ok) {
+        const int plane = g.ho * g.wo;
+        img = p / plane;
+        const int q = p - img * plane;
+        if (g.time_major) {
+          ow = q / g.ho;
+          oh = q - ow * g.ho;
+        } else {
+          oh = q / g.wo;
+          ow = q - oh * g.wo;
+        }
+      }
+      const T* ximg = x + static_cast<long long>(img) * g.h * g.w * g.c;
+      for (int kb = 0; kb < nkb; ++kb, ++c) {
+        const int s = c % S;
+        const uint32_t ph = (c / S) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1u)) {
+          timed_out();
+          ok = false;
+          break;
+        }
+        if (threadIdx.x == 0) {
+          mbar_arrive_expect_tx(&full[s], Cfg::kBBytes);
+          tma_load_2d(&tmB, &full[s], sB + s * Cfg::kBBytes, kb * kBK, n0);
+        }
+        const uint32_t arow = smem_u32(sA + s * Cfg::kABytes) + r * 128;
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          const int k = kb * kBK + ch * 8;
+          const int tap = k / g.c;
+          const int ic = k - tap * g.c;
+          const int ih = 2 * oh + tap / 3 - 1, iw = 2 * ow + tap % 3 - 1;
+          const bool v = row_ok && k < K && ih >= 0 && ih < g.h && iw >= 0 && iw < g.w;
+          const T* src = v ? ximg + (static_cast<long long>(ih) * g.w + iw) * g.c + ic : x;
+          cp_async16_zfill(arow + ((ch ^ (r & 7)) * 16), src, v);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        if (pending >= 0) {
+          asm volatile("cp.async.wait_group 1;" ::: "memory");
+          fence_proxy_async_smem();
+          mbar_arrive(&full[pending]);
+        }
+        pending = s;
+      }
+    }
+    if (pending >= 0) {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+      fence_proxy_async_smem();
+      mbar_arrive(&full[pending]);
+    }
+  } else if (warp == 4) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = f16_instr_desc(kBM, BN, H16Traits<T>::kBf16);
+      uint32_t c = 0;
+      int lt = 0;
+      for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x, ++lt) {
+        const int buf = lt & 1;
+        if (!mbar_wait(&tempty[buf], ((lt >> 1) & 1) ^ 1u)) {
+          timed_out();
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc = tbase + buf * kAccCols;
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb, ++c) {
+          const int s = c % S;
+          const uint32_t ph = (c / S) & 1;
+          if (!mbar_wait(&full[s], ph)) {
+            timed_out();
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + s * Cfg::kABytes);
+          const uint32_t b_addr = smem_u32(sB + s * Cfg::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t da = sw128_kmajor_desc(a_addr + k * 32);
+            const uint64_t db = sw128_kmajor_desc(b_addr + k * 32);
+            mma_f16(acc, da, db, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        mma_commit(&tfull[buf]);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    int lt = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++lt) {
+      const int buf = lt & 1;
+      if (*abort_flag || !mbar_wait(&tfull[buf], (lt >> 1) & 1)) {
+        if (lane == 0) timed_out();
+        break;
+      }
+      tc_fence_after();
+      const int m0 = (t / n_tiles_n) * kBM, n0 = (t % n_tiles_n) * BN;
+      const int row = m0 + q * 32 + lane;
+      const uint32_t trow = tbase + buf * kAccCols + (static_cast<uint32_t>(q * 32) << 16);
+      int cb, ce;
+      epi_range<BN>(ep.mode, 0, 1, cb, ce);
+      epilogue<BN, T>(ep, trow, row, M, n0, N, cb, ce);
+      tc_fence_before();
+      mbar_arrive(&tempty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kAllocCols);
+  }
+}
+
+template <int BN, typename T>
+int launch_conv(const void* x, const ConvGeom& g, const void* B, int M, int N, int K,
+                const EpiParams& ep, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN>;
+  CUtensorMap tb;
+  int rc = make_tmap_2d(&tb, B, H16Traits<T>::kBf16, K, N, K, kBK, BN);
+  if (rc) return rc;
+  auto kern = conv_gemm_kernel<BN, T>;
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmem);
+  if (e != cudaSuccess) return (int)e;
+  const int tiles = ((N + BN - 1) / BN) * ((M + kBM - 1) / kBM);
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  kern<<<grid, 288, Cfg::kSmem, stream>>>(static_cast<const T*>(x), g, tb, M, N, K, ep);
+  return (int)cudaGetLastError();
+}
+
 template <int BN, typename T>
 int launch(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
            const EpiParams& ep, cudaStream_t stream) {
@@ -478,7 +743,7 @@ int launch(const void* A, long long lda, const void* B, long long ldb, int M, in
   if (e != cudaSuccess) return (int)e;
   const int tiles = ((N + BN - 1) / BN) * ((M + kBM - 1) / kBM);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  kern<<<grid, 192, Cfg::kSmem, stream>>>(ta, tb, M, N, K, ep);
+  kern<<<grid, kGemmThreads, Cfg::kSmem, stream>>>(ta, tb, M, N, K, ep);
   return (int)cudaGetLastError();
 }
 
@@ -514,6 +779,27 @@ int gemm_tc(const void* A, long long lda, const void* B, long long ldb, int M, i
       return (int)cudaErrorInvalidValue;
   }
 #undef QA_GEMM_CASE
+}
+
+int conv3x3s2_tc(const void* x, int n, int h, int w, int c, const void* wt, int c_out,
+                 bool time_major, bool bf16, const EpiParams& ep, cudaStream_t stream) {
+  if (n <= 0) return 0;
+  if (c % 8 || (reinterpret_cast<uintptr_t>(x) & 15u) || (reinterpret_cast<uintptr_t>(wt) & 15u))
+    return (int)cudaErrorInvalidValue;
+  ConvGeom g{h, w, c, (h - 1) / 2 + 1, (w - 1) / 2 + 1, time_major ? 1 : 0};
+  const int M = n * g.ho * g.wo, K = 9 * c;
+  const int bn = gemm_pick_bn(c_out);
+#define QA_CONV_CASE(BNV)                                                                 \
+  case BNV:                                                                               \
+    return bf16 ? launch_conv<BNV, __nv_bfloat16>(x, g, wt, M, c_out, K, ep, stream)       \
+                : launch_conv<BNV, __half>(x, g, wt, M, c_out, K, ep, stream);
+  switch (bn) {
+    QA_CONV_CASE(240)
+    QA_CONV_CASE(256)
+    default:
+      return (int)cudaErrorInvalidValue;
+  }
+#undef QA_CONV_CASE
 }
 
 }  // namespace qa

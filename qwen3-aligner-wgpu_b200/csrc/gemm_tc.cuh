@@ -75,4 +75,11 @@ int gemm_tc(const void* A, long long lda, const void* B, long long ldb, int M, i
 // Tile width the launcher picks for N (exposed for SwiGLU weight packing).
 int gemm_pick_bn(int N);
 
+// Implicit-GEMM conv2d (3x3, stride 2, pad 1) on the tensor cores: x is NHWC
+// [n][h][w][c] 16-bit, wt is [c_out][9c] with k = (kh*3 + kw)*c + ic; output
+// rows are positions (oh, ow) per image, or (ow, oh) when time_major, written
+// by the epilogue `ep` as an [n*ho*wo, c_out] matrix.  No im2col buffer.
+int conv3x3s2_tc(const void* x, int n, int h, int w, int c, const void* wt, int c_out,
+                 bool time_major, bool bf16, const EpiParams& ep, cudaStream_t stream);
+
 }  // namespace qa

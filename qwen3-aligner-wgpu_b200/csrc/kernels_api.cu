@@ -25,3 +25,18 @@ extern "C" int qa_k_gemm(const void* A, long long lda, const void* B, long long 
                    force_bn);
   return rc == 0 ? QA_OK : QA_ERR_CUDA;
 }
+
+extern "C" int qa_k_conv3x3s2(const void* x, int n, int h, int w, int c, const void* wt, int c_out,
+                              int time_major, int bf16, int mode, int act, void* out, long long ldo,
+                              const float* bias, unsigned* status, void* stream) {
+  EpiParams ep;
+  ep.mode = mode;
+  ep.act = act;
+  ep.out = out;
+  ep.ldo = ldo;
+  ep.bias = bias;
+  ep.status = status;
+  int rc = conv3x3s2_tc(x, n, h, w, c, wt, c_out, time_major != 0, bf16 != 0, ep,
+                        static_cast<cudaStream_t>(stream));
+  return rc == 0 ? QA_OK : QA_ERR_CUDA;
+}

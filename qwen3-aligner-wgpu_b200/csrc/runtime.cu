@@ -767,7 +767,6 @@ int run_encoder(qa_ctx* ctx, const Plan& P, const PlanDev& D, void* out16, const
   const int tpc = w3;
   const int G = std::max(1, std::min(P.total_chunks, 256));  // chunks per conv group
   TRY(ensure(ctx, ctx->act1, static_cast<size_t>(G) * h1 * w1 * ds * 2));
-  TRY(ensure(ctx, ctx->cols, static_cast<size_t>(G) * h2 * w2 * 9 * ds * 2));
   TRY(ensure(ctx, ctx->act2, static_cast<size_t>(G) * h2 * w2 * ds * 2));
   TRY(ensure(ctx, ctx->act3, static_cast<size_t>(G) * h3 * w3 * ds * 2));
   TRY(ensure(ctx, ctx->xenc, static_cast<size_t>(std::max(P.T_a, 1)) * dm * 4));
@@ -778,22 +777,21 @@ int run_encoder(qa_ctx* ctx, const Plan& P, const PlanDev& D, void* out16, const
     const float* mel = ctx->mel_chunked.as<float>() + static_cast<size_t>(g0) * c.num_mel_bins * cs;
     KL("conv1", 18.0 * g * h1 * w1 * ds, 4.0 * g * c.num_mel_bins * cs + 2.0 * g * h1 * w1 * ds,
        conv1_direct(mel, g, c.num_mel_bins, cs, W.c1_w, W.c1_b, ds, ctx->act1.p, bf, s));
-    KL("im2col", 0, 2.0 * g * h2 * w2 * 9.0 * ds * 2.0,
-       im2col_3x3s2(ctx->act1.p, g, h1, w1, ds, ctx->cols.p, false, s));
+    // conv2 / conv3: implicit GEMM on the tensor cores, A gathered from NHWC
     ep.mode = EPI_STORE16;
     ep.act = ACT_GELU;
     ep.bias = W.c2_b;
     ep.out = ctx->act2.p;
     ep.ldo = ds;
     ep.row_map = nullptr;
-    KL("gemm", gemm_flops(g * h2 * w2, ds, 9 * ds), gemm_bytes(g * h2 * w2, ds, 9 * ds, 2),
-       gemm_tc(ctx->cols.p, 9LL * ds, W.c2_w, 9LL * ds, g * h2 * w2, ds, 9 * ds, bf, ep, s));
-    KL("im2col", 0, 2.0 * g * h3 * w3 * 9.0 * ds * 2.0,
-       im2col_3x3s2(ctx->act2.p, g, h2, w2, ds, ctx->cols.p, true, s));
+    KL("conv_gemm", gemm_flops(g * h2 * w2, ds, 9 * ds),
+       2.0 * g * (h1 * w1 * ds + h2 * w2 * ds) + 2.0 * ds * 9 * ds,
+       conv3x3s2_tc(ctx->act1.p, g, h1, w1, ds, W.c2_w, ds, false, bf, ep, s));
     ep.bias = W.c3_b;
     ep.out = ctx->act3.p;
-    KL("gemm", gemm_flops(g * h3 * w3, ds, 9 * ds), gemm_bytes(g * h3 * w3, ds, 9 * ds, 2),
-       gemm_tc(ctx->cols.p, 9LL * ds, W.c3_w, 9LL * ds, g * h3 * w3, ds, 9 * ds, bf, ep, s));
+    KL("conv_gemm", gemm_flops(g * h3 * w3, ds, 9 * ds),
+       2.0 * g * (h2 * w2 * ds + h3 * w3 * ds) + 2.0 * ds * 9 * ds,
+       conv3x3s2_tc(ctx->act2.p, g, h2, w2, ds, W.c3_w, ds, true, bf, ep, s));
     // conv_out + bias + PE[t], scattered into the packed token rows
     EpiParams eo;
     eo.status = ep.status;

@@ -148,3 +148,37 @@ def test_argmax():
     idx = (0xFFFFFFFF - (keys & 0xFFFFFFFF)).cpu()
     got_from_logits = logits.argmax(1).cpu()
     assert torch.equal(idx, got_from_logits)
+
+
+def _conv_ref(x_nhwc, w4, bias, time_major):
+    """fp32 torch conv2d (3x3, stride 2, pad 1) + bias + erf-GELU, rows in the
+    kernel's output order."""
+    y = torch.nn.functional.conv2d(x_nhwc.float().permute(0, 3, 1, 2), w4.float(), bias,
+                                   stride=2, padding=1)
+    y = torch.nn.functional.gelu(y)  # [n, c_out, ho, wo]
+    if time_major:
+        y = y.permute(0, 3, 2, 1)    # [n, wo, ho, c]
+    else:
+        y = y.permute(0, 2, 3, 1)    # [n, ho, wo, c]
+    return y.reshape(-1, y.shape[-1])
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("n,h,w,c,co,tm", [(3, 64, 50, 480, 480, False), (3, 32, 25, 480, 480, True),
+                                          (2, 9, 7, 16, 256, False), (1, 5, 5, 480, 480, True)])
+def test_implicit_conv(dtype, n, h, w, c, co, tm):
+    L = _lib()
+    g = torch.Generator(device="cuda").manual_seed(n * h + c)
+    x = (torch.randn(n, h, w, c, device="cuda", generator=g) * 0.5).to(dtype)
+    w4 = (torch.randn(co, c, 3, 3, device="cuda", generator=g) * 0.05).to(dtype)
+    bias = torch.randn(co, device="cuda", generator=g) * 0.1
+    wk = w4.permute(0, 2, 3, 1).reshape(co, 9 * c).contiguous()  # k = (kh*3 + kw)*c + ic
+    ho, wo = (h - 1) // 2 + 1, (w - 1) // 2 + 1
+    out = torch.full((n * ho * wo, co), float("nan"), device="cuda", dtype=dtype)
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    L.conv3x3s2(x, wk, out, time_major=tm, act=L.ACT_GELU, bias=bias, status=st)
+    torch.cuda.synchronize()
+    assert st.item() == 0
+    ref = _conv_ref(x, w4, bias, tm)
+    assert torch.isfinite(out.float()).all()
+    assert _rel(out, ref) < TOL16[dtype]
