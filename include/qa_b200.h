@@ -165,6 +165,24 @@ int qa_head(qa_ctx* ctx, const float* hidden, int seq, const int* rows, int n_ro
  * are interpolated in f64 and truncated toward zero.  out may alias data. */
 int qa_fix_timestamps(const int64_t* data, int n, int64_t* out);
 
+/* Timestamp head without any device allocation.  No counterpart in the
+ * reference; it is the qa_head computation for callers that cannot allocate
+ * device memory: a host that has given the whole GPU to its own memory pool,
+ * or a latency-bound caller (a live audio pipeline) that must not stall on
+ * cudaMalloc/cudaFree.  hidden [seq, hidden_size] f32, rows [n_rows] int32,
+ * raw_ms [n_rows] int64 and the optional logits [n_rows, num_labels] f32 are
+ * DEVICE pointers the caller owns.  The scratch is one fixed array inside the
+ * library (about 8.4 MB, held by every GPU that loads it until exit), so
+ * n_rows <= QA_NOALLOC_HEAD_MAX_ROWS and hidden_size <= 1024, else
+ * QA_ERR_CAP.  The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * Work runs on the context's stream and the call waits (bounded) for it.
+ * Every call shares the one array, so calls that overlap on the GPU (other
+ * threads or contexts on the same device) race; serialise them. */
+#define QA_NOALLOC_HEAD_MAX_ROWS 2048
+int qa_head_noalloc(qa_ctx* ctx, const float* hidden, int seq, const int* rows, int n_rows,
+                    int64_t* raw_ms, float* logits);
+
 /* ---------------------------------------------------------------- batched path */
 
 typedef struct {

@@ -57,6 +57,7 @@ EXPORTED = [
     "qa_get_timings", "qa_mel", "qa_audio_embeds", "qa_ensure_capacity", "qa_text_hidden",
     "qa_head", "qa_align_batch", "qa_batch_stage", "qa_batch_run", "qa_batch_fetch",
     "qa_set_stream", "qa_set_profile", "qa_get_profile", "qa_fix_timestamps",
+    "qa_head_noalloc",
     "qa_k_gemm", "qa_k_conv3x3s2",
 ]
 
@@ -194,6 +195,8 @@ def _declare(L: ctypes.CDLL) -> None:
         L.qa_align_batch.argtypes = [c_void_p, c_void_p, c_int, c_void_p]
         L.qa_batch_stage.argtypes = [c_void_p, c_void_p, c_int, c_void_p]
         L.qa_fix_timestamps.argtypes = [c_void_p, c_int, c_void_p]
+        L.qa_head_noalloc.argtypes = [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p,
+                                      c_void_p]
         L.qa_batch_run.argtypes = [c_void_p]
         L.qa_batch_fetch.argtypes = [c_void_p, c_void_p]
         L.qa_set_stream.argtypes = [c_void_p, c_void_p]
