@@ -518,8 +518,9 @@ int num_sms() {
 // channels [ic, ic + 8) of tap (kh, kw), read from input pixel
 // (2*oh + kh - 1, 2*ow + kw - 1) with cp.async (zero-filled off the image) and
 // written at the 128B-swizzled place TMA would have used.  Each producer
-// thread keeps two k-blocks in flight: after issuing block i it waits for
-// block i-1, fences the async proxy and arrives on that stage's barrier.
+// thread keeps two k-blocks of copies in flight: after issuing block i it
+// waits for block i-1, fences the async proxy and arrives on that stage's
+// barrier.
 // Warp roles (288 threads): 0-3 gather A (thread 0 also TMA-loads B),
 // 4 MMA + TMEM, 5-8 epilogue.
 struct ConvGeom {
@@ -587,8 +588,13 @@ __global__ void __launch_bounds__(288, 1)
   if (warp < 4) {
     // ---- A gather (+ B TMA from thread 0)
     const int r = threadIdx.x;  // tile row of this thread
+    // k-blocks of copies a thread keeps unpublished.  1 is measured best: every
+    // unpublished block is one the MMA warp cannot start, and a longer lag
+    // leaves it waiting on each publish (S - 1 ran 30 % slower on conv2).
+    constexpr int kLag = 1;
     uint32_t c = 0;
-    int pending = -1;  // stage whose copies this thread still has to publish
+    int pend[S];                // stages issued but not yet published, oldest first
+    int npend = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < n_tiles && ok && !*abort_flag; t += gridDim.x) {
       const int m0 = (t / n_tiles_n) * kBM, n0 = (t % n_tiles_n) * BN;
@@ -632,19 +638,21 @@ __global__ void __launch_bounds__(288, 1)
           cp_async16_zfill(arow + ((ch ^ (r & 7)) * 16), src, v);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
-        if (pending >= 0) {
-          asm volatile("cp.async.wait_group 1;" ::: "memory");
+        pend[npend++] = s;
+        if (npend > kLag) {
+          // all but the kLag newest groups have landed: publish the oldest
+          asm volatile("cp.async.wait_group %0;" ::"n"(kLag) : "memory");
           fence_proxy_async_smem();
-          mbar_arrive(&full[pending]);
+          mbar_arrive(&full[pend[0]]);
+#pragma unroll
+          for (int i = 0; i + 1 < S; ++i) pend[i] = pend[i + 1];
+          --npend;
         }
-        pending = s;
       }
     }
-    if (pending >= 0) {
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
-      fence_proxy_async_smem();
-      mbar_arrive(&full[pending]);
-    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    fence_proxy_async_smem();
+    for (int i = 0; i < npend; ++i) mbar_arrive(&full[pend[i]]);
   } else if (warp == 4) {
     if (lane == 0) {
       constexpr uint32_t idesc = f16_instr_desc(kBM, BN, H16Traits<T>::kBf16);

@@ -419,13 +419,18 @@ class InputBuilder:
         n_audio = audio_token_count(valid_mel, self.n_window)
         if n_audio <= 0:
             raise ValueError(f"audio produced 0 tokens ({valid_mel} mel frames)")
-        text = AUDIO_START + AUDIO_PAD * n_audio + AUDIO_END
+        # The reference tokenises "<|audio_start|>" + pads + "<|audio_end|>" +
+        # words in one string; the markers are atomic tokens (no merge crosses
+        # them), so the marker run is emitted directly and only the words part
+        # goes through the tokenizer — the same ids without scanning N pads.
+        text = ""
         for i, w in enumerate(words):
             if i > 0:
                 text += TIMESTAMP + TIMESTAMP
             text += w
         text += TIMESTAMP + TIMESTAMP
-        ids = self.tok.encode(text)
+        ids = ([self.tok.token_to_id(AUDIO_START)] + [self.tok.token_to_id(AUDIO_PAD)] * n_audio
+               + [self.tok.token_to_id(AUDIO_END)] + self.tok.encode(text))
         if sum(1 for t in ids if t == AUDIO_PAD_ID) != n_audio:
             raise ValueError("audio token count mismatch")
         if ids[0] != AUDIO_START_ID or ids[n_audio + 1] != AUDIO_END_ID:

@@ -1,0 +1,97 @@
+"""BASELINE configs 1 and 3 on the GPU.
+
+Config 1 (60 s, 180 words, ~1.7k decoder tokens) is checked end to end against
+the oracle.  Config 3 (300 s, 900 words, ~7.6k tokens, bf16 storage) is too
+long for the CPU oracle, so it is checked through properties that hold at any
+length, and the oracle is run on a prefix:
+
+* the conv stem works per 100-frame chunk and the tower's attention per
+  104-token window, so the first two windows of the full clip's audio rows
+  equal the oracle's rows for the first 1600 mel frames;
+* the prefill is causal, so the first K hidden rows of the full sequence are
+  bit-identical to a K-token prefill of the same embeddings, and that prefix
+  prefill is checked against the oracle.
+"""
+import numpy as np
+import pytest
+
+from conftest import cuda_ok
+
+pytestmark = pytest.mark.gpu
+
+REL = 2e-2
+MARGIN = 1e-2
+
+
+@pytest.fixture(scope="module")
+def env():
+    if not cuda_ok():
+        pytest.skip("no CUDA device")
+    import pipeline_env as E
+    return E
+
+
+def test_config1_end_to_end(env):
+    E = env
+    clip = E.qa.synth.workload(1)[0]
+    al = E.gpu_aligner()
+    inp = al.build_input(clip.samples, clip.text, clip.language)
+    assert 1200 < inp.seq_len() < 2200
+    [(raw, extra)] = al.align_inputs([clip.samples], [inp], want_logits=True)
+    ref = E.cpu_model().align_raw(clip.samples, inp.input_ids, inp.timestamp_positions)
+    assert E.rel_err(extra["logits"], ref["logits"]) <= REL
+    gated = ref["margin"] > MARGIN
+    assert gated.sum() >= len(gated) // 2
+    assert np.array_equal(raw[gated], ref["raw_ms"][gated])
+
+
+@pytest.fixture(scope="module")
+def config3(env):
+    E = env
+    clip = E.qa.synth.workload(3)[0]
+    al = E.gpu_aligner()
+    inp = al.build_input(clip.samples, clip.text, clip.language)
+    return clip, inp
+
+
+@pytest.mark.parametrize("half", ["f16", "bf16"])
+def test_config3_long_context(env, config3, half):
+    E = env
+    clip, inp = config3
+    assert 7000 < inp.seq_len() <= 8192
+    al = E.gpu_aligner(half)
+    om = E.cpu_model()
+    mel_ref = E.oracle.mel(clip.samples)
+    mel = al.mel(clip.samples)
+    assert mel.shape == mel_ref.shape == (128, 30000)
+    assert np.abs(mel - mel_ref).max() <= 1e-3
+
+    # audio tower: windows are local, so a mel prefix reproduces the first windows
+    audio_bits = al.audio_embeds(mel_ref)
+    audio = E.bits_to_f32(audio_bits, half)
+    assert audio.shape == (inp.n_audio_tokens, 1024)
+    pre = om.audio_embeds(mel_ref[:, :1600])
+    tol = REL if half == "f16" else 6e-2
+    assert E.rel_err(audio[: pre.shape[0]], pre) <= tol
+
+    # decoder: causal, so a prefix prefill equals the full prefill's first rows
+    if half == "f16":
+        emb = om.gather(inp.input_ids, audio_bits)
+    else:
+        emb16 = om.gather(inp.input_ids, E.oracle.f32_to_f16_array(audio))
+        f = E.oracle.f16_bits_to_f32(emb16)
+        emb = ((f.view(np.uint32) + 0x7FFF + ((f.view(np.uint32) >> 16) & 1)) >> 16).astype(np.uint16)
+    full = al.text_hidden(emb)
+    K = 640
+    prefix = al.text_hidden(emb[:K])
+    assert np.array_equal(full[:K], prefix)
+    ref = E.oracle.f16_bits_to_f32(om.text_hidden(E.oracle.f32_to_f16_array(
+        E.bits_to_f32(emb[:K], half))))
+    assert E.rel_err(prefix, ref) <= tol
+    assert np.isfinite(full).all()
+
+    # the whole path at full length, and the head on the full hidden states agree
+    [(raw, _)] = al.align_inputs([clip.samples], [inp])
+    assert len(raw) == 1800 and (raw >= 0).all() and (raw < 5000 * 80).all()
+    fixed = E.qa._lib.fix_timestamps(raw)
+    assert all(a <= b for a, b in zip(fixed, fixed[1:]))
