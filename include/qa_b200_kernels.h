@@ -54,6 +54,21 @@ int qa_k_conv3x3s2(const void* x, int n, int h, int w, int c, const void* wt, in
                    int time_major, int bf16, int mode, int act, void* out, long long ldo,
                    const float* bias, unsigned* status, void* stream);
 
+/*
+ * Causal GQA attention of the decoder prefill over the paged K/V cache
+ * (src/cpu_decoder.rs:327-412; the reference GPU path's
+ * prefill_attention_paged dispatch, src/decoder.rs:1463-1520).
+ * qkv [q_rows][ldq] 16-bit with query head h at column h*128; kpool/vpool
+ * [kv_pages][nkvh][64][128]; tiles [n_tiles][4] = (clip, q0, tok0, len), one
+ * per 64 (impl 0) or 128 (impl 1) query positions of a clip; block_tab
+ * [clips][max_pages] page ids; out [q_rows][nqh*128].  impl 0 = mma.sync
+ * kernel, 1 = persistent tcgen05/TMEM kernel (the one the pipeline runs).
+ */
+int qa_k_causal_attention(const void* qkv, long long ldq, long long q_rows, int nqh, int nkvh,
+                          const int* tiles, int n_tiles, const int* block_tab, int max_pages,
+                          const void* kpool, const void* vpool, int kv_pages, void* out, int bf16,
+                          int impl, unsigned* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -58,7 +58,7 @@ EXPORTED = [
     "qa_head", "qa_align_batch", "qa_batch_stage", "qa_batch_run", "qa_batch_fetch",
     "qa_set_stream", "qa_set_profile", "qa_get_profile", "qa_fix_timestamps",
     "qa_head_noalloc",
-    "qa_k_gemm", "qa_k_conv3x3s2",
+    "qa_k_gemm", "qa_k_conv3x3s2", "qa_k_causal_attention",
 ]
 
 c_void_p = ctypes.c_void_p
@@ -176,6 +176,9 @@ def _declare(L: ctypes.CDLL) -> None:
     L.qa_k_gemm.restype = c_int
     L.qa_k_conv3x3s2.argtypes = [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_int,
                                  c_int, c_int, c_int, c_void_p, c_ll, c_void_p, c_void_p, c_void_p]
+    L.qa_k_causal_attention.argtypes = [c_void_p, c_ll, c_ll, c_int, c_int, c_void_p, c_int,
+                                        c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p,
+                                        c_int, c_int, c_void_p, c_void_p]
     if hasattr(L, "qa_open"):
         L.qa_open.argtypes = [c_int, c_int, ctypes.POINTER(c_void_p)]
         L.qa_load.argtypes = [c_void_p, c_void_p, c_int, c_void_p]
@@ -253,3 +256,44 @@ def conv3x3s2(x, wt, out, time_major=False, mode=EPI_STORE16, act=ACT_NONE, bias
     rc = lib().qa_k_conv3x3s2(ptr(x), n, h, w, c, ptr(wt), wt.shape[0], 1 if time_major else 0,
                               bf16, mode, act, ptr(out), out.stride(0), ptr(bias), ptr(status), s)
     check(rc)
+
+
+def causal_attention(qkv, nqh, nkvh, tiles, block_tab, kpool, vpool, out, impl=1, status=None,
+                     stream=None):
+    """Paged causal attention on torch CUDA tensors.
+
+    qkv [T, ldq] 16-bit, tiles int32 [n, 4] (clip, q0, tok0, len), block_tab
+    int32 [clips, max_pages], kpool/vpool [pages, nkvh, 64, 128], out [T, nqh*128].
+    """
+    import torch
+    check_attention_args(qkv, nqh, nkvh, tiles, block_tab, kpool, vpool, out)
+    bf16 = 1 if qkv.dtype == torch.bfloat16 else 0
+    s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
+    rc = lib().qa_k_causal_attention(ptr(qkv), qkv.stride(0), qkv.shape[0], nqh, nkvh,
+                                     ptr(tiles), tiles.shape[0], ptr(block_tab),
+                                     block_tab.shape[1], ptr(kpool), ptr(vpool), kpool.shape[0],
+                                     ptr(out), bf16, impl, ptr(status), s)
+    check(rc)
+
+
+def check_attention_args(qkv, nqh, nkvh, tiles, block_tab, kpool, vpool, out) -> None:
+    """Host-side shape and range checks for causal_attention (ValueError on failure)."""
+    import torch
+    T = qkv.shape[0]
+    if (tiles.dim() != 2 or tiles.shape[1] != 4 or tiles.dtype != torch.int32
+            or block_tab.dim() != 2 or block_tab.dtype != torch.int32):
+        raise ValueError("tiles must be int32 [n, 4] and block_tab int32 [clips, max_pages]")
+    if tuple(kpool.shape[1:]) != (nkvh, 64, 128) or kpool.shape != vpool.shape:
+        raise ValueError("kpool/vpool must be [pages, nkvh, 64, 128]")
+    if qkv.dim() != 2 or qkv.shape[1] < (nqh + 2 * nkvh) * 128 or tuple(out.shape) != (
+            T, nqh * 128) or not (qkv.dtype == kpool.dtype == vpool.dtype == out.dtype):
+        raise ValueError("qkv [T, >= (nqh + 2 nkvh) 128], out [T, nqh 128], one 16-bit dtype")
+    t = tiles.cpu()
+    bt = block_tab.cpu()
+    if t.numel() and (int(t[:, 0].min()) < 0 or int(t[:, 0].max()) >= bt.shape[0]
+                      or int(t[:, 1].min()) < 0 or int((t[:, 1] - t[:, 3]).max()) >= 0
+                      or int((t[:, 2] + t[:, 3]).max()) > T
+                      or int(t[:, 3].max()) > 64 * bt.shape[1]):
+        raise ValueError("tile (clip, q0, tok0, len) out of range")
+    if bt.numel() and (int(bt.min()) < 0 or int(bt.max()) >= kpool.shape[0]):
+        raise ValueError("block_tab names a page outside the pools")

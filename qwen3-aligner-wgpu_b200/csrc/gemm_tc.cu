@@ -757,6 +757,8 @@ int launch(const void* A, long long lda, const void* B, long long ldb, int M, in
 
 }  // namespace
 
+int device_sm_count() { return num_sms(); }
+
 int gemm_pick_bn(int N) {
   if (N % 256 == 0) return 256;
   if (N % 240 == 0) return 240;

@@ -82,4 +82,7 @@ int gemm_pick_bn(int N);
 int conv3x3s2_tc(const void* x, int n, int h, int w, int c, const void* wt, int c_out,
                  bool time_major, bool bf16, const EpiParams& ep, cudaStream_t stream);
 
+// SMs of the current device (cached per device), for persistent grids.
+int device_sm_count();
+
 }  // namespace qa

@@ -92,6 +92,16 @@ int causal_attention(const void* qkv, long long ldq, int nqh, int nkvh, int hd,
                      const AttnTile* tiles, int n_tiles, const int* block_tab, int max_pages,
                      PagedKV kv, void* out, bool bf16, cudaStream_t s);
 
+// (e) on the tcgen05 tensor cores: the same contract as causal_attention
+// except that each tile covers 128 query positions (q0 a multiple of 128 is
+// not required); K/V pages are read by TMA from the layer's pool of
+// `kv_pages` pages; the qkv buffer has `q_rows` rows.  Persistent: one CTA per
+// SM.  Malformed tiles and out-of-pool page ids set status bit 2.
+int causal_attention_tc(const void* qkv, long long ldq, long long q_rows, int nqh, int nkvh,
+                        int hd, const AttnTile* tiles, int n_tiles, const int* block_tab,
+                        int max_pages, PagedKV kv, int kv_pages, void* out, bool bf16,
+                        unsigned* status, cudaStream_t s);
+
 // Embedding gather: rows of the device table for every non-audio token.
 int embed_gather(const uint32_t* ids, int T, const void* table, int vocab, int d, int audio_id,
                  void* out, int* bad, cudaStream_t s);

@@ -3,6 +3,7 @@
 #include "qa_b200_kernels.h"
 
 #include "gemm_tc.cuh"
+#include "kernels.cuh"
 
 using namespace qa;
 
@@ -38,5 +39,27 @@ extern "C" int qa_k_conv3x3s2(const void* x, int n, int h, int w, int c, const v
   ep.status = status;
   int rc = conv3x3s2_tc(x, n, h, w, c, wt, c_out, time_major != 0, bf16 != 0, ep,
                         static_cast<cudaStream_t>(stream));
+  return rc == 0 ? QA_OK : QA_ERR_CUDA;
+}
+
+extern "C" int qa_k_causal_attention(const void* qkv, long long ldq, long long q_rows, int nqh,
+                                     int nkvh, const int* tiles, int n_tiles, const int* block_tab,
+                                     int max_pages, const void* kpool, const void* vpool,
+                                     int kv_pages, void* out, int bf16, int impl,
+                                     unsigned* status, void* stream) {
+  if (!qkv || !tiles || !block_tab || !kpool || !vpool || !out || n_tiles < 0 || kv_pages <= 0)
+    return QA_ERR_ARG;
+  PagedKV kv{const_cast<void*>(kpool), const_cast<void*>(vpool), 64};
+  const AttnTile* t = reinterpret_cast<const AttnTile*>(tiles);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc;
+  if (impl == 0)
+    rc = causal_attention(qkv, ldq, nqh, nkvh, 128, t, n_tiles, block_tab, max_pages, kv, out,
+                          bf16 != 0, s);
+  else if (impl == 1)
+    rc = causal_attention_tc(qkv, ldq, q_rows, nqh, nkvh, 128, t, n_tiles, block_tab, max_pages,
+                             kv, kv_pages, out, bf16 != 0, status, s);
+  else
+    return QA_ERR_ARG;
   return rc == 0 ? QA_OK : QA_ERR_CUDA;
 }

@@ -653,10 +653,12 @@ int load_weights(qa_ctx* ctx, const qa_tensor* tensors, int n, const qa_cfg& c) 
 
 // ------------------------------------------------------------ batched-path plan
 
+// Attention work items: 128 query positions of one clip (each K/V head of the
+// item is one CTA-sized unit of the persistent tcgen05 attention kernel).
 void plan_tiles(Plan& P) {
   P.tiles.clear();
   for (int c = 0; c < P.n; ++c)
-    for (int q0 = 0; q0 < P.seq[c]; q0 += 64) P.tiles.push_back({c, q0, P.tok0[c], P.seq[c]});
+    for (int q0 = 0; q0 < P.seq[c]; q0 += 128) P.tiles.push_back({c, q0, P.tok0[c], P.seq[c]});
   // longest causal work first for load balance
   std::stable_sort(P.tiles.begin(), P.tiles.end(),
                    [](const AttnTile& a, const AttnTile& b) { return a.q0 > b.q0; });
@@ -874,6 +876,10 @@ int ensure_kv(qa_ctx* ctx, int pages) {
   const size_t bytes = static_cast<size_t>(c.num_layers) * pages * c.num_kv_heads * 64 * c.head_dim * 2;
   TRY(ensure(ctx, ctx->kcache, bytes));
   TRY(ensure(ctx, ctx->vcache, bytes));
+  // Page rows past a clip's end are read by the attention tiles and masked;
+  // start them at zero so that 0 * (stale value) is always 0.
+  CK(cudaMemset(ctx->kcache.p, 0, ctx->kcache.cap));
+  CK(cudaMemset(ctx->vcache.p, 0, ctx->vcache.cap));
   ctx->kv_pages = pages;
   ctx->kv_cap_tokens = std::min(pages * 64, c.max_seq);
   return QA_OK;
@@ -926,8 +932,9 @@ int run_decoder(qa_ctx* ctx, const Plan& P, const PlanDev& D) {
     KL("gemm", gemm_flops(T, ldq, H), gemm_bytes(T, ldq, H, 2),
        gemm_tc(ctx->xn.p, H, L.qkv_w, H, T, ldq, H, bf, ep, s, 256));
     KL("causal_attn", attn_flops, T * (2.0 * qd * 2 + 2.0 * nkv * hd * 2),
-       causal_attention(ctx->qkv.p, ldq, nq, nkv, hd, D.tiles, static_cast<int>(P.tiles.size()),
-                        D.block_tab, P.max_pages, kv, ctx->attn.p, bf, s));
+       causal_attention_tc(ctx->qkv.p, ldq, T, nq, nkv, hd, D.tiles,
+                           static_cast<int>(P.tiles.size()), D.block_tab, P.max_pages, kv,
+                           ctx->kv_pages, ctx->attn.p, bf, ctx->status.as<unsigned>(), s));
     ep.mode = EPI_RESID16;
     ep.out = ctx->hid.p;
     ep.ldo = H;
