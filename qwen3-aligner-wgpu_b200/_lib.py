@@ -259,14 +259,15 @@ def conv3x3s2(x, wt, out, time_major=False, mode=EPI_STORE16, act=ACT_NONE, bias
 
 
 def causal_attention(qkv, nqh, nkvh, tiles, block_tab, kpool, vpool, out, impl=1, status=None,
-                     stream=None):
+                     stream=None, validate=True):
     """Paged causal attention on torch CUDA tensors.
 
     qkv [T, ldq] 16-bit, tiles int32 [n, 4] (clip, q0, tok0, len), block_tab
     int32 [clips, max_pages], kpool/vpool [pages, nkvh, 64, 128], out [T, nqh*128].
     """
     import torch
-    check_attention_args(qkv, nqh, nkvh, tiles, block_tab, kpool, vpool, out)
+    if validate:  # copies tiles and block_tab to the host
+        check_attention_args(qkv, nqh, nkvh, tiles, block_tab, kpool, vpool, out)
     bf16 = 1 if qkv.dtype == torch.bfloat16 else 0
     s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
     rc = lib().qa_k_causal_attention(ptr(qkv), qkv.stride(0), qkv.shape[0], nqh, nkvh,

@@ -655,13 +655,19 @@ int load_weights(qa_ctx* ctx, const qa_tensor* tensors, int n, const qa_cfg& c) 
 
 // Attention work items: 128 query positions of one clip (each K/V head of the
 // item is one CTA-sized unit of the persistent tcgen05 attention kernel).
+// Longest clips first for load balance; the blocks of one clip stay adjacent
+// (last block first), so the CTAs running at the same time read the same K/V
+// pages and most of those reads hit L2.
 void plan_tiles(Plan& P) {
   P.tiles.clear();
-  for (int c = 0; c < P.n; ++c)
-    for (int q0 = 0; q0 < P.seq[c]; q0 += 128) P.tiles.push_back({c, q0, P.tok0[c], P.seq[c]});
-  // longest causal work first for load balance
-  std::stable_sort(P.tiles.begin(), P.tiles.end(),
-                   [](const AttnTile& a, const AttnTile& b) { return a.q0 > b.q0; });
+  std::vector<int> order(P.n);
+  for (int c = 0; c < P.n; ++c) order[c] = c;
+  std::stable_sort(order.begin(), order.end(),
+                   [&](int a, int b) { return P.seq[a] > P.seq[b]; });
+  for (int c : order) {
+    const int nb = (P.seq[c] + 127) / 128;
+    for (int b = nb - 1; b >= 0; --b) P.tiles.push_back({c, b * 128, P.tok0[c], P.seq[c]});
+  }
 }
 
 void plan_decoder(Plan& P) {

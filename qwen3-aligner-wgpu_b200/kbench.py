@@ -2,11 +2,17 @@
 
     python qwen3-aligner-wgpu_b200/kbench.py gemm --m 16384 --n 6144 --k 1024 --mode swiglu
     python qwen3-aligner-wgpu_b200/kbench.py gemm --m 16384 --n 1024 --k 3072 --mode resid16
+    python qwen3-aligner-wgpu_b200/kbench.py attention --clips 64 --impl 1
 
 Each run times `--iters` launches with CUDA events on the launching stream
 (after `--warmup` launches) and prints one JSON line with the mean launch time
 and the achieved TFLOP/s.  Used for the ncu captures under profiles/ (one
 kernel, a handful of launches, inputs larger than L2).
+
+`attention` runs one decoder layer's paged causal attention over `--clips`
+clips whose lengths are drawn uniformly from [--min-len, --max-len] tokens
+(the batched 30 s workload's decoder clips average about 400 tokens), 16 query
+and 8 K/V heads of 128, pages shuffled; FLOP/s counts the exact causal work.
 """
 import argparse
 import importlib
@@ -20,7 +26,11 @@ sys.path.insert(0, os.path.dirname(HERE))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemm"])
+    ap.add_argument("kernel", choices=["gemm", "attention"])
+    ap.add_argument("--clips", type=int, default=64)
+    ap.add_argument("--min-len", type=int, default=130)
+    ap.add_argument("--max-len", type=int, default=750)
+    ap.add_argument("--impl", type=int, default=1)
     ap.add_argument("--m", type=int, default=16384)
     ap.add_argument("--n", type=int, default=6144)
     ap.add_argument("--k", type=int, default=1024)
@@ -35,6 +45,8 @@ def main():
     qa = importlib.import_module("qwen3-aligner-wgpu_b200")
     L = qa._lib
     dt = torch.float16 if a.dtype == "f16" else torch.bfloat16
+    if a.kernel == "attention":
+        return attention(a, L, dt)
     g = torch.Generator(device="cuda").manual_seed(0)
     A = (torch.randn(a.m, a.k, device="cuda", generator=g) * 0.5).to(dt)
     B = (torch.randn(a.n, a.k, device="cuda", generator=g) * 0.05).to(dt)
@@ -59,6 +71,58 @@ def main():
     print(json.dumps({"kernel": "gemm_tc", "m": a.m, "n": a.n, "k": a.k, "mode": a.mode,
                       "dtype": a.dtype, "ms": ms, "tflops": flops / ms / 1e9,
                       "algorithmic_bytes": (a.m * a.k + a.n * a.k) * 2 + a.m * out_cols * out.element_size()}))
+
+
+def attention(a, L, dt):
+    import numpy as np
+    import torch
+    nq, nkv, hd, page = 16, 8, 128, 64
+    rng = np.random.default_rng(0)
+    lens = [int(x) for x in rng.integers(a.min_len, a.max_len + 1, a.clips)]
+    T = sum(lens)
+    pages_per = [(n + page - 1) // page for n in lens]
+    n_pages = sum(pages_per)
+    perm = rng.permutation(n_pages)
+    bt = np.zeros((len(lens), max(pages_per)), dtype=np.int32)
+    tiles, k, tok0 = [], 0, 0
+    step = 128 if a.impl == 1 else 64
+    for c, n in enumerate(lens):
+        bt[c, : pages_per[c]] = perm[k: k + pages_per[c]]
+        k += pages_per[c]
+        tiles += [(c, q0, tok0, n) for q0 in range(0, n, step)]
+        tok0 += n
+    if a.impl == 1:  # the runtime's order: longest clip first, a clip's blocks adjacent
+        tiles.sort(key=lambda t: (-t[3], t[0], -t[1]))
+    else:
+        tiles.sort(key=lambda t: -t[1])
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev).manual_seed(0)
+    qkv = (torch.randn(T, (nq + 2 * nkv) * hd, device=dev, generator=g)).to(dt)
+    kpool = torch.randn(n_pages, nkv, page, hd, device=dev, generator=g).to(dt)
+    vpool = torch.randn(n_pages, nkv, page, hd, device=dev, generator=g).to(dt)
+    out = torch.empty(T, nq * hd, device=dev, dtype=dt)
+    t = torch.tensor(tiles, dtype=torch.int32, device=dev)
+    btd = torch.from_numpy(bt).to(dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    L.check_attention_args(qkv, nq, nkv, t, btd, kpool, vpool, out)
+    run = lambda: L.causal_attention(qkv, nq, nkv, tiles=t, block_tab=btd, kpool=kpool,
+                                     vpool=vpool, out=out, impl=a.impl, status=status,
+                                     validate=False)
+    for _ in range(a.warmup):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.iters):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    ms = e0.elapsed_time(e1) / a.iters
+    flops = sum(4.0 * hd * nq * 0.5 * n * (n + 1) for n in lens)
+    print(json.dumps({"kernel": "causal_attention", "impl": a.impl, "clips": a.clips,
+                      "tokens": T, "items": len(tiles) * nkv, "dtype": a.dtype, "ms": ms,
+                      "tflops": flops / ms / 1e9}))
 
 
 if __name__ == "__main__":
