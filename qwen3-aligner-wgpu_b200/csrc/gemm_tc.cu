@@ -12,6 +12,8 @@
 //               epilogue and stores to global memory.
 // Nothing here uses cluster multicast: each CTA loads its own tiles.
 #include "gemm_tc.cuh"
+
+#include <algorithm>
 #include "sm100.cuh"
 #include "tma_host.h"
 
@@ -497,6 +499,186 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// 3x3 / stride 2 / pad 1 convolution as a persistent GEMM whose A operand is
+// loaded by TMA straight from the NHWC activations: an M tile is R whole
+// output rows of one image (R = floor(128 / wo)), and the k-block for tap
+// (kh, kw) and channels [cb, cb + 32) is ONE 4-D box of the input viewed as
+// [n][h][w][c] with traversal strides (1, 2, 2, 1): wo pixels along w from
+// kw - 1 and R rows along h from 2*oh0 + kh - 1, 32 channels each (64-byte
+// rows, 64-byte swizzle).  Padding pixels (coordinate -1 or past the edge)
+// arrive as zeros from the TMA unit.  The box fills tile rows m = r*wo + c;
+// rows past R*wo (and rows past the image's last output row) are computed
+// from stale shared memory and never stored.  Same warp roles, TMEM
+// double-buffering and epilogue as gemm_tc_kernel.
+constexpr int kCvBK = 32;  // k-block: 32 channels of one tap
+
+template <int BN>
+struct ConvCfg {
+  static constexpr int kStages = 8;
+  static constexpr uint32_t kABytes = kBM * kCvBK * 2;  // 8 KB (the box fills R*wo rows)
+  static constexpr uint32_t kBBytes = BN * kCvBK * 2;
+  static constexpr uint32_t kTmemCols = GemmCfg<BN>::kTmemCols;
+  static constexpr size_t kSmem = 1024 + kStages * (kABytes + kBBytes) + 256;
+};
+
+struct ConvTiles {
+  int ho, wo, c;       // output geometry, input channels
+  int rows;            // output rows per tile (R)
+  int tiles_per_img;   // ceil(ho / R)
+  int n_mtiles;        // images x tiles_per_img
+  int time_major;      // output positions ordered (ow, oh) instead of (oh, ow)
+  uint32_t a_bytes;    // bytes one A box delivers: R * wo * 64
+};
+
+template <int BN, typename T>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    conv_tma_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmB,
+                    ConvTiles g, int N, int K, EpiParams ep) {
+  using Cfg = ConvCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  constexpr uint32_t kAccCols = Cfg::kTmemCols;
+  constexpr uint32_t kAllocCols = 2 * Cfg::kTmemCols;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * Cfg::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBBytes);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nkb = K / kCvBK;
+  const int n_tiles_n = (N + BN - 1) / BN;
+  const int n_tiles = n_tiles_n * g.n_mtiles;
+  const int M = g.n_mtiles / g.tiles_per_img * g.ho * g.wo;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 32 * kGemmEpiWarps);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmX);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tslot, kAllocCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+
+  auto timed_out = [&]() {
+    *abort_flag = 1;
+    if (ep.status) atomicOr(ep.status, kStatusTimeout);
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t c = 0;
+      for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
+        const int mt = t / n_tiles_n, n0 = (t % n_tiles_n) * BN;
+        const int img = mt / g.tiles_per_img;
+        const int oh0 = (mt % g.tiles_per_img) * g.rows;
+        for (int kb = 0; kb < nkb; ++kb, ++c) {
+          const int s = c % S;
+          const uint32_t ph = (c / S) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1u)) {
+            timed_out();
+            break;
+          }
+          const int k0 = kb * kCvBK;
+          const int tap = k0 / g.c, cb = k0 - tap * g.c;
+          const int kh = tap / 3, kw = tap - kh * 3;
+          mbar_arrive_expect_tx(&full[s], g.a_bytes + Cfg::kBBytes);
+          tma_load_4d(&tmX, &full[s], sA + s * Cfg::kABytes, cb, kw - 1, 2 * oh0 + kh - 1, img);
+          tma_load_2d(&tmB, &full[s], sB + s * Cfg::kBBytes, k0, n0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = f16_instr_desc(kBM, BN, H16Traits<T>::kBf16);
+      uint32_t c = 0;
+      int lt = 0;
+      for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x, ++lt) {
+        const int buf = lt & 1;
+        if (!mbar_wait(&tempty[buf], ((lt >> 1) & 1) ^ 1u)) {
+          timed_out();
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc = tbase + buf * kAccCols;
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb, ++c) {
+          const int s = c % S;
+          const uint32_t ph = (c / S) & 1;
+          if (!mbar_wait(&full[s], ph)) {
+            timed_out();
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + s * Cfg::kABytes);
+          const uint32_t b_addr = smem_u32(sB + s * Cfg::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kCvBK / 16; ++k)
+            mma_f16(acc, sw64_kmajor_desc(a_addr + k * 32), sw64_kmajor_desc(b_addr + k * 32),
+                    idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          mma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        mma_commit(&tfull[buf]);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int wg = (warp - 2) / 4;
+    int cb, ce;
+    epi_range<BN>(ep.mode, wg, kGemmEpiWarps / 4, cb, ce);
+    int lt = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++lt) {
+      const int buf = lt & 1;
+      if (*abort_flag || !mbar_wait(&tfull[buf], (lt >> 1) & 1)) {
+        if (lane == 0) timed_out();
+        break;
+      }
+      tc_fence_after();
+      const int mt = t / n_tiles_n, n0 = (t % n_tiles_n) * BN;
+      const int img = mt / g.tiles_per_img;
+      const int oh0 = (mt % g.tiles_per_img) * g.rows;
+      const int m = q * 32 + lane;
+      const int oh = oh0 + m / g.wo, ow = m % g.wo;
+      const bool valid = m < g.rows * g.wo && oh < g.ho;
+      const int orow = img * g.ho * g.wo + (g.time_major ? ow * g.ho + oh : oh * g.wo + ow);
+      const uint32_t trow = tbase + buf * kAccCols + (static_cast<uint32_t>(q * 32) << 16);
+      epilogue<BN, T>(ep, trow, valid ? orow : M, M, n0, N, cb, ce);
+      tc_fence_before();
+      mbar_arrive(&tempty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kAllocCols);
+  }
+}
+
 int num_sms() {
   static int sms[64] = {0};
   int dev = 0;
@@ -737,6 +919,45 @@ int launch_conv(const void* x, const ConvGeom& g, const void* B, int M, int N, i
 }
 
 template <int BN, typename T>
+int launch_conv_tma(const void* x, int n, int h, int w, int c, const void* wt, int N,
+                    bool time_major, const EpiParams& ep, cudaStream_t stream) {
+  using Cfg = ConvCfg<BN>;
+  ConvTiles g;
+  g.ho = (h - 1) / 2 + 1;
+  g.wo = (w - 1) / 2 + 1;
+  g.c = c;
+  g.rows = std::min(kBM / g.wo, g.ho);
+  g.tiles_per_img = (g.ho + g.rows - 1) / g.rows;
+  g.n_mtiles = n * g.tiles_per_img;
+  g.time_major = time_major ? 1 : 0;
+  g.a_bytes = static_cast<uint32_t>(g.rows * g.wo * kCvBK * 2);
+  const int K = 9 * c;
+  // the input as [n][h][w][c]; spans 2*wo-1 and 2*rows-1 with stride 2 load
+  // wo columns and rows rows (and never exceed the tensor's own extent)
+  const long long dims[4] = {c, w, h, n};
+  const long long strides[3] = {2LL * c, 2LL * c * w, 2LL * c * w * h};
+  const int box[4] = {kCvBK, 2 * g.wo - 1, 2 * g.rows - 1, 1};
+  const int estr[4] = {1, 2, 2, 1};
+  CUtensorMap tx, tb;
+  int rc = make_tmap_nd(&tx, x, H16Traits<T>::kBf16, 4, dims, strides, box, estr, 64);
+  if (rc) return rc;
+  const long long bdims[2] = {K, N};
+  const long long bstr[1] = {2LL * K};
+  const int bbox[2] = {kCvBK, BN};
+  const int bestr[2] = {1, 1};
+  rc = make_tmap_nd(&tb, wt, H16Traits<T>::kBf16, 2, bdims, bstr, bbox, bestr, 64);
+  if (rc) return rc;
+  auto kern = conv_tma_kernel<BN, T>;
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmem);
+  if (e != cudaSuccess) return (int)e;
+  const int tiles = ((N + BN - 1) / BN) * g.n_mtiles;
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  kern<<<grid, kGemmThreads, Cfg::kSmem, stream>>>(tx, tb, g, N, K, ep);
+  return (int)cudaGetLastError();
+}
+
+template <int BN, typename T>
 int launch(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
            const EpiParams& ep, cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
@@ -799,6 +1020,14 @@ int conv3x3s2_tc(const void* x, int n, int h, int w, int c, const void* wt, int 
   ConvGeom g{h, w, c, (h - 1) / 2 + 1, (w - 1) / 2 + 1, time_major ? 1 : 0};
   const int M = n * g.ho * g.wo, K = 9 * c;
   const int bn = gemm_pick_bn(c_out);
+  // TMA path: whole 32-channel k-blocks per tap and output rows that fit a tile
+  if (c % kCvBK == 0 && g.wo <= kBM && (bn == 240 || bn == 256)) {
+    if (bn == 240)
+      return bf16 ? launch_conv_tma<240, __nv_bfloat16>(x, n, h, w, c, wt, c_out, time_major, ep, stream)
+                  : launch_conv_tma<240, __half>(x, n, h, w, c, wt, c_out, time_major, ep, stream);
+    return bf16 ? launch_conv_tma<256, __nv_bfloat16>(x, n, h, w, c, wt, c_out, time_major, ep, stream)
+                : launch_conv_tma<256, __half>(x, n, h, w, c, wt, c_out, time_major, ep, stream);
+  }
 #define QA_CONV_CASE(BNV)                                                                 \
   case BNV:                                                                               \
     return bf16 ? launch_conv<BNV, __nv_bfloat16>(x, g, wt, M, c_out, K, ep, stream)       \

@@ -3,6 +3,7 @@
     python qwen3-aligner-wgpu_b200/kbench.py gemm --m 16384 --n 6144 --k 1024 --mode swiglu
     python qwen3-aligner-wgpu_b200/kbench.py gemm --m 16384 --n 1024 --k 3072 --mode resid16
     python qwen3-aligner-wgpu_b200/kbench.py attention --clips 64 --impl 1
+    python qwen3-aligner-wgpu_b200/kbench.py conv --n 256 --h 64 --w 50 --c 480
 
 Each run times `--iters` launches with CUDA events on the launching stream
 (after `--warmup` launches) and prints one JSON line with the mean launch time
@@ -26,13 +27,17 @@ sys.path.insert(0, os.path.dirname(HERE))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemm", "attention"])
+    ap.add_argument("kernel", choices=["gemm", "attention", "conv"])
+    ap.add_argument("--h", type=int, default=64)
+    ap.add_argument("--w", type=int, default=50)
+    ap.add_argument("--c", type=int, default=480)
+    ap.add_argument("--time-major", action="store_true")
     ap.add_argument("--clips", type=int, default=64)
     ap.add_argument("--min-len", type=int, default=130)
     ap.add_argument("--max-len", type=int, default=750)
     ap.add_argument("--impl", type=int, default=1)
     ap.add_argument("--m", type=int, default=16384)
-    ap.add_argument("--n", type=int, default=6144)
+    ap.add_argument("--n", type=int, default=6144, help="gemm N, or images for conv")
     ap.add_argument("--k", type=int, default=1024)
     ap.add_argument("--mode", default="store16",
                     choices=["store16", "resid16", "swiglu", "resid32", "store32", "argmax"])
@@ -47,6 +52,8 @@ def main():
     dt = torch.float16 if a.dtype == "f16" else torch.bfloat16
     if a.kernel == "attention":
         return attention(a, L, dt)
+    if a.kernel == "conv":
+        return conv(a, L, dt)
     g = torch.Generator(device="cuda").manual_seed(0)
     A = (torch.randn(a.m, a.k, device="cuda", generator=g) * 0.5).to(dt)
     B = (torch.randn(a.n, a.k, device="cuda", generator=g) * 0.05).to(dt)
@@ -122,6 +129,36 @@ def attention(a, L, dt):
     flops = sum(4.0 * hd * nq * 0.5 * n * (n + 1) for n in lens)
     print(json.dumps({"kernel": "causal_attention", "impl": a.impl, "clips": a.clips,
                       "tokens": T, "items": len(tiles) * nkv, "dtype": a.dtype, "ms": ms,
+                      "tflops": flops / ms / 1e9}))
+
+
+def conv(a, L, dt):
+    """3x3 / stride 2 / pad 1 conv (+bias, GELU) over NHWC [n, h, w, c] -> c outputs."""
+    import torch
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = (torch.randn(a.n, a.h, a.w, a.c, device=dev, generator=g) * 0.5).to(dt)
+    wk = (torch.randn(a.c, 9 * a.c, device=dev, generator=g) * 0.02).to(dt)
+    bias = torch.randn(a.c, device=dev, generator=g) * 0.1
+    ho, wo = (a.h - 1) // 2 + 1, (a.w - 1) // 2 + 1
+    out = torch.empty(a.n * ho * wo, a.c, device=dev, dtype=dt)
+    st = torch.zeros(1, dtype=torch.int32, device=dev)
+    run = lambda: L.conv3x3s2(x, wk, out, time_major=a.time_major, act=L.ACT_GELU, bias=bias,
+                              status=st)
+    for _ in range(a.warmup):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.iters):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    ms = e0.elapsed_time(e1) / a.iters
+    flops = 2.0 * a.n * ho * wo * a.c * 9 * a.c
+    print(json.dumps({"kernel": "conv3x3s2", "n": a.n, "h": a.h, "w": a.w, "c": a.c,
+                      "time_major": a.time_major, "dtype": a.dtype, "ms": ms,
                       "tflops": flops / ms / 1e9}))
 
 
