@@ -55,6 +55,15 @@ int qa_k_conv3x3s2(const void* x, int n, int h, int w, int c, const void* wt, in
                    const float* bias, unsigned* status, void* stream);
 
 /*
+ * First conv level of the audio tower: conv2d(1 -> c_out, 3x3, stride 2,
+ * pad 1) + bias + erf-GELU over mel chunks [n][h][w] (f32), output NHWC
+ * [n][ho][wo][c_out] 16-bit (CpuConvStem::conv_block_stages level 1,
+ * src/audio_encoder.rs:361-447).  wt [c_out][9] f32, bias [c_out] f32.
+ */
+int qa_k_conv1(const float* mel, int n, int h, int w, const float* wt, const float* bias,
+               int c_out, void* out, int bf16, void* stream);
+
+/*
  * Causal GQA attention of the decoder prefill over the paged K/V cache
  * (src/cpu_decoder.rs:327-412; the reference GPU path's
  * prefill_attention_paged dispatch, src/decoder.rs:1463-1520).

@@ -58,7 +58,7 @@ EXPORTED = [
     "qa_head", "qa_align_batch", "qa_batch_stage", "qa_batch_run", "qa_batch_fetch",
     "qa_set_stream", "qa_set_profile", "qa_get_profile", "qa_fix_timestamps",
     "qa_head_noalloc",
-    "qa_k_gemm", "qa_k_conv3x3s2", "qa_k_causal_attention",
+    "qa_k_gemm", "qa_k_conv3x3s2", "qa_k_causal_attention", "qa_k_conv1",
 ]
 
 c_void_p = ctypes.c_void_p
@@ -176,6 +176,8 @@ def _declare(L: ctypes.CDLL) -> None:
     L.qa_k_gemm.restype = c_int
     L.qa_k_conv3x3s2.argtypes = [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_int,
                                  c_int, c_int, c_int, c_void_p, c_ll, c_void_p, c_void_p, c_void_p]
+    L.qa_k_conv1.argtypes = [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p,
+                             c_int, c_void_p]
     L.qa_k_causal_attention.argtypes = [c_void_p, c_ll, c_ll, c_int, c_int, c_void_p, c_int,
                                         c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p,
                                         c_int, c_int, c_void_p, c_void_p]
@@ -298,3 +300,12 @@ def check_attention_args(qkv, nqh, nkvh, tiles, block_tab, kpool, vpool, out) ->
         raise ValueError("tile (clip, q0, tok0, len) out of range")
     if bt.numel() and (int(bt.min()) < 0 or int(bt.max()) >= kpool.shape[0]):
         raise ValueError("block_tab names a page outside the pools")
+
+
+def conv1(mel, wt, bias, out, stream=None):
+    """conv1 + bias + GELU on torch CUDA tensors: mel [n, h, w] f32 -> out [n*ho*wo, c_out]."""
+    import torch
+    n, h, w = mel.shape
+    bf16 = 1 if out.dtype == torch.bfloat16 else 0
+    s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
+    check(lib().qa_k_conv1(ptr(mel), n, h, w, ptr(wt), ptr(bias), wt.shape[0], ptr(out), bf16, s))

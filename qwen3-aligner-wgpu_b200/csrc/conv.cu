@@ -17,51 +17,63 @@ __device__ __forceinline__ float gelu_erf(float x) {
   return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
 }
 
-// One CTA per (chunk, output row oh).  The three input rows are staged in
-// shared memory; thread j owns output channels 2j and 2j+1, keeps their 18
-// weights and 2 biases in registers and walks the row's output positions, so
-// each input tap is a shared-memory broadcast and each store is a coalesced
-// 2 x 16-bit word.
+// One CTA per (chunk, pair of output rows oh0, oh0 + 1).  The five input rows
+// 2*oh0 - 1 .. 2*oh0 + 3 are staged in shared memory with a zero column on
+// each side (the padding), so the taps need no bounds checks.  Thread j of a
+// row owns output channels 4j .. 4j+3: their 36 weights and 4 biases stay in
+// registers, each tap read from shared memory (a broadcast) feeds four FMAs,
+// and each output position is one 8-byte store, contiguous across the row's
+// threads.
+constexpr int kC1Ch = 4;  // output channels per thread
+
 template <typename T>
 __global__ void __launch_bounds__(256) conv1_kernel(const float* __restrict__ mel, int h, int w,
                                                     const float* __restrict__ wt,
                                                     const float* __restrict__ bias, int c_out,
                                                     T* __restrict__ out) {
-  extern __shared__ float s_in[];  // [3][w]
+  extern __shared__ float s_in[];  // [5][w + 2]
   const int ho = (h + 2 - 3) / 2 + 1, wo = (w + 2 - 3) / 2 + 1;
-  const int chunk = blockIdx.y, oh = blockIdx.x;
+  const int wp = w + 2;
+  const int chunk = blockIdx.y, oh0 = 2 * blockIdx.x;
   const float* src = mel + static_cast<long long>(chunk) * h * w;
-  for (int i = threadIdx.x; i < 3 * w; i += blockDim.x) {
-    const int r = i / w, col = i % w;
-    const int ih = 2 * oh + r - 1;
-    s_in[i] = (ih >= 0 && ih < h) ? src[ih * w + col] : 0.0f;
+  for (int i = threadIdx.x; i < 5 * wp; i += blockDim.x) {
+    const int r = i / wp, col = i % wp - 1;
+    const int ih = 2 * oh0 + r - 1;
+    s_in[i] = (ih >= 0 && ih < h && col >= 0 && col < w) ? src[ih * w + col] : 0.0f;
   }
   __syncthreads();
-  T* dst = out + (static_cast<long long>(chunk) * ho + oh) * wo * c_out;
-  for (int pair = threadIdx.x; pair < c_out / 2; pair += blockDim.x) {
-    const int oc = 2 * pair;
-    float w0[9], w1[9];
+  const int nq = c_out / kC1Ch;
+  const int rr = threadIdx.x / nq, quad = threadIdx.x % nq;
+  const int oh = oh0 + rr;
+  if (rr >= 2 || oh >= ho) return;
+  const int oc = quad * kC1Ch;
+  float wk[kC1Ch][9], b[kC1Ch];
 #pragma unroll
-    for (int k = 0; k < 9; ++k) {
-      w0[k] = wt[oc * 9 + k];
-      w1[k] = wt[(oc + 1) * 9 + k];
-    }
-    const float b0 = bias[oc], b1 = bias[oc + 1];
-    for (int ow = 0; ow < wo; ++ow) {
-      float a0 = 0.0f, a1 = 0.0f;
+  for (int c = 0; c < kC1Ch; ++c) {
 #pragma unroll
-      for (int kh = 0; kh < 3; ++kh)
+    for (int k = 0; k < 9; ++k) wk[c][k] = wt[(oc + c) * 9 + k];
+    b[c] = bias[oc + c];
+  }
+  const float* rows = s_in + 2 * rr * wp;  // input rows 2*oh - 1 .. 2*oh + 1 (padded)
+  T* dst = out + (static_cast<long long>(chunk) * ho + oh) * wo * c_out + oc;
+#pragma unroll 2
+  for (int ow = 0; ow < wo; ++ow) {
+    float a[kC1Ch];
 #pragma unroll
-        for (int kw = 0; kw < 3; ++kw) {
-          const int iw = 2 * ow + kw - 1;
-          const float v = (iw >= 0 && iw < w) ? s_in[kh * w + iw] : 0.0f;
-          a0 = fmaf(w0[kh * 3 + kw], v, a0);
-          a1 = fmaf(w1[kh * 3 + kw], v, a1);
-        }
-      T pr[2] = {f2h<T>(gelu_erf(a0 + b0)), f2h<T>(gelu_erf(a1 + b1))};
-      *reinterpret_cast<uint32_t*>(dst + static_cast<long long>(ow) * c_out + oc) =
-          *reinterpret_cast<const uint32_t*>(pr);
-    }
+    for (int c = 0; c < kC1Ch; ++c) a[c] = 0.0f;
+#pragma unroll
+    for (int kh = 0; kh < 3; ++kh)
+#pragma unroll
+      for (int kw = 0; kw < 3; ++kw) {
+        const float v = rows[kh * wp + 2 * ow + kw];  // column 2*ow + kw - 1, shifted by the pad
+#pragma unroll
+        for (int c = 0; c < kC1Ch; ++c) a[c] = fmaf(wk[c][kh * 3 + kw], v, a[c]);
+      }
+    alignas(8) T pr[kC1Ch];
+#pragma unroll
+    for (int c = 0; c < kC1Ch; ++c) pr[c] = f2h<T>(gelu_erf(a[c] + b[c]));  // taps, then bias
+    *reinterpret_cast<uint2*>(dst + static_cast<long long>(ow) * c_out) =
+        *reinterpret_cast<const uint2*>(pr);
   }
 }
 
@@ -97,10 +109,11 @@ __global__ void im2col_kernel(const uint4* __restrict__ x, int n, int h, int w, 
 int conv1_direct(const float* mel, int n, int h, int w, const float* wt, const float* bias,
                  int c_out, void* out, bool bf16, cudaStream_t s) {
   if (n <= 0) return 0;
-  if (c_out % 2 || 3 * w * sizeof(float) > 48 * 1024) return (int)cudaErrorInvalidValue;
+  if (c_out % kC1Ch || 2 * (c_out / kC1Ch) > 256 || 5 * (w + 2) * sizeof(float) > 48 * 1024)
+    return (int)cudaErrorInvalidValue;
   const int ho = (h + 2 - 3) / 2 + 1;
-  const size_t smem = 3 * w * sizeof(float);
-  dim3 grid(ho, n);
+  const size_t smem = 5 * (w + 2) * sizeof(float);
+  dim3 grid((ho + 1) / 2, n);
   if (bf16)
     conv1_kernel<__nv_bfloat16><<<grid, 256, smem, s>>>(mel, h, w, wt, bias, c_out,
                                                         static_cast<__nv_bfloat16*>(out));

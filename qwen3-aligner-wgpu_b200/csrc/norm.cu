@@ -93,9 +93,12 @@ __global__ void rmsnorm_kernel(const T* __restrict__ x, int rows, int d,
   for (int k = 0; k < 4; ++k) {
     const int vi = lane + 32 * k;
     if (vi < nv) {
+      const float4 g0 = reinterpret_cast<const float4*>(w)[2 * vi];
+      const float4 g1 = reinterpret_cast<const float4*>(w)[2 * vi + 1];
+      const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
       alignas(16) T e[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) e[j] = f2h<T>(__fmul_rn(__fmul_rn(v[k * 8 + j], inv), w[vi * 8 + j]));
+      for (int j = 0; j < 8; ++j) e[j] = f2h<T>(__fmul_rn(__fmul_rn(v[k * 8 + j], inv), g[j]));
       orow[vi] = *reinterpret_cast<const uint4*>(e);
     }
   }
@@ -187,7 +190,7 @@ int layernorm_rows(const float* x, int rows, int d, const float* g, const float*
 int rmsnorm_rows(const void* x, int rows, int d, const float* w, float eps, void* out, bool bf16,
                  cudaStream_t s) {
   if (rows <= 0) return 0;
-  if (d % 8 || d > 1024) return (int)cudaErrorInvalidValue;
+  if (d % 8 || d > 1024 || (reinterpret_cast<uintptr_t>(w) & 15u)) return (int)cudaErrorInvalidValue;
   const unsigned blocks = (rows + 7) / 8;
   if (bf16)
     rmsnorm_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), rows, d, w, eps,

@@ -4,6 +4,7 @@
     python qwen3-aligner-wgpu_b200/kbench.py gemm --m 16384 --n 1024 --k 3072 --mode resid16
     python qwen3-aligner-wgpu_b200/kbench.py attention --clips 64 --impl 1
     python qwen3-aligner-wgpu_b200/kbench.py conv --n 256 --h 64 --w 50 --c 480
+    python qwen3-aligner-wgpu_b200/kbench.py conv1 --n 256 --h 128 --w 100 --c 480
 
 Each run times `--iters` launches with CUDA events on the launching stream
 (after `--warmup` launches) and prints one JSON line with the mean launch time
@@ -27,7 +28,7 @@ sys.path.insert(0, os.path.dirname(HERE))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemm", "attention", "conv"])
+    ap.add_argument("kernel", choices=["gemm", "attention", "conv", "conv1"])
     ap.add_argument("--h", type=int, default=64)
     ap.add_argument("--w", type=int, default=50)
     ap.add_argument("--c", type=int, default=480)
@@ -54,6 +55,8 @@ def main():
         return attention(a, L, dt)
     if a.kernel == "conv":
         return conv(a, L, dt)
+    if a.kernel == "conv1":
+        return conv1(a, L, dt)
     g = torch.Generator(device="cuda").manual_seed(0)
     A = (torch.randn(a.m, a.k, device="cuda", generator=g) * 0.5).to(dt)
     B = (torch.randn(a.n, a.k, device="cuda", generator=g) * 0.05).to(dt)
@@ -160,6 +163,33 @@ def conv(a, L, dt):
     print(json.dumps({"kernel": "conv3x3s2", "n": a.n, "h": a.h, "w": a.w, "c": a.c,
                       "time_major": a.time_major, "dtype": a.dtype, "ms": ms,
                       "tflops": flops / ms / 1e9}))
+
+
+def conv1(a, L, dt):
+    """First conv level: mel [n, h, w] f32 -> GELU(conv 1 -> c) NHWC 16-bit."""
+    import torch
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev).manual_seed(0)
+    mel = torch.randn(a.n, a.h, a.w, device=dev, generator=g)
+    wt = torch.randn(a.c, 9, device=dev, generator=g) * 0.3
+    bias = torch.randn(a.c, device=dev, generator=g) * 0.1
+    ho, wo = (a.h - 1) // 2 + 1, (a.w - 1) // 2 + 1
+    out = torch.empty(a.n * ho * wo, a.c, device=dev, dtype=dt)
+    run = lambda: L.conv1(mel, wt, bias, out)
+    for _ in range(a.warmup):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.iters):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.iters
+    nbytes = out.numel() * out.element_size() + mel.numel() * 4
+    print(json.dumps({"kernel": "conv1", "n": a.n, "h": a.h, "w": a.w, "c": a.c, "dtype": a.dtype,
+                      "ms": ms, "gbs": nbytes / ms / 1e6,
+                      "outputs_per_s": out.numel() / ms * 1e3}))
 
 
 if __name__ == "__main__":
