@@ -500,6 +500,169 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// CTA-pair version (tcgen05 cta_group::2) for 256 x 256 output tiles: the two
+// CTAs of a cluster run on neighbouring SMs; each TMA-loads its own 128 rows
+// of A and its own 128 rows (output columns) of B per k-block, the first CTA
+// issues M=256, N=256 MMAs that read both CTAs' shared memory, and each CTA
+// holds its 128 accumulator rows (all 256 columns) in its own TMEM, drained by
+// its own epilogue warps.  Per SM this moves half the B bytes of a 128 x 256
+// tile for the same MMA work, which takes the operand stream from about three
+// quarters of the L2-to-SM bandwidth down to one half.
+//   full[s]    (first CTA) both CTAs' A and B halves of stage s landed;
+//   empty[s]   (each CTA, by multicast commit) stage s may be refilled;
+//   tfull[b]   (each CTA, by multicast commit) accumulator b complete;
+//   tempty[b]  (first CTA) both CTAs' epilogues drained accumulator b
+//              (one remote arrival per epilogue warp, 16 in all).
+constexpr int kPairStages = 6;
+constexpr uint32_t kPairHalf = kBM * kBK * 2;  // 16 KB: 128 rows x 64 k of A or of B
+constexpr size_t kPairSmem = 1024 + kPairStages * 2 * kPairHalf + 256;
+
+template <typename T>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     int M, int N, int K, EpiParams ep) {
+  constexpr int S = kPairStages;
+  constexpr int BN = 256;
+  constexpr uint32_t kAccCols = 256;
+  constexpr uint32_t kAllocCols = 512;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * kPairHalf;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + S * kPairHalf);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+  const int nkb = (K + kBK - 1) / kBK;
+  const int n_tiles_n = N / BN;
+  const int n_tiles = n_tiles_n * ((M + 2 * kBM - 1) / (2 * kBM));
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 2 * kGemmEpiWarps);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc_pair(tslot, kAllocCols);
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+
+  auto timed_out = [&]() {
+    *abort_flag = 1;
+    if (ep.status) atomicOr(ep.status, kStatusTimeout);
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t full_lead = mapa_shared(smem_u32(full), 0);
+      uint32_t c = 0;
+      for (int t = pair; t < n_tiles && !*abort_flag; t += n_pairs) {
+        const int m0 = (t / n_tiles_n) * 2 * kBM, n0 = (t % n_tiles_n) * BN;
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb, ++c) {
+          const int s = c % S;
+          const uint32_t ph = (c / S) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1u)) {
+            timed_out();
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 4 * kPairHalf);  // both CTAs' halves
+          const uint32_t bar = full_lead + s * 8;
+          tma_load_2d_pair(&tmA, bar, sA + s * kPairHalf, kb * kBK, m0 + rank * kBM);
+          tma_load_2d_pair(&tmB, bar, sB + s * kPairHalf, kb * kBK, n0 + rank * kBM);
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = f16_instr_desc(2 * kBM, BN, H16Traits<T>::kBf16);
+      uint32_t c = 0;
+      int lt = 0;
+      for (int t = pair; t < n_tiles && !*abort_flag; t += n_pairs, ++lt) {
+        const int buf = lt & 1;
+        if (!mbar_wait_cluster(&tempty[buf], ((lt >> 1) & 1) ^ 1u)) {
+          timed_out();
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc = tbase + buf * kAccCols;
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb, ++c) {
+          const int s = c % S;
+          const uint32_t ph = (c / S) & 1;
+          if (!mbar_wait(&full[s], ph)) {
+            timed_out();
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + s * kPairHalf);
+          const uint32_t b_addr = smem_u32(sB + s * kPairHalf);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            mma_f16_pair(acc, sw128_kmajor_desc(a_addr + k * 32), sw128_kmajor_desc(b_addr + k * 32),
+                         idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          mma_commit_pair(&empty[s], 0x3);
+        }
+        if (!ok) break;
+        mma_commit_pair(&tfull[buf], 0x3);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int wg = (warp - 2) / 4;
+    int cb, ce;
+    epi_range<BN>(ep.mode, wg, kGemmEpiWarps / 4, cb, ce);
+    const uint32_t tempty_lead = mapa_shared(smem_u32(tempty), 0);
+    int lt = 0;
+    for (int t = pair; t < n_tiles; t += n_pairs, ++lt) {
+      const int buf = lt & 1;
+      if (*abort_flag || !mbar_wait(&tfull[buf], (lt >> 1) & 1)) {
+        if (lane == 0) timed_out();
+        break;
+      }
+      tc_fence_after();
+      const int m0 = (t / n_tiles_n) * 2 * kBM, n0 = (t % n_tiles_n) * BN;
+      const int row = m0 + rank * kBM + q * 32 + lane;
+      const uint32_t trow = tbase + buf * kAccCols + (static_cast<uint32_t>(q * 32) << 16);
+      epilogue<BN, T>(ep, trow, row, M, n0, N, cb, ce);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(tempty_lead + buf * 8);
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // neither CTA leaves while the other may still signal it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tbase, kAllocCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // 3x3 / stride 2 / pad 1 convolution as a persistent GEMM whose A operand is
 // loaded by TMA straight from the NHWC activations: an M tile is R whole
 // output rows of one image (R = floor(128 / wo)), and the k-block for tap
@@ -957,6 +1120,48 @@ int launch_conv_tma(const void* x, int n, int h, int w, int c, const void* wt, i
   return (int)cudaGetLastError();
 }
 
+template <typename T>
+int launch_pair(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
+                const EpiParams& ep, cudaStream_t stream) {
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d(&ta, A, H16Traits<T>::kBf16, K, M, lda, kBK, kBM);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tb, B, H16Traits<T>::kBf16, K, N, ldb, kBK, kBM);
+  if (rc) return rc;
+  auto kern = gemm_pair_kernel<T>;
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairSmem);
+  if (e != cudaSuccess) return (int)e;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = kPairSmem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // persistent: as many pairs as can be resident at once (cached per device)
+  static int max_pairs[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!max_pairs[dev]) {
+    cfg.gridDim = dim3(2 * (num_sms() / 2), 1, 1);
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) n = num_sms() / 2;
+    max_pairs[dev] = n;
+  }
+  const int tiles = (N / 256) * ((M + 255) / 256);
+  const int pairs = tiles < max_pairs[dev] ? tiles : max_pairs[dev];
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  e = cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, ep);
+  if (e != cudaSuccess) return (int)e;
+  return (int)cudaGetLastError();
+}
+
 template <int BN, typename T>
 int launch(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
            const EpiParams& ep, cudaStream_t stream) {
@@ -994,6 +1199,13 @@ int gemm_tc(const void* A, long long lda, const void* B, long long ldb, int M, i
   if ((reinterpret_cast<uintptr_t>(A) & 15u) || (reinterpret_cast<uintptr_t>(B) & 15u) ||
       (lda % 8) || (ldb % 8))
     return (int)cudaErrorInvalidValue;
+  // 256 x 256 tiles on CTA pairs whenever N allows (force_bn 0 = choose, -1 =
+  // require the pair kernel, > 0 = one CTA per tile with that width)
+  if (force_bn == -1 || (force_bn == 0 && N % 256 == 0 && M > 128)) {
+    if (N % 256) return (int)cudaErrorInvalidValue;
+    return bf16 ? launch_pair<__nv_bfloat16>(A, lda, B, ldb, M, N, K, ep, stream)
+                : launch_pair<__half>(A, lda, B, ldb, M, N, K, ep, stream);
+  }
   const int bn = force_bn ? force_bn : gemm_pick_bn(N);
   if (ep.mode == EPI_SWIGLU16 && ((N % bn) || (bn % 64))) return (int)cudaErrorInvalidValue;
   if (ep.mode == EPI_QKV_ROPE && ((N % 128) || (bn % 128))) return (int)cudaErrorInvalidValue;

@@ -936,7 +936,7 @@ int run_decoder(qa_ctx* ctx, const Plan& P, const PlanDev& D) {
     ep.rk.nq = nq;
     ep.rk.nkv = nkv;
     KL("gemm", gemm_flops(T, ldq, H), gemm_bytes(T, ldq, H, 2),
-       gemm_tc(ctx->xn.p, H, L.qkv_w, H, T, ldq, H, bf, ep, s, 256));
+       gemm_tc(ctx->xn.p, H, L.qkv_w, H, T, ldq, H, bf, ep, s, 0));
     KL("causal_attn", attn_flops, T * (2.0 * qd * 2 + 2.0 * nkv * hd * 2),
        causal_attention_tc(ctx->qkv.p, ldq, T, nq, nkv, hd, D.tiles,
                            static_cast<int>(P.tiles.size()), D.block_tab, P.max_pages, kv,
@@ -951,7 +951,7 @@ int run_decoder(qa_ctx* ctx, const Plan& P, const PlanDev& D) {
     ep.out = ctx->mlp.p;
     ep.ldo = I;
     KL("gemm", gemm_flops(T, 2 * I, H), gemm_bytes(T, I, H, 2) + 2.0 * I * H,
-       gemm_tc(ctx->xn.p, H, L.gu_w, H, T, 2 * I, H, bf, ep, s, 256));
+       gemm_tc(ctx->xn.p, H, L.gu_w, H, T, 2 * I, H, bf, ep, s, 0));
     ep.mode = EPI_RESID16;
     ep.out = ctx->hid.p;
     ep.ldo = H;

@@ -40,6 +40,8 @@ def main():
     ap.add_argument("--m", type=int, default=16384)
     ap.add_argument("--n", type=int, default=6144, help="gemm N, or images for conv")
     ap.add_argument("--k", type=int, default=1024)
+    ap.add_argument("--bn", type=int, default=0,
+                    help="gemm tile: 0 = library choice, -1 = CTA-pair 256x256, >0 = one CTA, that width")
     ap.add_argument("--mode", default="store16",
                     choices=["store16", "resid16", "swiglu", "resid32", "store32", "argmax"])
     ap.add_argument("--dtype", default="f16", choices=["f16", "bf16"])
@@ -66,7 +68,7 @@ def main():
     out_dt = torch.float32 if a.mode in ("resid32", "store32", "argmax") else dt
     out = torch.zeros(a.m, out_cols, device="cuda", dtype=out_dt)
     keys = torch.zeros(a.m, dtype=torch.int64, device="cuda") if a.mode == "argmax" else None
-    bn = 256 if a.mode == "swiglu" else 0
+    bn = a.bn
     for _ in range(a.warmup):
         L.gemm(A, B, out, mode=mode, keys=keys, force_bn=bn)
     torch.cuda.synchronize()
@@ -78,7 +80,7 @@ def main():
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / a.iters
     flops = 2.0 * a.m * a.n * a.k
-    print(json.dumps({"kernel": "gemm_tc", "m": a.m, "n": a.n, "k": a.k, "mode": a.mode,
+    print(json.dumps({"kernel": "gemm_tc", "m": a.m, "n": a.n, "k": a.k, "mode": a.mode, "bn": a.bn,
                       "dtype": a.dtype, "ms": ms, "tflops": flops / ms / 1e9,
                       "algorithmic_bytes": (a.m * a.k + a.n * a.k) * 2 + a.m * out_cols * out.element_size()}))
 
