@@ -513,16 +513,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 //   tfull[b]   (each CTA, by multicast commit) accumulator b complete;
 //   tempty[b]  (first CTA) both CTAs' epilogues drained accumulator b
 //              (one remote arrival per epilogue warp, 16 in all).
+// BN (256 or 224) is the pair tile's width: each CTA loads BN/2 rows of B.
 constexpr int kPairStages = 6;
-constexpr uint32_t kPairHalf = kBM * kBK * 2;  // 16 KB: 128 rows x 64 k of A or of B
-constexpr size_t kPairSmem = 1024 + kPairStages * 2 * kPairHalf + 256;
+constexpr uint32_t kPairHalf = kBM * kBK * 2;  // 16 KB: 128 rows x 64 k of A
+template <int BN>
+struct PairCfg {
+  static constexpr uint32_t kBHalf = (BN / 2) * kBK * 2;  // BN/2 rows x 64 k of B
+  static constexpr size_t kSmem = 1024 + kPairStages * (kPairHalf + kBHalf) + 256;
+};
 
-template <typename T>
+template <int BN, typename T>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      int M, int N, int K, EpiParams ep) {
   constexpr int S = kPairStages;
-  constexpr int BN = 256;
+  constexpr uint32_t kBHalf = PairCfg<BN>::kBHalf;
   constexpr uint32_t kAccCols = 256;
   constexpr uint32_t kAllocCols = 512;
   extern __shared__ uint8_t smem_raw[];
@@ -530,7 +535,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + S * kPairHalf;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + S * kPairHalf);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + S * kBHalf);
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + 2;
@@ -587,10 +592,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             ok = false;
             break;
           }
-          if (rank == 0) mbar_arrive_expect_tx(&full[s], 4 * kPairHalf);  // both CTAs' halves
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * (kPairHalf + kBHalf));  // both CTAs
           const uint32_t bar = full_lead + s * 8;
           tma_load_2d_pair(&tmA, bar, sA + s * kPairHalf, kb * kBK, m0 + rank * kBM);
-          tma_load_2d_pair(&tmB, bar, sB + s * kPairHalf, kb * kBK, n0 + rank * kBM);
+          tma_load_2d_pair(&tmB, bar, sB + s * kBHalf, kb * kBK, n0 + rank * (BN / 2));
         }
         if (!ok) break;
       }
@@ -619,7 +624,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(sA + s * kPairHalf);
-          const uint32_t b_addr = smem_u32(sB + s * kPairHalf);
+          const uint32_t b_addr = smem_u32(sB + s * kBHalf);
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k)
             mma_f16_pair(acc, sw128_kmajor_desc(a_addr + k * 32), sw128_kmajor_desc(b_addr + k * 32),
@@ -1120,15 +1125,16 @@ int launch_conv_tma(const void* x, int n, int h, int w, int c, const void* wt, i
   return (int)cudaGetLastError();
 }
 
-template <typename T>
+template <int BN, typename T>
 int launch_pair(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
                 const EpiParams& ep, cudaStream_t stream) {
+  constexpr size_t kPairSmem = PairCfg<BN>::kSmem;
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, A, H16Traits<T>::kBf16, K, M, lda, kBK, kBM);
   if (rc) return rc;
-  rc = make_tmap_2d(&tb, B, H16Traits<T>::kBf16, K, N, ldb, kBK, kBM);
+  rc = make_tmap_2d(&tb, B, H16Traits<T>::kBf16, K, N, ldb, kBK, BN / 2);
   if (rc) return rc;
-  auto kern = gemm_pair_kernel<T>;
+  auto kern = gemm_pair_kernel<BN, T>;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairSmem);
   if (e != cudaSuccess) return (int)e;
@@ -1144,7 +1150,7 @@ int launch_pair(const void* A, long long lda, const void* B, long long ldb, int 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   // persistent: as many pairs as can be resident at once (cached per device)
-  static int max_pairs[64] = {0};
+  static int max_pairs[64] = {0};  // per instantiation
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
@@ -1154,7 +1160,7 @@ int launch_pair(const void* A, long long lda, const void* B, long long ldb, int 
     if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) n = num_sms() / 2;
     max_pairs[dev] = n;
   }
-  const int tiles = (N / 256) * ((M + 255) / 256);
+  const int tiles = (N / BN) * ((M + 255) / 256);
   const int pairs = tiles < max_pairs[dev] ? tiles : max_pairs[dev];
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   e = cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, ep);
@@ -1199,12 +1205,17 @@ int gemm_tc(const void* A, long long lda, const void* B, long long ldb, int M, i
   if ((reinterpret_cast<uintptr_t>(A) & 15u) || (reinterpret_cast<uintptr_t>(B) & 15u) ||
       (lda % 8) || (ldb % 8))
     return (int)cudaErrorInvalidValue;
-  // 256 x 256 tiles on CTA pairs whenever N allows (force_bn 0 = choose, -1 =
-  // require the pair kernel, > 0 = one CTA per tile with that width)
-  if (force_bn == -1 || (force_bn == 0 && N % 256 == 0 && M > 128)) {
-    if (N % 256) return (int)cudaErrorInvalidValue;
-    return bf16 ? launch_pair<__nv_bfloat16>(A, lda, B, ldb, M, N, K, ep, stream)
-                : launch_pair<__half>(A, lda, B, ldb, M, N, K, ep, stream);
+  // 256 x 256 (or 256 x 224) tiles on CTA pairs whenever N allows (force_bn 0
+  // = choose, -1 = require the pair kernel, > 0 = one CTA per tile, that width)
+  const bool pair224 = N % 224 == 0 && ep.mode != EPI_SWIGLU16 && ep.mode != EPI_QKV_ROPE;
+  if (force_bn == -1 || (force_bn == 0 && M > 128 && (N % 256 == 0 || pair224))) {
+    if (N % 256 == 0)
+      return bf16 ? launch_pair<256, __nv_bfloat16>(A, lda, B, ldb, M, N, K, ep, stream)
+                  : launch_pair<256, __half>(A, lda, B, ldb, M, N, K, ep, stream);
+    if (pair224)
+      return bf16 ? launch_pair<224, __nv_bfloat16>(A, lda, B, ldb, M, N, K, ep, stream)
+                  : launch_pair<224, __half>(A, lda, B, ldb, M, N, K, ep, stream);
+    return (int)cudaErrorInvalidValue;
   }
   const int bn = force_bn ? force_bn : gemm_pick_bn(N);
   if (ep.mode == EPI_SWIGLU16 && ((N % bn) || (bn % 64))) return (int)cudaErrorInvalidValue;
