@@ -120,7 +120,9 @@ int qa_set_timeout_ms(qa_ctx* ctx, int ms);
 int qa_half(const qa_ctx* ctx);
 int qa_get_timings(const qa_ctx* ctx, qa_timings* out);
 /* Launch on the caller's CUDA stream (a cudaStream_t; NULL restores the
- * context's own stream).  No reference counterpart: wgpu owns its queue. */
+ * context's own non-blocking stream, so the legacy default stream cannot be
+ * selected: pass a created stream to order the library's work with other work
+ * on it).  No reference counterpart: wgpu owns its queue. */
 int qa_set_stream(qa_ctx* ctx, void* stream);
 /* Record CUDA events around every kernel launch (on = 1) and accumulate them
  * per kernel class; qa_get_profile returns up to `max` classes.  No reference
@@ -212,10 +214,15 @@ int qa_align_batch(qa_ctx* ctx, const qa_clip* clips, int n, qa_result* results)
  *   qa_batch_stage  validates and plans the batch and copies its inputs to
  *                   the device (results give the n_ts per clip and which
  *                   optional outputs to produce);
- *   qa_batch_run    enqueues the device pass over the staged inputs on the
- *                   context's stream and returns without waiting; it may be
- *                   called repeatedly on the same staged batch;
- *   qa_batch_fetch  copies the results back (bounded wait) into `results`. */
+ *   qa_batch_run    enqueues the device pass over the oldest staged batch on
+ *                   the context's stream, followed by the copy of its results
+ *                   to pinned host memory, and returns without waiting; with
+ *                   no batch staged it runs the last batch again;
+ *   qa_batch_fetch  waits (bounded) for the oldest batch that was run and
+ *                   copies its results into `results`.
+ * Up to two batches may be between stage and fetch, so the next batch can be
+ * staged (host copies, uploads queued behind the running kernels) while the
+ * previous one runs: stage(1) run(1) stage(2) run(2) fetch(1) stage(3) ... */
 int qa_batch_stage(qa_ctx* ctx, const qa_clip* clips, int n, const qa_result* results);
 int qa_batch_run(qa_ctx* ctx);
 int qa_batch_fetch(qa_ctx* ctx, qa_result* results);

@@ -144,6 +144,47 @@ class Aligner:
             out.append((r, items) if not (want_logits or want_normed) else (r, items, extra))
         return out
 
+    def align_stream(self, batches, want_logits: bool = False, want_normed: bool = False):
+        """Align an iterable of batches ([(samples, text, language)] each),
+        yielding one align_batch result list per batch, in order.
+
+        The host work of neighbouring batches overlaps the device pass:
+        while batch k runs on the GPU, batch k+1's words are split and
+        tokenised, its audio and ids staged and its pass queued behind batch
+        k (the library holds two batches between stage and fetch), and batch
+        k-1's timestamps are repaired and paired with words.  Every batch's
+        inputs are still copied to the device and its results read back."""
+        def build(batch):
+            return batch, [self.build_input(s, t, l) for s, t, l in batch]
+
+        def post(inputs, raws):
+            out = []
+            for (r, extra), inp in zip(raws, inputs):
+                items = postprocess.pair_words(inp.words, _lib.fix_timestamps(r))
+                out.append((r, items) if not (want_logits or want_normed) else (r, items, extra))
+            return out
+
+        it = iter(batches)
+        pending = []  # (inputs, staged) of batches run but not yet fetched, oldest first
+        nxt = next(it, None)
+        if nxt is None:
+            return
+        batch, inputs = build(nxt)
+        pending.append((inputs, self.stage([c[0] for c in batch], inputs, want_logits, want_normed)))
+        self.run()
+        while pending:
+            nxt = next(it, None)
+            if nxt is not None:
+                # built and staged while the previous batch runs; its uploads
+                # and kernels queue behind that batch's on the stream
+                batch, inputs = build(nxt)
+                pending.append((inputs, self.stage([c[0] for c in batch], inputs, want_logits,
+                                                   want_normed)))
+                self.run()
+            done_inputs, staged = pending.pop(0)
+            raws = self.fetch(staged)
+            yield post(done_inputs, raws)  # overlaps the next batch's device pass
+
     def align_inputs(self, samples_list, inputs, want_logits=False, want_normed=False):
         """The device-resident batched call on prebuilt inputs: [(raw_ms, extra)]."""
         b = self.stage(samples_list, inputs, want_logits, want_normed)

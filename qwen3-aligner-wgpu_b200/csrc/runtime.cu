@@ -695,7 +695,8 @@ size_t pad16(size_t n) {
   return (n * sizeof(T) + 15) / 16 * 16;
 }
 
-int upload_plan(qa_ctx* ctx, const Plan& P, const std::vector<uint32_t>& ids, PlanDev& D) {
+int upload_plan(qa_ctx* ctx, const Plan& P, const std::vector<uint32_t>& ids, PlanDev& D,
+                PinBuf& pin, DevBuf& dev, cudaStream_t st) {
   const size_t sz_mel = pad16<MelClip>(P.mel.size()), sz_cc = pad16<int>(P.chunk_clip.size()),
                sz_co = pad16<int>(P.co_map.size()), sz_w = pad16<int2>(P.windows.size()),
                sz_p2 = pad16<int>(P.p2_map.size()), sz_clip = pad16<int>(P.clip_of.size()),
@@ -704,10 +705,10 @@ int upload_plan(qa_ctx* ctx, const Plan& P, const std::vector<uint32_t>& ids, Pl
                sz_ids = pad16<uint32_t>(ids.size());
   const size_t total = sz_mel + sz_cc + sz_co + sz_w + sz_p2 + sz_clip + sz_pos + sz_bt + sz_t +
                        sz_ts + sz_ids;
-  TRY(ensure(ctx, ctx->idx_dev, total));
-  TRY(ensure_pin(ctx, ctx->pin_in, total));
-  uint8_t* h = static_cast<uint8_t*>(ctx->pin_in.p);
-  uint8_t* d = ctx->idx_dev.as<uint8_t>();
+  TRY(ensure(ctx, dev, total));
+  TRY(ensure_pin(ctx, pin, total));
+  uint8_t* h = static_cast<uint8_t*>(pin.p);
+  uint8_t* d = dev.as<uint8_t>();
   size_t off = 0;
   auto put = [&](const void* src, size_t bytes, size_t padded) {
     if (bytes) std::memcpy(h + off, src, bytes);
@@ -726,7 +727,7 @@ int upload_plan(qa_ctx* ctx, const Plan& P, const std::vector<uint32_t>& ids, Pl
   D.tiles = static_cast<AttnTile*>(put(P.tiles.data(), P.tiles.size() * sizeof(AttnTile), sz_t));
   D.ts_rows = static_cast<int*>(put(P.ts_rows.data(), P.ts_rows.size() * 4, sz_ts));
   D.ids = static_cast<uint32_t*>(put(ids.data(), ids.size() * 4, sz_ids));
-  CK(cudaMemcpyAsync(d, h, total, cudaMemcpyHostToDevice, ctx->stream));
+  CK(cudaMemcpyAsync(d, h, total, cudaMemcpyHostToDevice, st));
   return QA_OK;
 }
 
@@ -1011,6 +1012,37 @@ float elapsed(qa_ctx* ctx, int a, int b) {
   return ms;
 }
 
+float elapsed(const Staged& S, int a, int b) {
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, S.ev[a], S.ev[b]);
+  return ms;
+}
+
+// The oldest batch in `state`, or nullptr.
+Staged* oldest(qa_ctx* ctx, int state) {
+  Staged* best = nullptr;
+  for (auto& sl : ctx->slots)
+    if (sl && sl->state == state && (!best || sl->seq < best->seq)) best = sl.get();
+  return best;
+}
+
+// Bounded wait for one event.
+int wait_event(qa_ctx* ctx, cudaEvent_t e) {
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t q = cudaEventQuery(e);
+    if (q == cudaSuccess) return QA_OK;
+    if (q != cudaErrorNotReady)
+      return fail(ctx, QA_ERR_CUDA, "device error: %s", cudaGetErrorString(q));
+    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                        std::chrono::steady_clock::now() - t0)
+                        .count();
+    if (ms > ctx->timeout_ms)
+      return fail(ctx, QA_ERR_TIMEOUT, "device did not finish within %d ms", ctx->timeout_ms);
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
 }  // namespace
 
 // ====================================================================== C ABI
@@ -1031,7 +1063,8 @@ int qa_open(int device, int half, qa_ctx** out) {
     return QA_ERR_CUDA;
   }
   if (cudaSetDevice(device) != cudaSuccess ||
-      cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
+      cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&ctx->copy_stream, cudaStreamNonBlocking) != cudaSuccess) {
     delete ctx;
     return QA_ERR_CUDA;
   }
@@ -1080,11 +1113,21 @@ int qa_close(qa_ctx* ctx) {
   if (ctx->pin_in.p) cudaFreeHost(ctx->pin_in.p);
   if (ctx->pin_out.p) cudaFreeHost(ctx->pin_out.p);
   if (ctx->pin_res.p) cudaFreeHost(ctx->pin_res.p);
+  for (auto& sl : ctx->slots) {
+    if (!sl) continue;
+    for (PinBuf* b : {&sl->pin_samples, &sl->pin_plan, &sl->pin_res})
+      if (b->p) cudaFreeHost(b->p);
+    for (DevBuf* b : {&sl->samples, &sl->plan})
+      if (b->p) cudaFree(b->p);
+    for (auto& e : sl->ev)
+      if (e) cudaEventDestroy(e);
+  }
   for (auto& e : ctx->ev)
     if (e) cudaEventDestroy(e);
   for (auto& e : ctx->prof_pool)
     if (e) cudaEventDestroy(e);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+  if (ctx->copy_stream) cudaStreamDestroy(ctx->copy_stream);
   delete ctx;
   return QA_OK;
 }
@@ -1171,7 +1214,7 @@ int qa_audio_embeds(qa_ctx* ctx, const float* mel, int n_mels, int valid_frames,
   TRY(ensure(ctx, ctx->mel_chunked, chunk_elems * 4));
   CK(cudaMemcpyAsync(ctx->mel_chunked.p, ch, chunk_elems * 4, cudaMemcpyHostToDevice, ctx->stream));
   PlanDev D{};
-  TRY(upload_plan(ctx, P, {}, D));
+  TRY(upload_plan(ctx, P, {}, D, ctx->pin_in, ctx->idx_dev, ctx->stream));
   TRY(ensure(ctx, ctx->emb_out, static_cast<size_t>(na) * c.output_dim * 2));
   TRY(run_encoder(ctx, P, D, ctx->emb_out.p, nullptr));
   CK(cudaMemcpyAsync(out, ctx->emb_out.p, static_cast<size_t>(na) * c.output_dim * 2,
@@ -1203,7 +1246,7 @@ int qa_text_hidden(qa_ctx* ctx, const uint16_t* emb, int seq, float* out) {
   P.T_d = seq;
   plan_decoder(P);
   PlanDev D{};
-  TRY(upload_plan(ctx, P, {}, D));
+  TRY(upload_plan(ctx, P, {}, D, ctx->pin_in, ctx->idx_dev, ctx->stream));
   const int H = c.hidden_size;
   TRY(ensure(ctx, ctx->hid, static_cast<size_t>(seq) * H * 2));
   TRY(ensure(ctx, ctx->hidden_f32, static_cast<size_t>(seq) * H * 4));
@@ -1243,9 +1286,20 @@ int qa_batch_stage(qa_ctx* ctx, const qa_clip* clips, int n, const qa_result* re
   TRY(need_loaded(ctx));
   const qa_cfg& c = ctx->cfg;
   if (!clips || !results || n <= 0) return fail(ctx, QA_ERR_ARG, "empty batch");
-  if (!ctx->staged) ctx->staged.reset(new Staged());
-  Staged& S = *ctx->staged;
-  S.valid = false;
+  Staged* slot = nullptr;
+  for (auto& sl : ctx->slots) {
+    if (!sl) {
+      sl.reset(new Staged());
+      for (auto& e : sl->ev) CK(cudaEventCreate(&e));
+    }
+    if (sl->state == Staged::kFree) {
+      slot = sl.get();
+      break;
+    }
+  }
+  if (!slot)
+    return fail(ctx, QA_ERR_STATE, "two batches are already staged or running; fetch one first");
+  Staged& S = *slot;
   cudaStream_t s = ctx->stream;
   const int cs = 2 * c.n_window;
   Plan& P = S.P;
@@ -1307,11 +1361,12 @@ int qa_batch_stage(qa_ctx* ctx, const qa_clip* clips, int n, const qa_result* re
   plan_decoder(P);
   S.R = static_cast<int>(P.ts_rows.size());
   // ---- inputs to the device (sample staging is pinned; one copy each)
-  CK(cudaEventRecord(ctx->ev[0], s));
-  TRY(reset_flags(ctx));
-  TRY(ensure(ctx, ctx->samples, total_samples * 4));
-  TRY(ensure_pin(ctx, ctx->pin_out, total_samples * 4));
-  float* st = static_cast<float*>(ctx->pin_out.p);
+  // The other slot's batch may still be running: this batch's pinned and
+  // device input buffers are its own (their previous batch has been fetched),
+  // and the uploads go on the copy stream, overlapping that batch's kernels.
+  TRY(ensure(ctx, S.samples, total_samples * 4));
+  TRY(ensure_pin(ctx, S.pin_samples, total_samples * 4));
+  float* st = static_cast<float*>(S.pin_samples.p);
   // clips spread over the host cores: one pass, pageable -> pinned
   {
     std::atomic<int> next{0};
@@ -1325,9 +1380,11 @@ int qa_batch_stage(qa_ctx* ctx, const qa_clip* clips, int n, const qa_result* re
     worker();
     for (auto& x : th) x.join();
   }
-  CK(cudaMemcpyAsync(ctx->samples.p, st, total_samples * 4, cudaMemcpyHostToDevice, s));
-  TRY(upload_plan(ctx, P, ids, S.D));
-  CK(cudaEventRecord(ctx->ev[1], s));
+  cudaStream_t cp = ctx->copy_stream;
+  CK(cudaEventRecord(S.ev[0], cp));
+  CK(cudaMemcpyAsync(S.samples.p, st, total_samples * 4, cudaMemcpyHostToDevice, cp));
+  TRY(upload_plan(ctx, P, ids, S.D, S.pin_plan, S.plan, cp));
+  CK(cudaEventRecord(S.ev[1], cp));
   S.h2d_bytes = total_samples * 4 + static_cast<long long>(ids.size()) * 4 +
                  static_cast<long long>(P.mel.size() * sizeof(MelClip) + P.chunk_clip.size() * 4 +
                                         P.co_map.size() * 4 + P.windows.size() * 8 +
@@ -1340,81 +1397,112 @@ int qa_batch_stage(qa_ctx* ctx, const qa_clip* clips, int n, const qa_result* re
   TRY(ensure(ctx, ctx->mel_chunked, static_cast<size_t>(P.total_chunks) * 128 * cs * 4));
   TRY(ensure(ctx, ctx->maxkey, static_cast<size_t>(n) * 4));
   TRY(ensure(ctx, ctx->hid, static_cast<size_t>(P.T_d) * H * 2));
-  S.valid = true;
+  S.seq = ++ctx->batch_seq;
+  S.state = Staged::kStaged;
   return QA_OK;
 }
 
 int qa_batch_run(qa_ctx* ctx) {
   if (!ctx) return QA_ERR_ARG;
-  if (!ctx->loaded || !ctx->staged || !ctx->staged->valid)
-    return fail(ctx, QA_ERR_STATE, "qa_batch_run needs a staged batch (qa_batch_stage)");
+  // the oldest batch not yet run, else the most recently run one again
+  Staged* slot = ctx->loaded ? oldest(ctx, Staged::kStaged) : nullptr;
+  if (!slot && ctx->loaded)
+    for (auto& sl : ctx->slots)
+      if (sl && sl->state == Staged::kRunning && (!slot || sl->seq > slot->seq)) slot = sl.get();
+  if (!slot) return fail(ctx, QA_ERR_STATE, "qa_batch_run needs a staged batch (qa_batch_stage)");
   CK(cudaSetDevice(ctx->device));
   ctx->launches = 0;
-  Staged& S = *ctx->staged;
+  Staged& S = *slot;
   const Plan& P = S.P;
   const PlanDev& D = S.D;
   const qa_cfg& c = ctx->cfg;
   cudaStream_t s = ctx->stream;
   const int cs = 2 * c.n_window, n = P.n, H = c.hidden_size;
-  CK(cudaEventRecord(ctx->ev[2], s));
+  CK(cudaStreamWaitEvent(s, S.ev[1], 0));  // this batch's uploads
+  CK(cudaEventRecord(S.ev[2], s));
   TRY(reset_flags(ctx));
   // (a) mel
   CK(cudaMemsetAsync(ctx->maxkey.p, 0, static_cast<size_t>(n) * 4, s));
   const Weights& W = ctx->w;
   MelBank bank{W.fb_start, W.fb_len, W.fb_woff, W.fb_w};
   KL("mel", 0, 4.0 * P.mel.back().sample_off + 4.0 * P.mel.back().n_samples + 512.0 * P.total_frames,
-     mel_logpower(ctx->samples.as<float>(), D.mel, n, P.max_frames, W.window, W.twiddle, bank,
+     mel_logpower(S.samples.as<float>(), D.mel, n, P.max_frames, W.window, W.twiddle, bank,
                   1.0f / std::log(10.0f), ctx->mel_scratch.as<float>(), ctx->maxkey.as<unsigned>(), s));
   KL("mel_finalize", 0, 512.0 * P.total_frames + 512.0 * P.total_chunks * cs,
      mel_finalize_chunked(ctx->mel_scratch.as<float>(), D.mel, D.chunk_clip, P.total_chunks, cs,
                           ctx->maxkey.as<unsigned>(), ctx->mel_chunked.as<float>(), s));
-  CK(cudaEventRecord(ctx->ev[3], s));
+  CK(cudaEventRecord(S.ev[3], s));
   // (b) audio tower, projected rows scattered straight into the decoder input
   TRY(run_encoder(ctx, P, D, ctx->hid.p, D.p2_map));
-  CK(cudaEventRecord(ctx->ev[4], s));
+  CK(cudaEventRecord(S.ev[4], s));
   // embedding gather for the text rows
   KL("embed", 0, 4.0 * (P.T_d - P.T_a) * H,
      embed_gather(D.ids, P.T_d, W.embed, c.vocab_size, H, c.audio_token_id, ctx->hid.p,
                   ctx->badflag.as<int>(), s));
-  CK(cudaEventRecord(ctx->ev[5], s));
+  CK(cudaEventRecord(S.ev[5], s));
   // (c)(d)(e) decoder prefill
   TRY(run_decoder(ctx, P, D));
-  CK(cudaEventRecord(ctx->ev[6], s));
+  CK(cudaEventRecord(S.ev[6], s));
   // (f) head
   TRY(run_head(ctx, ctx->hid.p, ctx->bf16 ? 1 : 0, D.ts_rows, S.R, S.want_logits, S.want_normed));
-  CK(cudaEventRecord(ctx->ev[7], s));
+  CK(cudaEventRecord(S.ev[7], s));
+  // results and the two status words to this batch's pinned buffer, queued
+  // before any later batch can overwrite them
+  const size_t raw_bytes = static_cast<size_t>(S.R) * 8;
+  const size_t lg_bytes = S.want_logits ? static_cast<size_t>(S.R) * c.num_labels * 4 : 0;
+  const size_t nm_bytes = S.want_normed ? static_cast<size_t>(S.R) * H * 4 : 0;
+  TRY(ensure_pin(ctx, S.pin_res, 16 + raw_bytes + lg_bytes + nm_bytes));
+  uint8_t* pr = static_cast<uint8_t*>(S.pin_res.p);
+  CK(cudaEventRecord(S.ev[8], s));
+  CK(cudaMemcpyAsync(pr, ctx->status.p, 4, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(pr + 4, ctx->badflag.p, 4, cudaMemcpyDeviceToHost, s));
+  if (raw_bytes) CK(cudaMemcpyAsync(pr + 16, ctx->head_raw.p, raw_bytes, cudaMemcpyDeviceToHost, s));
+  if (lg_bytes)
+    CK(cudaMemcpyAsync(pr + 16 + raw_bytes, ctx->head_logits.p, lg_bytes, cudaMemcpyDeviceToHost, s));
+  if (nm_bytes)
+    CK(cudaMemcpyAsync(pr + 16 + raw_bytes + lg_bytes, ctx->head_normed.p, nm_bytes,
+                       cudaMemcpyDeviceToHost, s));
+  CK(cudaEventRecord(S.ev[9], s));
+  S.launches = ctx->launches;
+  S.state = Staged::kRunning;
   ctx->timings.gpu_launches = ctx->launches;
   return QA_OK;
 }
 
 int qa_batch_fetch(qa_ctx* ctx, qa_result* results) {
   if (!ctx || !results) return QA_ERR_ARG;
-  if (!ctx->staged || !ctx->staged->valid) return fail(ctx, QA_ERR_STATE, "no staged batch");
+  Staged* slot = oldest(ctx, Staged::kRunning);
+  if (!slot) {
+    if (oldest(ctx, Staged::kStaged)) return fail(ctx, QA_ERR_STATE, "the staged batch has not been run");
+    return fail(ctx, QA_ERR_STATE, "no staged batch");
+  }
   CK(cudaSetDevice(ctx->device));
-  Staged& S = *ctx->staged;
+  Staged& S = *slot;
   const Plan& P = S.P;
   const qa_cfg& c = ctx->cfg;
   const int H = c.hidden_size;
-  cudaStream_t s = ctx->stream;
   for (int i = 0; i < P.n; ++i)
     if (results[i].n_ts != S.n_ts[i] || (S.n_ts[i] > 0 && !results[i].raw_ms))
       return fail(ctx, QA_ERR_SHAPE, "clip %d: result holds %d timestamps, the batch has %d", i,
                   results[i].n_ts, S.n_ts[i]);
-  CK(cudaEventRecord(ctx->ev[8], s));
+  // the batch is consumed by this call whatever happens next
+  S.state = Staged::kFree;
+  TRY(wait_event(ctx, S.ev[9]));
+  if (!ctx->prof_recs.empty() && !oldest(ctx, Staged::kRunning)) prof_resolve(ctx);
+  const uint8_t* pr = static_cast<const uint8_t*>(S.pin_res.p);
+  unsigned st = 0;
+  int bad = 0;
+  std::memcpy(&st, pr, 4);
+  std::memcpy(&bad, pr + 4, 4);
+  if (st & kStatusTimeout)
+    return fail(ctx, QA_ERR_TIMEOUT, "a tensor-core pipeline wait ran out (status %u)", st);
+  if (bad) return fail(ctx, QA_ERR_SHAPE, "a token id is outside the vocabulary");
   const size_t raw_bytes = static_cast<size_t>(S.R) * 8;
   const size_t lg_bytes = S.want_logits ? static_cast<size_t>(S.R) * c.num_labels * 4 : 0;
   const size_t nm_bytes = S.want_normed ? static_cast<size_t>(S.R) * H * 4 : 0;
-  TRY(ensure_pin(ctx, ctx->pin_res, raw_bytes + lg_bytes + nm_bytes + 16));
-  uint8_t* pr = static_cast<uint8_t*>(ctx->pin_res.p);
-  CK(cudaMemcpyAsync(pr, ctx->head_raw.p, raw_bytes, cudaMemcpyDeviceToHost, s));
-  if (lg_bytes) CK(cudaMemcpyAsync(pr + raw_bytes, ctx->head_logits.p, lg_bytes, cudaMemcpyDeviceToHost, s));
-  if (nm_bytes) CK(cudaMemcpyAsync(pr + raw_bytes + lg_bytes, ctx->head_normed.p, nm_bytes, cudaMemcpyDeviceToHost, s));
-  CK(cudaEventRecord(ctx->ev[9], s));
-  TRY(wait_stream(ctx));
-  TRY(check_status(ctx));
-  const int64_t* raw = reinterpret_cast<const int64_t*>(pr);
-  const float* lg = reinterpret_cast<const float*>(pr + raw_bytes);
-  const float* nm = reinterpret_cast<const float*>(pr + raw_bytes + lg_bytes);
+  const int64_t* raw = reinterpret_cast<const int64_t*>(pr + 16);
+  const float* lg = reinterpret_cast<const float*>(pr + 16 + raw_bytes);
+  const float* nm = reinterpret_cast<const float*>(pr + 16 + raw_bytes + lg_bytes);
   for (int i = 0; i < P.n; ++i) {
     const int o = P.ts_off[i], k = P.ts_off[i + 1] - o;
     if (k) std::memcpy(results[i].raw_ms, raw + o, static_cast<size_t>(k) * 8);
@@ -1424,16 +1512,17 @@ int qa_batch_fetch(qa_ctx* ctx, qa_result* results) {
       std::memcpy(results[i].normed, nm + static_cast<size_t>(o) * H, static_cast<size_t>(k) * H * 4);
   }
   qa_timings& t = ctx->timings;
-  t.h2d_ms = elapsed(ctx, 0, 1);
-  t.mel_ms = elapsed(ctx, 2, 3);
-  t.enc_ms = elapsed(ctx, 3, 4);
-  t.gather_ms = elapsed(ctx, 4, 5);
-  t.prefill_ms = elapsed(ctx, 5, 6);
-  t.head_ms = elapsed(ctx, 6, 7);
-  t.d2h_ms = elapsed(ctx, 8, 9);
-  t.total_ms = t.h2d_ms + elapsed(ctx, 2, 7) + t.d2h_ms;
+  t.h2d_ms = elapsed(S, 0, 1);
+  t.mel_ms = elapsed(S, 2, 3);
+  t.enc_ms = elapsed(S, 3, 4);
+  t.gather_ms = elapsed(S, 4, 5);
+  t.prefill_ms = elapsed(S, 5, 6);
+  t.head_ms = elapsed(S, 6, 7);
+  t.d2h_ms = elapsed(S, 8, 9);
+  t.total_ms = t.h2d_ms + elapsed(S, 2, 7) + t.d2h_ms;
   t.h2d_bytes = S.h2d_bytes;
-  t.d2h_bytes = static_cast<long long>(raw_bytes + lg_bytes + nm_bytes);
+  t.d2h_bytes = static_cast<long long>(8 + raw_bytes + lg_bytes + nm_bytes);
+  t.gpu_launches = S.launches;
   return QA_OK;
 }
 

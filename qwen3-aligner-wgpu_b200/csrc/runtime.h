@@ -124,14 +124,27 @@ struct PlanDev {
 
 
 // A batch staged by qa_batch_stage, kept until the next stage call.
+// One batch between qa_batch_stage and qa_batch_fetch.  A context holds two,
+// so that the next batch can be staged while the previous one runs: each has
+// its own pinned staging and result buffers and its own events; the device
+// workspaces are shared (every write to them is ordered on the stream after
+// the previous batch's kernels).
 struct Staged {
+  enum State { kFree = 0, kStaged = 1, kRunning = 2 };
   Plan P;
   PlanDev D;
   std::vector<int> n_ts;
   int R = 0;
   bool want_logits = false, want_normed = false;
   long long h2d_bytes = 0;
-  bool valid = false;
+  int state = kFree;
+  unsigned long long seq = 0;       // staging order
+  int launches = 0;
+  PinBuf pin_samples, pin_plan, pin_res;
+  DevBuf samples, plan;  // this batch's device inputs (uploaded on the copy stream)
+  // 0/1 around the uploads (copy stream), 2..7 phases of the run, 8/9 around
+  // the result copy
+  cudaEvent_t ev[10] = {};
 };
 
 // One profiled launch: CUDA events around it on the launching stream.
@@ -165,7 +178,9 @@ struct qa_ctx {
   int kv_cap_tokens = 0;
   cudaEvent_t ev[12] = {};
   cudaStream_t own_stream = nullptr;  // the context's stream (stream may be the caller's)
-  std::unique_ptr<qa::Staged> staged;
+  cudaStream_t copy_stream = nullptr;  // batch uploads, overlapping the previous batch's pass
+  std::unique_ptr<qa::Staged> slots[2];  // batches between stage and fetch
+  unsigned long long batch_seq = 0;
   // live profile (qa_set_profile)
   bool profile = false;
   std::vector<cudaEvent_t> prof_pool;

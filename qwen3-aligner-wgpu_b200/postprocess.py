@@ -11,7 +11,7 @@ from __future__ import annotations
 from dataclasses import dataclass
 
 
-@dataclass
+@dataclass(slots=True)
 class AlignItem:
     text: str
     start_time: float
@@ -71,8 +71,9 @@ def pair_words(words, fixed_ms) -> list:
     if len(fixed_ms) != 2 * len(words):
         raise ValueError(f"expected {2 * len(words)} timestamps for {len(words)} words, "
                          f"got {len(fixed_ms)}")
-    return [AlignItem(w, fixed_ms[2 * i] / 1000.0, fixed_ms[2 * i + 1] / 1000.0)
-            for i, w in enumerate(words)]
+    import numpy as np
+    sec = (np.asarray(fixed_ms, dtype=np.int64) / 1000.0).tolist()  # IEEE division, as in Python
+    return [AlignItem(w, sec[2 * i], sec[2 * i + 1]) for i, w in enumerate(words)]
 
 
 def decode_timestamps(words, raw_ms) -> list:

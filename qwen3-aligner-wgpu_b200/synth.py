@@ -277,9 +277,14 @@ class SyntheticTokenizer:
     def token_to_id(self, s: str):
         return self.MARKERS.get(s)
 
+    _IDS: dict = {}  # piece -> id (the mapping is a pure function of the piece)
+
     def _piece_id(self, piece: str) -> int:
-        h = hashlib.blake2b(piece.encode(), digest_size=8).digest()
-        return int.from_bytes(h, "little") % self.ORDINARY
+        i = self._IDS.get(piece)
+        if i is None:
+            h = hashlib.blake2b(piece.encode(), digest_size=8).digest()
+            i = self._IDS[piece] = int.from_bytes(h, "little") % self.ORDINARY
+        return i
 
     _SPLIT = None
 
@@ -295,6 +300,10 @@ class SyntheticTokenizer:
             m = self.MARKERS.get(part)
             if m is not None:
                 ids.append(m)
+                continue
+            if part.isascii():  # no CJK: one run, cut in threes
+                pid = self._piece_id
+                ids += [pid(part[j:j + 3]) for j in range(0, len(part), 3)]
                 continue
             buf = ""
             for ch in part:
@@ -336,15 +345,40 @@ def is_kept_char(c: str) -> bool:
     return c == "'" or unicodedata.category(c)[0] in "LN" or is_cjk_char(c)
 
 
+_ASCII_DROP = None
+
+
 def split_words(text: str, language=None) -> list:
     """src/words.rs:107-118 + split_default (:190-232) for every language but
     Japanese (which needs the reference's nagisa tagger and is out of scope)."""
+    import re
     import unicodedata
+    global _ASCII_DROP
     text = text.strip()
     lang = (language or "").lower()
     if lang in ("japanese", "ja"):
         raise ValueError("Japanese word splitting requires the nagisa tagger (not available)")
-    tokens, buf, buf_hangul = [], "", None
+    # Whitespace ends a word and resets the Hangul/other state, so the text is
+    # split on it first.  An ASCII piece has no CJK or Hangul: its letters,
+    # digits and apostrophes are kept and every other character is dropped;
+    # other pieces go through the character-by-character rules.
+    if _ASCII_DROP is None:
+        _ASCII_DROP = re.compile(r"[^A-Za-z0-9']+")
+    tokens = []
+    for piece in text.split():
+        if piece.isascii():
+            w = _ASCII_DROP.sub("", piece)
+            if w:
+                tokens.append(w)
+        else:
+            _split_piece(piece, tokens)
+    return tokens
+
+
+def _split_piece(text: str, tokens: list) -> None:
+    """split_default's character rules over a run without whitespace."""
+    import unicodedata
+    buf, buf_hangul = "", None
     for c in text:
         if is_cjk_char(c):
             if buf:
@@ -366,7 +400,6 @@ def split_words(text: str, language=None) -> list:
             buf += c
     if buf:
         tokens.append(buf)
-    return tokens
 
 
 def conv3_length(n: int) -> int:
@@ -429,13 +462,17 @@ class InputBuilder:
                 text += TIMESTAMP + TIMESTAMP
             text += w
         text += TIMESTAMP + TIMESTAMP
-        ids = ([self.tok.token_to_id(AUDIO_START)] + [self.tok.token_to_id(AUDIO_PAD)] * n_audio
-               + [self.tok.token_to_id(AUDIO_END)] + self.tok.encode(text))
-        if sum(1 for t in ids if t == AUDIO_PAD_ID) != n_audio:
+        head = ([self.tok.token_to_id(AUDIO_START)] + [self.tok.token_to_id(AUDIO_PAD)] * n_audio
+                + [self.tok.token_to_id(AUDIO_END)])
+        enc = self.tok.encode(text)
+        ids = head + enc
+        if head.count(AUDIO_PAD_ID) + enc.count(AUDIO_PAD_ID) != n_audio:
             raise ValueError("audio token count mismatch")
         if ids[0] != AUDIO_START_ID or ids[n_audio + 1] != AUDIO_END_ID:
             raise ValueError("sequence must be <|audio_start|> pads <|audio_end|> ...")
-        ts = [i for i, t in enumerate(ids) if t == TIMESTAMP_ID]
+        off = len(head)
+        ts = [off + i for i, t in enumerate(enc) if t == TIMESTAMP_ID]
+        ts = [i for i, t in enumerate(head) if t == TIMESTAMP_ID] + ts
         if len(ts) != 2 * len(words):
             raise ValueError(f"expected {2 * len(words)} timestamp tokens, got {len(ts)}")
         return AlignerInput(ids, list(words), n_audio, valid_mel,

@@ -124,6 +124,54 @@ def test_batch_matches_single_clips(env):
         assert np.array_equal(ex_b["logits"], ex_1["logits"])
 
 
+def test_align_stream_matches_align_batch(env):
+    """The pipelined stream API gives each batch exactly what align_batch gives
+    it, in order, with batches of different sizes and lengths."""
+    E = env
+    al = E.gpu_aligner()
+    clips = E.qa.synth.workload(2, n_clips=7)
+    batches = [[(c.samples, c.text, c.language) for c in clips[a:b]]
+               for a, b in [(0, 3), (3, 4), (4, 7)]]
+    streamed = list(al.align_stream(iter(batches)))
+    assert len(streamed) == len(batches)
+    for batch, got in zip(batches, streamed):
+        want = al.align_batch(batch)
+        assert len(got) == len(want)
+        for (raw_s, items_s), (raw_b, items_b) in zip(got, want):
+            assert np.array_equal(raw_s, raw_b)
+            assert items_s == items_b
+    assert list(al.align_stream([])) == []
+
+
+def test_two_batches_in_flight(env):
+    """Two batches staged and run back to back come back in order, each equal
+    to its own single call; a third stage before a fetch is refused; run with
+    nothing staged re-runs the last batch."""
+    E = env
+    al = E.gpu_aligner()
+    a = [_inputs(E, sec, w, seed) for sec, w, seed in [(2.5, 7, 41), (6.0, 15, 42)]]
+    b = [_inputs(E, sec, w, seed) for sec, w, seed in [(4.2, 11, 43)]]
+    want_a = al.align_inputs([x[0] for x in a], [x[1] for x in a])
+    want_b = al.align_inputs([x[0] for x in b], [x[1] for x in b])
+    sa = al.stage([x[0] for x in a], [x[1] for x in a])
+    al.run()
+    sb = al.stage([x[0] for x in b], [x[1] for x in b])
+    with pytest.raises(E.qa.QaError):
+        al.stage([x[0] for x in b], [x[1] for x in b])
+    al.run()
+    got_a = al.fetch(sa)
+    got_b = al.fetch(sb)
+    for (g, _), (w, _) in zip(got_a + got_b, want_a + want_b):
+        assert np.array_equal(g, w)
+    with pytest.raises(E.qa.QaError):
+        al.fetch(sb)
+    sb = al.stage([x[0] for x in b], [x[1] for x in b])
+    al.run()
+    al.run()
+    [(g, _)] = al.fetch(sb)
+    assert np.array_equal(g, want_b[0][0])
+
+
 def test_batch_parity_mixed_language(env):
     """A few config-2 style clips (English + CJK) against the oracle."""
     E = env
