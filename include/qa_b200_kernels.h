@@ -43,6 +43,21 @@ int qa_k_gemm(const void* A, long long lda, const void* B, long long ldb, int M,
               unsigned* status, int force_bn, void* stream);
 
 /*
+ * The decoder's fused QKV projection: qkv = A · Bᵀ (B = [q|k|v] rows), with
+ * the epilogue of cpu_decoder.rs:305-321 per 128-column head: q and k heads
+ * are rounded, RMS-normalised (gains qn / kn), rotated by RoPE at the row's
+ * position (cos_t / sin_t [max_seq][64] in the storage format); q is written
+ * to q_out (row stride ldo), k and v are appended to the paged caches kc / vc
+ * [page][nkv][64][128] at (block_tab[clip_of[row]][pos / 64], pos % 64) with
+ * pos = pos_of[row].  N = (nq + 2 nkv) * 128.
+ */
+int qa_k_gemm_qkv_rope(const void* A, long long lda, const void* B, long long ldb, int M, int N,
+                       int K, int bf16, void* q_out, long long ldo, const int* pos_of,
+                       const int* clip_of, const int* block_tab, int max_pages, void* kc, void* vc,
+                       const void* cos_t, const void* sin_t, const float* qn, const float* kn,
+                       float eps, int nq, int nkv, unsigned* status, int force_bn, void* stream);
+
+/*
  * Implicit-GEMM conv2d, 3x3 / stride 2 / pad 1, on the tcgen05 tensor cores:
  * x NHWC [n][h][w][c] 16-bit, wt [c_out][9c] (k = (kh*3 + kw)*c + ic),
  * output [n*ho*wo][c_out] through the same epilogues as qa_k_gemm (rows in

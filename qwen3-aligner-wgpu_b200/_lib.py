@@ -59,6 +59,7 @@ EXPORTED = [
     "qa_set_stream", "qa_set_profile", "qa_get_profile", "qa_fix_timestamps",
     "qa_head_noalloc",
     "qa_k_gemm", "qa_k_conv3x3s2", "qa_k_causal_attention", "qa_k_conv1",
+    "qa_k_gemm_qkv_rope",
 ]
 
 c_void_p = ctypes.c_void_p
@@ -176,6 +177,10 @@ def _declare(L: ctypes.CDLL) -> None:
     L.qa_k_gemm.restype = c_int
     L.qa_k_conv3x3s2.argtypes = [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_int,
                                  c_int, c_int, c_int, c_void_p, c_ll, c_void_p, c_void_p, c_void_p]
+    L.qa_k_gemm_qkv_rope.argtypes = [c_void_p, c_ll, c_void_p, c_ll, c_int, c_int, c_int, c_int,
+                                     c_void_p, c_ll, c_void_p, c_void_p, c_void_p, c_int,
+                                     c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                     ctypes.c_float, c_int, c_int, c_void_p, c_int, c_void_p]
     L.qa_k_conv1.argtypes = [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p,
                              c_int, c_void_p]
     L.qa_k_causal_attention.argtypes = [c_void_p, c_ll, c_ll, c_int, c_int, c_void_p, c_int,
@@ -309,3 +314,18 @@ def conv1(mel, wt, bias, out, stream=None):
     bf16 = 1 if out.dtype == torch.bfloat16 else 0
     s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
     check(lib().qa_k_conv1(ptr(mel), n, h, w, ptr(wt), ptr(bias), wt.shape[0], ptr(out), bf16, s))
+
+
+def gemm_qkv_rope(A, B, q_out, pos_of, clip_of, block_tab, kc, vc, cos_t, sin_t, qn, kn, eps,
+                  nq, nkv, status=None, force_bn=0, stream=None):
+    """The fused decoder QKV GEMM on torch CUDA tensors (see qa_k_gemm_qkv_rope)."""
+    import torch
+    M, K = A.shape
+    N = B.shape[0]
+    bf16 = 1 if A.dtype == torch.bfloat16 else 0
+    s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
+    check(lib().qa_k_gemm_qkv_rope(ptr(A), A.stride(0), ptr(B), B.stride(0), M, N, K, bf16,
+                                   ptr(q_out), q_out.stride(0), ptr(pos_of), ptr(clip_of),
+                                   ptr(block_tab), block_tab.shape[1], ptr(kc), ptr(vc),
+                                   ptr(cos_t), ptr(sin_t), ptr(qn), ptr(kn), eps, nq, nkv,
+                                   ptr(status), force_bn, s))

@@ -100,75 +100,151 @@ __device__ __forceinline__ float word_half(uint32_t w, int hi) {
   return h2f<T>(*reinterpret_cast<const T*>(&b));
 }
 
+// Packed f32 pairs (sm_100 f32x2 arithmetic: one instruction, two
+// separately rounded lanes, so the results equal two scalar __fmul_rn /
+// __fadd_rn).
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;"
+      : "=l"(r)
+      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)));
+  return *reinterpret_cast<const float2*>(&r);
+}
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;"
+      : "=l"(r)
+      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)));
+  return *reinterpret_cast<const float2*>(&r);
+}
+
+// The two 16-bit values of a packed word, widened.
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t w) {
+  return make_float2(word_half<T>(w, 0), word_half<T>(w, 1));
+}
+template <typename T>
+__device__ __forceinline__ uint32_t pack2_rn(float2 v) {
+  return pack_bits(bits_of(f2h<T>(v.x)), bits_of(f2h<T>(v.y)));
+}
+
+// Per-row inputs of EPI_QKV_ROPE, loaded before the tile's accumulator is
+// ready (their latency then overlaps the tile's MMAs): the row's position,
+// its offset in the paged K/V cache (without the K/V head's term), and L1
+// prefetches of the row's cos / sin table lines.
+struct QkvRow {
+  int pos = 0;
+  long long kv_off = 0;
+};
+
+template <typename T>
+__device__ __forceinline__ QkvRow qkv_row_meta(const EpiParams& ep, int row, int M) {
+  QkvRow r;
+  if (row >= M) return r;
+  const RopeKV& rk = ep.rk;
+  r.pos = rk.pos_of[row];
+  const int clip = rk.clip_of[row];
+  const int page = rk.block_tab[clip * rk.max_pages + r.pos / rk.page_size];
+  r.kv_off = (static_cast<long long>(page) * rk.nkv * rk.page_size + r.pos % rk.page_size) * 128;
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(static_cast<const T*>(rk.cos_t) + r.pos * 64));
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(static_cast<const T*>(rk.sin_t) + r.pos * 64));
+  return r;
+}
+
 // EPI_QKV_ROPE for one 128-column head of this thread's row.  The head's
-// values are rounded to the storage type (the GEMM output's rounding point)
-// and kept packed, two per register.
+// values are rounded to the storage type (the GEMM output's rounding point).
+// A v head is appended to the cache as rounded.  A q or k head takes RMSNorm
+// (the sum of squares of the rounded values in four partial sums), the
+// per-element gain and the rotate-half RoPE at the row's position, with every
+// product and sum rounded as in the reference's loop (norm_rope_head,
+// src/cpu_decoder.rs:305-321), two lanes per f32x2 instruction.  The head is
+// read from TMEM twice (sums, then the 32-column chunks d and d + 64 together)
+// instead of being held in registers.
 template <typename T>
 __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem_col0, int row,
-                                              int M, int head) {
+                                              int M, int head, const QkvRow& meta) {
   constexpr int HD = 128;
-  uint32_t hv[HD / 2];
-#pragma unroll
-  for (int c = 0; c < HD / 32; ++c) {
-    float v[32];
-    tmem_ld32(tmem_col0 + c * 32, v);  // warp-collective: every lane loads
-#pragma unroll
-    for (int i = 0; i < 16; ++i)
-      hv[c * 16 + i] = pack_bits(bits_of(f2h<T>(v[2 * i])), bits_of(f2h<T>(v[2 * i + 1])));
-  }
-  if (row >= M) return;
   const RopeKV& rk = ep.rk;
-  const int pos = rk.pos_of[row];
+  const bool ok = row < M;
+  const bool is_q = head < rk.nq, is_v = head >= rk.nq + rk.nkv;
   T* dst;
-  if (head < rk.nq) {
+  if (is_q) {
     dst = static_cast<T*>(ep.out) + (long long)row * ep.ldo + head * HD;
   } else {
-    const int clip = rk.clip_of[row];
-    const int page = rk.block_tab[clip * rk.max_pages + pos / rk.page_size];
-    const int kvh = head < rk.nq + rk.nkv ? head - rk.nq : head - rk.nq - rk.nkv;
-    const long long off =
-        ((static_cast<long long>(page) * rk.nkv + kvh) * rk.page_size + pos % rk.page_size) * HD;
-    dst = static_cast<T*>(head < rk.nq + rk.nkv ? rk.kc : rk.vc) + off;
+    const int kvh = is_v ? head - rk.nq - rk.nkv : head - rk.nq;
+    dst = static_cast<T*>(is_v ? rk.vc : rk.kc) + meta.kv_off +
+          static_cast<long long>(kvh) * rk.page_size * HD;
   }
-  if (head >= rk.nq + rk.nkv) {  // v: appended as rounded
+  if (is_v) {
+#pragma unroll 1
+    for (int c = 0; c < HD / 32; ++c) {
+      float v[32];
+      tmem_ld32(tmem_col0 + c * 32, v);  // warp-collective: every lane loads
+      if (!ok) continue;
+      uint32_t w[16];
 #pragma unroll
-    for (int j = 0; j < HD / 8; ++j)
-      reinterpret_cast<uint4*>(dst)[j] =
-          make_uint4(hv[4 * j], hv[4 * j + 1], hv[4 * j + 2], hv[4 * j + 3]);
+      for (int i = 0; i < 16; ++i) w[i] = pack2_rn<T>(make_float2(v[2 * i], v[2 * i + 1]));
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        reinterpret_cast<uint4*>(dst + c * 32)[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+    }
     return;
   }
-  // RMSNorm over the head's raw values (sequential sum, no FMA, as the
-  // reference's loop), per-element gain, then rotate-half RoPE at `pos`:
-  // out[d] = x_d c_d - x_{d+64} s_d and out[d+64] = x_{d+64} c_d + x_d s_d.
-  const float* nw = head < rk.nq ? rk.qn : rk.kn;
-  float s2 = 0.0f;
+  // pass 1: sum of squares of the rounded values
+  float2 s2a = make_float2(0.0f, 0.0f), s2b = make_float2(0.0f, 0.0f);
+#pragma unroll 1
+  for (int c = 0; c < HD / 32; ++c) {
+    float v[32];
+    tmem_ld32(tmem_col0 + c * 32, v);
 #pragma unroll
-  for (int j = 0; j < HD; ++j) {
-    const float x = word_half<T>(hv[j / 2], j & 1);
-    s2 = __fadd_rn(s2, __fmul_rn(x, x));
-  }
-  const float inv = 1.0f / sqrtf(s2 / static_cast<float>(HD) + rk.eps);
-  const T* ct = static_cast<const T*>(rk.cos_t) + pos * (HD / 2);
-  const T* st = static_cast<const T*>(rk.sin_t) + pos * (HD / 2);
-#pragma unroll
-  for (int j0 = 0; j0 < HD / 2; j0 += 8) {
-    const uint4 cu = *reinterpret_cast<const uint4*>(ct + j0);
-    const uint4 su = *reinterpret_cast<const uint4*>(st + j0);
-    const T* cv = reinterpret_cast<const T*>(&cu);
-    const T* sv = reinterpret_cast<const T*>(&su);
-    alignas(16) T lo[8], hi[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int d = j0 + j;
-      const float xa = __fmul_rn(__fmul_rn(word_half<T>(hv[d / 2], d & 1), inv), nw[d]);
-      const float xb =
-          __fmul_rn(__fmul_rn(word_half<T>(hv[(d + 64) / 2], d & 1), inv), nw[d + 64]);
-      const float c = h2f<T>(cv[j]), sn = h2f<T>(sv[j]);
-      lo[j] = f2h<T>(__fadd_rn(__fmul_rn(xa, c), __fmul_rn(-xb, sn)));
-      hi[j] = f2h<T>(__fadd_rn(__fmul_rn(xb, c), __fmul_rn(xa, sn)));
+    for (int i = 0; i < 32; i += 4) {
+      const float2 x0 = make_float2(round16<T>(v[i]), round16<T>(v[i + 1]));
+      const float2 x1 = make_float2(round16<T>(v[i + 2]), round16<T>(v[i + 3]));
+      s2a = add2_rn(s2a, mul2_rn(x0, x0));
+      s2b = add2_rn(s2b, mul2_rn(x1, x1));
     }
-    *reinterpret_cast<uint4*>(dst + j0) = *reinterpret_cast<const uint4*>(lo);
-    *reinterpret_cast<uint4*>(dst + j0 + 64) = *reinterpret_cast<const uint4*>(hi);
+  }
+  const float s2 = __fadd_rn(__fadd_rn(s2a.x, s2a.y), __fadd_rn(s2b.x, s2b.y));
+  const float inv = 1.0f / sqrtf(s2 / static_cast<float>(HD) + rk.eps);
+  const float2 inv2 = make_float2(inv, inv);
+  const float* nw = is_q ? rk.qn : rk.kn;
+  const T* ct = static_cast<const T*>(rk.cos_t) + meta.pos * (HD / 2);
+  const T* st = static_cast<const T*>(rk.sin_t) + meta.pos * (HD / 2);
+  // pass 2: elements d in [32c, 32c + 32) with their partners d + 64
+#pragma unroll 1
+  for (int c = 0; c < 2; ++c) {
+    float va[32], vb[32];
+    tmem_ld32(tmem_col0 + c * 32, va);
+    tmem_ld32(tmem_col0 + 64 + c * 32, vb);
+    if (!ok) continue;
+#pragma unroll
+    for (int j0 = 0; j0 < 32; j0 += 8) {
+      const int d0 = c * 32 + j0;
+      const uint4 cu = *reinterpret_cast<const uint4*>(ct + d0);
+      const uint4 su = *reinterpret_cast<const uint4*>(st + d0);
+      const uint32_t cw[4] = {cu.x, cu.y, cu.z, cu.w}, sw[4] = {su.x, su.y, su.z, su.w};
+      const float4 na0 = *reinterpret_cast<const float4*>(nw + d0);
+      const float4 na1 = *reinterpret_cast<const float4*>(nw + d0 + 4);
+      const float4 nb0 = *reinterpret_cast<const float4*>(nw + d0 + 64);
+      const float4 nb1 = *reinterpret_cast<const float4*>(nw + d0 + 68);
+      const float2 ga[4] = {make_float2(na0.x, na0.y), make_float2(na0.z, na0.w),
+                            make_float2(na1.x, na1.y), make_float2(na1.z, na1.w)};
+      const float2 gb[4] = {make_float2(nb0.x, nb0.y), make_float2(nb0.z, nb0.w),
+                            make_float2(nb1.x, nb1.y), make_float2(nb1.z, nb1.w)};
+      uint32_t lo[4], hi[4];
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const int i = j0 + 2 * p;
+        const float2 xa = mul2_rn(mul2_rn(make_float2(round16<T>(va[i]), round16<T>(va[i + 1])), inv2), ga[p]);
+        const float2 xb = mul2_rn(mul2_rn(make_float2(round16<T>(vb[i]), round16<T>(vb[i + 1])), inv2), gb[p]);
+        const float2 cc = unpack2<T>(cw[p]), sn = unpack2<T>(sw[p]);
+        const float2 nxb = make_float2(-xb.x, -xb.y);
+        lo[p] = pack2_rn<T>(add2_rn(mul2_rn(xa, cc), mul2_rn(nxb, sn)));
+        hi[p] = pack2_rn<T>(add2_rn(mul2_rn(xb, cc), mul2_rn(xa, sn)));
+      }
+      *reinterpret_cast<uint4*>(dst + d0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      *reinterpret_cast<uint4*>(dst + d0 + 64) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    }
   }
 }
 
@@ -177,12 +253,13 @@ __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem
 // SwiGLU the range is over the output columns [0, BN/2).
 template <int BN, typename T>
 __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row, int row, int M,
-                                         int n0, int N, int cb, int ce) {
+                                         int n0, int N, int cb, int ce, const QkvRow& meta = {}) {
   if constexpr (BN % 128 == 0) {
     if (ep.mode == EPI_QKV_ROPE) {
 #pragma unroll 1
       for (int hb = cb / 128; hb < ce / 128; ++hb)
-        if (n0 + hb * 128 < N) qkv_rope_head<T>(ep, tmem_row + hb * 128, row, M, (n0 + hb * 128) / 128);
+        if (n0 + hb * 128 < N)
+          qkv_rope_head<T>(ep, tmem_row + hb * 128, row, M, (n0 + hb * 128) / 128, meta);
       return;
     }
   }
@@ -477,15 +554,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int lt = 0;
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++lt) {
       const int buf = lt & 1;
+      const int m0 = (t / n_tiles_n) * kBM, n0 = (t % n_tiles_n) * BN;
+      const int row = m0 + q * 32 + lane;
+      QkvRow meta;
+      if (ep.mode == EPI_QKV_ROPE) meta = qkv_row_meta<T>(ep, row, M);  // before the wait
       if (*abort_flag || !mbar_wait(&tfull[buf], (lt >> 1) & 1)) {
         if (lane == 0) timed_out();
         break;
       }
       tc_fence_after();
-      const int m0 = (t / n_tiles_n) * kBM, n0 = (t % n_tiles_n) * BN;
-      const int row = m0 + q * 32 + lane;
       const uint32_t trow = tbase + buf * kAccCols + (static_cast<uint32_t>(q * 32) << 16);
-      epilogue<BN, T>(ep, trow, row, M, n0, N, cb, ce);
+      epilogue<BN, T>(ep, trow, row, M, n0, N, cb, ce, meta);
       tc_fence_before();
       mbar_arrive(&tempty[buf]);
     }
@@ -644,15 +723,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int lt = 0;
     for (int t = pair; t < n_tiles; t += n_pairs, ++lt) {
       const int buf = lt & 1;
+      const int m0 = (t / n_tiles_n) * 2 * kBM, n0 = (t % n_tiles_n) * BN;
+      const int row = m0 + rank * kBM + q * 32 + lane;
+      QkvRow meta;
+      if (ep.mode == EPI_QKV_ROPE) meta = qkv_row_meta<T>(ep, row, M);  // before the wait
       if (*abort_flag || !mbar_wait(&tfull[buf], (lt >> 1) & 1)) {
         if (lane == 0) timed_out();
         break;
       }
       tc_fence_after();
-      const int m0 = (t / n_tiles_n) * 2 * kBM, n0 = (t % n_tiles_n) * BN;
-      const int row = m0 + rank * kBM + q * 32 + lane;
       const uint32_t trow = tbase + buf * kAccCols + (static_cast<uint32_t>(q * 32) << 16);
-      epilogue<BN, T>(ep, trow, row, M, n0, N, cb, ce);
+      epilogue<BN, T>(ep, trow, row, M, n0, N, cb, ce, meta);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(tempty_lead + buf * 8);

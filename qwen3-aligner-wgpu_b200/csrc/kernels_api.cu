@@ -27,6 +27,39 @@ extern "C" int qa_k_gemm(const void* A, long long lda, const void* B, long long 
   return rc == 0 ? QA_OK : QA_ERR_CUDA;
 }
 
+extern "C" int qa_k_gemm_qkv_rope(const void* A, long long lda, const void* B, long long ldb,
+                                  int M, int N, int K, int bf16, void* q_out, long long ldo,
+                                  const int* pos_of, const int* clip_of, const int* block_tab,
+                                  int max_pages, void* kc, void* vc, const void* cos_t,
+                                  const void* sin_t, const float* qn, const float* kn, float eps,
+                                  int nq, int nkv, unsigned* status, int force_bn, void* stream) {
+  if (!A || !B || !q_out || !pos_of || !clip_of || !block_tab || !kc || !vc || !cos_t || !sin_t ||
+      !qn || !kn || nq <= 0 || nkv <= 0 || N != (nq + 2 * nkv) * 128)
+    return QA_ERR_ARG;
+  EpiParams ep;
+  ep.mode = EPI_QKV_ROPE;
+  ep.out = q_out;
+  ep.ldo = ldo;
+  ep.status = status;
+  ep.rk.pos_of = pos_of;
+  ep.rk.clip_of = clip_of;
+  ep.rk.block_tab = block_tab;
+  ep.rk.max_pages = max_pages;
+  ep.rk.page_size = 64;
+  ep.rk.kc = kc;
+  ep.rk.vc = vc;
+  ep.rk.cos_t = cos_t;
+  ep.rk.sin_t = sin_t;
+  ep.rk.qn = qn;
+  ep.rk.kn = kn;
+  ep.rk.eps = eps;
+  ep.rk.nq = nq;
+  ep.rk.nkv = nkv;
+  int rc = gemm_tc(A, lda, B, ldb, M, N, K, bf16 != 0, ep, static_cast<cudaStream_t>(stream),
+                   force_bn);
+  return rc == 0 ? QA_OK : QA_ERR_CUDA;
+}
+
 extern "C" int qa_k_conv3x3s2(const void* x, int n, int h, int w, int c, const void* wt, int c_out,
                               int time_major, int bf16, int mode, int act, void* out, long long ldo,
                               const float* bias, unsigned* status, void* stream) {

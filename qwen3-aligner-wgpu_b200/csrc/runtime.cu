@@ -811,7 +811,7 @@ int run_encoder(qa_ctx* ctx, const Plan& P, const PlanDev& D, void* out16, const
     eo.out = ctx->xenc.p;
     eo.ldo = dm;
     eo.row_map = D.co_map + static_cast<size_t>(g0) * tpc;
-    KL("gemm", gemm_flops(g * tpc, dm, h3 * ds), gemm_bytes(g * tpc, dm, h3 * ds, 4),
+    KL("gemm:conv_out", gemm_flops(g * tpc, dm, h3 * ds), gemm_bytes(g * tpc, dm, h3 * ds, 4),
        gemm_tc(ctx->act3.p, (long long)h3 * ds, W.co_w, (long long)h3 * ds, g * tpc, dm, h3 * ds,
                bf, eo, s));
   }
@@ -829,7 +829,7 @@ int run_encoder(qa_ctx* ctx, const Plan& P, const PlanDev& D, void* out16, const
     ep.bias = L.qkv_b;
     ep.out = ctx->qkv_enc.p;
     ep.ldo = 3 * dm;
-    KL("gemm", gemm_flops(Ta, 3 * dm, dm), gemm_bytes(Ta, 3 * dm, dm, 2),
+    KL("gemm:enc_qkv", gemm_flops(Ta, 3 * dm, dm), gemm_bytes(Ta, 3 * dm, dm, 2),
        gemm_tc(ctx->h16a.p, dm, L.qkv_w, dm, Ta, 3 * dm, dm, bf, ep, s));
     KL("window_attn", win_flops, 2.0 * Ta * 4 * dm,
        window_attention(ctx->qkv_enc.p, dm, c.encoder_heads, 64, D.windows,
@@ -838,7 +838,7 @@ int run_encoder(qa_ctx* ctx, const Plan& P, const PlanDev& D, void* out16, const
     ep.bias = L.o_b;
     ep.out = ctx->xenc.p;
     ep.ldo = dm;
-    KL("gemm", gemm_flops(Ta, dm, dm), gemm_bytes(Ta, dm, dm, 8),
+    KL("gemm:enc_out", gemm_flops(Ta, dm, dm), gemm_bytes(Ta, dm, dm, 8),
        gemm_tc(ctx->attn_enc.p, dm, L.o_w, dm, Ta, dm, dm, bf, ep, s));
     KL("layernorm", 0, 6.0 * Ta * dm, layernorm_rows(ctx->xenc.as<float>(), Ta, dm, L.ln2_g, L.ln2_b, 1e-5f, ctx->h16a.p, bf, s));
     ep.mode = EPI_STORE16;
@@ -846,14 +846,14 @@ int run_encoder(qa_ctx* ctx, const Plan& P, const PlanDev& D, void* out16, const
     ep.bias = L.fc1_b;
     ep.out = ctx->ffn_enc.p;
     ep.ldo = c.encoder_ffn_dim;
-    KL("gemm", gemm_flops(Ta, c.encoder_ffn_dim, dm), gemm_bytes(Ta, c.encoder_ffn_dim, dm, 2),
+    KL("gemm:enc_fc1", gemm_flops(Ta, c.encoder_ffn_dim, dm), gemm_bytes(Ta, c.encoder_ffn_dim, dm, 2),
        gemm_tc(ctx->h16a.p, dm, L.fc1_w, dm, Ta, c.encoder_ffn_dim, dm, bf, ep, s));
     ep.mode = EPI_RESID32;
     ep.act = ACT_NONE;
     ep.bias = L.fc2_b;
     ep.out = ctx->xenc.p;
     ep.ldo = dm;
-    KL("gemm", gemm_flops(Ta, dm, c.encoder_ffn_dim), gemm_bytes(Ta, dm, c.encoder_ffn_dim, 8),
+    KL("gemm:enc_fc2", gemm_flops(Ta, dm, c.encoder_ffn_dim), gemm_bytes(Ta, dm, c.encoder_ffn_dim, 8),
        gemm_tc(ctx->ffn_enc.p, c.encoder_ffn_dim, L.fc2_w, c.encoder_ffn_dim, Ta, dm,
                c.encoder_ffn_dim, bf, ep, s));
   }
@@ -865,14 +865,14 @@ int run_encoder(qa_ctx* ctx, const Plan& P, const PlanDev& D, void* out16, const
   ep.bias = W.p1_b;
   ep.out = ctx->proj1.p;
   ep.ldo = dm;
-  KL("gemm", gemm_flops(Ta, dm, dm), gemm_bytes(Ta, dm, dm, 2),
+  KL("gemm:proj1", gemm_flops(Ta, dm, dm), gemm_bytes(Ta, dm, dm, 2),
      gemm_tc(ctx->h16a.p, dm, W.p1_w, dm, Ta, dm, dm, bf, ep, s));
   ep.act = ACT_NONE;
   ep.bias = W.p2_b;
   ep.out = out16;
   ep.ldo = c.output_dim;
   ep.row_map = p2_map;
-  KL("gemm", gemm_flops(Ta, c.output_dim, dm), gemm_bytes(Ta, c.output_dim, dm, 2),
+  KL("gemm:proj2", gemm_flops(Ta, c.output_dim, dm), gemm_bytes(Ta, c.output_dim, dm, 2),
      gemm_tc(ctx->proj1.p, dm, W.p2_w, dm, Ta, c.output_dim, dm, bf, ep, s));
   return QA_OK;
 }
@@ -936,7 +936,7 @@ int run_decoder(qa_ctx* ctx, const Plan& P, const PlanDev& D) {
     ep.rk.eps = eps;
     ep.rk.nq = nq;
     ep.rk.nkv = nkv;
-    KL("gemm", gemm_flops(T, ldq, H), gemm_bytes(T, ldq, H, 2),
+    KL("gemm:dec_qkv", gemm_flops(T, ldq, H), gemm_bytes(T, ldq, H, 2),
        gemm_tc(ctx->xn.p, H, L.qkv_w, H, T, ldq, H, bf, ep, s, 0));
     KL("causal_attn", attn_flops, T * (2.0 * qd * 2 + 2.0 * nkv * hd * 2),
        causal_attention_tc(ctx->qkv.p, ldq, T, nq, nkv, hd, D.tiles,
@@ -945,18 +945,18 @@ int run_decoder(qa_ctx* ctx, const Plan& P, const PlanDev& D) {
     ep.mode = EPI_RESID16;
     ep.out = ctx->hid.p;
     ep.ldo = H;
-    KL("gemm", gemm_flops(T, H, qd), gemm_bytes(T, H, qd, 4),
+    KL("gemm:dec_o", gemm_flops(T, H, qd), gemm_bytes(T, H, qd, 4),
        gemm_tc(ctx->attn.p, qd, L.o_w, qd, T, H, qd, bf, ep, s));
     KL("rmsnorm", 0, 4.0 * T * H, rmsnorm_rows(ctx->hid.p, T, H, L.pln, eps, ctx->xn.p, bf, s));
     ep.mode = EPI_SWIGLU16;
     ep.out = ctx->mlp.p;
     ep.ldo = I;
-    KL("gemm", gemm_flops(T, 2 * I, H), gemm_bytes(T, I, H, 2) + 2.0 * I * H,
+    KL("gemm:dec_gate_up", gemm_flops(T, 2 * I, H), gemm_bytes(T, I, H, 2) + 2.0 * I * H,
        gemm_tc(ctx->xn.p, H, L.gu_w, H, T, 2 * I, H, bf, ep, s, 0));
     ep.mode = EPI_RESID16;
     ep.out = ctx->hid.p;
     ep.ldo = H;
-    KL("gemm", gemm_flops(T, H, I), gemm_bytes(T, H, I, 4),
+    KL("gemm:dec_down", gemm_flops(T, H, I), gemm_bytes(T, H, I, 4),
        gemm_tc(ctx->mlp.p, I, L.down_w, I, T, H, I, bf, ep, s));
   }
   return QA_OK;
@@ -984,7 +984,7 @@ int run_head(qa_ctx* ctx, const void* hidden, int kind, const int* rows_dev, int
   ep.out = want_logits ? ctx->head_logits.p : nullptr;
   ep.ldo = c.num_labels;
   ep.keys = ctx->head_keys.as<unsigned long long>();
-  KL("gemm", gemm_flops(R, c.num_labels, 2 * H), gemm_bytes(R, c.num_labels, 2 * H, want_logits ? 4 : 0),
+  KL("gemm:head", gemm_flops(R, c.num_labels, 2 * H), gemm_bytes(R, c.num_labels, 2 * H, want_logits ? 4 : 0),
      gemm_tc(ctx->head_a.p, 2 * H, ctx->w.head_w2, 2 * H, R, c.num_labels, 2 * H, true, ep, s));
   KL("argmax", 0, 16.0 * R, argmax_finalize(ctx->head_keys.as<unsigned long long>(), R, c.timestamp_segment_time_ms,
                      ctx->head_raw.as<long long>(), s));

@@ -5,6 +5,7 @@
     python qwen3-aligner-wgpu_b200/kbench.py attention --clips 64 --impl 1
     python qwen3-aligner-wgpu_b200/kbench.py conv --n 256 --h 64 --w 50 --c 480
     python qwen3-aligner-wgpu_b200/kbench.py conv1 --n 256 --h 128 --w 100 --c 480
+    python qwen3-aligner-wgpu_b200/kbench.py qkv --clips 64
 
 Each run times `--iters` launches with CUDA events on the launching stream
 (after `--warmup` launches) and prints one JSON line with the mean launch time
@@ -28,7 +29,7 @@ sys.path.insert(0, os.path.dirname(HERE))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemm", "attention", "conv", "conv1"])
+    ap.add_argument("kernel", choices=["gemm", "attention", "conv", "conv1", "qkv"])
     ap.add_argument("--h", type=int, default=64)
     ap.add_argument("--w", type=int, default=50)
     ap.add_argument("--c", type=int, default=480)
@@ -59,6 +60,8 @@ def main():
         return conv(a, L, dt)
     if a.kernel == "conv1":
         return conv1(a, L, dt)
+    if a.kernel == "qkv":
+        return qkv(a, L, dt)
     g = torch.Generator(device="cuda").manual_seed(0)
     A = (torch.randn(a.m, a.k, device="cuda", generator=g) * 0.5).to(dt)
     B = (torch.randn(a.n, a.k, device="cuda", generator=g) * 0.05).to(dt)
@@ -192,6 +195,56 @@ def conv1(a, L, dt):
     print(json.dumps({"kernel": "conv1", "n": a.n, "h": a.h, "w": a.w, "c": a.c, "dtype": a.dtype,
                       "ms": ms, "gbs": nbytes / ms / 1e6,
                       "outputs_per_s": out.numel() / ms * 1e3}))
+
+
+def qkv(a, L, dt):
+    """The decoder's fused QKV GEMM (q/k RMSNorm + RoPE + paged K/V append) over
+    --clips clips of U(--min-len, --max-len) tokens, 16 q / 8 kv heads."""
+    import numpy as np
+    import torch
+    nq, nkv, hd, H, page = 16, 8, 128, 1024, 64
+    rng = np.random.default_rng(0)
+    lens = [int(x) for x in rng.integers(a.min_len, a.max_len + 1, a.clips)]
+    T = sum(lens)
+    pages_per = [(n + page - 1) // page for n in lens]
+    perm = rng.permutation(sum(pages_per))
+    bt = np.zeros((len(lens), max(pages_per)), dtype=np.int32)
+    pos = np.concatenate([np.arange(n) for n in lens]).astype(np.int32)
+    clip = np.concatenate([np.full(n, c) for c, n in enumerate(lens)]).astype(np.int32)
+    k = 0
+    for c in range(len(lens)):
+        bt[c, : pages_per[c]] = perm[k: k + pages_per[c]]
+        k += pages_per[c]
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev).manual_seed(0)
+    A = torch.randn(T, H, device=dev, generator=g).to(dt)
+    B = (torch.randn((nq + 2 * nkv) * hd, H, device=dev, generator=g) * 0.03).to(dt)
+    q = torch.empty(T, (nq + 2 * nkv) * hd, device=dev, dtype=dt)
+    kc = torch.zeros(sum(pages_per), nkv, page, hd, device=dev, dtype=dt)
+    vc = torch.zeros_like(kc)
+    ang = torch.arange(8192, device=dev)[:, None] * (1e6 ** (-torch.arange(64, device=dev) / 64))[None]
+    cos_t, sin_t = torch.cos(ang).to(dt), torch.sin(ang).to(dt)
+    qn = torch.rand(hd, device=dev, generator=g) + 0.5
+    kn = torch.rand(hd, device=dev, generator=g) + 0.5
+    t = lambda x: torch.from_numpy(x).to(dev)
+    pos_d, clip_d, bt_d = t(pos), t(clip), t(bt)
+    st = torch.zeros(1, dtype=torch.int32, device=dev)
+    run = lambda: L.gemm_qkv_rope(A, B, q, pos_d, clip_d, bt_d, kc, vc, cos_t, sin_t, qn, kn, 1e-6,
+                                  nq, nkv, status=st, force_bn=a.bn)
+    for _ in range(a.warmup):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.iters):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    ms = e0.elapsed_time(e1) / a.iters
+    flops = 2.0 * T * (nq + 2 * nkv) * hd * H
+    print(json.dumps({"kernel": "gemm_qkv_rope", "tokens": T, "bn": a.bn, "dtype": a.dtype,
+                      "ms": ms, "tflops": flops / ms / 1e9}))
 
 
 if __name__ == "__main__":

@@ -182,3 +182,64 @@ def test_implicit_conv(dtype, n, h, w, c, co, tm):
     ref = _conv_ref(x, w4, bias, tm)
     assert torch.isfinite(out.float()).all()
     assert _rel(out, ref) < TOL16[dtype]
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_qkv_rope_epilogue(dtype):
+    """The fused decoder QKV GEMM (norm_rope_head, src/cpu_decoder.rs:305-321)
+    against torch fp32 of the same rounding points: q rows in place, k and v
+    appended to shuffled pages of the paged cache, ragged clip lengths."""
+    L = _lib()
+    nq, nkv, hd, H, page = 16, 8, 128, 1024, 64
+    lens = [70, 1, 130, 64, 200]
+    g = torch.Generator(device="cuda").manual_seed(7)
+    T = sum(lens)
+    pages_per = [(n + page - 1) // page for n in lens]
+    perm = torch.randperm(sum(pages_per), generator=torch.Generator().manual_seed(3))
+    bt = torch.zeros(len(lens), max(pages_per), dtype=torch.int32)
+    k = 0
+    for c in range(len(lens)):
+        bt[c, : pages_per[c]] = perm[k: k + pages_per[c]]
+        k += pages_per[c]
+    pos = torch.cat([torch.arange(n) for n in lens]).int()
+    clip = torch.cat([torch.full((n,), c) for c, n in enumerate(lens)]).int()
+    A = (torch.randn(T, H, device="cuda", generator=g)).to(dtype)
+    B = (torch.randn((nq + 2 * nkv) * hd, H, device="cuda", generator=g) * 0.03).to(dtype)
+    q = torch.full((T, (nq + 2 * nkv) * hd), float("nan"), device="cuda", dtype=dtype)
+    kc = torch.zeros(sum(pages_per), nkv, page, hd, device="cuda", dtype=dtype)
+    vc = torch.zeros_like(kc)
+    ang = torch.arange(512, device="cuda")[:, None] * (1e6 ** (-torch.arange(64, device="cuda") / 64))[None]
+    cos_t, sin_t = torch.cos(ang).to(dtype), torch.sin(ang).to(dtype)
+    qn = (torch.rand(hd, device="cuda", generator=g) + 0.5).to(dtype).float()
+    kn = (torch.rand(hd, device="cuda", generator=g) + 0.5).to(dtype).float()
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    L.gemm_qkv_rope(A, B, q, pos.cuda(), clip.cuda(), bt.cuda(), kc, vc, cos_t, sin_t, qn, kn,
+                    1e-6, nq, nkv, status=st)
+    torch.cuda.synchronize()
+    assert st.item() == 0
+    x = (A.float() @ B.float().T).to(dtype).float()
+    c = cos_t.float()[pos.long().cuda()]
+    s = sin_t.float()[pos.long().cuda()]
+
+    def norm_rope(v, gain):
+        inv = 1.0 / torch.sqrt((v * v).mean(-1, keepdim=True) + 1e-6)
+        xn = (v * inv) * gain
+        a, b = xn[:, :64], xn[:, 64:]
+        return torch.cat([a * c - b * s, b * c + a * s], -1).to(dtype).float()
+
+    tol = 1e-2 if dtype == torch.float16 else 3e-2
+    for h in range(nq):
+        want = norm_rope(x[:, h * hd:(h + 1) * hd], qn)
+        got = q[:, h * hd:(h + 1) * hd].float()
+        assert torch.isfinite(got).all()
+        assert (got - want).abs().max().item() <= tol * want.abs().max().item()
+    pg = bt.cuda().long()[clip.long().cuda(), (pos // page).long().cuda()]
+    slot = (pos % page).long().cuda()
+    for h in range(nkv):
+        kw = norm_rope(x[:, (nq + h) * hd:(nq + h + 1) * hd], kn)
+        vw = x[:, (nq + nkv + h) * hd:(nq + nkv + h + 1) * hd]
+        kg = kc[pg, h, slot].float()
+        vg = vc[pg, h, slot].float()
+        assert (kg - kw).abs().max().item() <= tol * kw.abs().max().item()
+        # v is the rounded GEMM output; torch's fp32 matmul sums in another order
+        assert (vg - vw).abs().max().item() <= tol * vw.abs().max().item()
