@@ -30,7 +30,7 @@ template <typename T>
 __global__ void __launch_bounds__(256) conv1_kernel(const float* __restrict__ mel, int h, int w,
                                                     const float* __restrict__ wt,
                                                     const float* __restrict__ bias, int c_out,
-                                                    T* __restrict__ out) {
+                                                    int ldc, T* __restrict__ out) {
   extern __shared__ float s_in[];  // [5][w + 2]
   const int ho = (h + 2 - 3) / 2 + 1, wo = (w + 2 - 3) / 2 + 1;
   const int wp = w + 2;
@@ -55,7 +55,7 @@ __global__ void __launch_bounds__(256) conv1_kernel(const float* __restrict__ me
     b[c] = bias[oc + c];
   }
   const float* rows = s_in + 2 * rr * wp;  // input rows 2*oh - 1 .. 2*oh + 1 (padded)
-  T* dst = out + (static_cast<long long>(chunk) * ho + oh) * wo * c_out + oc;
+  T* dst = out + (static_cast<long long>(chunk) * ho + oh) * wo * ldc + oc;
 #pragma unroll 2
   for (int ow = 0; ow < wo; ++ow) {
     float a[kC1Ch];
@@ -72,7 +72,7 @@ __global__ void __launch_bounds__(256) conv1_kernel(const float* __restrict__ me
     alignas(8) T pr[kC1Ch];
 #pragma unroll
     for (int c = 0; c < kC1Ch; ++c) pr[c] = f2h<T>(gelu_erf(a[c] + b[c]));  // taps, then bias
-    *reinterpret_cast<uint2*>(dst + static_cast<long long>(ow) * c_out) =
+    *reinterpret_cast<uint2*>(dst + static_cast<long long>(ow) * ldc) =
         *reinterpret_cast<const uint2*>(pr);
   }
 }
@@ -107,18 +107,19 @@ __global__ void im2col_kernel(const uint4* __restrict__ x, int n, int h, int w, 
 }  // namespace
 
 int conv1_direct(const float* mel, int n, int h, int w, const float* wt, const float* bias,
-                 int c_out, void* out, bool bf16, cudaStream_t s) {
+                 int c_out, int ldc, void* out, bool bf16, cudaStream_t s) {
   if (n <= 0) return 0;
-  if (c_out % kC1Ch || 2 * (c_out / kC1Ch) > 256 || 5 * (w + 2) * sizeof(float) > 48 * 1024)
+  if (c_out % kC1Ch || 2 * (c_out / kC1Ch) > 256 || 5 * (w + 2) * sizeof(float) > 48 * 1024 ||
+      ldc < c_out || ldc % kC1Ch)
     return (int)cudaErrorInvalidValue;
   const int ho = (h + 2 - 3) / 2 + 1;
   const size_t smem = 5 * (w + 2) * sizeof(float);
   dim3 grid((ho + 1) / 2, n);
   if (bf16)
-    conv1_kernel<__nv_bfloat16><<<grid, 256, smem, s>>>(mel, h, w, wt, bias, c_out,
+    conv1_kernel<__nv_bfloat16><<<grid, 256, smem, s>>>(mel, h, w, wt, bias, c_out, ldc,
                                                         static_cast<__nv_bfloat16*>(out));
   else
-    conv1_kernel<__half><<<grid, 256, smem, s>>>(mel, h, w, wt, bias, c_out,
+    conv1_kernel<__half><<<grid, 256, smem, s>>>(mel, h, w, wt, bias, c_out, ldc,
                                                  static_cast<__half*>(out));
   return (int)cudaGetLastError();
 }

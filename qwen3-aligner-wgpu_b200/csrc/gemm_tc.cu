@@ -928,6 +928,187 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+// CTA-pair version of conv_tma_kernel: the two CTAs of a cluster take two
+// consecutive M tiles (R output rows each), each loads its own strided A box
+// and half of B (BN/2 output channels) per k-block, and the first CTA issues
+// M=256 MMAs over both (the same barrier protocol as gemm_pair_kernel).  With
+// an odd number of M tiles the last pair's second CTA loads an in-range box
+// and stores nothing.
+// BK = 64 (128-byte rows, 128B swizzle) when the channel count allows it,
+// else 32: the TMA unit's cost is per box row, so wider rows carry twice the
+// MMA work per request.
+template <int BN, int BK>
+struct ConvPairCfg {
+  static constexpr int kStages = BK == 64 ? 6 : 12;
+  static constexpr uint32_t kABytes = kBM * BK * 2;
+  static constexpr uint32_t kBHalf = (BN / 2) * BK * 2;  // BN/2 rows x BK k (a swizzle-atom multiple)
+  static constexpr size_t kSmem = 1024 + kStages * (kABytes + kBHalf) + 256;
+};
+
+template <int BK>
+__device__ __forceinline__ uint64_t conv_desc(uint32_t addr) {
+  return BK == 64 ? sw128_kmajor_desc(addr) : sw64_kmajor_desc(addr);
+}
+
+template <int BN, int BK, typename T>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    conv_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmB,
+                     ConvTiles g, int N, int K, EpiParams ep) {
+  using Cfg = ConvPairCfg<BN, BK>;
+  constexpr int S = Cfg::kStages;
+  constexpr uint32_t kAccCols = 256;
+  constexpr uint32_t kAllocCols = 512;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * Cfg::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBHalf);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+  const int nkb = K / BK;
+  const int n_tiles_n = N / BN;
+  const int n_tiles = n_tiles_n * ((g.n_mtiles + 1) / 2);
+  const int M = g.n_mtiles / g.tiles_per_img * g.ho * g.wo;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 2 * kGemmEpiWarps);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmX);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc_pair(tslot, kAllocCols);
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+
+  auto timed_out = [&]() {
+    *abort_flag = 1;
+    if (ep.status) atomicOr(ep.status, kStatusTimeout);
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t full_lead = mapa_shared(smem_u32(full), 0);
+      uint32_t c = 0;
+      for (int t = pair; t < n_tiles && !*abort_flag; t += n_pairs) {
+        const int mt0 = 2 * (t / n_tiles_n) + static_cast<int>(rank);
+        const int mt = mt0 < g.n_mtiles ? mt0 : 0;  // past the end: an in-range box, not stored
+        const int n0 = (t % n_tiles_n) * BN;
+        const int img = mt / g.tiles_per_img;
+        const int oh0 = (mt % g.tiles_per_img) * g.rows;
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb, ++c) {
+          const int s = c % S;
+          const uint32_t ph = (c / S) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1u)) {
+            timed_out();
+            ok = false;
+            break;
+          }
+          const int k0 = kb * BK;
+          const int tap = k0 / g.c, cb = k0 - tap * g.c;
+          const int kh = tap / 3, kw = tap - kh * 3;
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * (g.a_bytes + Cfg::kBHalf));
+          const uint32_t bar = full_lead + s * 8;
+          tma_load_4d_pair(&tmX, bar, sA + s * Cfg::kABytes, cb, kw - 1, 2 * oh0 + kh - 1, img);
+          tma_load_2d_pair(&tmB, bar, sB + s * Cfg::kBHalf, k0, n0 + static_cast<int>(rank) * (BN / 2));
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = f16_instr_desc(2 * kBM, BN, H16Traits<T>::kBf16);
+      uint32_t c = 0;
+      int lt = 0;
+      for (int t = pair; t < n_tiles && !*abort_flag; t += n_pairs, ++lt) {
+        const int buf = lt & 1;
+        if (!mbar_wait_cluster(&tempty[buf], ((lt >> 1) & 1) ^ 1u)) {
+          timed_out();
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc = tbase + buf * kAccCols;
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb, ++c) {
+          const int s = c % S;
+          const uint32_t ph = (c / S) & 1;
+          if (!mbar_wait(&full[s], ph)) {
+            timed_out();
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + s * Cfg::kABytes);
+          const uint32_t b_addr = smem_u32(sB + s * Cfg::kBHalf);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            mma_f16_pair(acc, conv_desc<BK>(a_addr + k * 32), conv_desc<BK>(b_addr + k * 32), idesc,
+                         (kb > 0 || k > 0) ? 1u : 0u);
+          mma_commit_pair(&empty[s], 0x3);
+        }
+        if (!ok) break;
+        mma_commit_pair(&tfull[buf], 0x3);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int wg = (warp - 2) / 4;
+    int cb, ce;
+    epi_range<BN>(ep.mode, wg, kGemmEpiWarps / 4, cb, ce);
+    const uint32_t tempty_lead = mapa_shared(smem_u32(tempty), 0);
+    int lt = 0;
+    for (int t = pair; t < n_tiles; t += n_pairs, ++lt) {
+      const int buf = lt & 1;
+      if (*abort_flag || !mbar_wait(&tfull[buf], (lt >> 1) & 1)) {
+        if (lane == 0) timed_out();
+        break;
+      }
+      tc_fence_after();
+      const int mt = 2 * (t / n_tiles_n) + static_cast<int>(rank);
+      const int n0 = (t % n_tiles_n) * BN;
+      const int img = mt / g.tiles_per_img;
+      const int oh0 = (mt % g.tiles_per_img) * g.rows;
+      const int m = q * 32 + lane;
+      const int oh = oh0 + m / g.wo, ow = m % g.wo;
+      const bool valid = mt < g.n_mtiles && m < g.rows * g.wo && oh < g.ho;
+      const int orow = img * g.ho * g.wo + (g.time_major ? ow * g.ho + oh : oh * g.wo + ow);
+      const uint32_t trow = tbase + buf * kAccCols + (static_cast<uint32_t>(q * 32) << 16);
+      epilogue<BN, T>(ep, trow, valid ? orow : M, M, n0, N, cb, ce);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(tempty_lead + buf * 8);
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tbase, kAllocCols);
+  }
+}
+
 int num_sms() {
   static int sms[64] = {0};
   int dev = 0;
@@ -1167,6 +1348,66 @@ int launch_conv(const void* x, const ConvGeom& g, const void* B, int M, int N, i
   return (int)cudaGetLastError();
 }
 
+template <int BN, int BK, typename T>
+int launch_conv_pair(const void* x, int n, int h, int w, int c, const void* wt, int N,
+                     bool time_major, const EpiParams& ep, cudaStream_t stream) {
+  using Cfg = ConvPairCfg<BN, BK>;
+  ConvTiles g;
+  g.ho = (h - 1) / 2 + 1;
+  g.wo = (w - 1) / 2 + 1;
+  g.c = c;
+  g.rows = std::min(kBM / g.wo, g.ho);
+  g.tiles_per_img = (g.ho + g.rows - 1) / g.rows;
+  g.n_mtiles = n * g.tiles_per_img;
+  g.time_major = time_major ? 1 : 0;
+  g.a_bytes = static_cast<uint32_t>(g.rows * g.wo * BK * 2);
+  const int K = 9 * c;
+  const long long dims[4] = {c, w, h, n};
+  const long long strides[3] = {2LL * c, 2LL * c * w, 2LL * c * w * h};
+  const int box[4] = {BK, 2 * g.wo - 1, 2 * g.rows - 1, 1};
+  const int estr[4] = {1, 2, 2, 1};
+  CUtensorMap tx, tb;
+  int rc = make_tmap_nd(&tx, x, H16Traits<T>::kBf16, 4, dims, strides, box, estr, 2 * BK);
+  if (rc) return rc;
+  const long long bdims[2] = {K, N};
+  const long long bstr[1] = {2LL * K};
+  const int bbox[2] = {BK, BN / 2};
+  const int bestr[2] = {1, 1};
+  rc = make_tmap_nd(&tb, wt, H16Traits<T>::kBf16, 2, bdims, bstr, bbox, bestr, 2 * BK);
+  if (rc) return rc;
+  auto kern = conv_pair_kernel<BN, BK, T>;
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmem);
+  if (e != cudaSuccess) return (int)e;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  static int max_pairs[64] = {0};  // per instantiation
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!max_pairs[dev]) {
+    cfg.gridDim = dim3(2 * (num_sms() / 2), 1, 1);
+    int np = 0;
+    if (cudaOccupancyMaxActiveClusters(&np, kern, &cfg) != cudaSuccess || np <= 0) np = num_sms() / 2;
+    max_pairs[dev] = np;
+  }
+  const int tiles = (N / BN) * ((g.n_mtiles + 1) / 2);
+  const int pairs = tiles < max_pairs[dev] ? tiles : max_pairs[dev];
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  e = cudaLaunchKernelEx(&cfg, kern, tx, tb, g, N, K, ep);
+  if (e != cudaSuccess) return (int)e;
+  return (int)cudaGetLastError();
+}
+
 template <int BN, typename T>
 int launch_conv_tma(const void* x, int n, int h, int w, int c, const void* wt, int N,
                     bool time_major, const EpiParams& ep, cudaStream_t stream) {
@@ -1325,6 +1566,12 @@ int conv3x3s2_tc(const void* x, int n, int h, int w, int c, const void* wt, int 
   const int M = n * g.ho * g.wo, K = 9 * c;
   const int bn = gemm_pick_bn(c_out);
   // TMA path: whole 32-channel k-blocks per tap and output rows that fit a tile
+  if (c % 64 == 0 && g.wo <= kBM && c_out % 240 == 0)  // CTA pairs, 256 x 240 tiles, 64-wide k
+    return bf16 ? launch_conv_pair<240, 64, __nv_bfloat16>(x, n, h, w, c, wt, c_out, time_major, ep, stream)
+                : launch_conv_pair<240, 64, __half>(x, n, h, w, c, wt, c_out, time_major, ep, stream);
+  if (c % kCvBK == 0 && g.wo <= kBM && c_out % 240 == 0)  // 32-wide k
+    return bf16 ? launch_conv_pair<240, 32, __nv_bfloat16>(x, n, h, w, c, wt, c_out, time_major, ep, stream)
+                : launch_conv_pair<240, 32, __half>(x, n, h, w, c, wt, c_out, time_major, ep, stream);
   if (c % kCvBK == 0 && g.wo <= kBM && (bn == 240 || bn == 256)) {
     if (bn == 240)
       return bf16 ? launch_conv_tma<240, __nv_bfloat16>(x, n, h, w, c, wt, c_out, time_major, ep, stream)

@@ -44,7 +44,12 @@ int mel_finalize_rows(const float* scratch, int n_frames, const unsigned* maxkey
 // conv1: chunked mel [n][h][w] f32 (c_in = 1) -> NHWC [n][ho][wo][c_out] 16-bit,
 // gelu(w·x + b).  w [c_out][9] f32 (k = kh*3 + kw).
 int conv1_direct(const float* mel, int n, int h, int w, const float* wt, const float* bias,
-                 int c_out, void* out, bool bf16, cudaStream_t s);
+                 int c_out, int ldc, void* out, bool bf16, cudaStream_t s);
+
+// Channels per pixel of the conv activations that feed the implicit GEMMs:
+// c rounded up to 64 (the pad channels hold zeros), so that a 64-channel
+// (128-byte) k-block of the TMA im2col boxes never straddles two taps.
+inline int conv_channels_padded(int c) { return (c + 63) / 64 * 64; }
 // im2col for a 3x3 / stride 2 / pad 1 conv over NHWC [n][h][w][c] 16-bit:
 // cols [n*ho*wo][9*c] with k = (kh*3 + kw)*c + ic.  Positions are ordered
 // (oh, ow) when !time_major, (ow, oh) when time_major.

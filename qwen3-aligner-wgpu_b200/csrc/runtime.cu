@@ -214,6 +214,16 @@ int ensure(qa_ctx* ctx, DevBuf& b, size_t bytes) {
   return QA_OK;
 }
 
+// ensure() for a buffer whose bytes that kernels never write must read as zero
+// (the pad channels of the conv activations): zeroed on the stream whenever it
+// is (re)allocated.
+int ensure_zeroed(qa_ctx* ctx, DevBuf& b, size_t bytes) {
+  if (bytes <= b.cap) return QA_OK;
+  TRY(ensure(ctx, b, bytes));
+  CK(cudaMemsetAsync(b.p, 0, b.cap, ctx->stream));
+  return QA_OK;
+}
+
 int ensure_pin(qa_ctx* ctx, PinBuf& b, size_t bytes) {
   if (bytes <= b.cap) return QA_OK;
   if (b.p) cudaFreeHost(b.p);
@@ -479,12 +489,16 @@ int load_weights(qa_ctx* ctx, const qa_tensor* tensors, int n, const qa_cfg& c) 
     auto b2 = L.f32(A + "conv2d2.bias", {ds});
     auto b3 = L.f32(A + "conv2d3.bias", {ds});
     if (!L.missing.empty()) return fail(ctx, QA_ERR_WEIGHTS, "%s", L.missing.c_str());
+    // conv2/conv3 weights as [oc][(kh*3 + kw)*cp + ic]: the activations carry
+    // cp = ds rounded up to 64 channels per pixel (the pad channels are zero),
+    // so a 64-channel k-block never straddles two taps
+    const int cp = conv_channels_padded(ds);
     auto perm = [&](const std::vector<float>& w) {
-      std::vector<float> o(w.size());
+      std::vector<float> o(static_cast<size_t>(ds) * 9 * cp, 0.0f);
       for (int oc = 0; oc < ds; ++oc)
         for (int ic = 0; ic < ds; ++ic)
           for (int k = 0; k < 9; ++k)
-            o[(static_cast<size_t>(oc) * 9 + k) * ds + ic] = w[(static_cast<size_t>(oc) * ds + ic) * 9 + k];
+            o[(static_cast<size_t>(oc) * 9 + k) * cp + ic] = w[(static_cast<size_t>(oc) * ds + ic) * 9 + k];
       return o;
     };
     std::vector<float> cop(co.size());
@@ -775,8 +789,9 @@ int run_encoder(qa_ctx* ctx, const Plan& P, const PlanDev& D, void* out16, const
   const int h3 = (h2 - 1) / 2 + 1, w3 = (w2 - 1) / 2 + 1;
   const int tpc = w3;
   const int G = std::max(1, std::min(P.total_chunks, 256));  // chunks per conv group
-  TRY(ensure(ctx, ctx->act1, static_cast<size_t>(G) * h1 * w1 * ds * 2));
-  TRY(ensure(ctx, ctx->act2, static_cast<size_t>(G) * h2 * w2 * ds * 2));
+  const int cp = conv_channels_padded(ds);  // channels per pixel of act1 / act2 (pads zero)
+  TRY(ensure_zeroed(ctx, ctx->act1, static_cast<size_t>(G) * h1 * w1 * cp * 2));
+  TRY(ensure_zeroed(ctx, ctx->act2, static_cast<size_t>(G) * h2 * w2 * cp * 2));
   TRY(ensure(ctx, ctx->act3, static_cast<size_t>(G) * h3 * w3 * ds * 2));
   TRY(ensure(ctx, ctx->xenc, static_cast<size_t>(std::max(P.T_a, 1)) * dm * 4));
   EpiParams ep;
@@ -785,22 +800,23 @@ int run_encoder(qa_ctx* ctx, const Plan& P, const PlanDev& D, void* out16, const
     const int g = std::min(G, P.total_chunks - g0);
     const float* mel = ctx->mel_chunked.as<float>() + static_cast<size_t>(g0) * c.num_mel_bins * cs;
     KL("conv1", 18.0 * g * h1 * w1 * ds, 4.0 * g * c.num_mel_bins * cs + 2.0 * g * h1 * w1 * ds,
-       conv1_direct(mel, g, c.num_mel_bins, cs, W.c1_w, W.c1_b, ds, ctx->act1.p, bf, s));
+       conv1_direct(mel, g, c.num_mel_bins, cs, W.c1_w, W.c1_b, ds, cp, ctx->act1.p, bf, s));
     // conv2 / conv3: implicit GEMM on the tensor cores, A gathered from NHWC
     ep.mode = EPI_STORE16;
     ep.act = ACT_GELU;
     ep.bias = W.c2_b;
     ep.out = ctx->act2.p;
-    ep.ldo = ds;
+    ep.ldo = cp;
     ep.row_map = nullptr;
     KL("conv_gemm", gemm_flops(g * h2 * w2, ds, 9 * ds),
        2.0 * g * (h1 * w1 * ds + h2 * w2 * ds) + 2.0 * ds * 9 * ds,
-       conv3x3s2_tc(ctx->act1.p, g, h1, w1, ds, W.c2_w, ds, false, bf, ep, s));
+       conv3x3s2_tc(ctx->act1.p, g, h1, w1, cp, W.c2_w, ds, false, bf, ep, s));
     ep.bias = W.c3_b;
     ep.out = ctx->act3.p;
+    ep.ldo = ds;
     KL("conv_gemm", gemm_flops(g * h3 * w3, ds, 9 * ds),
        2.0 * g * (h2 * w2 * ds + h3 * w3 * ds) + 2.0 * ds * 9 * ds,
-       conv3x3s2_tc(ctx->act2.p, g, h2, w2, ds, W.c3_w, ds, true, bf, ep, s));
+       conv3x3s2_tc(ctx->act2.p, g, h2, w2, cp, W.c3_w, ds, true, bf, ep, s));
     // conv_out + bias + PE[t], scattered into the packed token rows
     EpiParams eo;
     eo.status = ep.status;

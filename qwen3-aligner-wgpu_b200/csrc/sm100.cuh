@@ -442,6 +442,17 @@ __device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, uint32_
       : "memory");
 }
 
+// 4-D variant of tma_load_2d_pair (coordinates innermost first).  Not multicast.
+__device__ __forceinline__ void tma_load_4d_pair(const CUtensorMap* map, uint32_t bar_cluster,
+                                                 void* dst, int32_t c0, int32_t c1, int32_t c2,
+                                                 int32_t c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 // TMEM allocation for a CTA pair: executed by the same warp in both CTAs.
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* slot, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(

@@ -33,6 +33,7 @@ def main():
     ap.add_argument("--h", type=int, default=64)
     ap.add_argument("--w", type=int, default=50)
     ap.add_argument("--c", type=int, default=480)
+    ap.add_argument("--cout", type=int, default=0, help="conv output channels (0 = --c)")
     ap.add_argument("--time-major", action="store_true")
     ap.add_argument("--clips", type=int, default=64)
     ap.add_argument("--min-len", type=int, default=130)
@@ -145,11 +146,12 @@ def conv(a, L, dt):
     import torch
     dev = torch.device("cuda:0")
     g = torch.Generator(device=dev).manual_seed(0)
+    co = a.cout or a.c
     x = (torch.randn(a.n, a.h, a.w, a.c, device=dev, generator=g) * 0.5).to(dt)
-    wk = (torch.randn(a.c, 9 * a.c, device=dev, generator=g) * 0.02).to(dt)
-    bias = torch.randn(a.c, device=dev, generator=g) * 0.1
+    wk = (torch.randn(co, 9 * a.c, device=dev, generator=g) * 0.02).to(dt)
+    bias = torch.randn(co, device=dev, generator=g) * 0.1
     ho, wo = (a.h - 1) // 2 + 1, (a.w - 1) // 2 + 1
-    out = torch.empty(a.n * ho * wo, a.c, device=dev, dtype=dt)
+    out = torch.empty(a.n * ho * wo, co, device=dev, dtype=dt)
     st = torch.zeros(1, dtype=torch.int32, device=dev)
     run = lambda: L.conv3x3s2(x, wk, out, time_major=a.time_major, act=L.ACT_GELU, bias=bias,
                               status=st)
@@ -164,8 +166,8 @@ def conv(a, L, dt):
     torch.cuda.synchronize()
     assert int(st.item()) == 0
     ms = e0.elapsed_time(e1) / a.iters
-    flops = 2.0 * a.n * ho * wo * a.c * 9 * a.c
-    print(json.dumps({"kernel": "conv3x3s2", "n": a.n, "h": a.h, "w": a.w, "c": a.c,
+    flops = 2.0 * a.n * ho * wo * co * 9 * a.c
+    print(json.dumps({"kernel": "conv3x3s2", "n": a.n, "h": a.h, "w": a.w, "c": a.c, "cout": co,
                       "time_major": a.time_major, "dtype": a.dtype, "ms": ms,
                       "tflops": flops / ms / 1e9}))
 

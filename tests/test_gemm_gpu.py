@@ -165,7 +165,9 @@ def _conv_ref(x_nhwc, w4, bias, time_major):
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("n,h,w,c,co,tm", [(3, 64, 50, 480, 480, False), (3, 32, 25, 480, 480, True),
-                                          (2, 9, 7, 16, 256, False), (1, 5, 5, 480, 480, True)])
+                                          (2, 9, 7, 16, 256, False), (1, 5, 5, 480, 480, True),
+                                          (3, 64, 50, 512, 480, False), (3, 32, 25, 512, 480, True),
+                                          (1, 5, 5, 512, 480, False)])
 def test_implicit_conv(dtype, n, h, w, c, co, tm):
     L = _lib()
     g = torch.Generator(device="cuda").manual_seed(n * h + c)
