@@ -42,6 +42,7 @@ def main():
     ap.add_argument("--m", type=int, default=16384)
     ap.add_argument("--n", type=int, default=6144, help="gemm N, or images for conv")
     ap.add_argument("--k", type=int, default=1024)
+    ap.add_argument("--act", default="none", choices=["none", "gelu"])
     ap.add_argument("--bn", type=int, default=0,
                     help="gemm tile: 0 = library choice, -1 = CTA-pair 256x256, >0 = one CTA, that width")
     ap.add_argument("--mode", default="store16",
@@ -73,18 +74,19 @@ def main():
     out = torch.zeros(a.m, out_cols, device="cuda", dtype=out_dt)
     keys = torch.zeros(a.m, dtype=torch.int64, device="cuda") if a.mode == "argmax" else None
     bn = a.bn
+    act = L.ACT_GELU if a.act == "gelu" else L.ACT_NONE
     for _ in range(a.warmup):
-        L.gemm(A, B, out, mode=mode, keys=keys, force_bn=bn)
+        L.gemm(A, B, out, mode=mode, keys=keys, force_bn=bn, act=act)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(a.iters):
-        L.gemm(A, B, out, mode=mode, keys=keys, force_bn=bn)
+        L.gemm(A, B, out, mode=mode, keys=keys, force_bn=bn, act=act)
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / a.iters
     flops = 2.0 * a.m * a.n * a.k
-    print(json.dumps({"kernel": "gemm_tc", "m": a.m, "n": a.n, "k": a.k, "mode": a.mode, "bn": a.bn,
+    print(json.dumps({"kernel": "gemm_tc", "m": a.m, "n": a.n, "k": a.k, "mode": a.mode, "act": a.act, "bn": a.bn,
                       "dtype": a.dtype, "ms": ms, "tflops": flops / ms / 1e9,
                       "algorithmic_bytes": (a.m * a.k + a.n * a.k) * 2 + a.m * out_cols * out.element_size()}))
 
