@@ -159,10 +159,13 @@ __device__ __forceinline__ QkvRow qkv_row_meta(const EpiParams& ep, int row, int
 // product and sum rounded as in the reference's loop (norm_rope_head,
 // src/cpu_decoder.rs:305-321), two lanes per f32x2 instruction.  The head is
 // read from TMEM twice (sums, then the 32-column chunks d and d + 64 together)
-// instead of being held in registers.
+// instead of being held in registers.  `gain` is the q_norm | k_norm gains
+// staged in shared memory; each chunk's cos / sin are loaded (read-only path)
+// before its TMEM reads so that their latency overlaps.
 template <typename T>
 __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem_col0, int row,
-                                              int M, int head, const QkvRow& meta) {
+                                              int M, int head, const QkvRow& meta,
+                                              const float* gain) {
   constexpr int HD = 128;
   const RopeKV& rk = ep.rk;
   const bool ok = row < M;
@@ -207,9 +210,9 @@ __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem
   const float s2 = __fadd_rn(__fadd_rn(s2a.x, s2a.y), __fadd_rn(s2b.x, s2b.y));
   const float inv = 1.0f / sqrtf(s2 / static_cast<float>(HD) + rk.eps);
   const float2 inv2 = make_float2(inv, inv);
-  const float* nw = is_q ? rk.qn : rk.kn;
-  const T* ct = static_cast<const T*>(rk.cos_t) + meta.pos * (HD / 2);
-  const T* st = static_cast<const T*>(rk.sin_t) + meta.pos * (HD / 2);
+  const float* nw = is_q ? gain : gain + HD;
+  const uint4* ct = reinterpret_cast<const uint4*>(static_cast<const T*>(rk.cos_t) + meta.pos * (HD / 2));
+  const uint4* st = reinterpret_cast<const uint4*>(static_cast<const T*>(rk.sin_t) + meta.pos * (HD / 2));
   // pass 2: elements d in [32c, 32c + 32) with their partners d + 64
 #pragma unroll 1
   for (int c = 0; c < 2; ++c) {
@@ -220,8 +223,7 @@ __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem
 #pragma unroll
     for (int j0 = 0; j0 < 32; j0 += 8) {
       const int d0 = c * 32 + j0;
-      const uint4 cu = *reinterpret_cast<const uint4*>(ct + d0);
-      const uint4 su = *reinterpret_cast<const uint4*>(st + d0);
+      const uint4 cu = __ldg(ct + d0 / 8), su = __ldg(st + d0 / 8);
       const uint32_t cw[4] = {cu.x, cu.y, cu.z, cu.w}, sw[4] = {su.x, su.y, su.z, su.w};
       const float4 na0 = *reinterpret_cast<const float4*>(nw + d0);
       const float4 na1 = *reinterpret_cast<const float4*>(nw + d0 + 4);
@@ -248,18 +250,29 @@ __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem
   }
 }
 
+// The epilogue warps (threads 64 .. 64 + 32 * 8 - 1 of the two GEMM kernels)
+// copy the q_norm | k_norm gains into shared memory and meet at named
+// barrier 1.
+__device__ __forceinline__ void stage_qkv_gains(const EpiParams& ep, float* gain) {
+  constexpr int kEpiThreads = 256;
+  for (int e = threadIdx.x - 64; e < 256; e += kEpiThreads)
+    gain[e] = e < 128 ? ep.rk.qn[e] : ep.rk.kn[e - 128];
+  asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+}
+
 // The fused epilogue over columns [cb, ce) of this thread's tile row (cb, ce
 // multiples of 32; two epilogue warpgroups split a tile between them).  For
 // SwiGLU the range is over the output columns [0, BN/2).
 template <int BN, typename T>
 __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row, int row, int M,
-                                         int n0, int N, int cb, int ce, const QkvRow& meta = {}) {
+                                         int n0, int N, int cb, int ce, const QkvRow& meta = {},
+                                         const float* gain = nullptr) {
   if constexpr (BN % 128 == 0) {
     if (ep.mode == EPI_QKV_ROPE) {
 #pragma unroll 1
       for (int hb = cb / 128; hb < ce / 128; ++hb)
         if (n0 + hb * 128 < N)
-          qkv_rope_head<T>(ep, tmem_row + hb * 128, row, M, (n0 + hb * 128) / 128, meta);
+          qkv_rope_head<T>(ep, tmem_row + hb * 128, row, M, (n0 + hb * 128) / 128, meta, gain);
       return;
     }
   }
@@ -335,7 +348,7 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
         const float4* b4 = reinterpret_cast<const float4*>(bp);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const float4 t = b4[i];
+          const float4 t = __ldg(b4 + i);
           v[4 * i] += t.x;
           v[4 * i + 1] += t.y;
           v[4 * i + 2] += t.z;
@@ -551,6 +564,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int wg = (warp - 2) / 4;       // column half of the tile
     int cb, ce;
     epi_range<BN>(ep.mode, wg, kGemmEpiWarps / 4, cb, ce);
+    __shared__ float gain[256];  // EPI_QKV_ROPE: q_norm | k_norm gains
+    if (ep.mode == EPI_QKV_ROPE) stage_qkv_gains(ep, gain);
     int lt = 0;
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++lt) {
       const int buf = lt & 1;
@@ -564,7 +579,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       tc_fence_after();
       const uint32_t trow = tbase + buf * kAccCols + (static_cast<uint32_t>(q * 32) << 16);
-      epilogue<BN, T>(ep, trow, row, M, n0, N, cb, ce, meta);
+      epilogue<BN, T>(ep, trow, row, M, n0, N, cb, ce, meta, gain);
       tc_fence_before();
       mbar_arrive(&tempty[buf]);
     }
@@ -720,6 +735,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int cb, ce;
     epi_range<BN>(ep.mode, wg, kGemmEpiWarps / 4, cb, ce);
     const uint32_t tempty_lead = mapa_shared(smem_u32(tempty), 0);
+    __shared__ float gain[256];  // EPI_QKV_ROPE: q_norm | k_norm gains
+    if (ep.mode == EPI_QKV_ROPE) stage_qkv_gains(ep, gain);
     int lt = 0;
     for (int t = pair; t < n_tiles; t += n_pairs, ++lt) {
       const int buf = lt & 1;
@@ -733,7 +750,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       tc_fence_after();
       const uint32_t trow = tbase + buf * kAccCols + (static_cast<uint32_t>(q * 32) << 16);
-      epilogue<BN, T>(ep, trow, row, M, n0, N, cb, ce, meta);
+      epilogue<BN, T>(ep, trow, row, M, n0, N, cb, ce, meta, gain);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(tempty_lead + buf * 8);
