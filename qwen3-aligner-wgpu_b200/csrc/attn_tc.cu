@@ -320,7 +320,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) fail();
     }
   } else if (warp == 2) {
-    if (lane == 0) {
+    // the whole warp runs this role (warp-uniform values); one elected lane
+    // issues each tcgen05 instruction
+    auto wait = [&](uint64_t* bar, uint32_t par) -> bool {
+      return __all_sync(0xFFFFFFFFu, !*abort_flag && mbar_wait(bar, par));
+    };
+    {
       const bool bf = H16Traits<T>::kBf16;
       const uint32_t idS128 = f16_instr_desc(kRows, 128, bf);
       const uint32_t idS64 = f16_instr_desc(kRows, 64, bf);
@@ -331,24 +336,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto issue_s = [&](uint32_t g, int keys, int qb) -> bool {
         const int st = g & 1;
         const uint32_t kst = g % kKStages, kph = (g / kKStages) & 1;
-        if (*abort_flag || !mbar_wait(&k_full[kst], kph)) return false;
+        if (!wait(&k_full[kst], kph)) return false;
         tc_fence_after();
         const uint32_t id = keys == 128 ? idS128 : idS64;
 #pragma unroll
         for (int ks = 0; ks < kHD / 16; ++ks)
-          mma_f16_ts(tS0 + st * 128, tQ0 + qb * 64 + ks * 8,
-                     sw128_kmajor_desc(ka + kst * kTile + (ks >> 2) * kHalf + (ks & 3) * 32), id,
-                     ks > 0 ? 1u : 0u);
-        mma_commit(&s_full[st]);
-        mma_commit(&k_empty[kst]);
+          mma_f16_ts_e(tS0 + st * 128, tQ0 + qb * 64 + ks * 8,
+                       sw128_kmajor_desc(ka + kst * kTile + (ks >> 2) * kHalf + (ks & 3) * 32), id,
+                       ks > 0 ? 1u : 0u);
+        mma_commit_e(&s_full[st]);
+        mma_commit_e(&k_empty[kst]);
         return true;
       };
       // first S of the n-th item (Q in TMEM buffer n & 1)
       auto issue_first_s = [&](const Item& it, uint32_t n, uint32_t g) -> bool {
-        if (*abort_flag || !mbar_wait(&qt_full[n & 1], (n >> 1) & 1)) return false;
+        if (!wait(&qt_full[n & 1], (n >> 1) & 1)) return false;
         tc_fence_after();
         if (!issue_s(g, tile_keys(it, 0), n & 1)) return false;
-        if (it.n_tiles == 1) mma_commit(&qt_free[n & 1]);
+        if (it.n_tiles == 1) mma_commit_e(&qt_free[n & 1]);
         return true;
       };
       bool ok = true;
@@ -370,17 +375,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         Item nxt{};
         if (!last) {
           ok = issue_s(g + 1, tile_keys(cur, j + 1), cq & 1);
-          if (ok && j + 2 == cur.n_tiles) mma_commit(&qt_free[cq & 1]);
+          if (ok && j + 2 == cur.n_tiles) mma_commit_e(&qt_free[cq & 1]);
         } else {
           ni = next_valid(ap, ci + gridDim.x, false);
           if (ni < ap.n_items) {
             nxt = get_item(ap, ni);
-            ok = mbar_wait(o_free, o_par) && issue_first_s(nxt, cq + 1, g + 1);
+            ok = wait(o_free, o_par) && issue_first_s(nxt, cq + 1, g + 1);
           }
         }
         const int st = g & 1;
-        if (!ok || !mbar_wait(&p_full[st], (g >> 1) & 1) || !mbar_wait(&v_full[st], (g >> 1) & 1) ||
-            (j == 0 && !mbar_wait(o_free, o_par))) {
+        if (!ok || !wait(&p_full[st], (g >> 1) & 1) || !wait(&v_full[st], (g >> 1) & 1) ||
+            (j == 0 && !wait(o_free, o_par))) {
           ok = false;
           break;
         }
@@ -388,12 +393,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int keys = tile_keys(cur, j);
         // P for keys 0-63 in S columns 0-31, for keys 64-127 in columns 64-95
         for (int ks = 0; ks < keys / 16; ++ks)
-          mma_f16_ts(tO0, tS0 + st * 128 + (ks >> 2) * 64 + (ks & 3) * 8,
-                     sw128_mn_desc(va + st * kTile + ks * 16 * 128, kHalf, 1024), idPV,
-                     (j > 0 || ks > 0) ? 1u : 0u);
-        mma_commit(&v_empty[st]);
-        mma_commit(o_ready);
-        if (last) mma_commit(o_done);
+          mma_f16_ts_e(tO0, tS0 + st * 128 + (ks >> 2) * 64 + (ks & 3) * 8,
+                       sw128_mn_desc(va + st * kTile + ks * 16 * 128, kHalf, 1024), idPV,
+                       (j > 0 || ks > 0) ? 1u : 0u);
+        mma_commit_e(&v_empty[st]);
+        mma_commit_e(o_ready);
+        if (last) mma_commit_e(o_done);
         ++g;
         if (!last) {
           ++j;
@@ -404,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           j = 0;
         }
       }
-      if (!ok) fail();
+      if (!ok && lane == 0) fail();
     }
   } else if (warp < 3 + kSoftmaxWarps) {
     // softmax: half hf of the keys (and of the O columns), row r

@@ -523,13 +523,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {  // the whole warp; one elected lane issues
       constexpr uint32_t idesc = f16_instr_desc(kBM, BN, H16Traits<T>::kBf16);
       uint32_t c = 0;
       int lt = 0;  // tiles done by this CTA
-      for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x, ++lt) {
+      for (int t = blockIdx.x; t < n_tiles && !__any_sync(0xFFFFFFFFu, *abort_flag != 0); t += gridDim.x, ++lt) {
         const int buf = lt & 1;
-        if (!mbar_wait(&tempty[buf], ((lt >> 1) & 1) ^ 1u)) {
+        if (!mbar_wait_warp(&tempty[buf], ((lt >> 1) & 1) ^ 1u)) {
           timed_out();
           break;
         }
@@ -539,7 +539,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int kb = 0; kb < nkb; ++kb, ++c) {
           const int s = c % S;
           const uint32_t ph = (c / S) & 1;
-          if (!mbar_wait(&full[s], ph)) {
+          if (!mbar_wait_warp(&full[s], ph)) {
             timed_out();
             ok = false;
             break;
@@ -551,12 +551,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t da = sw128_kmajor_desc(a_addr + k * 32);
             const uint64_t db = sw128_kmajor_desc(b_addr + k * 32);
-            mma_f16(acc, da, db, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            mma_f16_e(acc, da, db, idesc, (kb > 0 || k > 0) ? 1u : 0u);
           }
-          mma_commit(&empty[s]);
+          mma_commit_e(&empty[s]);
         }
         if (!ok) break;
-        mma_commit(&tfull[buf]);
+        mma_commit_e(&tfull[buf]);
       }
     }
   } else {
@@ -695,13 +695,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && rank == 0) {
+    if (rank == 0) {  // the whole warp; one elected lane issues
       constexpr uint32_t idesc = f16_instr_desc(2 * kBM, BN, H16Traits<T>::kBf16);
       uint32_t c = 0;
       int lt = 0;
-      for (int t = pair; t < n_tiles && !*abort_flag; t += n_pairs, ++lt) {
+      for (int t = pair; t < n_tiles && !__any_sync(0xFFFFFFFFu, *abort_flag != 0); t += n_pairs, ++lt) {
         const int buf = lt & 1;
-        if (!mbar_wait_cluster(&tempty[buf], ((lt >> 1) & 1) ^ 1u)) {
+        if (!mbar_wait_cluster_warp(&tempty[buf], ((lt >> 1) & 1) ^ 1u)) {
           timed_out();
           break;
         }
@@ -711,7 +711,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int kb = 0; kb < nkb; ++kb, ++c) {
           const int s = c % S;
           const uint32_t ph = (c / S) & 1;
-          if (!mbar_wait(&full[s], ph)) {
+          if (!mbar_wait_warp(&full[s], ph)) {
             timed_out();
             ok = false;
             break;
@@ -721,12 +721,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint32_t b_addr = smem_u32(sB + s * kBHalf);
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k)
-            mma_f16_pair(acc, sw128_kmajor_desc(a_addr + k * 32), sw128_kmajor_desc(b_addr + k * 32),
+            mma_f16_pair_e(acc, sw128_kmajor_desc(a_addr + k * 32), sw128_kmajor_desc(b_addr + k * 32),
                          idesc, (kb > 0 || k > 0) ? 1u : 0u);
-          mma_commit_pair(&empty[s], 0x3);
+          mma_commit_pair_e(&empty[s], 0x3);
         }
         if (!ok) break;
-        mma_commit_pair(&tfull[buf], 0x3);
+        mma_commit_pair_e(&tfull[buf], 0x3);
       }
     }
   } else {
@@ -876,13 +876,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {  // the whole warp; one elected lane issues
       constexpr uint32_t idesc = f16_instr_desc(kBM, BN, H16Traits<T>::kBf16);
       uint32_t c = 0;
       int lt = 0;
-      for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x, ++lt) {
+      for (int t = blockIdx.x; t < n_tiles && !__any_sync(0xFFFFFFFFu, *abort_flag != 0); t += gridDim.x, ++lt) {
         const int buf = lt & 1;
-        if (!mbar_wait(&tempty[buf], ((lt >> 1) & 1) ^ 1u)) {
+        if (!mbar_wait_warp(&tempty[buf], ((lt >> 1) & 1) ^ 1u)) {
           timed_out();
           break;
         }
@@ -892,7 +892,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int kb = 0; kb < nkb; ++kb, ++c) {
           const int s = c % S;
           const uint32_t ph = (c / S) & 1;
-          if (!mbar_wait(&full[s], ph)) {
+          if (!mbar_wait_warp(&full[s], ph)) {
             timed_out();
             ok = false;
             break;
@@ -902,12 +902,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint32_t b_addr = smem_u32(sB + s * Cfg::kBBytes);
 #pragma unroll
           for (int k = 0; k < kCvBK / 16; ++k)
-            mma_f16(acc, sw64_kmajor_desc(a_addr + k * 32), sw64_kmajor_desc(b_addr + k * 32),
+            mma_f16_e(acc, sw64_kmajor_desc(a_addr + k * 32), sw64_kmajor_desc(b_addr + k * 32),
                     idesc, (kb > 0 || k > 0) ? 1u : 0u);
-          mma_commit(&empty[s]);
+          mma_commit_e(&empty[s]);
         }
         if (!ok) break;
-        mma_commit(&tfull[buf]);
+        mma_commit_e(&tfull[buf]);
       }
     }
   } else {
@@ -1054,13 +1054,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && rank == 0) {
+    if (rank == 0) {  // the whole warp; one elected lane issues
       constexpr uint32_t idesc = f16_instr_desc(2 * kBM, BN, H16Traits<T>::kBf16);
       uint32_t c = 0;
       int lt = 0;
-      for (int t = pair; t < n_tiles && !*abort_flag; t += n_pairs, ++lt) {
+      for (int t = pair; t < n_tiles && !__any_sync(0xFFFFFFFFu, *abort_flag != 0); t += n_pairs, ++lt) {
         const int buf = lt & 1;
-        if (!mbar_wait_cluster(&tempty[buf], ((lt >> 1) & 1) ^ 1u)) {
+        if (!mbar_wait_cluster_warp(&tempty[buf], ((lt >> 1) & 1) ^ 1u)) {
           timed_out();
           break;
         }
@@ -1070,7 +1070,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int kb = 0; kb < nkb; ++kb, ++c) {
           const int s = c % S;
           const uint32_t ph = (c / S) & 1;
-          if (!mbar_wait(&full[s], ph)) {
+          if (!mbar_wait_warp(&full[s], ph)) {
             timed_out();
             ok = false;
             break;
@@ -1080,12 +1080,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint32_t b_addr = smem_u32(sB + s * Cfg::kBHalf);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
-            mma_f16_pair(acc, conv_desc<BK>(a_addr + k * 32), conv_desc<BK>(b_addr + k * 32), idesc,
+            mma_f16_pair_e(acc, conv_desc<BK>(a_addr + k * 32), conv_desc<BK>(b_addr + k * 32), idesc,
                          (kb > 0 || k > 0) ? 1u : 0u);
-          mma_commit_pair(&empty[s], 0x3);
+          mma_commit_pair_e(&empty[s], 0x3);
         }
         if (!ok) break;
-        mma_commit_pair(&tfull[buf], 0x3);
+        mma_commit_pair_e(&tfull[buf], 0x3);
       }
     }
   } else {
@@ -1283,13 +1283,13 @@ __global__ void __launch_bounds__(288, 1)
     fence_proxy_async_smem();
     for (int i = 0; i < npend; ++i) mbar_arrive(&full[pend[i]]);
   } else if (warp == 4) {
-    if (lane == 0) {
+    {  // the whole warp; one elected lane issues
       constexpr uint32_t idesc = f16_instr_desc(kBM, BN, H16Traits<T>::kBf16);
       uint32_t c = 0;
       int lt = 0;
-      for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x, ++lt) {
+      for (int t = blockIdx.x; t < n_tiles && !__any_sync(0xFFFFFFFFu, *abort_flag != 0); t += gridDim.x, ++lt) {
         const int buf = lt & 1;
-        if (!mbar_wait(&tempty[buf], ((lt >> 1) & 1) ^ 1u)) {
+        if (!mbar_wait_warp(&tempty[buf], ((lt >> 1) & 1) ^ 1u)) {
           timed_out();
           break;
         }
@@ -1299,7 +1299,7 @@ __global__ void __launch_bounds__(288, 1)
         for (int kb = 0; kb < nkb; ++kb, ++c) {
           const int s = c % S;
           const uint32_t ph = (c / S) & 1;
-          if (!mbar_wait(&full[s], ph)) {
+          if (!mbar_wait_warp(&full[s], ph)) {
             timed_out();
             ok = false;
             break;
@@ -1311,12 +1311,12 @@ __global__ void __launch_bounds__(288, 1)
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t da = sw128_kmajor_desc(a_addr + k * 32);
             const uint64_t db = sw128_kmajor_desc(b_addr + k * 32);
-            mma_f16(acc, da, db, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            mma_f16_e(acc, da, db, idesc, (kb > 0 || k > 0) ? 1u : 0u);
           }
-          mma_commit(&empty[s]);
+          mma_commit_e(&empty[s]);
         }
         if (!ok) break;
-        mma_commit(&tfull[buf]);
+        mma_commit_e(&tfull[buf]);
       }
     }
   } else {
