@@ -18,6 +18,14 @@ __device__ __forceinline__ float to_f32(float x) { return x; }
 __device__ __forceinline__ float to_f32(__half x) { return __half2float(x); }
 __device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
 
+// Two f32 values rounded to 16 bits, a in the low half.
+template <typename T>
+__device__ __forceinline__ uint32_t pack_pair(float a, float b) {
+  const T ha = f2h<T>(a), hb = f2h<T>(b);
+  return static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&ha)) |
+         (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&hb)) << 16);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
@@ -62,6 +70,57 @@ __global__ void layernorm_kernel(const float* __restrict__ x, int rows, int d,
   }
 }
 
+// The same row arithmetic with 16-byte loads: rows of d % 4 == 0 f32 elements,
+// 16-byte aligned x / g / b, 8-byte aligned output rows.  Lane l holds float4
+// vectors l, l + 32, ... of its row.
+template <typename T>
+__global__ void layernorm_vec_kernel(const float* __restrict__ x, int rows, int d,
+                                     const float* __restrict__ g, const float* __restrict__ b,
+                                     float eps, T* __restrict__ out) {
+  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int nv = d / 4;
+  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<long long>(row) * d);
+  float4 v[8];
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int i = lane + 32 * k;
+    v[k] = i < nv ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+  }
+  const float mean = warp_sum(s) / static_cast<float>(d);
+  float q = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    if (lane + 32 * k < nv) {
+      const float t0 = v[k].x - mean, t1 = v[k].y - mean, t2 = v[k].z - mean, t3 = v[k].w - mean;
+      q = fmaf(t0, t0, q);
+      q = fmaf(t1, t1, q);
+      q = fmaf(t2, t2, q);
+      q = fmaf(t3, t3, q);
+    }
+  }
+  const float var = warp_sum(q) / static_cast<float>(d);
+  const float inv = 1.0f / sqrtf(var + eps);
+  uint2* o = reinterpret_cast<uint2*>(out + static_cast<long long>(row) * d);
+  const float4* g4 = reinterpret_cast<const float4*>(g);
+  const float4* b4 = reinterpret_cast<const float4*>(b);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int i = lane + 32 * k;
+    if (i < nv) {
+      const float4 gg = __ldg(g4 + i), bb = __ldg(b4 + i);
+      const float e0 = __fadd_rn(__fmul_rn(__fmul_rn(v[k].x - mean, inv), gg.x), bb.x);
+      const float e1 = __fadd_rn(__fmul_rn(__fmul_rn(v[k].y - mean, inv), gg.y), bb.y);
+      const float e2 = __fadd_rn(__fmul_rn(__fmul_rn(v[k].z - mean, inv), gg.z), bb.z);
+      const float e3 = __fadd_rn(__fmul_rn(__fmul_rn(v[k].w - mean, inv), gg.w), bb.w);
+      o[i] = make_uint2(pack_pair<T>(e0, e1), pack_pair<T>(e2, e3));
+    }
+  }
+}
+
 // ---------------------------------------------------------------- RMSNorm
 // rms_norm_row (src/cpu_decoder.rs:289-300): f16(x * inv * w), d % 256 == 0.
 template <typename T>
@@ -93,8 +152,8 @@ __global__ void rmsnorm_kernel(const T* __restrict__ x, int rows, int d,
   for (int k = 0; k < 4; ++k) {
     const int vi = lane + 32 * k;
     if (vi < nv) {
-      const float4 g0 = reinterpret_cast<const float4*>(w)[2 * vi];
-      const float4 g1 = reinterpret_cast<const float4*>(w)[2 * vi + 1];
+      const float4 g0 = __ldg(reinterpret_cast<const float4*>(w) + 2 * vi);
+      const float4 g1 = __ldg(reinterpret_cast<const float4*>(w) + 2 * vi + 1);
       const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
       alignas(16) T e[8];
 #pragma unroll
@@ -180,7 +239,14 @@ int layernorm_rows(const float* x, int rows, int d, const float* g, const float*
   if (rows <= 0) return 0;
   if (d > 1024) return (int)cudaErrorInvalidValue;
   const unsigned blocks = (rows + 7) / 8;
-  if (bf16)
+  const bool vec = d % 4 == 0 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(g) |
+                                   reinterpret_cast<uintptr_t>(b)) & 15u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(out) & 7u) == 0;
+  if (vec && bf16)
+    layernorm_vec_kernel<<<blocks, 256, 0, s>>>(x, rows, d, g, b, eps, static_cast<__nv_bfloat16*>(out));
+  else if (vec)
+    layernorm_vec_kernel<<<blocks, 256, 0, s>>>(x, rows, d, g, b, eps, static_cast<__half*>(out));
+  else if (bf16)
     layernorm_kernel<<<blocks, 256, 0, s>>>(x, rows, d, g, b, eps, static_cast<__nv_bfloat16*>(out));
   else
     layernorm_kernel<<<blocks, 256, 0, s>>>(x, rows, d, g, b, eps, static_cast<__half*>(out));
