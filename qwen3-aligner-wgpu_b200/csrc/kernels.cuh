@@ -27,10 +27,25 @@ struct MelBank {
 };
 
 // Pass 1: log10 mel power of every frame -> scratch [total_frames][128] and
-// per-clip running max (ordered-uint encoding) in maxkey[clip].
-int mel_logpower(const float* samples, const MelClip* clips, int n_clips, int max_frames,
-                 const float* window, const float2* twiddle, MelBank bank, float log10_factor,
-                 float* scratch, unsigned* maxkey, cudaStream_t s);
+// per-clip running max (ordered-uint encoding) in maxkey[clip], on the tensor
+// cores: every frame's 400 reflected samples, scaled by
+// 2^12 and split into f16 hi + lo, are one row of A = [hi | lo | hi]
+// (kMelDftK columns) in frames_ws; dft_hilo is B = [w_hi | w_hi | w_lo] over
+// the Hann-windowed DFT rows (cos for bins [0, 201) at rows [0, 201), -sin at
+// rows [224, 425)), so one GEMM gives re / im of every bin with the three
+// products hi*hi + lo*hi + hi*lo (relative error about 2^-21 per product) into
+// spec_ws [total_frames][kMelDftRows] f32.  Power, filterbank, log10 and the
+// per-clip max then follow the reference's operation order.
+constexpr int kMelDftK = 1200;
+constexpr int kMelDftRows = 448;
+constexpr int kMelImRow = 224;
+int mel_logpower_tc(const float* samples, const MelClip* clips, int n_clips, int max_frames,
+                    int total_frames, const void* dft_hilo, MelBank bank, float log10_factor,
+                    void* frames_ws, float* spec_ws, float* scratch, unsigned* maxkey,
+                    unsigned* status, cudaStream_t s);
+// Host construction of dft_hilo (f16 bits, [kMelDftRows][kMelDftK]) from the
+// f32 periodic Hann window.
+void mel_dft_hilo(const float* window400, uint16_t* out);
 // Pass 2a: clamp at max - 8 and (x + 4) / 4 into the chunked encoder input
 // [chunk][128][chunk_frames] (tail zero padded).
 int mel_finalize_chunked(const float* scratch, const MelClip* clips, const int* chunk_clip,

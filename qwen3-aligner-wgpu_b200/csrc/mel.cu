@@ -5,13 +5,16 @@
 // ascending-bin order, log10 with a 1e-10 floor, per-clip max, clamp at
 // max - 8, (x + 4) / 4, trailing frame dropped (n_samples / 160 frames).
 //
-// Pass 1 computes 16 frames per CTA: the frames' samples (with reflection)
-// are staged in shared memory once, each thread evaluates one DFT bin for 8
-// frames at a time from a 400-entry twiddle table (the direct DFT is 32
-// MFLOP per audio-second — well under a millisecond for a whole batch — and
-// keeps every frame's arithmetic independent of the batch layout), then the
-// sparse filterbank and the log run out of shared memory.  The per-clip
-// maximum is an atomicMax on an order-preserving integer encoding.
+// Pass 1 runs the DFT on the tensor cores: a row builder writes every frame's
+// reflected samples (scaled by 2^12, an exact power of two) as f16 hi + lo
+// parts, one GEMM against the Hann-windowed cos / -sin rows (also split into
+// hi + lo) gives re and im in f32, and a third kernel forms the power (the
+// scaling undone exactly), applies the sparse filterbank and the log, and
+// takes the per-clip maximum as an atomicMax on an order-preserving integer
+// encoding.  Pass 2 clamps and writes the chunked encoder input.
+#include <cmath>
+
+#include "gemm_tc.cuh"
 #include "kernels.cuh"
 #include "sm100.cuh"
 
@@ -24,8 +27,7 @@ constexpr int kBins = 201;
 constexpr int kHop = 160;
 constexpr int kPad = 200;
 constexpr int kMels = 128;
-constexpr int kFT = 16;                          // frames per CTA
-constexpr int kSpan = (kFT - 1) * kHop + kNfft;  // samples staged per CTA
+constexpr int kFT = 16;  // frames per CTA of the power / filterbank kernel
 
 __device__ __forceinline__ long long reflect_index(long long i, long long n) {
   if (n <= 1) return 0;
@@ -43,62 +45,60 @@ __device__ __forceinline__ float key_float(unsigned k) {
   return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
 }
 
-__global__ void __launch_bounds__(256) mel_logpower_kernel(
-    const float* __restrict__ samples, const MelClip* __restrict__ clips,
-    const float* __restrict__ window, const float2* __restrict__ twiddle, MelBank bank,
-    float log10_factor, float* __restrict__ scratch, unsigned* __restrict__ maxkey) {
-  __shared__ float s_x[kSpan];
-  __shared__ float s_win[kNfft];
-  __shared__ float2 s_tw[kNfft];
+// ---- tensor-core pass 1
+constexpr int kFrRows = 8;          // frames per CTA of the row builder
+constexpr float kMelScale = 4096.0f;  // 2^12: keeps the lo halves normal f16
+
+// A rows: frame f of clip c -> row frame_off + f, [hi | lo | hi] of
+// 2^12 * x[reflect(160 f + j - 200)], two samples per thread.
+__global__ void __launch_bounds__(256) mel_frames_kernel(const float* __restrict__ samples,
+                                                         const MelClip* __restrict__ clips,
+                                                         __half* __restrict__ a) {
+  const MelClip c = clips[blockIdx.y];
+  const int f0 = blockIdx.x * kFrRows;
+  if (f0 >= c.n_frames) return;
+  const float* x = samples + c.sample_off;
+  const long long n = c.n_samples;
+  for (int item = threadIdx.x; item < kFrRows * (kNfft / 2); item += blockDim.x) {
+    const int f = f0 + item / (kNfft / 2);
+    if (f >= c.n_frames) break;
+    const int j = 2 * (item % (kNfft / 2));
+    const long long p0 = static_cast<long long>(f) * kHop + j - kPad;
+    const float v0 = x[reflect_index(p0, n)] * kMelScale;
+    const float v1 = x[reflect_index(p0 + 1, n)] * kMelScale;
+    const __half2 hi = __floats2half2_rn(v0, v1);
+    const float2 hf = __half22float2(hi);
+    const __half2 lo = __floats2half2_rn(v0 - hf.x, v1 - hf.y);
+    __half2* row = reinterpret_cast<__half2*>(a + static_cast<long long>(c.frame_off + f) * kMelDftK);
+    row[j / 2] = hi;
+    row[(kNfft + j) / 2] = lo;
+    row[(2 * kNfft + j) / 2] = hi;
+  }
+}
+
+// Power (the scaling undone exactly), filterbank in ascending-bin order, log10,
+// per-clip max, in the reference's operation order.
+__global__ void __launch_bounds__(256) mel_power_kernel(const float* __restrict__ spec,
+                                                        const MelClip* __restrict__ clips,
+                                                        MelBank bank, float log10_factor,
+                                                        float* __restrict__ scratch,
+                                                        unsigned* __restrict__ maxkey) {
   __shared__ float s_pow[kFT][kBins + 1];
   __shared__ unsigned s_max;
-
   const MelClip c = clips[blockIdx.y];
   const int f0 = blockIdx.x * kFT;
   if (f0 >= c.n_frames) return;
   const int nf = min(kFT, c.n_frames - f0);
-  const float* x = samples + c.sample_off;
-  const long long n = c.n_samples;
-
-  for (int i = threadIdx.x; i < kSpan; i += blockDim.x) {
-    const long long pp = static_cast<long long>(f0) * kHop + i;  // index into the padded signal
-    s_x[i] = x[reflect_index(pp - kPad, n)];
-  }
-  for (int i = threadIdx.x; i < kNfft; i += blockDim.x) {
-    s_win[i] = window[i];
-    s_tw[i] = twiddle[i];
-  }
   if (threadIdx.x == 0) s_max = 0u;
-  __syncthreads();
-
-  // DFT power: item = (bin, group of 8 frames)
-  for (int item = threadIdx.x; item < kBins * (kFT / 8); item += blockDim.x) {
-    const int k = item % kBins;
-    const int g = item / kBins;
-    float re[8], im[8];
-#pragma unroll
-    for (int f = 0; f < 8; ++f) re[f] = im[f] = 0.f;
-    int idx = 0;
-    const float* xs = s_x + g * 8 * kHop;
-    for (int j = 0; j < kNfft; ++j) {
-      const float2 t = s_tw[idx];
-      const float wj = s_win[j];
-#pragma unroll
-      for (int f = 0; f < 8; ++f) {
-        const float v = xs[f * kHop + j] * wj;
-        re[f] = fmaf(v, t.x, re[f]);
-        im[f] = fmaf(-v, t.y, im[f]);
-      }
-      idx += k;
-      if (idx >= kNfft) idx -= kNfft;
-    }
-#pragma unroll
-    for (int f = 0; f < 8; ++f)
-      s_pow[g * 8 + f][k] = __fadd_rn(__fmul_rn(re[f], re[f]), __fmul_rn(im[f], im[f]));
+  constexpr float kUnscale = 1.0f / (kMelScale * kMelScale);
+  for (int item = threadIdx.x; item < kFT * kBins; item += blockDim.x) {
+    const int f = item / kBins, k = item % kBins;
+    if (f >= nf) break;
+    const float* r = spec + static_cast<long long>(c.frame_off + f0 + f) * kMelDftRows;
+    const float re = r[k], im = r[kMelImRow + k];
+    s_pow[f][k] = __fmul_rn(__fadd_rn(__fmul_rn(re, re), __fmul_rn(im, im)), kUnscale);
   }
   __syncthreads();
-
-  // filterbank + log10, ascending bins (src/mel.rs:215-234)
   float local_max = -INFINITY;
   for (int item = threadIdx.x; item < kMels * kFT; item += blockDim.x) {
     const int m = item % kMels;
@@ -153,14 +153,47 @@ __global__ void mel_finalize_rows_kernel(const float* __restrict__ scratch, int 
 
 }  // namespace
 
-int mel_logpower(const float* samples, const MelClip* clips, int n_clips, int max_frames,
-                 const float* window, const float2* twiddle, MelBank bank, float log10_factor,
-                 float* scratch, unsigned* maxkey, cudaStream_t s) {
-  if (n_clips <= 0 || max_frames <= 0) return 0;
-  dim3 grid((max_frames + kFT - 1) / kFT, n_clips);
-  mel_logpower_kernel<<<grid, 256, 0, s>>>(samples, clips, window, twiddle, bank, log10_factor,
-                                           scratch, maxkey);
+int mel_logpower_tc(const float* samples, const MelClip* clips, int n_clips, int max_frames,
+                    int total_frames, const void* dft_hilo, MelBank bank, float log10_factor,
+                    void* frames_ws, float* spec_ws, float* scratch, unsigned* maxkey,
+                    unsigned* status, cudaStream_t s) {
+  if (n_clips <= 0 || max_frames <= 0 || total_frames <= 0) return 0;
+  mel_frames_kernel<<<dim3((max_frames + kFrRows - 1) / kFrRows, n_clips), 256, 0, s>>>(
+      samples, clips, static_cast<__half*>(frames_ws));
+  int rc = (int)cudaGetLastError();
+  if (rc) return rc;
+  EpiParams ep;
+  ep.mode = EPI_STORE32;
+  ep.out = spec_ws;
+  ep.ldo = kMelDftRows;
+  ep.status = status;
+  rc = gemm_tc(frames_ws, kMelDftK, dft_hilo, kMelDftK, total_frames, kMelDftRows, kMelDftK, false,
+               ep, s);
+  if (rc) return rc;
+  mel_power_kernel<<<dim3((max_frames + kFT - 1) / kFT, n_clips), 256, 0, s>>>(
+      spec_ws, clips, bank, log10_factor, scratch, maxkey);
   return (int)cudaGetLastError();
+}
+
+void mel_dft_hilo(const float* window400, uint16_t* out) {
+  for (int n = 0; n < kMelDftRows * kMelDftK; ++n) out[n] = 0;
+  for (int n = 0; n < kMelDftRows; ++n) {
+    const bool is_re = n < kBins;
+    const bool is_im = n >= kMelImRow && n < kMelImRow + kBins;
+    if (!is_re && !is_im) continue;
+    const int k = is_re ? n : n - kMelImRow;
+    for (int j = 0; j < kNfft; ++j) {
+      const double ang = 2.0 * M_PI * static_cast<double>((k * j) % kNfft) / kNfft;
+      const double t = is_re ? std::cos(ang) : -std::sin(ang);
+      const float w = static_cast<float>(static_cast<double>(window400[j]) * t);
+      const __half hi = __float2half_rn(w);
+      const __half lo = __float2half_rn(w - __half2float(hi));
+      uint16_t* row = out + static_cast<long long>(n) * kMelDftK;
+      row[j] = __half_as_ushort(hi);
+      row[kNfft + j] = __half_as_ushort(hi);
+      row[2 * kNfft + j] = __half_as_ushort(lo);
+    }
+  }
 }
 
 int mel_finalize_chunked(const float* scratch, const MelClip* clips, const int* chunk_clip,

@@ -462,15 +462,12 @@ int load_weights(qa_ctx* ctx, const qa_tensor* tensors, int n, const qa_cfg& c) 
       const float x = 2.0f * static_cast<float>(M_PI) * static_cast<float>(i) / 400.0f;
       win[i] = 0.5f * (1.0f - std::cos(x));
     }
-    std::vector<float2> tw(400);
-    for (int k = 0; k < 400; ++k)
-      tw[k] = make_float2(static_cast<float>(std::cos(2.0 * M_PI * k / 400.0)),
-                          static_cast<float>(std::sin(2.0 * M_PI * k / 400.0)));
     std::vector<int> st, ln, wo;
     std::vector<float> fw;
     mel_bank(st, ln, wo, fw);
-    W.window = up_f32(ctx, win, &rc);
-    W.twiddle = upload<float2>(ctx, tw.data(), tw.size() * sizeof(float2), &rc);
+    std::vector<uint16_t> dft(static_cast<size_t>(kMelDftRows) * kMelDftK);
+    mel_dft_hilo(win.data(), dft.data());
+    W.mel_dft = upload<uint16_t>(ctx, dft.data(), dft.size() * 2, &rc);
     W.fb_start = upload<int>(ctx, st.data(), st.size() * 4, &rc);
     W.fb_len = upload<int>(ctx, ln.data(), ln.size() * 4, &rc);
     W.fb_woff = upload<int>(ctx, wo.data(), wo.size() * 4, &rc);
@@ -1118,6 +1115,7 @@ int qa_close(qa_ctx* ctx) {
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   for (void* p : ctx->allocations) cudaFree(p);
   DevBuf* bufs[] = {&ctx->samples, &ctx->mel_scratch, &ctx->mel_chunked, &ctx->maxkey,
+                    &ctx->mel_frames, &ctx->mel_spec,
                     &ctx->clips_dev, &ctx->idx_dev, &ctx->act1, &ctx->cols, &ctx->act2,
                     &ctx->act3, &ctx->xenc, &ctx->h16a, &ctx->qkv_enc, &ctx->attn_enc,
                     &ctx->ffn_enc, &ctx->proj1, &ctx->emb_out, &ctx->hid, &ctx->xn, &ctx->qkv,
@@ -1178,6 +1176,8 @@ int qa_mel(qa_ctx* ctx, const float* samples, int64_t n, float* out, int64_t out
   TRY(ensure(ctx, ctx->samples, n * 4));
   TRY(ensure(ctx, ctx->mel_scratch, static_cast<size_t>(frames) * 128 * 4));
   TRY(ensure(ctx, ctx->mel_chunked, static_cast<size_t>(frames) * 128 * 4));
+  TRY(ensure(ctx, ctx->mel_frames, static_cast<size_t>(frames) * kMelDftK * 2));
+  TRY(ensure(ctx, ctx->mel_spec, static_cast<size_t>(frames) * kMelDftRows * 4));
   TRY(ensure(ctx, ctx->maxkey, 16));
   TRY(ensure(ctx, ctx->clips_dev, sizeof(MelClip)));
   MelClip mc{0, static_cast<int>(n), 0, frames, 0};
@@ -1186,9 +1186,12 @@ int qa_mel(qa_ctx* ctx, const float* samples, int64_t n, float* out, int64_t out
   CK(cudaMemsetAsync(ctx->maxkey.p, 0, 4, s));
   const Weights& W = ctx->w;
   MelBank bank{W.fb_start, W.fb_len, W.fb_woff, W.fb_w};
-  KL("mel", 0, 4.0 * n + 512.0 * frames, mel_logpower(ctx->samples.as<float>(), ctx->clips_dev.as<MelClip>(), 1, frames, W.window,
-                  W.twiddle, bank, 1.0f / std::log(10.0f), ctx->mel_scratch.as<float>(),
-                  ctx->maxkey.as<unsigned>(), s));
+  KL("mel", 2.0 * frames * kMelDftRows * kMelDftK, 4.0 * n + 512.0 * frames,
+     mel_logpower_tc(ctx->samples.as<float>(), ctx->clips_dev.as<MelClip>(), 1, frames, frames,
+                     W.mel_dft, bank, 1.0f / std::log(10.0f), ctx->mel_frames.p,
+                     ctx->mel_spec.as<float>(), ctx->mel_scratch.as<float>(),
+                     ctx->maxkey.as<unsigned>(), ctx->status.as<unsigned>(), s));
+  ctx->launches += 2;  // mel_logpower_tc is three launches (rows, GEMM, power)
   KL("mel_finalize", 0, 1024.0 * frames, mel_finalize_rows(ctx->mel_scratch.as<float>(), frames, ctx->maxkey.as<unsigned>(),
                        ctx->mel_chunked.as<float>(), s));
   CK(cudaMemcpyAsync(out, ctx->mel_chunked.p, static_cast<size_t>(frames) * 128 * 4,
@@ -1411,6 +1414,8 @@ int qa_batch_stage(qa_ctx* ctx, const qa_clip* clips, int n, const qa_result* re
   const int H = c.hidden_size;
   TRY(ensure(ctx, ctx->mel_scratch, static_cast<size_t>(P.total_frames) * 128 * 4));
   TRY(ensure(ctx, ctx->mel_chunked, static_cast<size_t>(P.total_chunks) * 128 * cs * 4));
+  TRY(ensure(ctx, ctx->mel_frames, static_cast<size_t>(P.total_frames) * kMelDftK * 2));
+  TRY(ensure(ctx, ctx->mel_spec, static_cast<size_t>(P.total_frames) * kMelDftRows * 4));
   TRY(ensure(ctx, ctx->maxkey, static_cast<size_t>(n) * 4));
   TRY(ensure(ctx, ctx->hid, static_cast<size_t>(P.T_d) * H * 2));
   S.seq = ++ctx->batch_seq;
@@ -1441,9 +1446,13 @@ int qa_batch_run(qa_ctx* ctx) {
   CK(cudaMemsetAsync(ctx->maxkey.p, 0, static_cast<size_t>(n) * 4, s));
   const Weights& W = ctx->w;
   MelBank bank{W.fb_start, W.fb_len, W.fb_woff, W.fb_w};
-  KL("mel", 0, 4.0 * P.mel.back().sample_off + 4.0 * P.mel.back().n_samples + 512.0 * P.total_frames,
-     mel_logpower(S.samples.as<float>(), D.mel, n, P.max_frames, W.window, W.twiddle, bank,
-                  1.0f / std::log(10.0f), ctx->mel_scratch.as<float>(), ctx->maxkey.as<unsigned>(), s));
+  KL("mel", 2.0 * P.total_frames * kMelDftRows * kMelDftK,
+     4.0 * P.mel.back().sample_off + 4.0 * P.mel.back().n_samples + 512.0 * P.total_frames,
+     mel_logpower_tc(S.samples.as<float>(), D.mel, n, P.max_frames, P.total_frames, W.mel_dft,
+                     bank, 1.0f / std::log(10.0f), ctx->mel_frames.p, ctx->mel_spec.as<float>(),
+                     ctx->mel_scratch.as<float>(), ctx->maxkey.as<unsigned>(),
+                     ctx->status.as<unsigned>(), s));
+  ctx->launches += 2;  // mel_logpower_tc is three launches (rows, GEMM, power)
   KL("mel_finalize", 0, 512.0 * P.total_frames + 512.0 * P.total_chunks * cs,
      mel_finalize_chunked(ctx->mel_scratch.as<float>(), D.mel, D.chunk_clip, P.total_chunks, cs,
                           ctx->maxkey.as<unsigned>(), ctx->mel_chunked.as<float>(), s));

@@ -53,8 +53,7 @@ struct DecLayerW {
 
 struct Weights {
   // mel constants
-  float* window;     // [400]
-  float2* twiddle;   // [400]
+  void* mel_dft;     // [kMelDftRows][kMelDftK] f16: windowed DFT rows as [hi | hi | lo]
   int *fb_start, *fb_len, *fb_woff;
   float* fb_w;
   // conv stem
@@ -170,6 +169,7 @@ struct qa_ctx {
   std::vector<void*> allocations;  // weights, freed at close
   // workspace (grow-only)
   qa::DevBuf samples, mel_scratch, mel_chunked, maxkey, clips_dev, idx_dev;
+  qa::DevBuf mel_frames, mel_spec;  // tensor-core mel: A rows, re / im
   qa::DevBuf act1, cols, act2, act3, xenc, h16a, qkv_enc, attn_enc, ffn_enc, proj1;
   qa::DevBuf emb_out, hid, xn, qkv, attn, mlp, kcache, vcache;
   qa::DevBuf head_a, head_keys, head_raw, head_logits, head_normed, hidden_f32, status, badflag;
