@@ -47,33 +47,46 @@ __global__ void __launch_bounds__(256) conv1_kernel(const float* __restrict__ me
   const int oh = oh0 + rr;
   if (rr >= 2 || oh >= ho) return;
   const int oc = quad * kC1Ch;
-  float wk[kC1Ch][9], b[kC1Ch];
+  // channel pairs (oc, oc+1) and (oc+2, oc+3) as f32x2 lanes: every packed
+  // instruction rounds each lane exactly as the scalar one would
+  float2 wk[kC1Ch / 2][9], b[kC1Ch / 2];
 #pragma unroll
-  for (int c = 0; c < kC1Ch; ++c) {
+  for (int c = 0; c < kC1Ch / 2; ++c) {
 #pragma unroll
-    for (int k = 0; k < 9; ++k) wk[c][k] = wt[(oc + c) * 9 + k];
-    b[c] = bias[oc + c];
+    for (int k = 0; k < 9; ++k)
+      wk[c][k] = make_float2(wt[(oc + 2 * c) * 9 + k], wt[(oc + 2 * c + 1) * 9 + k]);
+    b[c] = make_float2(bias[oc + 2 * c], bias[oc + 2 * c + 1]);
   }
+  const float2 kRsqrt2 = make_float2(0.70710678118654752f, 0.70710678118654752f);
+  const float2 kHalf = make_float2(0.5f, 0.5f), kOne = make_float2(1.0f, 1.0f);
   const float* rows = s_in + 2 * rr * wp;  // input rows 2*oh - 1 .. 2*oh + 1 (padded)
   T* dst = out + (static_cast<long long>(chunk) * ho + oh) * wo * ldc + oc;
 #pragma unroll 2
   for (int ow = 0; ow < wo; ++ow) {
-    float a[kC1Ch];
+    float2 a[kC1Ch / 2];
 #pragma unroll
-    for (int c = 0; c < kC1Ch; ++c) a[c] = 0.0f;
+    for (int c = 0; c < kC1Ch / 2; ++c) a[c] = make_float2(0.0f, 0.0f);
 #pragma unroll
     for (int kh = 0; kh < 3; ++kh)
 #pragma unroll
       for (int kw = 0; kw < 3; ++kw) {
         const float v = rows[kh * wp + 2 * ow + kw];  // column 2*ow + kw - 1, shifted by the pad
+        const float2 vv = make_float2(v, v);
 #pragma unroll
-        for (int c = 0; c < kC1Ch; ++c) a[c] = fmaf(wk[c][kh * 3 + kw], v, a[c]);
+        for (int c = 0; c < kC1Ch / 2; ++c) a[c] = fma2_rn(wk[c][kh * 3 + kw], vv, a[c]);
       }
-    alignas(8) T pr[kC1Ch];
+    uint32_t pr[kC1Ch / 2];
 #pragma unroll
-    for (int c = 0; c < kC1Ch; ++c) pr[c] = f2h<T>(gelu_erf(a[c] + b[c]));  // taps, then bias
-    *reinterpret_cast<uint2*>(dst + static_cast<long long>(ow) * ldc) =
-        *reinterpret_cast<const uint2*>(pr);
+    for (int c = 0; c < kC1Ch / 2; ++c) {
+      // gelu_erf on both lanes: taps, then bias; 0.5 * x * (1 + erf(x / sqrt 2))
+      const float2 x = add2_rn(a[c], b[c]);
+      const float2 z = mul2_rn(x, kRsqrt2);
+      const float2 g = mul2_rn(mul2_rn(kHalf, x), add2_rn(kOne, make_float2(erff(z.x), erff(z.y))));
+      const T lo = f2h<T>(g.x), hi = f2h<T>(g.y);
+      pr[c] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&lo)) |
+              (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&hi)) << 16);
+    }
+    *reinterpret_cast<uint2*>(dst + static_cast<long long>(ow) * ldc) = make_uint2(pr[0], pr[1]);
   }
 }
 

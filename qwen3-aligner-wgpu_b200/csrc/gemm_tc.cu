@@ -100,23 +100,6 @@ __device__ __forceinline__ float word_half(uint32_t w, int hi) {
   return h2f<T>(*reinterpret_cast<const T*>(&b));
 }
 
-// Packed f32 pairs (sm_100 f32x2 arithmetic: one instruction, two
-// separately rounded lanes, so the results equal two scalar __fmul_rn /
-// __fadd_rn).
-__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
-  uint64_t r;
-  asm("mul.rn.f32x2 %0, %1, %2;"
-      : "=l"(r)
-      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)));
-  return *reinterpret_cast<const float2*>(&r);
-}
-__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
-  uint64_t r;
-  asm("add.rn.f32x2 %0, %1, %2;"
-      : "=l"(r)
-      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)));
-  return *reinterpret_cast<const float2*>(&r);
-}
 
 // The two 16-bit values of a packed word, widened.
 template <typename T>

@@ -557,6 +557,32 @@ __device__ __forceinline__ bool mbar_wait_cluster_warp(uint64_t* bar, uint32_t p
   return __all_sync(0xFFFFFFFFu, mbar_wait_cluster(bar, parity));
 }
 
+// ---------------------------------------------------------------- packed f32 pairs
+// sm_100 f32x2 arithmetic: one instruction, two separately rounded lanes, so
+// the results equal two scalar __fmul_rn / __fadd_rn / fmaf.
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;"
+      : "=l"(r)
+      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)));
+  return *reinterpret_cast<const float2*>(&r);
+}
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;"
+      : "=l"(r)
+      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)));
+  return *reinterpret_cast<const float2*>(&r);
+}
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(r)
+      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)),
+        "l"(*reinterpret_cast<const uint64_t*>(&c)));
+  return *reinterpret_cast<const float2*>(&r);
+}
+
 // ---------------------------------------------------------------- 16-bit helpers
 
 template <typename T>
