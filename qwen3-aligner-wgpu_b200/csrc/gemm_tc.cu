@@ -163,29 +163,40 @@ __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem
   }
   if (is_v) {
 #pragma unroll 1
-    for (int c = 0; c < HD / 32; ++c) {
-      float v[32];
-      tmem_ld32(tmem_col0 + c * 32, v);  // warp-collective: every lane loads
+    for (int c = 0; c < HD / 32; c += 2) {
+      float v[2][32];
+      tmem_ld2x32(tmem_col0 + c * 32, tmem_col0 + (c + 1) * 32, v[0], v[1]);  // warp-collective
       if (!ok) continue;
-      uint32_t w[16];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) w[i] = pack2_rn<T>(make_float2(v[2 * i], v[2 * i + 1]));
+      for (int h = 0; h < 2; ++h) {
+        uint32_t w[16];
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        reinterpret_cast<uint4*>(dst + c * 32)[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+        for (int i = 0; i < 16; ++i) w[i] = pack2_rn<T>(make_float2(v[h][2 * i], v[h][2 * i + 1]));
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          reinterpret_cast<uint4*>(dst + (c + h) * 32)[j] =
+              make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+      }
     }
     return;
   }
-  // pass 1: sum of squares of the rounded values
+  // pass 1: sum of squares of the rounded values (two 32-column chunks per wait)
   float2 s2a = make_float2(0.0f, 0.0f), s2b = make_float2(0.0f, 0.0f);
 #pragma unroll 1
-  for (int c = 0; c < HD / 32; ++c) {
-    float v[32];
-    tmem_ld32(tmem_col0 + c * 32, v);
+  for (int c = 0; c < HD / 32; c += 2) {
+    float v[32], w[32];
+    tmem_ld2x32(tmem_col0 + c * 32, tmem_col0 + (c + 1) * 32, v, w);
 #pragma unroll
     for (int i = 0; i < 32; i += 4) {
       const float2 x0 = make_float2(round16<T>(v[i]), round16<T>(v[i + 1]));
       const float2 x1 = make_float2(round16<T>(v[i + 2]), round16<T>(v[i + 3]));
+      s2a = add2_rn(s2a, mul2_rn(x0, x0));
+      s2b = add2_rn(s2b, mul2_rn(x1, x1));
+    }
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      const float2 x0 = make_float2(round16<T>(w[i]), round16<T>(w[i + 1]));
+      const float2 x1 = make_float2(round16<T>(w[i + 2]), round16<T>(w[i + 3]));
       s2a = add2_rn(s2a, mul2_rn(x0, x0));
       s2b = add2_rn(s2b, mul2_rn(x1, x1));
     }
@@ -200,8 +211,7 @@ __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem
 #pragma unroll 1
   for (int c = 0; c < 2; ++c) {
     float va[32], vb[32];
-    tmem_ld32(tmem_col0 + c * 32, va);
-    tmem_ld32(tmem_col0 + 64 + c * 32, vb);
+    tmem_ld2x32(tmem_col0 + c * 32, tmem_col0 + 64 + c * 32, va, vb);
     if (!ok) continue;
 #pragma unroll
     for (int j0 = 0; j0 < 32; j0 += 8) {
@@ -266,8 +276,7 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
 #pragma unroll 1
     for (int c0 = cb; c0 < ce; c0 += 32) {
       float g[32], u[32];
-      tmem_ld32(tmem_row + c0, g);
-      tmem_ld32(tmem_row + H + c0, u);
+      tmem_ld2x32(tmem_row + c0, tmem_row + H + c0, g, u);
       if (row < M) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
@@ -317,14 +326,12 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
     return;
   }
 
-#pragma unroll 1
-  for (int c0 = cb; c0 < ce; c0 += 32) {
-    float v[32];
-    tmem_ld32(tmem_row + c0, v);
-    if (row >= M) continue;
+  // one 32-column chunk: bias, then the mode's operation
+  auto chunk = [&](int c0, float (&v)[32]) {
+    if (row >= M) return;
     const int col = n0 + c0;
     const int nc = min(min(32, BN - c0), N - col);  // BN need not be a multiple of 32
-    if (nc <= 0) continue;
+    if (nc <= 0) return;
     if (ep.bias) {
       const float* bp = ep.bias + col;
       if (vec_ok(bp, nc)) {
@@ -406,6 +413,19 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
       }
       default:
         break;
+    }
+  };
+  // chunks are read from TMEM two at a time behind one wait
+#pragma unroll 1
+  for (int c0 = cb; c0 < ce; c0 += 64) {
+    float v[32], w[32];
+    if (c0 + 32 < ce) {
+      tmem_ld2x32(tmem_row + c0, tmem_row + c0 + 32, v, w);
+      chunk(c0, v);
+      chunk(c0 + 32, w);
+    } else {
+      tmem_ld32(tmem_row + c0, v);
+      chunk(c0, v);
     }
   }
 }
