@@ -16,6 +16,9 @@
 // XOR-swizzled shared memory.  Rows past a clip's or window's end are
 // zero-filled on load (0·NaN from stale cache rows would otherwise poison the
 // P·V product) and masked to -inf in the scores.
+#include <algorithm>
+
+#include "gemm_tc.cuh"
 #include "kernels.cuh"
 #include "sm100.cuh"
 
@@ -268,33 +271,41 @@ __global__ void __launch_bounds__(128 * REP)
 }
 
 // ======================================================================
-// Audio tower: windowed attention, HD = 64, window <= 128, one CTA per
-// (window, head), 8 warps x 16 query rows.
+// Audio tower: windowed attention, HD = 64, window <= 128.  Persistent: each
+// CTA (8 warps x 16 query rows) walks items (window, head) = blockIdx.x,
+// +gridDim.x, ... with the next item's Q, K and V prefetched by cp.async into
+// the other of two shared-memory stages while the current item computes.
 // ======================================================================
-template <typename T>
-__global__ void __launch_bounds__(256)
-    window_attn_kernel(const T* __restrict__ qkv, int dm, const int2* __restrict__ windows,
-                       T* __restrict__ out, float scale_log2) {
-  constexpr int HD = 64, W = 128, CPR = HD * 2 / 16;  // 8 chunks per row
-  __shared__ __align__(128) uint8_t sQ[W * HD * 2];
-  __shared__ __align__(128) uint8_t sK[W * HD * 2];
-  __shared__ __align__(128) uint8_t sV[W * HD * 2];
-  const int2 win = windows[blockIdx.x];
-  const int head = blockIdx.y;
-  const int len = win.y;
-  const long long ld = 3LL * dm;
-  for (int i = threadIdx.x; i < W * CPR; i += 256) {
-    const int c = i % CPR, r = i / CPR;
-    const bool ok = r < len;
-    const T* row = qkv + (static_cast<long long>(win.x) + (ok ? r : 0)) * ld + head * HD + c * 8;
-    cp_async16(sQ + swz<CPR>(r, c), row, ok);
-    cp_async16(sK + swz<CPR>(r, c), row + dm, ok);
-    cp_async16(sV + swz<CPR>(r, c), row + 2 * dm, ok);
-  }
-  cp_async_commit();
-  cp_async_wait<0>();
-  __syncthreads();
+constexpr int kWinHD = 64, kWinW = 128, kWinCPR = kWinHD * 2 / 16;  // 8 chunks per row
+constexpr int kWinStage = 3 * kWinW * kWinHD * 2;                  // Q, K, V: 48 KB
+constexpr int kWinSmem = 2 * kWinStage;
 
+template <typename T>
+__device__ __forceinline__ void window_load(const T* __restrict__ qkv, int dm, int2 win, int head,
+                                            uint8_t* st) {
+  const long long ld = 3LL * dm;
+  uint8_t* sQ = st;
+  uint8_t* sK = st + kWinW * kWinHD * 2;
+  uint8_t* sV = sK + kWinW * kWinHD * 2;
+  for (int i = threadIdx.x; i < kWinW * kWinCPR; i += 256) {
+    const int c = i % kWinCPR, r = i / kWinCPR;
+    const bool ok = r < win.y;
+    const T* row = qkv + (static_cast<long long>(win.x) + (ok ? r : 0)) * ld + head * kWinHD + c * 8;
+    cp_async16(sQ + swz<kWinCPR>(r, c), row, ok);
+    cp_async16(sK + swz<kWinCPR>(r, c), row + dm, ok);
+    cp_async16(sV + swz<kWinCPR>(r, c), row + 2 * dm, ok);
+  }
+}
+
+// One item: this warp's 16 query rows against the window's keys.
+template <typename T>
+__device__ __forceinline__ void window_item(const uint8_t* st, int2 win, int head, int dm,
+                                            T* __restrict__ out, float scale_log2) {
+  constexpr int HD = kWinHD, W = kWinW, CPR = kWinCPR;
+  const uint8_t* sQ = st;
+  const uint8_t* sK = st + W * HD * 2;
+  const uint8_t* sV = sK + W * HD * 2;
+  const int len = win.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wrow = warp * 16;
   if (wrow >= len) return;
@@ -320,16 +331,15 @@ __global__ void __launch_bounds__(256)
       mma16816<T>(s[2 * np], qf[ks], b[0], b[1]);
       mma16816<T>(s[2 * np + 1], qf[ks], b[2], b[3]);
     }
+  // raw scores: masked keys (past the window) at -inf, row max over the rest
   float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
   for (int nt = 0; nt < W / 8; ++nt)
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int key = nt * 8 + 2 * tq + (e & 1);
-      float v = s[nt][e] * scale_log2;
-      if (key >= len) v = -INFINITY;
-      s[nt][e] = v;
-      mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      if (key >= len) s[nt][e] = -INFINITY;
+      mx[e >> 1] = fmaxf(mx[e >> 1], s[nt][e]);
     }
   float rs[2] = {0.f, 0.f};
 #pragma unroll
@@ -337,11 +347,13 @@ __global__ void __launch_bounds__(256)
     mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xFFFFFFFFu, mx[h], 1));
     mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xFFFFFFFFu, mx[h], 2));
   }
+  // 2^((s - max) * scale_log2) = e^((s - max) / sqrt(64)), one FMA + ex2 each
+  const float neg[2] = {-mx[0] * scale_log2, -mx[1] * scale_log2};
 #pragma unroll
   for (int nt = 0; nt < W / 8; ++nt)
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const float p = exp2f(s[nt][e] - mx[e >> 1]);
+      const float p = ex2_approx(fmaf(s[nt][e], scale_log2, neg[e >> 1]));
       s[nt][e] = p;
       rs[e >> 1] += p;
     }
@@ -383,6 +395,31 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+template <typename T>
+__global__ void __launch_bounds__(256, 2)
+    window_attn_kernel(const T* __restrict__ qkv, int dm, int nh, const int2* __restrict__ windows,
+                       int n_items, T* __restrict__ out, float scale_log2) {
+  extern __shared__ __align__(128) uint8_t wsm[];
+  int i = blockIdx.x;
+  if (i >= n_items) return;
+  window_load<T>(qkv, dm, windows[i / nh], i % nh, wsm);
+  cp_async_commit();
+  for (int k = 0; i < n_items; i += gridDim.x, ++k) {
+    uint8_t* cur = wsm + (k & 1) * kWinStage;
+    const int nx = i + gridDim.x;
+    if (nx < n_items) {  // the other stage was last read by item k-1 (behind the barrier below)
+      window_load<T>(qkv, dm, windows[nx / nh], nx % nh, wsm + ((k + 1) & 1) * kWinStage);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    window_item<T>(cur, windows[i / nh], i % nh, dm, out, scale_log2);
+    __syncthreads();  // the next prefetch overwrites this stage
+  }
+}
+
 }  // namespace
 
 int causal_attention(const void* qkv, long long ldq, int nqh, int nkvh, int hd,
@@ -413,13 +450,21 @@ int window_attention(const void* qkv, int dm, int nh, int hd, const int2* window
   if (n_windows <= 0) return 0;
   if (hd != 64 || dm != nh * hd) return (int)cudaErrorInvalidValue;
   const float sl2 = (1.0f / sqrtf(64.0f)) * kLog2e;
-  dim3 grid(n_windows, nh);
-  if (bf16)
-    window_attn_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
-        static_cast<const __nv_bfloat16*>(qkv), dm, windows, static_cast<__nv_bfloat16*>(out), sl2);
-  else
-    window_attn_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(qkv), dm, windows,
-                                                    static_cast<__half*>(out), sl2);
+  const int n_items = n_windows * nh;
+  const int grid = std::min(n_items, 2 * device_sm_count());  // two CTAs (96 KB each) per SM
+  if (bf16) {
+    auto k = window_attn_kernel<__nv_bfloat16>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kWinSmem);
+    if (e != cudaSuccess) return (int)e;
+    k<<<grid, 256, kWinSmem, s>>>(static_cast<const __nv_bfloat16*>(qkv), dm, nh, windows, n_items,
+                                 static_cast<__nv_bfloat16*>(out), sl2);
+  } else {
+    auto k = window_attn_kernel<__half>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kWinSmem);
+    if (e != cudaSuccess) return (int)e;
+    k<<<grid, 256, kWinSmem, s>>>(static_cast<const __half*>(qkv), dm, nh, windows, n_items,
+                                 static_cast<__half*>(out), sl2);
+  }
   return (int)cudaGetLastError();
 }
 
