@@ -400,6 +400,8 @@ __global__ void __launch_bounds__(256, 2)
     window_attn_kernel(const T* __restrict__ qkv, int dm, int nh, const int2* __restrict__ windows,
                        int n_items, T* __restrict__ out, float scale_log2) {
   extern __shared__ __align__(128) uint8_t wsm[];
+  pdl_wait();  // the previous kernel's results are visible from here
+  pdl_trigger();
   int i = blockIdx.x;
   if (i >= n_items) return;
   window_load<T>(qkv, dm, windows[i / nh], i % nh, wsm);
@@ -456,14 +458,16 @@ int window_attention(const void* qkv, int dm, int nh, int hd, const int2* window
     auto k = window_attn_kernel<__nv_bfloat16>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kWinSmem);
     if (e != cudaSuccess) return (int)e;
-    k<<<grid, 256, kWinSmem, s>>>(static_cast<const __nv_bfloat16*>(qkv), dm, nh, windows, n_items,
-                                 static_cast<__nv_bfloat16*>(out), sl2);
+    e = launch_pdl(k, dim3(grid), dim3(256), kWinSmem, s, static_cast<const __nv_bfloat16*>(qkv), dm,
+                   nh, windows, n_items, static_cast<__nv_bfloat16*>(out), sl2);
+    if (e != cudaSuccess) return (int)e;
   } else {
     auto k = window_attn_kernel<__half>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kWinSmem);
     if (e != cudaSuccess) return (int)e;
-    k<<<grid, 256, kWinSmem, s>>>(static_cast<const __half*>(qkv), dm, nh, windows, n_items,
-                                 static_cast<__half*>(out), sl2);
+    e = launch_pdl(k, dim3(grid), dim3(256), kWinSmem, s, static_cast<const __half*>(qkv), dm, nh,
+                   windows, n_items, static_cast<__half*>(out), sl2);
+    if (e != cudaSuccess) return (int)e;
   }
   return (int)cudaGetLastError();
 }

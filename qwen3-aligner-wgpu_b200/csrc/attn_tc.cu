@@ -222,6 +222,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tslot;
+  pdl_wait();  // the previous kernel's results are visible from here
+  pdl_trigger();
   const uint32_t tS0 = tbase, tO0 = tbase + 256;  // S_h at tS0 + 128 h, O_h at tO0 + 128 h
   auto fail = [&]() {
     *abort_flag = 1;
@@ -540,12 +542,14 @@ int causal_attention_tc(const void* qkv, long long ldq, long long q_rows, int nq
     auto k = attn_tc_kernel<__nv_bfloat16>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
     if (e != cudaSuccess) return (int)e;
-    k<<<grid, kThreads, kSmem, s>>>(tq, tk, tv, ap);
+    e = launch_pdl(k, dim3(grid), dim3(kThreads), kSmem, s, tq, tk, tv, ap);
+    if (e != cudaSuccess) return (int)e;
   } else {
     auto k = attn_tc_kernel<__half>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
     if (e != cudaSuccess) return (int)e;
-    k<<<grid, kThreads, kSmem, s>>>(tq, tk, tv, ap);
+    e = launch_pdl(k, dim3(grid), dim3(kThreads), kSmem, s, tq, tk, tv, ap);
+    if (e != cudaSuccess) return (int)e;
   }
   return (int)cudaGetLastError();
 }

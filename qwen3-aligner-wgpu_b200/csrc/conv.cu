@@ -32,6 +32,9 @@ __global__ void __launch_bounds__(256) conv1_kernel(const float* __restrict__ me
                                                     const float* __restrict__ bias, int c_out,
                                                     int ldc, T* __restrict__ out) {
   extern __shared__ float s_in[];  // [5][w + 2]
+  pdl_wait();  // the previous kernel's results are visible from here
+  pdl_trigger();
+
   const int ho = (h + 2 - 3) / 2 + 1, wo = (w + 2 - 3) / 2 + 1;
   const int wp = w + 2;
   const int chunk = blockIdx.y, oh0 = 2 * blockIdx.x;
@@ -129,12 +132,10 @@ int conv1_direct(const float* mel, int n, int h, int w, const float* wt, const f
   const size_t smem = 5 * (w + 2) * sizeof(float);
   dim3 grid((ho + 1) / 2, n);
   if (bf16)
-    conv1_kernel<__nv_bfloat16><<<grid, 256, smem, s>>>(mel, h, w, wt, bias, c_out, ldc,
-                                                        static_cast<__nv_bfloat16*>(out));
-  else
-    conv1_kernel<__half><<<grid, 256, smem, s>>>(mel, h, w, wt, bias, c_out, ldc,
-                                                 static_cast<__half*>(out));
-  return (int)cudaGetLastError();
+    return (int)launch_pdl(conv1_kernel<__nv_bfloat16>, grid, dim3(256), smem, s, mel, h, w, wt,
+                           bias, c_out, ldc, static_cast<__nv_bfloat16*>(out));
+  return (int)launch_pdl(conv1_kernel<__half>, grid, dim3(256), smem, s, mel, h, w, wt, bias,
+                         c_out, ldc, static_cast<__half*>(out));
 }
 
 int im2col_3x3s2(const void* x, int n, int h, int w, int c, void* cols, bool time_major,

@@ -501,6 +501,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tslot;
+  pdl_wait();  // the previous kernel's results are visible from here
+  pdl_trigger();
 
   auto timed_out = [&]() {
     *abort_flag = 1;
@@ -668,6 +670,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
   tc_fence_after();
   const uint32_t tbase = *tslot;
+  pdl_wait();  // the previous kernel's results are visible from here
+  pdl_trigger();
 
   auto timed_out = [&]() {
     *abort_flag = 1;
@@ -849,6 +853,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tslot;
+  pdl_wait();  // the previous kernel's results are visible from here
+  pdl_trigger();
 
   auto timed_out = [&]() {
     *abort_flag = 1;
@@ -1020,6 +1026,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tbase = *tslot;
+  pdl_wait();  // the previous kernel's results are visible from here
+  pdl_trigger();
 
   auto timed_out = [&]() {
     *abort_flag = 1;
@@ -1212,6 +1220,8 @@ __global__ void __launch_bounds__(288, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tslot;
+  pdl_wait();  // the previous kernel's results are visible from here
+  pdl_trigger();
   auto timed_out = [&]() {
     *abort_flag = 1;
     if (ep.status) atomicOr(ep.status, kStatusTimeout);
@@ -1364,7 +1374,9 @@ int launch_conv(const void* x, const ConvGeom& g, const void* B, int M, int N, i
   if (e != cudaSuccess) return (int)e;
   const int tiles = ((N + BN - 1) / BN) * ((M + kBM - 1) / kBM);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  kern<<<grid, 288, Cfg::kSmem, stream>>>(static_cast<const T*>(x), g, tb, M, N, K, ep);
+  e = launch_pdl(kern, dim3(grid), dim3(288), Cfg::kSmem, stream, static_cast<const T*>(x), g, tb,
+                 M, N, K, ep);
+  if (e != cudaSuccess) return (int)e;
   return (int)cudaGetLastError();
 }
 
@@ -1400,11 +1412,13 @@ int launch_conv_pair(const void* x, int n, int h, int w, int c, const void* wt, 
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmem);
   if (e != cudaSuccess) return (int)e;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // added for the launch
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.blockDim = dim3(kGemmThreads, 1, 1);
   cfg.dynamicSmemBytes = Cfg::kSmem;
   cfg.stream = stream;
@@ -1423,6 +1437,7 @@ int launch_conv_pair(const void* x, int n, int h, int w, int c, const void* wt, 
   const int tiles = (N / BN) * ((g.n_mtiles + 1) / 2);
   const int pairs = tiles < max_pairs[dev] ? tiles : max_pairs[dev];
   cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.numAttrs = 2;  // cluster + programmatic serialization
   e = cudaLaunchKernelEx(&cfg, kern, tx, tb, g, N, K, ep);
   if (e != cudaSuccess) return (int)e;
   return (int)cudaGetLastError();
@@ -1463,7 +1478,8 @@ int launch_conv_tma(const void* x, int n, int h, int w, int c, const void* wt, i
   if (e != cudaSuccess) return (int)e;
   const int tiles = ((N + BN - 1) / BN) * g.n_mtiles;
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  kern<<<grid, kGemmThreads, Cfg::kSmem, stream>>>(tx, tb, g, N, K, ep);
+  e = launch_pdl(kern, dim3(grid), dim3(kGemmThreads), Cfg::kSmem, stream, tx, tb, g, N, K, ep);
+  if (e != cudaSuccess) return (int)e;
   return (int)cudaGetLastError();
 }
 
@@ -1481,11 +1497,13 @@ int launch_pair(const void* A, long long lda, const void* B, long long ldb, int 
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairSmem);
   if (e != cudaSuccess) return (int)e;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // added for the launch
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.blockDim = dim3(kGemmThreads, 1, 1);
   cfg.dynamicSmemBytes = kPairSmem;
   cfg.stream = stream;
@@ -1505,6 +1523,7 @@ int launch_pair(const void* A, long long lda, const void* B, long long ldb, int 
   const int tiles = (N / BN) * ((M + 255) / 256);
   const int pairs = tiles < max_pairs[dev] ? tiles : max_pairs[dev];
   cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.numAttrs = 2;  // cluster + programmatic serialization
   e = cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, ep);
   if (e != cudaSuccess) return (int)e;
   return (int)cudaGetLastError();
@@ -1525,7 +1544,8 @@ int launch(const void* A, long long lda, const void* B, long long ldb, int M, in
   if (e != cudaSuccess) return (int)e;
   const int tiles = ((N + BN - 1) / BN) * ((M + kBM - 1) / kBM);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  kern<<<grid, kGemmThreads, Cfg::kSmem, stream>>>(ta, tb, M, N, K, ep);
+  e = launch_pdl(kern, dim3(grid), dim3(kGemmThreads), Cfg::kSmem, stream, ta, tb, M, N, K, ep);
+  if (e != cudaSuccess) return (int)e;
   return (int)cudaGetLastError();
 }
 

@@ -8,6 +8,8 @@
 
 namespace qa {
 
+
+
 // ---------------------------------------------------------------- (a) mel
 // Per-clip geometry of a batched mel pass.
 struct MelClip {

@@ -77,6 +77,8 @@ template <typename T>
 __global__ void layernorm_vec_kernel(const float* __restrict__ x, int rows, int d,
                                      const float* __restrict__ g, const float* __restrict__ b,
                                      float eps, T* __restrict__ out) {
+  pdl_wait();  // the previous kernel's results are visible from here
+  pdl_trigger();
   const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -126,6 +128,8 @@ __global__ void layernorm_vec_kernel(const float* __restrict__ x, int rows, int 
 template <typename T>
 __global__ void rmsnorm_kernel(const T* __restrict__ x, int rows, int d,
                                const float* __restrict__ w, float eps, T* __restrict__ out) {
+  pdl_wait();  // the previous kernel's results are visible from here
+  pdl_trigger();
   const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -243,10 +247,12 @@ int layernorm_rows(const float* x, int rows, int d, const float* g, const float*
                                    reinterpret_cast<uintptr_t>(b)) & 15u) == 0 &&
                    (reinterpret_cast<uintptr_t>(out) & 7u) == 0;
   if (vec && bf16)
-    layernorm_vec_kernel<<<blocks, 256, 0, s>>>(x, rows, d, g, b, eps, static_cast<__nv_bfloat16*>(out));
-  else if (vec)
-    layernorm_vec_kernel<<<blocks, 256, 0, s>>>(x, rows, d, g, b, eps, static_cast<__half*>(out));
-  else if (bf16)
+    return (int)launch_pdl(layernorm_vec_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, s, x,
+                           rows, d, g, b, eps, static_cast<__nv_bfloat16*>(out));
+  if (vec)
+    return (int)launch_pdl(layernorm_vec_kernel<__half>, dim3(blocks), dim3(256), 0, s, x, rows, d,
+                           g, b, eps, static_cast<__half*>(out));
+  if (bf16)
     layernorm_kernel<<<blocks, 256, 0, s>>>(x, rows, d, g, b, eps, static_cast<__nv_bfloat16*>(out));
   else
     layernorm_kernel<<<blocks, 256, 0, s>>>(x, rows, d, g, b, eps, static_cast<__half*>(out));
@@ -259,12 +265,11 @@ int rmsnorm_rows(const void* x, int rows, int d, const float* w, float eps, void
   if (d % 8 || d > 1024 || (reinterpret_cast<uintptr_t>(w) & 15u)) return (int)cudaErrorInvalidValue;
   const unsigned blocks = (rows + 7) / 8;
   if (bf16)
-    rmsnorm_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), rows, d, w, eps,
-                                          static_cast<__nv_bfloat16*>(out));
-  else
-    rmsnorm_kernel<<<blocks, 256, 0, s>>>(static_cast<const __half*>(x), rows, d, w, eps,
-                                          static_cast<__half*>(out));
-  return (int)cudaGetLastError();
+    return (int)launch_pdl(rmsnorm_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, s,
+                           static_cast<const __nv_bfloat16*>(x), rows, d, w, eps,
+                           static_cast<__nv_bfloat16*>(out));
+  return (int)launch_pdl(rmsnorm_kernel<__half>, dim3(blocks), dim3(256), 0, s,
+                         static_cast<const __half*>(x), rows, d, w, eps, static_cast<__half*>(out));
 }
 
 int embed_gather(const uint32_t* ids, int T_, const void* table, int vocab, int d, int audio_id,

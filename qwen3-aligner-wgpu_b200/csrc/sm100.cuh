@@ -9,7 +9,9 @@
 #pragma once
 
 #include <cstdint>
+#include <utility>
 #include <cuda.h>
+#include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 
@@ -574,6 +576,38 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity) {
 
 __device__ __forceinline__ bool mbar_wait_cluster_warp(uint64_t* bar, uint32_t parity) {
   return __all_sync(0xFFFFFFFFu, mbar_wait_cluster(bar, parity));
+}
+
+// ---------------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialization (launch_pdl) may
+// start while the previous kernel of the stream is still running: it does its
+// prologue (barrier init, TMEM allocation), then pdl_wait() blocks until that
+// kernel has completed and its memory operations are visible.  pdl_trigger()
+// lets the next such kernel's CTAs be scheduled (as SMs free up).  Every
+// kernel launched through launch_pdl calls pdl_wait() before its first global
+// memory access.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Launch `kern` on stream s with programmatic stream serialization, so that its
+// CTAs may start while the previous kernel finishes (the kernel must call
+// pdl_wait() before touching global memory).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 // ---------------------------------------------------------------- packed f32 pairs
