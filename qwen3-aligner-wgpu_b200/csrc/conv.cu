@@ -1,5 +1,5 @@
-// (b) Audio-tower conv stem helpers: conv1 as a direct convolution and the
-// im2col gather that turns conv2/conv3 into tcgen05 GEMMs.
+// (b) Audio-tower conv stem: conv1 as a direct convolution (conv2/conv3 are
+// implicit GEMMs on the tensor cores, gemm_tc.cu).
 //
 // Reference: CpuConvStem::conv_block_stages (src/audio_encoder.rs:361-447),
 // three conv2d(3x3, stride 2, pad 1) + bias + erf-GELU levels over
@@ -93,33 +93,6 @@ __global__ void __launch_bounds__(256) conv1_kernel(const float* __restrict__ me
   }
 }
 
-// One thread per 16-byte vector of the output row.
-__global__ void im2col_kernel(const uint4* __restrict__ x, int n, int h, int w, int cv,
-                              uint4* __restrict__ cols, bool time_major) {
-  const int ho = (h + 2 - 3) / 2 + 1, wo = (w + 2 - 3) / 2 + 1;
-  const long long total = static_cast<long long>(n) * ho * wo * 9 * cv;
-  const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
-  if (i >= total) return;
-  const int v = static_cast<int>(i % cv);
-  const int seg = static_cast<int>((i / cv) % 9);
-  const long long row = i / (9LL * cv);
-  const int p = static_cast<int>(row % (ho * wo));
-  const int chunk = static_cast<int>(row / (ho * wo));
-  int oh, ow;
-  if (time_major) {
-    ow = p / ho;
-    oh = p % ho;
-  } else {
-    oh = p / wo;
-    ow = p % wo;
-  }
-  const int ih = 2 * oh + seg / 3 - 1, iw = 2 * ow + seg % 3 - 1;
-  uint4 val = make_uint4(0, 0, 0, 0);
-  if (ih >= 0 && ih < h && iw >= 0 && iw < w)
-    val = x[((static_cast<long long>(chunk) * h + ih) * w + iw) * cv + v];
-  cols[i] = val;
-}
-
 }  // namespace
 
 int conv1_direct(const float* mel, int n, int h, int w, const float* wt, const float* bias,
@@ -136,17 +109,6 @@ int conv1_direct(const float* mel, int n, int h, int w, const float* wt, const f
                            bias, c_out, ldc, static_cast<__nv_bfloat16*>(out));
   return (int)launch_pdl(conv1_kernel<__half>, grid, dim3(256), smem, s, mel, h, w, wt, bias,
                          c_out, ldc, static_cast<__half*>(out));
-}
-
-int im2col_3x3s2(const void* x, int n, int h, int w, int c, void* cols, bool time_major,
-                 cudaStream_t s) {
-  if (n <= 0) return 0;
-  if (c % 8) return (int)cudaErrorInvalidValue;
-  const int ho = (h + 2 - 3) / 2 + 1, wo = (w + 2 - 3) / 2 + 1;
-  const long long total = static_cast<long long>(n) * ho * wo * 9 * (c / 8);
-  im2col_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(
-      static_cast<const uint4*>(x), n, h, w, c / 8, static_cast<uint4*>(cols), time_major);
-  return (int)cudaGetLastError();
 }
 
 }  // namespace qa

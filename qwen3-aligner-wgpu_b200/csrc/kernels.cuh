@@ -67,11 +67,6 @@ int conv1_direct(const float* mel, int n, int h, int w, const float* wt, const f
 // c rounded up to 64 (the pad channels hold zeros), so that a 64-channel
 // (128-byte) k-block of the TMA im2col boxes never straddles two taps.
 inline int conv_channels_padded(int c) { return (c + 63) / 64 * 64; }
-// im2col for a 3x3 / stride 2 / pad 1 conv over NHWC [n][h][w][c] 16-bit:
-// cols [n*ho*wo][9*c] with k = (kh*3 + kw)*c + ic.  Positions are ordered
-// (oh, ow) when !time_major, (ow, oh) when time_major.
-int im2col_3x3s2(const void* x, int n, int h, int w, int c, void* cols, bool time_major,
-                 cudaStream_t s);
 // LayerNorm (eps) over rows of f32 x [rows][d] -> 16-bit out.
 int layernorm_rows(const float* x, int rows, int d, const float* g, const float* b, float eps,
                    void* out, bool bf16, cudaStream_t s);

@@ -188,38 +188,8 @@ __host__ __device__ constexpr uint32_t f16_instr_desc(int M, int N, bool bf16) {
          | (static_cast<uint32_t>(M >> 4) << 24);  // M / 16
 }
 
-// D[tmem] (+)= A[smem] * B[smem]^T, issued by a single thread.
-__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                        uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 
-// D (+)= A·B with A read from tensor memory (K-major: lane = row, 16-bit
-// elements packed two per 32-bit column, K step of 16 = 8 columns) and B from
-// shared memory.  Issued by one thread.
-__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                           uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 
-// Arrive on `bar` once every tcgen05.mma previously issued by this thread has
-// completed (their shared-memory operands may then be overwritten).
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          smem_u32(bar))
-      : "memory");
-}
 
 // Load 32 consecutive f32 columns of this warp's 32 TMEM lanes (one lane per
 // thread).  taddr = base | (lane0 << 16) | column.
@@ -299,16 +269,6 @@ __device__ __forceinline__ void tmem_ld_x32(uint32_t taddr, uint32_t (&r)[32]) {
       : "memory");
 }
 
-// Store 16 consecutive 32-bit columns of this warp's 32 TMEM lanes (no wait).
-__device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t (&w)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};"
-      :
-      : "r"(taddr),
-        "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7]),
-        "r"(w[8]), "r"(w[9]), "r"(w[10]), "r"(w[11]), "r"(w[12]), "r"(w[13]), "r"(w[14]), "r"(w[15])
-      : "memory");
-}
 
 // Load 64 consecutive 32-bit columns of this warp's 32 TMEM lanes and wait
 // for them in the same asm statement, so no use of r can be scheduled before
@@ -487,27 +447,7 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
                : "memory");
 }
 
-// D (+)= A·B for the pair (M = 256 rows, half in each CTA), issued by one
-// thread of the first CTA; descriptors name the same offsets in both CTAs.
-__device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                             uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 
-// Arrive on the mbarrier at `bar`'s offset in every CTA of `cta_mask` once
-// the pair MMAs issued so far have completed.
-__device__ __forceinline__ void mma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-      " [%0], %1;" ::"r"(smem_u32(bar)),
-      "h"(cta_mask)
-      : "memory");
-}
 
 // ------------------------------------------- warp-converged MMA issue (elect.sync)
 // The whole warp executes these with warp-uniform operands and one elected
