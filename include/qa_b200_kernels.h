@@ -35,7 +35,9 @@ extern "C" {
  * epilogue.  Stands in for every `prefill_gemm*` dispatch of the reference
  * (src/shaders.rs:1817-2077; src/decoder.rs:1321-1657) and for the host
  * projections of src/audio_encoder.rs and src/align_inference.rs:789-790.
- * `status` (device, may be NULL) receives timeout bits.
+ * `status` (device, may be NULL) receives timeout bits.  `force_bn`: 0 = the
+ * library's tile choice, -1 = 256-row tiles on CTA pairs, > 0 = one CTA per
+ * 128-row tile of that width (128, 224, 240 or 256).
  */
 int qa_k_gemm(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
               int bf16, int mode, int act, void* out, long long ldo, const float* bias,
@@ -87,6 +89,8 @@ int qa_k_conv1(const float* mel, int n, int h, int w, const float* wt, const flo
  * per 64 (impl 0) or 128 (impl 1) query positions of a clip; block_tab
  * [clips][max_pages] page ids; out [q_rows][nqh*128].  impl 0 = mma.sync
  * kernel, 1 = persistent tcgen05/TMEM kernel (the one the pipeline runs).
+ * Both take GQA groups of two (nqh == 2 * nkvh, the model's geometry); other
+ * head counts return cudaErrorInvalidValue.
  */
 int qa_k_causal_attention(const void* qkv, long long ldq, long long q_rows, int nqh, int nkvh,
                           const int* tiles, int n_tiles, const int* block_tab, int max_pages,
