@@ -79,6 +79,32 @@ int or_head(or_model* m, const float* hidden, int seq, const int* rows, int n_ro
 /* --- post-processing (src/postprocess.rs:33-113) --- */
 void or_fix_timestamps(const int64_t* data, int n, int64_t* out);
 
+/* --- Local Head refinement (src/local_head.rs) --- */
+typedef struct or_local_head or_local_head;
+/* The package's F32 tensors (src/local_head.rs:810-916) and the [91]
+ * normalizer; NULL with a message in err on a missing or mis-shaped tensor. */
+or_local_head* or_lh_load(const qa_tensor* tensors, int n, const float* mean, const float* std_,
+                          char* err, int err_len);
+void or_lh_free(or_local_head* h);
+void or_lh_hann(int n, float* out);                         /* src/local_head.rs:917-925 */
+void or_lh_mel_bank(float* out /* [80][257] */);            /* src/local_head.rs:927-973 */
+void or_lh_band_edges(int bins, int* out /* [5] */);        /* src/local_head.rs:975-982 */
+int64_t or_lh_valid_class_count(double duration_ms, int64_t class_count); /* :1066-1069 */
+void or_lh_remove_overlaps(double* intervals /* [n][2] */, int n);        /* :1084-1100 */
+void or_lh_bound_to_duration(double* intervals, int n, double duration_ms); /* :1102-1130 */
+/* [41][91] normalised window centred on center_ms (src/local_head.rs:359-507). */
+void or_lh_features_one(const or_local_head* h, const float* samples, int64_t n,
+                        int64_t center_ms, float* out);
+/* One endpoint's offset in ms (src/local_head.rs:509-611); ctx [4][1024]. */
+float or_lh_endpoint_offset(const or_local_head* h, const float* feat, const float* ctx,
+                            const float* mask4, int is_end);
+/* LocalHead::refine (src/local_head.rs:179-307): out [W][2] seconds; the fixed
+ * centres [2W] and offsets [2W] too when non-NULL.  Returns 0, or 1 on bad
+ * arguments. */
+int or_lh_refine(const or_local_head* h, const float* samples, int64_t n, int W,
+                 const float* logits, int n_labels, const float* hidden, int hidden_size,
+                 double* out, int64_t* fixed_out, float* offsets_out);
+
 /* --- building blocks, for unit tests --- */
 void or_gemm(const float* A, int lda, const float* B, int ldb, float* C, int ldc, int M, int N,
              int K, int accumulate);

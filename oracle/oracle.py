@@ -59,6 +59,20 @@ def lib():
         L.or_head.argtypes = [vp, vp, i, vp, i, vp, vp, vp, vp]
         L.or_fix_timestamps.argtypes = [vp, i, vp]
         L.or_gemm.argtypes = [vp, i, vp, i, vp, i, i, i, i, i]
+        L.or_lh_load.argtypes = [vp, i, vp, vp, ctypes.c_char_p, i]
+        L.or_lh_load.restype = vp
+        L.or_lh_free.argtypes = [vp]
+        L.or_lh_hann.argtypes = [i, vp]
+        L.or_lh_mel_bank.argtypes = [vp]
+        L.or_lh_band_edges.argtypes = [i, vp]
+        L.or_lh_valid_class_count.argtypes = [ctypes.c_double, i64]
+        L.or_lh_valid_class_count.restype = i64
+        L.or_lh_remove_overlaps.argtypes = [vp, i]
+        L.or_lh_bound_to_duration.argtypes = [vp, i, ctypes.c_double]
+        L.or_lh_features_one.argtypes = [vp, vp, i64, i64, vp]
+        L.or_lh_endpoint_offset.argtypes = [vp, vp, vp, vp, i]
+        L.or_lh_endpoint_offset.restype = ctypes.c_float
+        L.or_lh_refine.argtypes = [vp, vp, i64, i, vp, i, vp, i, vp, vp, vp]
         _lib = L
     return _lib
 
@@ -222,3 +236,90 @@ def f32_to_f16_array(x: np.ndarray) -> np.ndarray:
 
 def f16_bits_to_f32(b: np.ndarray) -> np.ndarray:
     return np.ascontiguousarray(b, np.uint16).view(np.float16).astype(np.float32)
+
+
+# ---------------------------------------------------------------- Local Head
+def lh_hann(n: int) -> np.ndarray:
+    out = np.zeros(n, np.float32)
+    lib().or_lh_hann(n, _p(out))
+    return out
+
+
+def lh_mel_bank() -> np.ndarray:
+    out = np.zeros((80, 257), np.float32)
+    lib().or_lh_mel_bank(_p(out))
+    return out
+
+
+def lh_band_edges(bins: int) -> list:
+    out = np.zeros(5, np.int32)
+    lib().or_lh_band_edges(bins, _p(out))
+    return out.tolist()
+
+
+def lh_valid_class_count(duration_ms: float, class_count: int) -> int:
+    return int(lib().or_lh_valid_class_count(duration_ms, class_count))
+
+
+def lh_remove_overlaps(intervals) -> list:
+    iv = np.ascontiguousarray(intervals, np.float64).reshape(-1, 2).copy()
+    lib().or_lh_remove_overlaps(_p(iv), len(iv))
+    return iv.tolist()
+
+
+def lh_bound_to_duration(intervals, duration_ms: float) -> list:
+    iv = np.ascontiguousarray(intervals, np.float64).reshape(-1, 2).copy()
+    lib().or_lh_bound_to_duration(_p(iv), len(iv), duration_ms)
+    return iv.tolist()
+
+
+class LocalHead:
+    """The CPU Local Head over a package (name -> (dtype, array)) and normalizer."""
+
+    def __init__(self, tensors: dict, mean, std):
+        import importlib
+        qa = importlib.import_module("qwen3-aligner-wgpu_b200")
+        tens, keep = qa._lib.make_tensors(tensors)
+        self._mean = np.ascontiguousarray(mean, np.float32)
+        self._std = np.ascontiguousarray(std, np.float32)
+        err = ctypes.create_string_buffer(512)
+        self.h = lib().or_lh_load(ctypes.addressof(tens), len(tens), _p(self._mean),
+                                  _p(self._std), err, 512)
+        del keep
+        if not self.h:
+            raise ValueError(err.value.decode())
+
+    def __del__(self):
+        try:
+            if getattr(self, "h", None):
+                lib().or_lh_free(self.h)
+        except Exception:
+            pass
+
+    def features_one(self, samples: np.ndarray, center_ms: int) -> np.ndarray:
+        s = np.ascontiguousarray(samples, np.float32)
+        out = np.zeros((41, 91), np.float32)
+        lib().or_lh_features_one(self.h, _p(s), len(s), int(center_ms), _p(out))
+        return out
+
+    def endpoint_offset(self, feat, ctx, mask, is_end: int) -> float:
+        f = np.ascontiguousarray(feat, np.float32)
+        c = np.ascontiguousarray(ctx, np.float32)
+        m = np.ascontiguousarray(mask, np.float32)
+        return float(lib().or_lh_endpoint_offset(self.h, _p(f), _p(c), _p(m), int(is_end)))
+
+    def refine(self, samples, logits, hidden):
+        """(intervals [W][2] seconds, fixed centres [2W] ms, offsets [2W] ms)."""
+        s = np.ascontiguousarray(samples, np.float32)
+        lg = np.ascontiguousarray(logits, np.float32)
+        hd = np.ascontiguousarray(hidden, np.float32)
+        slots, n_labels = lg.shape
+        W = slots // 2
+        out = np.zeros((W, 2), np.float64)
+        fixed = np.zeros(slots, np.int64)
+        off = np.zeros(slots, np.float32)
+        rc = lib().or_lh_refine(self.h, _p(s), len(s), W, _p(lg), n_labels, _p(hd), hd.shape[1],
+                                _p(out), _p(fixed), _p(off))
+        if rc != 0:
+            raise ValueError(f"or_lh_refine rc={rc}")
+        return out, fixed, off

@@ -212,19 +212,25 @@ def random_weights(cfg: ModelConfig, seed: int = 0, std: float = 0.02) -> dict:
 
 
 def save_safetensors(path: str, tensors: dict) -> None:
-    """Write bf16 tensors (uint16 bits) as a safetensors file."""
+    """Write a safetensors file: values are bf16 bits (np.uint16) or
+    (dtype str, array) pairs with dtype "BF16" | "F16" | "F32"."""
+    np_t = {"BF16": np.uint16, "F16": np.float16, "F32": np.float32}
+    items = []
+    for name, v in tensors.items():
+        dt, arr = v if isinstance(v, tuple) else ("BF16", v)
+        items.append((name, dt, np.ascontiguousarray(arr, dtype=np_t[dt])))
     header, off = {}, 0
-    for name, arr in tensors.items():
-        nb = arr.size * 2
-        header[name] = {"dtype": "BF16", "shape": list(arr.shape), "data_offsets": [off, off + nb]}
+    for name, dt, arr in items:
+        nb = arr.nbytes
+        header[name] = {"dtype": dt, "shape": list(arr.shape), "data_offsets": [off, off + nb]}
         off += nb
     hb = json.dumps(header, separators=(",", ":")).encode()
     hb += b" " * ((8 - len(hb) % 8) % 8)
     with open(path, "wb") as f:
         f.write(struct.pack("<Q", len(hb)))
         f.write(hb)
-        for arr in tensors.values():
-            f.write(np.ascontiguousarray(arr, dtype=np.uint16).tobytes())
+        for _, _, arr in items:
+            f.write(arr.tobytes())
 
 
 def load_safetensors(path: str) -> dict:
@@ -258,6 +264,100 @@ def write_model_dir(path: str, cfg: ModelConfig, seed: int = 0) -> None:
         json.dump({"synthetic": True, "added_tokens": [
             {"id": AUDIO_START_ID, "content": AUDIO_START}, {"id": AUDIO_END_ID, "content": AUDIO_END},
             {"id": AUDIO_PAD_ID, "content": AUDIO_PAD}, {"id": TIMESTAMP_ID, "content": TIMESTAMP}]}, f)
+
+
+# ---------------------------------------------------------------- Local Head package
+
+LOCAL_HEAD_OFFSETS_MS = [float(o) for o in range(-60, 61, 10)]
+LOCAL_HEAD_FEATURES = 91
+
+
+def local_head_prior() -> np.ndarray:
+    """The canonical inference prior, -0.5 (o / 35)^2 x 2 (src/local_head.rs:709-714)."""
+    return np.array([-0.5 * (o / 35.0) ** 2 * 2.0 for o in LOCAL_HEAD_OFFSETS_MS], np.float32)
+
+
+def local_head_specs() -> list:
+    """(name, shape, kind, fan_in) of every Local Head tensor (src/local_head.rs:876-912).
+    kind: 'normal' (std 1/sqrt(fan_in)) | 'ones' | 'zeros' | 'prior' | 'scale'."""
+    d, q, f = 128, 1024, LOCAL_HEAD_FEATURES
+    s = [("audio.0.weight", (d, f, 5), "normal", f * 5), ("audio.0.bias", (d,), "normal", f * 5),
+         ("audio.2.weight", (d, d, 5), "normal", d * 5), ("audio.2.bias", (d,), "normal", d * 5),
+         ("context_projection.weight", (d, q), "normal", q),
+         ("context_projection.bias", (d,), "normal", q),
+         ("role_embedding.weight", (4, d), "normal", 1),
+         ("endpoint_embedding.weight", (2, d), "normal", 1)]
+    for att in ("context_attention", "audio_attention"):
+        s += [(att + ".in_proj_weight", (3 * d, d), "normal", d),
+              (att + ".in_proj_bias", (3 * d,), "zeros", d),
+              (att + ".out_proj.weight", (d, d), "normal", d),
+              (att + ".out_proj.bias", (d,), "zeros", d)]
+    for nm in ("query_norm", "audio_norm"):
+        s += [(nm + ".weight", (d,), "ones", 1), (nm + ".bias", (d,), "zeros", 1)]
+    s += [("activity_bias.weight", (1, d), "normal", d), ("activity_bias.bias", (1,), "normal", d),
+          ("boundary_bias.weight", (1, d), "normal", d), ("boundary_bias.bias", (1,), "normal", d),
+          ("derivative_scale", (), "scale", 1), ("qwen_prior", (13,), "prior", 1)]
+    return s
+
+
+def random_local_head(seed: int = 0):
+    """(tensors name -> ("F32", array), mean [91], std [91]) of a seeded random
+    Local Head with the canonical prior and a positive normalizer."""
+    out = {}
+    for name, shape, kind, fan_in in local_head_specs():
+        n = int(np.prod(shape)) if shape else 1
+        if kind == "ones":
+            v = np.ones(n, np.float32)
+        elif kind == "zeros":
+            v = np.zeros(n, np.float32)
+        elif kind == "prior":
+            v = local_head_prior()
+        elif kind == "scale":
+            v = np.array([0.5], np.float32)
+        else:
+            v = _rng(seed, "local_head:" + name).standard_normal(n, dtype=np.float32)
+            v *= np.float32(1.0 / np.sqrt(fan_in))
+        out[name] = ("F32", v.reshape(shape))
+    r = _rng(seed, "local_head:normalizer")
+    mean = np.concatenate([r.uniform(-9.0, -4.0, 80), r.uniform(-5.0, -3.0, 1),
+                           r.uniform(-0.1, 0.1, 1), r.uniform(0.2, 0.6, 1),
+                           r.uniform(0.3, 1.2, 8)]).astype(np.float32)
+    std = np.concatenate([r.uniform(1.5, 3.5, 80), r.uniform(1.0, 2.0, 1),
+                          r.uniform(0.2, 0.6, 1), r.uniform(0.2, 0.8, 1),
+                          r.uniform(0.2, 0.8, 8)]).astype(np.float32)
+    return out, mean, std
+
+
+def local_head_config_json() -> dict:
+    """config.json of a Local Head package, the contract of src/local_head.rs:617-700."""
+    return {
+        "schema": "qwen-fa-ultra.local-head.v1",
+        "architecture": "IdentityConditionedBoundaryHead",
+        "offsets_ms": LOCAL_HEAD_OFFSETS_MS,
+        "decoder_temperature": 1.5,
+        "decoder_amplitude": 1.0,
+        "inference_prior_scale": 2.0,
+        "context_roles": ["timestamp slot", "current avg", "prev avg", "next avg"],
+        "feature_contract": {"center_source": "fixed", "context_ms": 200, "feature_dim": 91,
+                             "frame_count": 41, "frame_ms": 25, "hop_ms": 10, "n_fft": 512,
+                             "n_mels": 80, "sample_rate": 16000, "spectral_distance_bands": 4},
+        "model_config": {"acoustic_dim": 91, "activity_weight": 0.25, "heads": 4,
+                         "model_dim": 128, "prior_sigma_ms": 35.0, "qwen_dim": 1024},
+    }
+
+
+def write_local_head_dir(model_dir: str, seed: int = 0) -> str:
+    """<model_dir>/local_head/ with config.json, normalizer.json and the F32
+    model.safetensors; returns the package directory."""
+    d = os.path.join(model_dir, "local_head")
+    os.makedirs(d, exist_ok=True)
+    tensors, mean, std = random_local_head(seed)
+    with open(os.path.join(d, "config.json"), "w") as f:
+        json.dump(local_head_config_json(), f)
+    with open(os.path.join(d, "normalizer.json"), "w") as f:
+        json.dump({"mean": mean.tolist(), "std": std.tolist()}, f)
+    save_safetensors(os.path.join(d, "model.safetensors"), tensors)
+    return d
 
 
 # ---------------------------------------------------------------- tokenizer

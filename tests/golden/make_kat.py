@@ -9,6 +9,8 @@ here, so its unit-test tables are read as text from its test modules:
   src/words.rs:235-...         split_words (Japanese cases skipped: nagisa)
   src/half16.rs:114-125        bf16 rounding of 0.1
   src/mrope.rs:95-117          dim-map layouts
+  src/local_head.rs:1136-1207  Local Head primitives (Hann, mel bank, bands,
+                               duration mask, overlap and duration repair)
 
 Usage: python tests/golden/make_kat.py [REFERENCE_ROOT]
 (REFERENCE_ROOT defaults to the path in $QA_REFERENCE_ROOT.)  The output is
@@ -93,6 +95,37 @@ def main(root):
     kat["dim_map"] = [{"section": [2, 1], "half": 4, "interleaved": False, "want": [0, 0, 1, 1]},
                       {"section": [24, 20, 20], "half": 64, "interleaved": True,
                        "prefix": [0, 1, 2, 0, 1, 2], "counts": [24, 20, 20]}]
+    lh = src("local_head.rs")
+    tests = lh[lh.index("#[cfg(test)]"):]
+    m = re.search(r"np\.hanning\((\d+)\)\.astype\(np\.float32\)\[([\d, ]+)\]\s*\n\s*//\s*->\s*([\d., ]+)",
+                  tests)
+    idx = [int(x) for x in m.group(2).split(",")]
+    vals = [float(x) for x in m.group(3).split(",")]
+    assert "(w[10] - w[389]).abs() < 1e-6" in tests
+    kat["lh_hann"] = {"n": int(m.group(1)), "index": idx, "want": vals, "tol": 1e-6,
+                      "symmetric": [10, 389]}
+    assert "(total - 1.0).abs() < 1e-5" in tests
+    kat["lh_mel_bank"] = {"rows": 80, "bins": 257, "row_sum_tol": 1e-5}
+    m = re.search(r"assert_eq!\(band_edges\((\d+)\),\s*\[([\d, ]+)\]\)", tests)
+    kat["lh_band_edges"] = {"bins": int(m.group(1)), "want": _nums(m.group(2))}
+    kat["lh_valid_class_count"] = [
+        [float(a), int(b), int(c)] for a, b, c in re.findall(
+            r"assert_eq!\(valid_class_count\(([\d.e]+),\s*(\d+)\),\s*(\d+)\)", tests)]
+    pair = r"vec!\[\[([\d.]+), ([\d.]+)\], \[([\d.]+), ([\d.]+)\]\]"
+    kat["lh_remove_overlaps"] = [
+        {"intervals": [[float(g[0]), float(g[1])], [float(g[2]), float(g[3])]],
+         "want": [[float(g[4]), float(g[5])], [float(g[6]), float(g[7])]]}
+        for g in re.findall(r"let mut v = " + pair + r";\s*remove_neighbor_overlaps\(&mut v\);"
+                            r"\s*assert_eq!\(v, " + pair + r"\)", tests)]
+    bd = re.findall(r"let mut v = " + pair + r";\s*bound_to_duration\(&mut v, ([\d.]+)\);", tests)
+    assert len(bd) == 2 and "assert!((v[1][1] - 10.0).abs() < 1e-9" in tests
+    kat["lh_bound_to_duration"] = [
+        {"intervals": [[float(g[0]), float(g[1])], [float(g[2]), float(g[3])]],
+         "duration_ms": float(g[4]), "want": [[float(g[0]), float(g[1])], [float(g[2]), float(g[3])]]}
+        for g in bd[:1]] + [
+        {"intervals": [[float(g[0]), float(g[1])], [float(g[2]), float(g[3])]],
+         "duration_ms": float(g[4]), "last_end": 10.0, "min_len": 5.0, "tol": 1e-9}
+        for g in bd[1:]]
     with open(os.path.join(HERE, "kat.json"), "w", encoding="utf-8") as f:
         json.dump(kat, f, indent=1, ensure_ascii=False)
     print({k: len(v) if isinstance(v, list) else 1 for k, v in kat.items()})
