@@ -93,6 +93,7 @@ typedef struct {
   int64_t gpu_launches; /* kernels this library launched in the call */
   int64_t h2d_bytes;    /* host->device bytes the call copied */
   int64_t d2h_bytes;    /* device->host bytes the call copied */
+  double local_ms;      /* the Local Head's refinement (Timings::local_ms); 0 when it did not run */
 } qa_timings;
 
 /* Live per-kernel statistics (qa_set_profile): CUDA-event time of every launch
@@ -185,6 +186,38 @@ int qa_fix_timestamps(const int64_t* data, int n, int64_t* out);
 int qa_head_noalloc(qa_ctx* ctx, const float* hidden, int seq, const int* rows, int n_rows,
                     int64_t* raw_ms, float* logits);
 
+/* ---------------------------------------------------------------- Local Head */
+
+/* The optional +-60 ms refinement a checkpoint ships in local_head/
+ * (src/local_head.rs).  qa_local_head_load uploads its model.safetensors
+ * tensors (all F32, the names and shapes of src/local_head.rs:810-916) and
+ * the [91] normalizer mean / std of normalizer.json; the host validates
+ * config.json (src/local_head.rs:661-715) before calling it.  Loading enables
+ * it (the reference turns it on whenever the package is present,
+ * src/align_inference.rs:449).  QA_ERR_WEIGHTS on a missing or mis-shaped
+ * tensor, QA_ERR_STATE if one is already loaded. */
+int qa_local_head_load(qa_ctx* ctx, const qa_tensor* tensors, int n, const float* mean,
+                       const float* std_);
+/* Aligner::set_local_head_enabled (src/align_inference.rs:584-593): enabling
+ * a context without a loaded Local Head is QA_ERR_STATE. */
+int qa_set_local_head_enabled(qa_ctx* ctx, int enabled);
+/* Aligner::local_head_enabled: 1 when loaded and enabled. */
+int qa_local_head_enabled(const qa_ctx* ctx);
+
+/* LocalHead::refine (src/local_head.rs:179-307) for one clip, on the device:
+ * samples [n] 16 kHz mono; logits [2 * n_words][n_labels], the timestamp
+ * head's pre-argmax output; hidden [2 * n_words][hidden_size] the unfolded
+ * final-norm rows at the timestamp slots.  intervals [n_words][2] receives
+ * (start, end) in seconds.  Optional (NULL to skip): fixed_ms [2 * n_words]
+ * the repaired coarse centres, offsets_ms [2 * n_words] the head's offsets,
+ * features [2 * n_words][41][91] the normalised acoustic windows.
+ * QA_ERR_SHAPE when hidden_size is not the head's 1024 context width or the
+ * audio is empty; QA_ERR_STATE without a loaded Local Head. */
+int qa_local_head_refine(qa_ctx* ctx, const float* samples, int64_t n, int n_words,
+                         const float* logits, int n_labels, const float* hidden, int hidden_size,
+                         double* intervals, int64_t* fixed_ms, float* offsets_ms,
+                         float* features);
+
 /* ---------------------------------------------------------------- batched path */
 
 typedef struct {
@@ -199,6 +232,8 @@ typedef struct {
   int n_ts;        /* number of <timestamp> tokens in the clip's input_ids */
   float* logits;   /* optional [n_ts, num_labels] */
   float* normed;   /* optional [n_ts, hidden_size] unfolded-norm rows */
+  double* intervals; /* optional [n_ts / 2][2] (start, end) seconds per word from
+                        the Local Head (LocalHead::refine); needs it enabled */
 } qa_result;
 
 /* Align a batch of independent clips in one device-resident pass:

@@ -57,7 +57,8 @@ EXPORTED = [
     "qa_get_timings", "qa_mel", "qa_audio_embeds", "qa_ensure_capacity", "qa_text_hidden",
     "qa_head", "qa_align_batch", "qa_batch_stage", "qa_batch_run", "qa_batch_fetch",
     "qa_set_stream", "qa_set_profile", "qa_get_profile", "qa_fix_timestamps",
-    "qa_head_noalloc",
+    "qa_head_noalloc", "qa_local_head_load", "qa_set_local_head_enabled",
+    "qa_local_head_enabled", "qa_local_head_refine",
     "qa_k_gemm", "qa_k_conv3x3s2", "qa_k_causal_attention", "qa_k_conv1",
     "qa_k_gemm_qkv_rope",
 ]
@@ -89,7 +90,7 @@ class QaTimings(ctypes.Structure):
     _fields_ = [(n, ctypes.c_double) for n in (
         "h2d_ms", "mel_ms", "enc_ms", "gather_ms", "prefill_ms", "head_ms", "d2h_ms",
         "total_ms")] + [("gpu_launches", ctypes.c_int64), ("h2d_bytes", ctypes.c_int64),
-                        ("d2h_bytes", ctypes.c_int64)]
+                        ("d2h_bytes", ctypes.c_int64), ("local_ms", ctypes.c_double)]
 
 
 class QaKernelStat(ctypes.Structure):
@@ -105,7 +106,7 @@ class QaClip(ctypes.Structure):
 
 class QaResult(ctypes.Structure):
     _fields_ = [("raw_ms", c_void_p), ("n_ts", c_int), ("logits", c_void_p),
-                ("normed", c_void_p)]
+                ("normed", c_void_p), ("intervals", c_void_p)]
 
 
 def make_cfg(mc) -> QaCfg:
@@ -212,6 +213,12 @@ def _declare(L: ctypes.CDLL) -> None:
         L.qa_set_stream.argtypes = [c_void_p, c_void_p]
         L.qa_set_profile.argtypes = [c_void_p, c_int]
         L.qa_get_profile.argtypes = [c_void_p, c_void_p, c_int, ctypes.POINTER(c_int)]
+        L.qa_local_head_load.argtypes = [c_void_p, c_void_p, c_int, c_void_p, c_void_p]
+        L.qa_set_local_head_enabled.argtypes = [c_void_p, c_int]
+        L.qa_local_head_enabled.argtypes = [c_void_p]
+        L.qa_local_head_refine.argtypes = [c_void_p, c_void_p, ctypes.c_int64, c_int, c_void_p,
+                                           c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p,
+                                           c_void_p]
 
 
 def check(rc: int, ctx=None) -> None:

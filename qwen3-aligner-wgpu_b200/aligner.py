@@ -7,7 +7,10 @@ applies:
 * ``Aligner.load_backend_with_dtype(model, half)`` — load weights onto one
   CUDA device in the given 16-bit storage format (``"f16"`` default, ``"bf16"``);
 * ``align_samples(samples, text, language)`` -> ``(raw_ms, items)`` — one clip
-  of 16 kHz mono f32 audio (src/align_inference.rs:521-569, Local Head off);
+  of 16 kHz mono f32 audio (src/align_inference.rs:521-569); with a Local
+  Head loaded and enabled the items are its refined word times;
+* ``local_head()``, ``local_head_enabled()``, ``set_local_head_enabled(on)``
+  (src/align_inference.rs:571-593);
 * ``align_batch([(samples, text, language), ...])`` — many independent clips
   in one device-resident pass (new: the reference aligns one clip per call);
 * the tower-boundary stages ``mel``, ``audio_embeds``, ``text_hidden`` and
@@ -26,6 +29,7 @@ import os
 import numpy as np
 
 from . import _lib
+from . import local_head as _lh
 from . import postprocess
 from . import synth
 
@@ -41,14 +45,18 @@ class Aligner:
         self._half = half
         self.input_builder = builder
         self.timings = None
+        self._local_head = None
 
     # ------------------------------------------------------------ load / close
 
     @classmethod
     def load_backend_with_dtype(cls, model, half: str = "f16", device: int = 0,
-                                cfg: synth.ModelConfig = None, tokenizer=None) -> "Aligner":
+                                cfg: synth.ModelConfig = None, tokenizer=None,
+                                local_head=None) -> "Aligner":
         """``model``: a model directory (config.json + model.safetensors, `-hf`
-        layout) or a dict of name -> bf16 bits / (dtype, array) with ``cfg``."""
+        layout, and the optional local_head/ package) or a dict of name ->
+        bf16 bits / (dtype, array) with ``cfg`` (and optionally ``local_head``
+        = (tensors, mean, std) of a Local Head package)."""
         half = half.lower()
         if half in ("f16", "fp16", "half"):
             code = _lib.QA_HALF_F16
@@ -61,6 +69,8 @@ class Aligner:
             with open(os.path.join(model, "config.json")) as f:
                 cfg = synth.ModelConfig.from_config_json(json.load(f))
             weights = synth.load_safetensors(os.path.join(model, "model.safetensors"))
+            if local_head is None:
+                local_head = _lh.load_package(model)
         else:
             if cfg is None:
                 raise ValueError("a weights dict needs its ModelConfig")
@@ -76,8 +86,15 @@ class Aligner:
             msg = L.qa_last_error(ctx)
             L.qa_close(ctx)
             raise _lib.QaError(rc, msg.decode() if msg else "")
-        return cls(ctx, cfg, "bf16" if code else "f16",
-                   synth.InputBuilder(tokenizer, n_window=cfg.n_window))
+        al = cls(ctx, cfg, "bf16" if code else "f16",
+                 synth.InputBuilder(tokenizer, n_window=cfg.n_window))
+        if local_head is not None:
+            try:
+                al._local_head = _lh.load_into(al, *local_head)
+            except Exception:
+                al.close()
+                raise
+        return al
 
     @classmethod
     def load_with_dtype(cls, model, half: str = "f16", **kw) -> "Aligner":
@@ -103,6 +120,23 @@ class Aligner:
 
     def backend_name(self) -> str:
         return "cuda"
+
+    # ------------------------------------------------------------ Local Head
+
+    def local_head(self):
+        """The Local Head this checkpoint ships, if any (a LocalHead handle)."""
+        return self._local_head
+
+    def local_head_enabled(self) -> bool:
+        """Whether align runs the Local Head."""
+        return bool(self._ctx) and _lib.lib().qa_local_head_enabled(self._ctx) == 1
+
+    def set_local_head_enabled(self, enabled: bool) -> None:
+        """Turn the Local Head on or off; enabling it on a checkpoint that
+        ships none raises (src/align_inference.rs:584-593)."""
+        if enabled and self._local_head is None:
+            raise ValueError("this checkpoint has no local_head/ package")
+        self._check(_lib.lib().qa_set_local_head_enabled(self._ctx, 1 if enabled else 0))
 
     def set_timeout_ms(self, ms: int) -> None:
         self._check(_lib.lib().qa_set_timeout_ms(self._ctx, int(ms)))
@@ -138,10 +172,21 @@ class Aligner:
         unrepaired argmax stream, items the repaired word times."""
         inputs = [self.build_input(s, t, l) for s, t, l in clips]
         raws = self.align_inputs([c[0] for c in clips], inputs, want_logits, want_normed)
+        return self._items(inputs, raws, want_logits or want_normed)
+
+    @staticmethod
+    def _items(inputs, raws, with_extra: bool) -> list:
+        """(raw_ms, items[, extra]) per clip: the Local Head's intervals when it
+        ran, else the repaired coarse stream paired with the words."""
         out = []
         for (r, extra), inp in zip(raws, inputs):
-            items = postprocess.pair_words(inp.words, _lib.fix_timestamps(r))
-            out.append((r, items) if not (want_logits or want_normed) else (r, items, extra))
+            iv = extra.get("intervals")
+            if iv is not None:
+                items = [postprocess.AlignItem(w, float(a), float(b))
+                         for w, (a, b) in zip(inp.words, iv)]
+            else:
+                items = postprocess.pair_words(inp.words, _lib.fix_timestamps(r))
+            out.append((r, items, extra) if with_extra else (r, items))
         return out
 
     def align_stream(self, batches, want_logits: bool = False, want_normed: bool = False):
@@ -158,11 +203,7 @@ class Aligner:
             return batch, [self.build_input(s, t, l) for s, t, l in batch]
 
         def post(inputs, raws):
-            out = []
-            for (r, extra), inp in zip(raws, inputs):
-                items = postprocess.pair_words(inp.words, _lib.fix_timestamps(r))
-                out.append((r, items) if not (want_logits or want_normed) else (r, items, extra))
-            return out
+            return self._items(inputs, raws, want_logits or want_normed)
 
         it = iter(batches)
         pending = []  # (inputs, staged) of batches run but not yet fetched, oldest first
@@ -198,6 +239,7 @@ class Aligner:
         clips = (_lib.QaClip * n)()
         res = (_lib.QaResult * n)()
         keep, outs = [], []
+        lh_on = self.local_head_enabled()
         for i, (s, inp) in enumerate(zip(samples_list, inputs)):
             s = np.ascontiguousarray(s, np.float32)
             ids = np.ascontiguousarray(inp.input_ids, np.uint32)
@@ -205,6 +247,7 @@ class Aligner:
             raw = np.zeros(n_ts, np.int64)
             lg = np.zeros((n_ts, self.cfg.num_labels), np.float32) if want_logits else None
             nm = np.zeros((n_ts, self.cfg.hidden_size), np.float32) if want_normed else None
+            iv = np.zeros((n_ts // 2, 2), np.float64) if lh_on else None
             keep += [s, ids]
             clips[i].samples = s.ctypes.data
             clips[i].n_samples = len(s)
@@ -214,7 +257,8 @@ class Aligner:
             res[i].n_ts = n_ts
             res[i].logits = lg.ctypes.data if lg is not None else None
             res[i].normed = nm.ctypes.data if nm is not None else None
-            outs.append((raw, {"logits": lg, "normed": nm}))
+            res[i].intervals = iv.ctypes.data if iv is not None else None
+            outs.append((raw, {"logits": lg, "normed": nm, "intervals": iv}))
         self._check(L.qa_batch_stage(self._ctx, ctypes.addressof(clips), n,
                                      ctypes.addressof(res)))
         return (clips, res, keep, outs)

@@ -46,6 +46,17 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int col) {
          static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(col));
 }
 
+// Output row of accumulator row `row` (< 0: skip): the periodic layout when
+// row_period > 0, else row_map, else the row itself.
+__device__ __forceinline__ int out_row(const EpiParams& ep, int row) {
+  if (ep.row_period > 0) {
+    const int r = row % ep.row_period;
+    if (r >= ep.row_valid) return -1;
+    return (row / ep.row_period) * ep.row_out_period + ep.row_out_off + r;
+  }
+  return ep.row_map ? ep.row_map[row] : row;
+}
+
 template <typename T>
 __device__ __forceinline__ void store16_row(T* dst, const float (&v)[32], int ncols) {
   if (ncols == 32 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
@@ -389,8 +400,7 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
         break;
       }
       case EPI_STORE32: {
-        int orow = row;
-        if (ep.row_map) orow = ep.row_map[row];
+        const int orow = out_row(ep, row);
         if (orow < 0) break;
         if (ep.pe) {
           const float* pe = ep.pe + (long long)(row % ep.pe_period) * N + col;
@@ -409,6 +419,39 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
           for (int i = 0; i < 32; ++i)
             if (i < nc) dst[i] = v[i];
         }
+        break;
+      }
+      case EPI_SPLIT3: {
+        const int orow = out_row(ep, row);
+        if (orow < 0) break;
+        if (ep.act == ACT_GELU) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+        }
+        if (ep.out2) {
+          float* dst = ep.out2 + (long long)orow * ep.ldo2 + col;
+          if (vec_ok(dst, nc)) {
+            float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (i < nc) dst[i] = v[i];
+          }
+        }
+        float lo[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float hi = h2f<T>(f2h<T>(v[i]));
+          lo[i] = v[i] - hi;
+          v[i] = hi;
+        }
+        T* base = static_cast<T*>(ep.out) + (long long)orow * ep.ldo + col;
+        store16_row<T>(base, v, nc);
+        store16_row<T>(base + N, lo, nc);
+        store16_row<T>(base + 2 * N, v, nc);
         break;
       }
       default:
@@ -522,7 +565,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           mbar_arrive_expect_tx(&full[s], Cfg::kABytes + Cfg::kBBytes);
-          tma_load_2d(&tmA, &full[s], sA + s * Cfg::kABytes, kb * kBK, m0);
+          if (ep.conv_kb > 0)  // implicit conv: tap kb / conv_kb shifts the A rows
+            tma_load_2d(&tmA, &full[s], sA + s * Cfg::kABytes, (kb % ep.conv_kb) * kBK,
+                        m0 + kb / ep.conv_kb);
+          else
+            tma_load_2d(&tmA, &full[s], sA + s * Cfg::kABytes, kb * kBK, m0);
           tma_load_2d(&tmB, &full[s], sB + s * Cfg::kBBytes, kb * kBK, n0);
         }
       }
@@ -1534,7 +1581,9 @@ int launch(const void* A, long long lda, const void* B, long long ldb, int M, in
            const EpiParams& ep, cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
   CUtensorMap ta, tb;
-  int rc = make_tmap_2d(&ta, A, /*bf16=*/H16Traits<T>::kBf16, K, M, lda, kBK, kBM);
+  // an implicit conv reads A as [M, conv_kb * 64]; K spans the taps
+  const int ka = ep.conv_kb > 0 ? ep.conv_kb * kBK : K;
+  int rc = make_tmap_2d(&ta, A, /*bf16=*/H16Traits<T>::kBf16, ka, M, lda, kBK, kBM);
   if (rc) return rc;
   rc = make_tmap_2d(&tb, B, H16Traits<T>::kBf16, K, N, ldb, kBK, BN);
   if (rc) return rc;
@@ -1567,6 +1616,13 @@ int gemm_tc(const void* A, long long lda, const void* B, long long ldb, int M, i
   if ((reinterpret_cast<uintptr_t>(A) & 15u) || (reinterpret_cast<uintptr_t>(B) & 15u) ||
       (lda % 8) || (ldb % 8))
     return (int)cudaErrorInvalidValue;
+  // an implicit conv runs on the one-CTA kernel only, with whole taps of
+  // 64-column k-blocks
+  if (ep.conv_kb > 0) {
+    if (force_bn == -1 || K % (ep.conv_kb * kBK) || lda < ep.conv_kb * kBK)
+      return (int)cudaErrorInvalidValue;
+    if (force_bn == 0) force_bn = gemm_pick_bn(N);
+  }
   // 256 x 256 (or 256 x 224) tiles on CTA pairs whenever N allows (force_bn 0
   // = choose, -1 = require the pair kernel, > 0 = one CTA per tile, that width)
   const bool pair224 = N % 224 == 0 && ep.mode != EPI_SWIGLU16 && ep.mode != EPI_QKV_ROPE;

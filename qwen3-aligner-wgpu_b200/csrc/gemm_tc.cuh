@@ -30,6 +30,13 @@ enum EpiMode : int {
   // out at the head's columns, K appended to the paged cache), v heads are
   // appended as they are.  Tiles must be 256 wide (two heads).
   EPI_QKV_ROPE = 6,
+  // v = act(acc + bias[c]) as an f32-accurate pair of 16-bit values
+  // hi = h16(v), lo = h16(v - hi), stored as three N-wide parts of the output
+  // row, out16[o, c] = hi, out16[o, N + c] = lo, out16[o, 2N + c] = hi (the A
+  // operand of the next three-term product, [hi | lo | hi] . [w_hi | w_hi |
+  // w_lo]); optional out2 f32[o, c] = v.  Output row o from the row period
+  // fields below (or row_map, or the row itself).
+  EPI_SPLIT3 = 7,
 };
 
 // Operands of EPI_QKV_ROPE (norm_rope_head, src/cpu_decoder.rs:305-321).
@@ -63,6 +70,18 @@ struct EpiParams {
   unsigned long long* keys = nullptr;  // EPI_ARGMAX: [M] packed (value, index) keys
   unsigned* status = nullptr;   // device status word (timeouts)
   RopeKV rk;                    // EPI_QKV_ROPE only
+  // EPI_SPLIT3 second output (f32) and its row stride
+  float* out2 = nullptr;
+  long long ldo2 = 0;
+  // Periodic row layout (EPI_SPLIT3 / EPI_STORE32 when row_period > 0): row r
+  // with r % row_period >= row_valid is skipped, the others go to output row
+  // (r / row_period) * row_out_period + row_out_off + r % row_period.
+  int row_period = 0, row_valid = 0, row_out_period = 0, row_out_off = 0;
+  // Implicit 1-D convolution along the rows of A (0 = plain GEMM): A is
+  // [M, conv_kb * 64] and k-block kb reads the 64 columns (kb % conv_kb) * 64
+  // of rows shifted down by kb / conv_kb, so K = taps * conv_kb * 64 covers
+  // rows m .. m + taps - 1 of A for output row m (rows past M read as zeros).
+  int conv_kb = 0;
 };
 
 // Launch D = A·Bᵀ.  A: [M, K] rows lda elements apart; B: [N, K] rows ldb

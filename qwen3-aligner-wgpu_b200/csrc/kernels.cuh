@@ -132,6 +132,60 @@ int head_gather_norm(const void* hidden, int hidden_kind, const int* rows, int n
 int argmax_finalize(const unsigned long long* keys, int n, double segment_ms, long long* raw_ms,
                     cudaStream_t s);
 
+// ---------------------------------------------------------------- Local Head
+// (src/local_head.rs).  Endpoints are the timestamp slots of the batch, clip
+// by clip (2 per word); E counts them.
+constexpr int kLhFrames = 41, kLhFrameLen = 400, kLhNfft = 512, kLhBins = 257;
+constexpr int kLhMels = 80, kLhBands = 4, kLhFeat = 91;
+constexpr int kLhRows = 45;        // rows of an endpoint's conv operand block: 2 + 41 + 2
+constexpr int kLhCh = 128;         // channels per part (91 features zero-padded; 128 hidden)
+constexpr int kLhXw = 3 * kLhCh;   // a conv operand row: [hi | lo | hi]
+
+struct LhClip {
+  long long sample_off;  // first sample of the clip in the batch's sample buffer
+  int n_samples;
+  int ep_off;            // first endpoint (even: clips hold whole words)
+  int n_words;
+  int valid;             // classes inside the audio, clamp(floor(ms / 80) + 1, 1, labels)
+};
+struct LhFeatConst {
+  const float* hann;         // [400] symmetric Hann
+  const float* bank;         // [80][257] unit-sum mel bank
+  const int2* bank_range;    // [80] nonzero bins [x, y) of each bank row
+  const float* mean;         // [91] normalizer
+  const float* stdv;
+  const double2* twiddle;    // [256] exp(-2 pi i k / 512)
+};
+struct LhTailW {
+  const float *cq, *ck, *cv, *co, *aq, *ao;  // [128 in][128 out] (transposed)
+  const float *cbq, *cbk, *cbv, *co_b, *abq, *ao_b;
+  const float *ctx_b, *role, *endpoint;      // [128], [4][128], [2][128]
+  const float *qn_w, *qn_b, *an_w, *an_b, *act_w, *bnd_w, *prior;
+  float act_b, bnd_b, derivative_scale;
+};
+// raw[e] = (first argmax of logits[e][0 .. valid)) * 80, one warp per row.
+int lh_masked_argmax(const float* logits, int E, int n_labels, const LhClip* clips,
+                     const int* ep_clip, long long* raw, cudaStream_t s);
+// fix_timestamps of each clip's raw slots (max_slots bounds 2 * n_words).
+int lh_fix(const long long* raw, const LhClip* clips, int n_clips, int max_slots, long long* fixed,
+           cudaStream_t s);
+// Features of every endpoint -> the first conv's A rows x1 [E * 45][384]
+// bf16 (and the padding rows of the second conv's x2); feat_out optional
+// [E][41][91] f32.
+int lh_features(const float* samples, const LhClip* clips, const int* ep_clip,
+                const long long* fixed, int E, const LhFeatConst& kc, uint16_t* x1, uint16_t* x2,
+                float* feat_out, cudaStream_t s);
+// Context rows [E + E/2][3H] bf16 ([hi | lo | hi]) from the unfolded norm rows.
+int lh_ctx_pack(const float* normed, int E, int H, uint16_t* out, cudaStream_t s);
+// Offsets (ms) of every endpoint from the projected context rows P
+// [E + E/2][128], the audio K/V kv [E * 41][256] and the audio rows
+// audio [E * 41][128].
+int lh_tail(const float* P, const float* kv, const float* audio, const LhClip* clips,
+            const int* ep_clip, int E, const LhTailW& w, float* offsets, cudaStream_t s);
+// Refined intervals [E/2][2] in seconds.
+int lh_repair(const long long* fixed, const float* offsets, const LhClip* clips, int n_clips,
+              double* intervals, cudaStream_t s);
+
 // 16-bit [rows][d] -> f32 widening (text_hidden readback).
 int widen16(const void* x, long long n, float* out, bool bf16, cudaStream_t s);
 

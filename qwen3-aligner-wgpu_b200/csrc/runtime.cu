@@ -12,6 +12,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <functional>
 #include <map>
 #include <numeric>
 #include <thread>
@@ -1056,6 +1057,313 @@ int wait_event(qa_ctx* ctx, cudaEvent_t e) {
   }
 }
 
+// ------------------------------------------------------------ Local Head
+
+constexpr int kLhDim = 128, kLhQwen = 1024, kLhTaps = 5;
+
+// `_mel_filterbank` of the Local Head (src/local_head.rs:927-973): HTK mel
+// points over 0..8 kHz, floored bin edges of a 512-point FFT, triangles, each
+// row normalised to unit sum; [80][257].
+std::vector<float> lh_mel_bank() {
+  auto hz_to_mel = [](double hz) { return 2595.0 * std::log10(1.0 + hz / 700.0); };
+  auto mel_to_hz = [](double m) { return 700.0 * (std::pow(10.0, m / 2595.0) - 1.0); };
+  const double lo = hz_to_mel(0.0), hi = hz_to_mel(8000.0);
+  std::vector<int> edge(kLhMels + 2);
+  for (int i = 0; i < kLhMels + 2; ++i) {
+    const double p = mel_to_hz(lo + (hi - lo) * i / (kLhMels + 1));
+    edge[i] = static_cast<int>(std::max<long long>(static_cast<long long>(std::floor(513.0 * p / 16000.0)), 0));
+  }
+  std::vector<float> bank(static_cast<size_t>(kLhMels) * kLhBins, 0.f);
+  for (int m = 0; m < kLhMels; ++m) {
+    const int l = edge[m], c = std::max(edge[m + 1], l + 1);
+    const int r = std::min(std::max(edge[m + 2], c + 1), kLhBins - 1);
+    if (c >= kLhBins) continue;
+    float* row = &bank[static_cast<size_t>(m) * kLhBins];
+    for (int i = 0; i < c - l; ++i) row[l + i] = static_cast<float>(i) / (c - l);
+    for (int i = 0; i < r - c; ++i) row[c + i] = 1.0f - static_cast<float>(i) / (r - c);
+    float tot = 0.f;
+    for (int b = 0; b < kLhBins; ++b) tot += row[b];
+    if (tot > 0.f)
+      for (int b = 0; b < kLhBins; ++b) row[b] /= tot;
+  }
+  return bank;
+}
+
+// The bf16 pair of an f32: hi = bf16(v), lo = bf16(v - hi).
+void split_bf16(float v, uint16_t* hi, uint16_t* lo) {
+  *hi = f32_to_bf16(v);
+  *lo = f32_to_bf16(v - bf16_to_f32(*hi));
+}
+
+// B operand rows of a three-term product: for output row d, the K-blocks of
+// `width` inputs each hold [w_hi | w_hi | w_lo] (zero past `n_in`).
+void put_b3(std::vector<uint16_t>& dst, size_t row_off, int width, int n_in,
+            const std::function<float(int)>& w) {
+  for (int i = 0; i < width; ++i) {
+    uint16_t h = 0, l = 0;
+    if (i < n_in) split_bf16(w(i), &h, &l);
+    dst[row_off + i] = h;
+    dst[row_off + width + i] = h;
+    dst[row_off + 2 * width + i] = l;
+  }
+}
+
+int lh_load(qa_ctx* ctx, const qa_tensor* t, int n, const float* mean, const float* stdv) {
+  std::map<std::string, const qa_tensor*> by;
+  for (int i = 0; i < n; ++i)
+    if (t[i].name) by[t[i].name] = &t[i];
+  std::map<std::string, std::vector<float>> w;
+  auto get = [&](const char* name, std::vector<int64_t> shape) -> int {
+    auto it = by.find(name);
+    if (it == by.end()) return fail(ctx, QA_ERR_WEIGHTS, "local head tensor %s is missing", name);
+    const qa_tensor& x = *it->second;
+    bool ok = x.dtype == QA_DTYPE_F32 && x.ndim == static_cast<int>(shape.size()) && x.data;
+    size_t count = 1;
+    for (int d = 0; ok && d < x.ndim; ++d) {
+      ok = x.shape[d] == shape[d];
+      count *= static_cast<size_t>(shape[d]);
+    }
+    if (!ok) return fail(ctx, QA_ERR_WEIGHTS, "local head tensor %s is not F32 of the expected shape", name);
+    const float* p = static_cast<const float*>(x.data);
+    w[name].assign(p, p + count);
+    return QA_OK;
+  };
+  const int D = kLhDim;
+  TRY(get("audio.0.weight", {D, kLhFeat, kLhTaps}));
+  TRY(get("audio.0.bias", {D}));
+  TRY(get("audio.2.weight", {D, D, kLhTaps}));
+  TRY(get("audio.2.bias", {D}));
+  TRY(get("context_projection.weight", {D, kLhQwen}));
+  TRY(get("context_projection.bias", {D}));
+  TRY(get("role_embedding.weight", {4, D}));
+  TRY(get("endpoint_embedding.weight", {2, D}));
+  for (const char* a : {"context_attention", "audio_attention"}) {
+    const std::string p(a);
+    TRY(get((p + ".in_proj_weight").c_str(), {3 * D, D}));
+    TRY(get((p + ".in_proj_bias").c_str(), {3 * D}));
+    TRY(get((p + ".out_proj.weight").c_str(), {D, D}));
+    TRY(get((p + ".out_proj.bias").c_str(), {D}));
+  }
+  for (const char* nm : {"query_norm", "audio_norm"}) {
+    TRY(get((std::string(nm) + ".weight").c_str(), {D}));
+    TRY(get((std::string(nm) + ".bias").c_str(), {D}));
+  }
+  TRY(get("activity_bias.weight", {1, D}));
+  TRY(get("activity_bias.bias", {1}));
+  TRY(get("boundary_bias.weight", {1, D}));
+  TRY(get("boundary_bias.bias", {1}));
+  TRY(get("qwen_prior", {13}));
+  {  // a scalar: one F32 element of any rank (src/local_head.rs:834-846)
+    auto it = by.find("derivative_scale");
+    long long cnt = 1;
+    if (it != by.end())
+      for (int d = 0; d < it->second->ndim; ++d) cnt *= it->second->shape[d];
+    if (it == by.end() || it->second->dtype != QA_DTYPE_F32 || cnt != 1 || !it->second->data)
+      return fail(ctx, QA_ERR_WEIGHTS, "local head tensor derivative_scale must be one F32 value");
+    w["derivative_scale"] = {*static_cast<const float*>(it->second->data)};
+  }
+  for (int c = 0; c < kLhFeat; ++c)
+    if (!std::isfinite(mean[c]) || !std::isfinite(stdv[c]) || !(stdv[c] > 0.f))
+      return fail(ctx, QA_ERR_WEIGHTS, "normalizer must be finite with positive std");
+
+  auto L = std::make_unique<LocalHeadDev>();
+  int rc = QA_OK;
+  // the two convs: B row c, tap k = [w_hi | w_hi | w_lo] over the 128 input channels
+  for (int layer = 0; layer < 2; ++layer) {
+    const std::vector<float>& cw = w[layer == 0 ? "audio.0.weight" : "audio.2.weight"];
+    const int cin = layer == 0 ? kLhFeat : D;
+    std::vector<uint16_t> b(static_cast<size_t>(D) * kLhTaps * kLhXw);
+    for (int c = 0; c < D; ++c)
+      for (int k = 0; k < kLhTaps; ++k)
+        put_b3(b, (static_cast<size_t>(c) * kLhTaps + k) * kLhXw, kLhCh, cin,
+               [&](int ic) { return cw[(static_cast<size_t>(c) * cin + ic) * kLhTaps + k]; });
+    void* dev = upload<void>(ctx, b.data(), b.size() * 2, &rc);
+    if (rc) return rc;
+    (layer == 0 ? L->conv1_w : L->conv2_w) = dev;
+  }
+  L->conv1_b = up_f32(ctx, w["audio.0.bias"], &rc);
+  L->conv2_b = up_f32(ctx, w["audio.2.bias"], &rc);
+  // audio attention k / v projections: rows 0..127 k, 128..255 v
+  {
+    const std::vector<float>& ip = w["audio_attention.in_proj_weight"];
+    const std::vector<float>& ib = w["audio_attention.in_proj_bias"];
+    std::vector<uint16_t> b(static_cast<size_t>(2 * D) * kLhXw);
+    for (int r = 0; r < 2 * D; ++r)
+      put_b3(b, static_cast<size_t>(r) * kLhXw, kLhCh, D,
+             [&](int j) { return ip[static_cast<size_t>(D + r) * D + j]; });
+    L->kv_w = upload<void>(ctx, b.data(), b.size() * 2, &rc);
+    L->kv_b = up_f32(ctx, std::vector<float>(ib.begin() + D, ib.end()), &rc);
+  }
+  // context projection over [hi | lo | hi] rows of the 1024-wide context
+  {
+    const std::vector<float>& cw = w["context_projection.weight"];
+    std::vector<uint16_t> b(static_cast<size_t>(D) * 3 * kLhQwen);
+    for (int d = 0; d < D; ++d)
+      put_b3(b, static_cast<size_t>(d) * 3 * kLhQwen, kLhQwen, kLhQwen,
+             [&](int j) { return cw[static_cast<size_t>(d) * kLhQwen + j]; });
+    L->ctx_w = upload<void>(ctx, b.data(), b.size() * 2, &rc);
+    L->ctx_b = up_f32(ctx, w["context_projection.bias"], &rc);
+  }
+  if (rc) return rc;
+  // the tail's 128 x 128 matrices, transposed to [in][out]
+  auto up_t = [&](const std::vector<float>& m, size_t off) {
+    std::vector<float> tr(static_cast<size_t>(D) * D);
+    for (int o = 0; o < D; ++o)
+      for (int i = 0; i < D; ++i) tr[static_cast<size_t>(i) * D + o] = m[off + static_cast<size_t>(o) * D + i];
+    return up_f32(ctx, tr, &rc);
+  };
+  auto slice = [&](const std::vector<float>& v, size_t a, size_t b2) {
+    return up_f32(ctx, std::vector<float>(v.begin() + a, v.begin() + b2), &rc);
+  };
+  LhTailW& T = L->tail;
+  const std::vector<float>& cip = w["context_attention.in_proj_weight"];
+  const std::vector<float>& cib = w["context_attention.in_proj_bias"];
+  const std::vector<float>& aip = w["audio_attention.in_proj_weight"];
+  const std::vector<float>& aib = w["audio_attention.in_proj_bias"];
+  const size_t blk = static_cast<size_t>(D) * D;
+  T.cq = up_t(cip, 0);
+  T.ck = up_t(cip, blk);
+  T.cv = up_t(cip, 2 * blk);
+  T.co = up_t(w["context_attention.out_proj.weight"], 0);
+  T.aq = up_t(aip, 0);
+  T.ao = up_t(w["audio_attention.out_proj.weight"], 0);
+  T.cbq = slice(cib, 0, D);
+  T.cbk = slice(cib, D, 2 * D);
+  T.cbv = slice(cib, 2 * D, 3 * D);
+  T.co_b = up_f32(ctx, w["context_attention.out_proj.bias"], &rc);
+  T.abq = slice(aib, 0, D);
+  T.ao_b = up_f32(ctx, w["audio_attention.out_proj.bias"], &rc);
+  T.ctx_b = L->ctx_b;
+  T.role = up_f32(ctx, w["role_embedding.weight"], &rc);
+  T.endpoint = up_f32(ctx, w["endpoint_embedding.weight"], &rc);
+  T.qn_w = up_f32(ctx, w["query_norm.weight"], &rc);
+  T.qn_b = up_f32(ctx, w["query_norm.bias"], &rc);
+  T.an_w = up_f32(ctx, w["audio_norm.weight"], &rc);
+  T.an_b = up_f32(ctx, w["audio_norm.bias"], &rc);
+  T.act_w = up_f32(ctx, w["activity_bias.weight"], &rc);
+  T.bnd_w = up_f32(ctx, w["boundary_bias.weight"], &rc);
+  T.prior = up_f32(ctx, w["qwen_prior"], &rc);
+  T.act_b = w["activity_bias.bias"][0];
+  T.bnd_b = w["boundary_bias.bias"][0];
+  T.derivative_scale = w["derivative_scale"][0];
+  // feature constants: symmetric Hann (src/local_head.rs:917-925), the mel
+  // bank and its nonzero ranges, the normalizer, the FFT twiddles
+  LhFeatConst& F = L->feat;
+  {
+    std::vector<float> hann(kLhFrameLen);
+    for (int i = 0; i < kLhFrameLen; ++i)
+      hann[i] = static_cast<float>(0.5 - 0.5 * std::cos(2.0 * M_PI * i / (kLhFrameLen - 1)));
+    F.hann = up_f32(ctx, hann, &rc);
+    const std::vector<float> bank = lh_mel_bank();
+    F.bank = up_f32(ctx, bank, &rc);
+    std::vector<int2> range(kLhMels, make_int2(0, 0));
+    for (int m = 0; m < kLhMels; ++m) {
+      int a = -1, z = -1;
+      for (int b = 0; b < kLhBins; ++b)
+        if (bank[static_cast<size_t>(m) * kLhBins + b] != 0.f) {
+          if (a < 0) a = b;
+          z = b + 1;
+        }
+      if (a >= 0) range[m] = make_int2(a, z);
+    }
+    F.bank_range = upload<int2>(ctx, range.data(), range.size() * sizeof(int2), &rc);
+    F.mean = up_f32(ctx, std::vector<float>(mean, mean + kLhFeat), &rc);
+    F.stdv = up_f32(ctx, std::vector<float>(stdv, stdv + kLhFeat), &rc);
+    std::vector<double2> tw(kLhNfft / 2);
+    for (int k = 0; k < kLhNfft / 2; ++k) {
+      const double a = 2.0 * M_PI * k / kLhNfft;
+      tw[k] = make_double2(std::cos(a), -std::sin(a));
+    }
+    F.twiddle = upload<double2>(ctx, tw.data(), tw.size() * sizeof(double2), &rc);
+  }
+  if (rc) return rc;
+  ctx->lh = std::move(L);
+  ctx->lh_on = true;
+  return QA_OK;
+}
+
+// One Local Head pass over E endpoints of n_clips clips, all inputs on the
+// device: samples (clip ranges in `clips`), the head's logits [E][n_labels]
+// and unfolded norm rows [E][1024]; intervals [E/2][2] seconds out.
+int run_local_head(qa_ctx* ctx, int E, int n_clips, const LhClip* clips, const int* ep_clip,
+                   int max_slots, const float* samples, const float* logits, int n_labels,
+                   const float* normed, double* intervals, float* feat_out) {
+  LocalHeadDev& L = *ctx->lh;
+  cudaStream_t s = ctx->stream;
+  const int Wt = E / 2, ctx_rows = E + Wt;
+  const size_t conv_rows = static_cast<size_t>(E) * kLhRows;
+  const size_t frame_rows = static_cast<size_t>(E) * kLhFrames;
+  TRY(ensure(ctx, L.raw, static_cast<size_t>(E) * 8));
+  TRY(ensure(ctx, L.fixed, static_cast<size_t>(E) * 8));
+  TRY(ensure(ctx, L.x1, conv_rows * kLhXw * 2));
+  TRY(ensure(ctx, L.x2, conv_rows * kLhXw * 2));
+  TRY(ensure(ctx, L.audio, frame_rows * kLhDim * 4));
+  TRY(ensure(ctx, L.asplit, frame_rows * kLhXw * 2));
+  TRY(ensure(ctx, L.kv, frame_rows * 2 * kLhDim * 4));
+  TRY(ensure(ctx, L.ctxa, static_cast<size_t>(ctx_rows) * 3 * kLhQwen * 2));
+  TRY(ensure(ctx, L.proj, static_cast<size_t>(ctx_rows) * kLhDim * 4));
+  TRY(ensure(ctx, L.off, static_cast<size_t>(E) * 4));
+  unsigned* status = ctx->status.as<unsigned>();
+  KL("lh_argmax", 0, 4.0 * E * n_labels,
+     lh_masked_argmax(logits, E, n_labels, clips, ep_clip, L.raw.as<long long>(), s));
+  KL("lh_fix", 0, 16.0 * E,
+     lh_fix(L.raw.as<long long>(), clips, n_clips, max_slots, L.fixed.as<long long>(), s));
+  // 41 FFTs of 512 points per endpoint (5 N log2 N flops each, f64)
+  KL("lh_features", 41.0 * 5 * 512 * 9 * E, 41.0 * 400 * 4 * E + 2.0 * conv_rows * kLhXw * 2,
+     lh_features(samples, clips, ep_clip, L.fixed.as<long long>(), E, L.feat, L.x1.as<uint16_t>(),
+                 L.x2.as<uint16_t>(), feat_out, s));
+  EpiParams ep;
+  ep.status = status;
+  ep.mode = EPI_SPLIT3;
+  ep.act = ACT_GELU;
+  ep.conv_kb = kLhXw / 64;
+  ep.row_period = kLhRows;
+  ep.row_valid = kLhFrames;
+  ep.bias = L.conv1_b;
+  ep.out = L.x2.p;
+  ep.ldo = kLhXw;
+  ep.row_out_period = kLhRows;
+  ep.row_out_off = 2;
+  const int Kc = kLhTaps * kLhXw;
+  KL("gemm:lh_conv1", 2.0 * conv_rows * kLhDim * Kc, conv_rows * kLhXw * 4.0,
+     gemm_tc(L.x1.p, kLhXw, L.conv1_w, Kc, static_cast<int>(conv_rows), kLhDim, Kc, true, ep, s, kLhDim));
+  ep.bias = L.conv2_b;
+  ep.out = L.asplit.p;
+  ep.out2 = L.audio.as<float>();
+  ep.ldo2 = kLhDim;
+  ep.row_out_period = kLhFrames;
+  ep.row_out_off = 0;
+  KL("gemm:lh_conv2", 2.0 * conv_rows * kLhDim * Kc, conv_rows * kLhXw * 2.0 + frame_rows * (kLhXw * 2.0 + kLhDim * 4.0),
+     gemm_tc(L.x2.p, kLhXw, L.conv2_w, Kc, static_cast<int>(conv_rows), kLhDim, Kc, true, ep, s, kLhDim));
+  EpiParams e2;
+  e2.status = status;
+  e2.mode = EPI_STORE32;
+  e2.bias = L.kv_b;
+  e2.out = L.kv.p;
+  e2.ldo = 2 * kLhDim;
+  KL("gemm:lh_kv", 2.0 * frame_rows * 2 * kLhDim * kLhXw, frame_rows * (kLhXw * 2.0 + 2 * kLhDim * 4.0),
+     gemm_tc(L.asplit.p, kLhXw, L.kv_w, kLhXw, static_cast<int>(frame_rows), 2 * kLhDim, kLhXw, true, e2, s));
+  KL("lh_ctx_pack", 0, E * kLhQwen * 4.0 + ctx_rows * 3.0 * kLhQwen * 2,
+     lh_ctx_pack(normed, E, kLhQwen, L.ctxa.as<uint16_t>(), s));
+  e2.bias = L.ctx_b;
+  e2.out = L.proj.p;
+  e2.ldo = kLhDim;
+  KL("gemm:lh_ctx", 2.0 * ctx_rows * kLhDim * 3 * kLhQwen, ctx_rows * (3.0 * kLhQwen * 2 + kLhDim * 4.0),
+     gemm_tc(L.ctxa.p, 3 * kLhQwen, L.ctx_w, 3 * kLhQwen, ctx_rows, kLhDim, 3 * kLhQwen, true, e2, s));
+  KL("lh_tail", 2.0 * E * (12.0 * kLhDim * kLhDim + 2.0 * kLhFrames * kLhDim), E * (kLhFrames * 2.0 * kLhDim * 4 + 14.0 * kLhDim * 4),
+     lh_tail(L.proj.as<float>(), L.kv.as<float>(), L.audio.as<float>(), clips, ep_clip, E, L.tail,
+             L.off.as<float>(), s));
+  KL("lh_repair", 0, 12.0 * E,
+     lh_repair(L.fixed.as<long long>(), L.off.as<float>(), clips, n_clips, intervals, s));
+  return QA_OK;
+}
+
+int lh_valid_classes(long long n_samples, int n_labels) {
+  const double ms = static_cast<double>(n_samples) * 1000.0 / 16000.0;
+  const long long by_audio = static_cast<long long>(std::floor(ms / 80.0)) + 1;
+  return static_cast<int>(std::min<long long>(std::max<long long>(by_audio, 1), n_labels));
+}
+
 }  // namespace
 
 // ====================================================================== C ABI
@@ -1124,14 +1432,20 @@ int qa_close(qa_ctx* ctx) {
                     &ctx->hidden_f32, &ctx->status, &ctx->badflag};
   for (DevBuf* b : bufs)
     if (b->p) cudaFree(b->p);
+  if (ctx->lh) {
+    LocalHeadDev& L = *ctx->lh;
+    for (DevBuf* b : {&L.raw, &L.fixed, &L.x1, &L.x2, &L.audio, &L.asplit, &L.kv, &L.ctxa, &L.proj,
+                      &L.off, &L.iv, &L.samples, &L.logits, &L.normed, &L.plan, &L.feat_out})
+      if (b->p) cudaFree(b->p);
+  }
   if (ctx->pin_in.p) cudaFreeHost(ctx->pin_in.p);
   if (ctx->pin_out.p) cudaFreeHost(ctx->pin_out.p);
   if (ctx->pin_res.p) cudaFreeHost(ctx->pin_res.p);
   for (auto& sl : ctx->slots) {
     if (!sl) continue;
-    for (PinBuf* b : {&sl->pin_samples, &sl->pin_plan, &sl->pin_res})
+    for (PinBuf* b : {&sl->pin_samples, &sl->pin_plan, &sl->pin_res, &sl->pin_lh})
       if (b->p) cudaFreeHost(b->p);
-    for (DevBuf* b : {&sl->samples, &sl->plan})
+    for (DevBuf* b : {&sl->samples, &sl->plan, &sl->lh_plan})
       if (b->p) cudaFree(b->p);
     for (auto& e : sl->ev)
       if (e) cudaEventDestroy(e);
@@ -1301,6 +1615,84 @@ int qa_head(qa_ctx* ctx, const float* hidden, int seq, const int* rows, int n_ro
   return check_status(ctx);
 }
 
+int qa_local_head_load(qa_ctx* ctx, const qa_tensor* tensors, int n, const float* mean,
+                       const float* std_) {
+  if (!ctx || !tensors || n <= 0 || !mean || !std_) return QA_ERR_ARG;
+  if (ctx->lh) return fail(ctx, QA_ERR_STATE, "a Local Head is already loaded on this context");
+  CK(cudaSetDevice(ctx->device));
+  const size_t before = ctx->allocations.size();
+  const int rc = lh_load(ctx, tensors, n, mean, std_);
+  if (rc) {
+    for (size_t i = before; i < ctx->allocations.size(); ++i) cudaFree(ctx->allocations[i]);
+    ctx->allocations.resize(before);
+  }
+  return rc;
+}
+
+int qa_set_local_head_enabled(qa_ctx* ctx, int enabled) {
+  if (!ctx) return QA_ERR_ARG;
+  if (enabled && !ctx->lh) return fail(ctx, QA_ERR_STATE, "this checkpoint has no local_head/ package");
+  ctx->lh_on = enabled != 0;
+  return QA_OK;
+}
+
+int qa_local_head_enabled(const qa_ctx* ctx) { return ctx && ctx->lh && ctx->lh_on ? 1 : 0; }
+
+int qa_local_head_refine(qa_ctx* ctx, const float* samples, int64_t n, int n_words,
+                         const float* logits, int n_labels, const float* hidden, int hidden_size,
+                         double* intervals, int64_t* fixed_ms, float* offsets_ms,
+                         float* features) {
+  if (!ctx) return QA_ERR_ARG;
+  if (!ctx->lh) return fail(ctx, QA_ERR_STATE, "no Local Head is loaded on this context");
+  CK(cudaSetDevice(ctx->device));
+  ctx->err.clear();
+  ctx->launches = 0;
+  if (hidden_size != kLhQwen)
+    return fail(ctx, QA_ERR_SHAPE, "hidden size %d != local head context input %d", hidden_size, kLhQwen);
+  if (n <= 0 || !samples) return fail(ctx, QA_ERR_SHAPE, "local head needs non-empty audio");
+  if (n > 0x7FFFFFFF) return fail(ctx, QA_ERR_CAP, "%lld samples exceed the local head's range", (long long)n);
+  if (n_labels <= 0) return fail(ctx, QA_ERR_SHAPE, "timestamp head has no classes");
+  if (n_words < 0) return fail(ctx, QA_ERR_ARG, "negative word count");
+  if (n_words == 0) return QA_OK;
+  if (!logits || !hidden || !intervals) return fail(ctx, QA_ERR_ARG, "null buffer");
+  const int E = 2 * n_words;
+  if (static_cast<size_t>(E) * 20 > 200 * 1024)
+    return fail(ctx, QA_ERR_CAP, "%d words exceed the per-clip repair capacity", n_words);
+  LocalHeadDev& L = *ctx->lh;
+  cudaStream_t s = ctx->stream;
+  TRY(reset_flags(ctx));
+  LhClip cl{0, static_cast<int>(n), 0, n_words, lh_valid_classes(n, n_labels)};
+  std::vector<uint8_t> plan(pad16<LhClip>(1) + static_cast<size_t>(E) * 4, 0);
+  std::memcpy(plan.data(), &cl, sizeof cl);
+  TRY(ensure(ctx, L.samples, static_cast<size_t>(n) * 4));
+  TRY(ensure(ctx, L.logits, static_cast<size_t>(E) * n_labels * 4));
+  TRY(ensure(ctx, L.normed, static_cast<size_t>(E) * kLhQwen * 4));
+  TRY(ensure(ctx, L.plan, plan.size()));
+  TRY(ensure(ctx, L.iv, static_cast<size_t>(E) * 8));
+  if (features) TRY(ensure(ctx, L.feat_out, static_cast<size_t>(E) * kLhFrames * kLhFeat * 4));
+  CK(cudaMemcpyAsync(L.samples.p, samples, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, s));
+  CK(cudaMemcpyAsync(L.logits.p, logits, static_cast<size_t>(E) * n_labels * 4, cudaMemcpyHostToDevice, s));
+  CK(cudaMemcpyAsync(L.normed.p, hidden, static_cast<size_t>(E) * kLhQwen * 4, cudaMemcpyHostToDevice, s));
+  CK(cudaMemcpyAsync(L.plan.p, plan.data(), plan.size(), cudaMemcpyHostToDevice, s));
+  const LhClip* clips_d = L.plan.as<LhClip>();
+  const int* ep_clip_d = reinterpret_cast<const int*>(L.plan.as<uint8_t>() + pad16<LhClip>(1));
+  CK(cudaEventRecord(ctx->ev[0], s));
+  TRY(run_local_head(ctx, E, 1, clips_d, ep_clip_d, E, L.samples.as<float>(), L.logits.as<float>(),
+                     n_labels, L.normed.as<float>(), L.iv.as<double>(),
+                     features ? L.feat_out.as<float>() : nullptr));
+  CK(cudaEventRecord(ctx->ev[1], s));
+  CK(cudaMemcpyAsync(intervals, L.iv.p, static_cast<size_t>(E) * 8, cudaMemcpyDeviceToHost, s));
+  if (fixed_ms) CK(cudaMemcpyAsync(fixed_ms, L.fixed.p, static_cast<size_t>(E) * 8, cudaMemcpyDeviceToHost, s));
+  if (offsets_ms) CK(cudaMemcpyAsync(offsets_ms, L.off.p, static_cast<size_t>(E) * 4, cudaMemcpyDeviceToHost, s));
+  if (features)
+    CK(cudaMemcpyAsync(features, L.feat_out.p, static_cast<size_t>(E) * kLhFrames * kLhFeat * 4,
+                       cudaMemcpyDeviceToHost, s));
+  TRY(wait_stream(ctx));
+  ctx->timings.local_ms = elapsed(ctx, 0, 1);
+  ctx->timings.gpu_launches = ctx->launches;
+  return check_status(ctx);
+}
+
 int qa_batch_stage(qa_ctx* ctx, const qa_clip* clips, int n, const qa_result* results) {
   TRY(need_loaded(ctx));
   const qa_cfg& c = ctx->cfg;
@@ -1327,7 +1719,7 @@ int qa_batch_stage(qa_ctx* ctx, const qa_clip* clips, int n, const qa_result* re
   std::vector<int> frames(n);
   std::vector<uint32_t> ids;
   long long total_samples = 0;
-  S.want_logits = S.want_normed = false;
+  S.want_logits = S.want_normed = S.want_intervals = false;
   S.n_ts.assign(n, 0);
   // ---- validate and plan (host)
   for (int i = 0; i < n; ++i) {
@@ -1352,6 +1744,17 @@ int qa_batch_stage(qa_ctx* ctx, const qa_clip* clips, int n, const qa_result* re
     S.n_ts[i] = ts;
     S.want_logits |= results[i].logits != nullptr;
     S.want_normed |= results[i].normed != nullptr;
+    if (results[i].intervals) {
+      if (!ctx->lh || !ctx->lh_on)
+        return fail(ctx, QA_ERR_STATE, "clip %d asks for Local Head intervals, but it is %s", i,
+                    ctx->lh ? "disabled" : "not loaded");
+      if (ts % 2) return fail(ctx, QA_ERR_SHAPE, "clip %d: %d timestamp tokens do not pair into words", i, ts);
+      if (c.hidden_size != kLhQwen)
+        return fail(ctx, QA_ERR_SHAPE, "hidden size %d != local head context input %d", c.hidden_size, kLhQwen);
+      if (static_cast<size_t>(ts) * 20 > 200 * 1024)
+        return fail(ctx, QA_ERR_CAP, "clip %d: %d timestamp slots exceed the repair capacity", i, ts);
+      S.want_intervals = true;
+    }
     P.mel.push_back({total_samples, static_cast<int>(cl.n_samples), P.total_frames, frames[i], P.total_chunks});
     const int nch = (frames[i] + cs - 1) / cs;
     for (int k = 0; k < nch; ++k) P.chunk_clip.push_back(i);
@@ -1379,6 +1782,20 @@ int qa_batch_stage(qa_ctx* ctx, const qa_clip* clips, int n, const qa_result* re
   }
   plan_decoder(P);
   S.R = static_cast<int>(P.ts_rows.size());
+  S.lh_clips.clear();
+  S.lh_ep_clip.clear();
+  S.lh_max_slots = 0;
+  if (S.want_intervals) {
+    for (int i = 0; i < n; ++i) {
+      // the Local Head runs over the whole batch: every clip's slots pair into words
+      if (S.n_ts[i] % 2)
+        return fail(ctx, QA_ERR_SHAPE, "clip %d: %d timestamp tokens do not pair into words", i, S.n_ts[i]);
+      S.lh_clips.push_back({P.mel[i].sample_off, P.mel[i].n_samples, P.ts_off[i], S.n_ts[i] / 2,
+                            lh_valid_classes(P.mel[i].n_samples, c.num_labels)});
+      S.lh_ep_clip.insert(S.lh_ep_clip.end(), S.n_ts[i], i);
+      S.lh_max_slots = std::max(S.lh_max_slots, S.n_ts[i]);
+    }
+  }
   // ---- inputs to the device (sample staging is pinned; one copy each)
   // The other slot's batch may still be running: this batch's pinned and
   // device input buffers are its own (their previous batch has been fetched),
@@ -1403,13 +1820,25 @@ int qa_batch_stage(qa_ctx* ctx, const qa_clip* clips, int n, const qa_result* re
   CK(cudaEventRecord(S.ev[0], cp));
   CK(cudaMemcpyAsync(S.samples.p, st, total_samples * 4, cudaMemcpyHostToDevice, cp));
   TRY(upload_plan(ctx, P, ids, S.D, S.pin_plan, S.plan, cp));
+  size_t lh_bytes = 0;
+  if (S.want_intervals) {  // the Local Head's clip table and endpoint -> clip map
+    const size_t a = pad16<LhClip>(S.lh_clips.size());
+    lh_bytes = a + S.lh_ep_clip.size() * 4;
+    TRY(ensure_pin(ctx, S.pin_lh, lh_bytes));
+    TRY(ensure(ctx, S.lh_plan, lh_bytes));
+    uint8_t* pl = static_cast<uint8_t*>(S.pin_lh.p);
+    std::memcpy(pl, S.lh_clips.data(), S.lh_clips.size() * sizeof(LhClip));
+    std::memcpy(pl + a, S.lh_ep_clip.data(), S.lh_ep_clip.size() * 4);
+    CK(cudaMemcpyAsync(S.lh_plan.p, pl, lh_bytes, cudaMemcpyHostToDevice, cp));
+  }
   CK(cudaEventRecord(S.ev[1], cp));
   S.h2d_bytes = total_samples * 4 + static_cast<long long>(ids.size()) * 4 +
                  static_cast<long long>(P.mel.size() * sizeof(MelClip) + P.chunk_clip.size() * 4 +
                                         P.co_map.size() * 4 + P.windows.size() * 8 +
                                         P.p2_map.size() * 4 + P.clip_of.size() * 8 +
                                         P.block_tab.size() * 4 + P.tiles.size() * sizeof(AttnTile) +
-                                        P.ts_rows.size() * 4);
+                                        P.ts_rows.size() * 4) +
+                 static_cast<long long>(lh_bytes);
   // workspaces sized here so that qa_batch_run allocates nothing
   const int H = c.hidden_size;
   TRY(ensure(ctx, ctx->mel_scratch, static_cast<size_t>(P.total_frames) * 128 * 4));
@@ -1469,14 +1898,29 @@ int qa_batch_run(qa_ctx* ctx) {
   TRY(run_decoder(ctx, P, D));
   CK(cudaEventRecord(S.ev[6], s));
   // (f) head
-  TRY(run_head(ctx, ctx->hid.p, ctx->bf16 ? 1 : 0, D.ts_rows, S.R, S.want_logits, S.want_normed));
+  TRY(run_head(ctx, ctx->hid.p, ctx->bf16 ? 1 : 0, D.ts_rows, S.R, S.want_logits || S.want_intervals,
+               S.want_normed || S.want_intervals));
   CK(cudaEventRecord(S.ev[7], s));
+  // the Local Head over every word of the batch (logits and unfolded rows
+  // stay on the device)
+  const size_t iv_bytes = S.want_intervals ? static_cast<size_t>(S.R) * 8 : 0;
+  if (S.want_intervals && S.R > 0) {
+    LocalHeadDev& L = *ctx->lh;
+    TRY(ensure(ctx, L.iv, iv_bytes));
+    const LhClip* clips_d = S.lh_plan.as<LhClip>();
+    const int* ep_clip_d = reinterpret_cast<const int*>(
+        S.lh_plan.as<uint8_t>() + pad16<LhClip>(S.lh_clips.size()));
+    TRY(run_local_head(ctx, S.R, n, clips_d, ep_clip_d, S.lh_max_slots, S.samples.as<float>(),
+                       ctx->head_logits.as<float>(), c.num_labels, ctx->head_normed.as<float>(),
+                       L.iv.as<double>(), nullptr));
+  }
+  CK(cudaEventRecord(S.ev[10], s));
   // results and the two status words to this batch's pinned buffer, queued
   // before any later batch can overwrite them
   const size_t raw_bytes = static_cast<size_t>(S.R) * 8;
   const size_t lg_bytes = S.want_logits ? static_cast<size_t>(S.R) * c.num_labels * 4 : 0;
   const size_t nm_bytes = S.want_normed ? static_cast<size_t>(S.R) * H * 4 : 0;
-  TRY(ensure_pin(ctx, S.pin_res, 16 + raw_bytes + lg_bytes + nm_bytes));
+  TRY(ensure_pin(ctx, S.pin_res, 16 + raw_bytes + lg_bytes + nm_bytes + iv_bytes));
   uint8_t* pr = static_cast<uint8_t*>(S.pin_res.p);
   CK(cudaEventRecord(S.ev[8], s));
   CK(cudaMemcpyAsync(pr, ctx->status.p, 4, cudaMemcpyDeviceToHost, s));
@@ -1486,6 +1930,9 @@ int qa_batch_run(qa_ctx* ctx) {
     CK(cudaMemcpyAsync(pr + 16 + raw_bytes, ctx->head_logits.p, lg_bytes, cudaMemcpyDeviceToHost, s));
   if (nm_bytes)
     CK(cudaMemcpyAsync(pr + 16 + raw_bytes + lg_bytes, ctx->head_normed.p, nm_bytes,
+                       cudaMemcpyDeviceToHost, s));
+  if (iv_bytes && S.R > 0)
+    CK(cudaMemcpyAsync(pr + 16 + raw_bytes + lg_bytes + nm_bytes, ctx->lh->iv.p, iv_bytes,
                        cudaMemcpyDeviceToHost, s));
   CK(cudaEventRecord(S.ev[9], s));
   S.launches = ctx->launches;
@@ -1525,12 +1972,16 @@ int qa_batch_fetch(qa_ctx* ctx, qa_result* results) {
   const size_t raw_bytes = static_cast<size_t>(S.R) * 8;
   const size_t lg_bytes = S.want_logits ? static_cast<size_t>(S.R) * c.num_labels * 4 : 0;
   const size_t nm_bytes = S.want_normed ? static_cast<size_t>(S.R) * H * 4 : 0;
+  const size_t iv_bytes = S.want_intervals ? static_cast<size_t>(S.R) * 8 : 0;
   const int64_t* raw = reinterpret_cast<const int64_t*>(pr + 16);
   const float* lg = reinterpret_cast<const float*>(pr + 16 + raw_bytes);
   const float* nm = reinterpret_cast<const float*>(pr + 16 + raw_bytes + lg_bytes);
+  const double* iv = reinterpret_cast<const double*>(pr + 16 + raw_bytes + lg_bytes + nm_bytes);
   for (int i = 0; i < P.n; ++i) {
     const int o = P.ts_off[i], k = P.ts_off[i + 1] - o;
     if (k) std::memcpy(results[i].raw_ms, raw + o, static_cast<size_t>(k) * 8);
+    if (results[i].intervals && iv_bytes && k)
+      std::memcpy(results[i].intervals, iv + o, static_cast<size_t>(k) * 8);
     if (results[i].logits && lg_bytes)
       std::memcpy(results[i].logits, lg + static_cast<size_t>(o) * c.num_labels, static_cast<size_t>(k) * c.num_labels * 4);
     if (results[i].normed && nm_bytes)
@@ -1543,10 +1994,11 @@ int qa_batch_fetch(qa_ctx* ctx, qa_result* results) {
   t.gather_ms = elapsed(S, 4, 5);
   t.prefill_ms = elapsed(S, 5, 6);
   t.head_ms = elapsed(S, 6, 7);
+  t.local_ms = S.want_intervals ? elapsed(S, 7, 10) : 0.0;
   t.d2h_ms = elapsed(S, 8, 9);
-  t.total_ms = t.h2d_ms + elapsed(S, 2, 7) + t.d2h_ms;
+  t.total_ms = t.h2d_ms + elapsed(S, 2, 10) + t.d2h_ms;
   t.h2d_bytes = S.h2d_bytes;
-  t.d2h_bytes = static_cast<long long>(8 + raw_bytes + lg_bytes + nm_bytes);
+  t.d2h_bytes = static_cast<long long>(8 + raw_bytes + lg_bytes + nm_bytes + iv_bytes);
   t.gpu_launches = S.launches;
   return QA_OK;
 }

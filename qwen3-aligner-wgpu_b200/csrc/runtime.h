@@ -122,6 +122,24 @@ struct PlanDev {
 };
 
 
+// The Local Head (src/local_head.rs) on the device: weights in the layouts
+// the kernels and GEMMs read, and the grow-only workspace of one pass.
+struct LocalHeadDev {
+  void* conv1_w = nullptr;  // [128][5 * 384] bf16: per tap [w_hi | w_hi | w_lo] (91 -> 128 ch)
+  void* conv2_w = nullptr;  // [128][5 * 384]
+  float *conv1_b = nullptr, *conv2_b = nullptr;
+  void* kv_w = nullptr;     // [256][384]: audio attention k rows, then v rows
+  float* kv_b = nullptr;    // [256]
+  void* ctx_w = nullptr;    // [128][3 * 1024]
+  float* ctx_b = nullptr;
+  LhTailW tail{};
+  LhFeatConst feat{};
+  // one pass
+  DevBuf raw, fixed, x1, x2, audio, asplit, kv, ctxa, proj, off, iv;
+  // qa_local_head_refine's own inputs and outputs
+  DevBuf samples, logits, normed, plan, feat_out;
+};
+
 // A batch staged by qa_batch_stage, kept until the next stage call.
 // One batch between qa_batch_stage and qa_batch_fetch.  A context holds two,
 // so that the next batch can be staged while the previous one runs: each has
@@ -135,6 +153,12 @@ struct Staged {
   std::vector<int> n_ts;
   int R = 0;
   bool want_logits = false, want_normed = false;
+  bool want_intervals = false;  // the Local Head runs on this batch
+  std::vector<LhClip> lh_clips;
+  std::vector<int> lh_ep_clip;
+  int lh_max_slots = 0;
+  PinBuf pin_lh;
+  DevBuf lh_plan;
   long long h2d_bytes = 0;
   int state = kFree;
   unsigned long long seq = 0;       // staging order
@@ -142,8 +166,8 @@ struct Staged {
   PinBuf pin_samples, pin_plan, pin_res;
   DevBuf samples, plan;  // this batch's device inputs (uploaded on the copy stream)
   // 0/1 around the uploads (copy stream), 2..7 phases of the run, 8/9 around
-  // the result copy
-  cudaEvent_t ev[10] = {};
+  // the result copy, 10 after the Local Head
+  cudaEvent_t ev[11] = {};
 };
 
 // One profiled launch: CUDA events around it on the launching stream.
@@ -190,4 +214,7 @@ struct qa_ctx {
   std::vector<qa_kernel_stat> prof_stats;
   qa_timings timings{};
   long long launches = 0;
+  // Local Head (qa_local_head_load); runs when lh_on
+  std::unique_ptr<qa::LocalHeadDev> lh;
+  bool lh_on = false;
 };

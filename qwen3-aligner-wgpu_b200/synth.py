@@ -218,7 +218,8 @@ def save_safetensors(path: str, tensors: dict) -> None:
     items = []
     for name, v in tensors.items():
         dt, arr = v if isinstance(v, tuple) else ("BF16", v)
-        items.append((name, dt, np.ascontiguousarray(arr, dtype=np_t[dt])))
+        # np.asarray keeps a rank-0 tensor rank 0 (ascontiguousarray would not)
+        items.append((name, dt, np.asarray(arr, dtype=np_t[dt], order="C")))
     header, off = {}, 0
     for name, dt, arr in items:
         nb = arr.nbytes

@@ -47,3 +47,22 @@ def bits_to_f32(bits, half: str):
     if half == "bf16":
         return (b.astype(np.uint32) << 16).view(np.float32)
     return b.view(np.float16).astype(np.float32)
+
+
+@functools.lru_cache(maxsize=None)
+def lh_package(seed: int = 0):
+    """(tensors, mean, std) of the seeded random-init Local Head."""
+    return qa.synth.random_local_head(seed)
+
+
+@functools.lru_cache(maxsize=None)
+def cpu_local_head(seed: int = 0):
+    oracle.build()
+    return oracle.LocalHead(*lh_package(seed))
+
+
+@functools.lru_cache(maxsize=None)
+def gpu_aligner_lh(half: str = "f16", seed: int = 0):
+    """An aligner over the seeded model with the seeded Local Head loaded."""
+    cfg, w = model(seed)
+    return qa.Aligner.load_backend_with_dtype(w, half, cfg=cfg, local_head=lh_package(seed))
