@@ -898,9 +898,12 @@ int ensure_kv(qa_ctx* ctx, int pages) {
   TRY(ensure(ctx, ctx->kcache, bytes));
   TRY(ensure(ctx, ctx->vcache, bytes));
   // Page rows past a clip's end are read by the attention tiles and masked;
-  // start them at zero so that 0 * (stale value) is always 0.
-  CK(cudaMemset(ctx->kcache.p, 0, ctx->kcache.cap));
-  CK(cudaMemset(ctx->vcache.p, 0, ctx->vcache.cap));
+  // start them at zero so that 0 * (stale value) is always 0.  The clear is
+  // ordered on the context's stream: the stream is non-blocking, so a memset
+  // on the legacy default stream could run after the QKV epilogues of the
+  // same pass had appended K/V and wipe them.
+  CK(cudaMemsetAsync(ctx->kcache.p, 0, ctx->kcache.cap, ctx->stream));
+  CK(cudaMemsetAsync(ctx->vcache.p, 0, ctx->vcache.cap, ctx->stream));
   ctx->kv_pages = pages;
   ctx->kv_cap_tokens = std::min(pages * 64, c.max_seq);
   return QA_OK;

@@ -32,12 +32,18 @@ def env():
 
 
 def test_config1_end_to_end(env):
+    """On a fresh context, so that the pass itself grows the paged K/V cache
+    (its clearing must be ordered before the pass's first K/V append)."""
     E = env
     clip = E.qa.synth.workload(1)[0]
-    al = E.gpu_aligner()
+    cfg, w = E.model()
+    al = E.qa.Aligner.load_backend_with_dtype(w, "f16", cfg=cfg)
     inp = al.build_input(clip.samples, clip.text, clip.language)
     assert 1200 < inp.seq_len() < 2200
-    [(raw, extra)] = al.align_inputs([clip.samples], [inp], want_logits=True)
+    try:
+        [(raw, extra)] = al.align_inputs([clip.samples], [inp], want_logits=True)
+    finally:
+        al.close()
     ref = E.cpu_model().align_raw(clip.samples, inp.input_ids, inp.timestamp_positions)
     assert E.rel_err(extra["logits"], ref["logits"]) <= REL
     gated = ref["margin"] > MARGIN
@@ -90,8 +96,11 @@ def test_config3_long_context(env, config3, half):
     assert E.rel_err(prefix, ref) <= tol
     assert np.isfinite(full).all()
 
-    # the whole path at full length, and the head on the full hidden states agree
-    [(raw, _)] = al.align_inputs([clip.samples], [inp])
+    # the whole batched path at full length agrees with the stage-by-stage
+    # path (the GPU tower's rows gathered, text_hidden, head) over all ~7.6k rows
+    [(raw, extra)] = al.align_inputs([clip.samples], [inp], want_logits=True)
     assert len(raw) == 1800 and (raw >= 0).all() and (raw < 5000 * 80).all()
+    _, stage_logits, _ = al.head(full, inp.timestamp_positions)
+    assert E.rel_err(extra["logits"], stage_logits) <= tol
     fixed = E.qa._lib.fix_timestamps(raw)
     assert all(a <= b for a, b in zip(fixed, fixed[1:]))
