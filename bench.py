@@ -25,6 +25,11 @@ over the paged K/V cache -> timestamp head -> argmax.
 
 `--impl reference` times that CPU path alone on the same workload (the
 reference crate is Rust and cannot be built here; the oracle restates it).
+
+`--workload 4` runs BASELINE config 4's clip distribution instead (U(5, 60) s
+English clips at 3 words/s) with the Local Head on: every step also refines
+each word's interval on the device, and the CPU baseline runs the oracle's
+Local Head after its head.
 """
 import argparse
 import datetime
@@ -43,6 +48,11 @@ sys.path.insert(0, ROOT)
 METRIC = "aligned audio-sec/sec per B200 at 1/2/4/8 GPUs; prefill tok/s; % TC/HBM peak"
 UNIT = "audio-s/s"
 L2_FLUSH_BYTES = 256 << 20
+WORKLOADS = {
+    2: "BASELINE config 2: 64 clips/GPU, U(5,30) s, 2.5-3.5 words/s, English + CJK, f16",
+    4: "BASELINE config 4 (per-GPU shard): clips U(5,60) s, English, 3 words/s, f16, "
+       "Local Head on (seed-0 random-init 405k-parameter head)",
+}
 
 
 def parse():
@@ -52,8 +62,13 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--clips", type=int, default=64, help="clips per GPU per step")
+    ap.add_argument("--workload", type=int, default=2, choices=[2, 4],
+                    help="BASELINE config: 2 = U(5,30) s English+CJK clips (the headline); "
+                         "4 = U(5,60) s English clips at 3 words/s with the Local Head on")
     ap.add_argument("--half", default="f16")
-    ap.add_argument("--cpu-sample-clips", type=int, default=4)
+    ap.add_argument("--cpu-sample-clips", type=int, default=None,
+                    help="clips of the CPU baseline's sample (default: about 15 s of CPU "
+                         "work, 12 clips of config 2 or 3 of config 4)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -130,15 +145,25 @@ def build_inputs(qa, clips, builder):
     return inps
 
 
-def cpu_reference(qa, orc, cfg, weights, clips, inps, threads):
+def cpu_align(orc, om, lh, c, inp):
+    """One clip through the CPU restatement: the whole path, and with `lh`
+    (an oracle LocalHead) the refinement of its word intervals as well."""
+    r = om.align_raw(c.samples, inp.input_ids, inp.timestamp_positions)
+    if lh is not None:
+        _, logits, normed, _ = om.head(r["hidden"], inp.timestamp_positions, want_normed=True)
+        lh.refine(c.samples, logits, normed)
+
+
+def cpu_reference(qa, orc, cfg, weights, clips, inps, threads, lh_pkg=None):
     """The oracle (CPU restatement of the reference's --device cpu path) over
     `clips`: audio-seconds per wall second, whole path per clip."""
     orc.set_threads(threads)
     om = orc.Model(weights, cfg)
+    lh = orc.LocalHead(*lh_pkg) if lh_pkg is not None else None
     t0 = time.perf_counter()
     audio = 0.0
     for c, inp in zip(clips, inps):
-        om.align_raw(c.samples, inp.input_ids, inp.timestamp_positions)
+        cpu_align(orc, om, lh, c, inp)
         audio += len(c.samples) / 16000.0
     dt = time.perf_counter() - t0
     return audio / dt, audio, dt
@@ -154,11 +179,12 @@ def run_reference(args):
     orc.build()
     cfg = qa.synth.ModelConfig()
     weights = qa.synth.random_weights(cfg)
-    clips = qa.synth.workload(2, n_clips=args.clips)
+    clips = qa.synth.workload(args.workload, n_clips=args.clips)
     inps = build_inputs(qa, clips, qa.synth.InputBuilder())
     threads = os.cpu_count() or 1
     orc.set_threads(threads)
     om = orc.Model(weights, cfg)
+    lh = orc.LocalHead(*qa.synth.random_local_head(0)) if args.workload == 4 else None
     per_step = 2
     audio = 0.0
     total = 0.0
@@ -167,7 +193,7 @@ def run_reference(args):
         t0 = time.perf_counter()
         a = 0.0
         for i in idx:
-            om.align_raw(clips[i].samples, inps[i].input_ids, inps[i].timestamp_positions)
+            cpu_align(orc, om, lh, clips[i], inps[i])
             a += len(clips[i].samples) / 16000.0
         dt = time.perf_counter() - t0
         if step >= args.warmup:
@@ -179,7 +205,7 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded audio/transcripts, random-init weights)",
-        "config": {"workload": "BASELINE config 2 (64 clips U(5,30) s, English+CJK)",
+        "config": {"workload": WORKLOADS[args.workload],
                    "sample_per_step": f"{per_step} clips of the workload, cycled"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": f"{args.steps} steps x {per_step} clips ({audio:.1f} audio-s); "
@@ -211,8 +237,10 @@ def main():
     qa = importlib.import_module("qwen3-aligner-wgpu_b200")
     cfg = qa.synth.ModelConfig()
     weights = qa.synth.random_weights(cfg)
-    al = qa.Aligner.load_backend_with_dtype(weights, args.half, device=local, cfg=cfg)
-    clips = qa.synth.workload(2, n_clips=args.clips, start=rank * args.clips)
+    lh_pkg = qa.synth.random_local_head(0) if args.workload == 4 else None
+    al = qa.Aligner.load_backend_with_dtype(weights, args.half, device=local, cfg=cfg,
+                                            local_head=lh_pkg)
+    clips = qa.synth.workload(args.workload, n_clips=args.clips, start=rank * args.clips)
     inps = build_inputs(qa, clips, al.input_builder)
     samples = [c.samples for c in clips]
     audio_s = sum(len(s) for s in samples) / 16000.0
@@ -323,8 +351,7 @@ def main():
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": args.half,
             "data": "synthetic (seeded audio/transcripts, random-init weights)",
-            "config": {"workload": "BASELINE config 2: 64 clips/GPU, U(5,30) s, 2.5-3.5 words/s, "
-                                   "English + CJK, f16, one device pass per step",
+            "config": {"workload": WORKLOADS[args.workload] + ", one device pass per step",
                        "clips_per_gpu": args.clips, "audio_s_per_gpu_step": audio_s,
                        "decoder_tokens_per_gpu_step": T_d, "audio_tokens_per_gpu_step": T_a,
                        "l2": "flushed between timed steps (256 MiB write, outside the events)",
@@ -334,7 +361,8 @@ def main():
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(t["h2d_bytes"]) * world,
                     "d2h_bytes_per_step": int(t["d2h_bytes"]) * world,
                     "includes": "split_words + tokenize + pinned staging + H2D + device pass + "
-                                "D2H raw_ms + LIS repair"},
+                                "D2H raw_ms + LIS repair"
+                                + (" + Local Head intervals (device) + D2H" if lh_pkg else "")},
             "gpu_launches": launches,
             "profiled_ms_per_step": prof_ms_max / args.steps,
             "roofline": {"bound": "tensor", "kernel": "gemm_pair_kernel + gemm_tc_kernel (tcgen05, all GEMM launches)",
@@ -346,7 +374,8 @@ def main():
                          "launches_per_step": g["launches"] / args.steps,
                          "flops_per_launch": g["flops"] / max(g["launches"], 1)},
             "kernels": kernels,
-            "phases_ms": {k: t[k] for k in ("mel_ms", "enc_ms", "gather_ms", "prefill_ms", "head_ms")},
+            "phases_ms": {k: t[k] for k in ("mel_ms", "enc_ms", "gather_ms", "prefill_ms", "head_ms",
+                                            "local_ms")},
             "clocks": clk.summary(),
         }
     # ---- CPU baseline (rank 0 at N=1 only; after the GPU phase)
@@ -354,9 +383,10 @@ def main():
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle as orc
         orc.build()
-        k = min(args.cpu_sample_clips, len(clips))
+        k = args.cpu_sample_clips or (12 if args.workload == 2 else 3)
+        k = min(k, len(clips))
         threads = os.cpu_count() or 1
-        v, a, dt = cpu_reference(qa, orc, cfg, weights, clips[:k], inps[:k], threads)
+        v, a, dt = cpu_reference(qa, orc, cfg, weights, clips[:k], inps[:k], threads, lh_pkg)
         out["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
                                "sample": f"first {k} clips of the workload ({a:.1f} audio-s in "
                                          f"{dt:.1f} s), whole path per clip"}

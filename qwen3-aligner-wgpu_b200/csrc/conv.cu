@@ -13,10 +13,6 @@ namespace qa {
 
 namespace {
 
-__device__ __forceinline__ float gelu_erf(float x) {
-  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
-}
-
 // One CTA per (chunk, pair of output rows oh0, oh0 + 1).  The five input rows
 // 2*oh0 - 1 .. 2*oh0 + 3 are staged in shared memory with a zero column on
 // each side (the padding), so the taps need no bounds checks.  Thread j of a
@@ -81,10 +77,11 @@ __global__ void __launch_bounds__(256) conv1_kernel(const float* __restrict__ me
     uint32_t pr[kC1Ch / 2];
 #pragma unroll
     for (int c = 0; c < kC1Ch / 2; ++c) {
-      // gelu_erf on both lanes: taps, then bias; 0.5 * x * (1 + erf(x / sqrt 2))
+      // GELU on both lanes: taps, then bias; 0.5 * x * (1 + erf(x / sqrt 2)),
+      // erf by A&S 7.1.26 (erf_as), as the reference's GPU tower computes it
       const float2 x = add2_rn(a[c], b[c]);
       const float2 z = mul2_rn(x, kRsqrt2);
-      const float2 g = mul2_rn(mul2_rn(kHalf, x), add2_rn(kOne, make_float2(erff(z.x), erff(z.y))));
+      const float2 g = mul2_rn(mul2_rn(kHalf, x), add2_rn(kOne, make_float2(erf_as(z.x), erf_as(z.y))));
       const T lo = f2h<T>(g.x), hi = f2h<T>(g.y);
       pr[c] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&lo)) |
               (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&hi)) << 16);

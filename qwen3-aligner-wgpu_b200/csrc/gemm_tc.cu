@@ -35,6 +35,8 @@ struct GemmCfg {
   static constexpr size_t kSmem = 1024 + kStages * (kABytes + kBBytes) + 256;
 };
 
+// GELU with libm-grade erff: the Local Head's conv layers (src/local_head.rs:
+// 984-986 computes it on the CPU with erff).
 __device__ __forceinline__ float gelu_erf(float x) {
   return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
 }
@@ -363,9 +365,9 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
     }
     switch (ep.mode) {
       case EPI_STORE16: {
-        if (ep.act == ACT_GELU) {
+        if (ep.act == ACT_GELU) {  // the tower's GELU (conv2/conv3, fc1, proj1)
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+          for (int i = 0; i < 32; ++i) v[i] = gelu_as(v[i]);
         }
         int orow = row;
         if (ep.row_map) orow = ep.row_map[row];

@@ -176,15 +176,24 @@ __global__ void lh_fix_kernel(const long long* __restrict__ raw, const LhClip* _
 constexpr int kFeatThreads = 256;
 constexpr int kMagStride = kLhBins;  // 257 floats per frame
 
+// The 41 real frames go through the FFT two at a time, frame 2p as the real
+// and frame 2p + 1 as the imaginary part of one complex transform (21 complex
+// transforms, the last with one frame), kFftGroup transforms at once.  The
+// transforms' buffers are dead once the magnitudes are out, so the
+// mean-removed log spectrum reuses their space.
+constexpr int kFftGroup = 5;
+constexpr int kFftPairs = (kLhFrames + 1) / 2;
+
 struct FeatSmem {
-  double2 buf[kLhNfft];
   double2 tw[kLhNfft / 2];
+  union {
+    double2 buf[kFftGroup][kLhNfft];
+    float nrm[kLhFrames * kMagStride];
+  };
   float mag[kLhFrames * kMagStride];
-  float nrm[kLhFrames * kMagStride];
   float feat[kLhFrames * kLhFeat];
   float energy[kLhFrames];
   float fmean[kLhFrames];
-  float red[kFeatThreads / 32];
 };
 
 __device__ __forceinline__ int bitrev9(int x) { return static_cast<int>(__brev(static_cast<unsigned>(x)) >> 23); }
@@ -206,45 +215,62 @@ __global__ void __launch_bounds__(kFeatThreads)
   const float* audio = samples + cl.sample_off;
   const long long center = fixed[e] * 16000 / 1000;
 
-  for (int f = 0; f < kLhFrames; ++f) {
-    const long long start = center + static_cast<long long>(f - kCtxFrames) * 160 - 200;
-    // bit-reversed load of the zero-padded windowed frame, and its energy
+  // sample j of frame f, Hann-windowed (zero past the audio and past the
+  // 400-sample frame: the FFT input is zero-padded to 512)
+  auto frame_sample = [&](int f, int j) -> float {
+    if (f >= kLhFrames || j >= kLhFrameLen) return 0.f;
+    const long long idx = center + static_cast<long long>(f - kCtxFrames) * 160 - 200 + j;
+    return (idx >= 0 && idx < cl.n_samples) ? audio[idx] * kc.hann[j] : 0.f;
+  };
+  // frame energies: one warp per frame, lanes strided over the samples
+  for (int f = tid >> 5; f < kLhFrames; f += kFeatThreads / 32) {
     float en = 0.f;
-    for (int i = tid; i < kLhNfft; i += kFeatThreads) {
-      const int src = bitrev9(i);
-      float x = 0.f;
-      if (src < kLhFrameLen) {
-        const long long idx = start + src;
-        if (idx >= 0 && idx < cl.n_samples) x = audio[idx] * kc.hann[src];
-      }
+    for (int j = tid & 31; j < kLhFrameLen; j += 32) {
+      const float x = frame_sample(f, j);
       en = fmaf(x, x, en);
-      S.buf[i] = make_double2(static_cast<double>(x), 0.0);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) en += __shfl_xor_sync(0xFFFFFFFFu, en, o);
-    if ((tid & 31) == 0) S.red[tid >> 5] = en;
-    __syncthreads();
-    if (tid == 0) {
-      float t = 0.f;
-      for (int w = 0; w < kFeatThreads / 32; ++w) t += S.red[w];
-      S.energy[f] = t;
+    if ((tid & 31) == 0) S.energy[f] = en;
+  }
+  for (int p0 = 0; p0 < kFftPairs; p0 += kFftGroup) {
+    const int ng = min(kFftGroup, kFftPairs - p0);
+    // bit-reversed load: element i of transform g holds sample bitrev(i) of
+    // frames 2(p0 + g) (real) and 2(p0 + g) + 1 (imaginary)
+    for (int idx = tid; idx < ng * kLhNfft; idx += kFeatThreads) {
+      const int g = idx / kLhNfft, i = idx - g * kLhNfft;
+      const int src = bitrev9(i), f = 2 * (p0 + g);
+      S.buf[g][i] = make_double2(static_cast<double>(frame_sample(f, src)),
+                                 static_cast<double>(frame_sample(f + 1, src)));
     }
-    // radix-2 decimation-in-time stages, one butterfly per thread
+    __syncthreads();
+    // radix-2 decimation-in-time stages, kLhNfft / 2 butterflies per transform
     for (int len = 2; len <= kLhNfft; len <<= 1) {
       const int half = len >> 1;
-      const int b = tid;  // 256 butterflies
-      const int grp = b / half, k = b - grp * half;
-      const int i0 = grp * len + k, i1 = i0 + half;
-      const double2 w = S.tw[k * (kLhNfft / len)];
-      const double2 u = S.buf[i0], x = S.buf[i1];
-      const double tr = w.x * x.x - w.y * x.y;
-      const double ti = w.x * x.y + w.y * x.x;
-      S.buf[i0] = make_double2(u.x + tr, u.y + ti);
-      S.buf[i1] = make_double2(u.x - tr, u.y - ti);
+      for (int b = tid; b < ng * (kLhNfft / 2); b += kFeatThreads) {
+        const int g = b / (kLhNfft / 2), bb = b - g * (kLhNfft / 2);
+        const int grp = bb / half, k = bb - grp * half;
+        const int i0 = grp * len + k, i1 = i0 + half;
+        const double2 w = S.tw[k * (kLhNfft / len)];
+        const double2 u = S.buf[g][i0], x = S.buf[g][i1];
+        const double tr = w.x * x.x - w.y * x.y;
+        const double ti = w.x * x.y + w.y * x.x;
+        S.buf[g][i0] = make_double2(u.x + tr, u.y + ti);
+        S.buf[g][i1] = make_double2(u.x - tr, u.y - ti);
+      }
       __syncthreads();
     }
-    for (int b = tid; b < kLhBins; b += kFeatThreads)
-      S.mag[f * kMagStride + b] = static_cast<float>(hypot(S.buf[b].x, S.buf[b].y));
+    // split Z = A + iB of the real frames a, b:
+    // A[k] = (Z[k] + conj Z[N-k]) / 2, B[k] = (Z[k] - conj Z[N-k]) / 2i
+    for (int idx = tid; idx < ng * kLhBins; idx += kFeatThreads) {
+      const int g = idx / kLhBins, k = idx - g * kLhBins;
+      const int f = 2 * (p0 + g);
+      const double2 z = S.buf[g][k], c = S.buf[g][(kLhNfft - k) & (kLhNfft - 1)];
+      S.mag[f * kMagStride + k] = static_cast<float>(hypot(0.5 * (z.x + c.x), 0.5 * (z.y - c.y)));
+      if (f + 1 < kLhFrames)
+        S.mag[(f + 1) * kMagStride + k] =
+            static_cast<float>(hypot(0.5 * (z.y + c.y), 0.5 * (c.x - z.x)));
+    }
     __syncthreads();
   }
 

@@ -353,6 +353,34 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// 1/x with the hardware approximation (PTX rcp.approx.ftz.f32).
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// erf by Abramowitz & Stegun 7.1.26, erf(a) = 1 - t (a1 + t (a2 + ... + t a5))
+// exp(-a^2) with t = 1 / (1 + p a) for a = |x| and the sign of x restored
+// (|error| <= 1.5e-7 for the exact formula; the approximate reciprocal and
+// exponential add a few 1e-8).  This is the erf of the reference's GPU tower
+// (src/shaders.rs:2607-2625); two MUFU operations and five FMAs per value.
+__device__ __forceinline__ float erf_as(float x) {
+  const float a = fabsf(x);
+  const float t = rcp_approx(fmaf(0.3275911f, a, 1.0f));
+  float p = fmaf(1.061405429f, t, -1.453152027f);
+  p = fmaf(p, t, 1.421413741f);
+  p = fmaf(p, t, -0.284496736f);
+  p = fmaf(p, t, 0.254829592f);
+  const float e = ex2_approx(-a * a * 1.4426950408889634f);  // exp(-a^2)
+  return copysignf(fmaf(-p * t, e, 1.0f), x);
+}
+
+// GELU(x) = x/2 (1 + erf(x / sqrt 2)) with erf_as.
+__device__ __forceinline__ float gelu_as(float x) {
+  return 0.5f * x * (1.0f + erf_as(x * 0.70710678118654752f));
+}
+
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
