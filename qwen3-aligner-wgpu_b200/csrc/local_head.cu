@@ -179,15 +179,26 @@ constexpr int kMagStride = kLhBins;  // 257 floats per frame
 // The 41 real frames go through the FFT two at a time, frame 2p as the real
 // and frame 2p + 1 as the imaginary part of one complex transform (21 complex
 // transforms, the last with one frame), kFftGroup transforms at once.  The
-// transforms' buffers are dead once the magnitudes are out, so the
-// mean-removed log spectrum reuses their space.
-constexpr int kFftGroup = 5;
+// endpoint's audio under the 41 frames (6,800 samples: the frames are 160
+// apart and 400 long) and the Hann window are staged in shared memory first,
+// so that the energy and FFT passes read no global memory.  The staging and
+// the transforms' buffers are dead once the magnitudes are out, so the
+// mean-removed log spectrum reuses their space.  Two CTAs fit on an SM.
+constexpr int kFftGroup = 3;
+static_assert(kLhNfft == 512 && kFeatThreads == 256, "the butterfly indexing assumes 512 points");
 constexpr int kFftPairs = (kLhFrames + 1) / 2;
+constexpr int kWinLen = (kLhFrames - 1) * 160 + kLhFrameLen;
+
+struct FftStage {
+  double2 tw[kLhNfft / 2];
+  double2 buf[kFftGroup][kLhNfft];
+  float win[kWinLen];       // audio[center - 3400 + i], zero outside the clip
+  float hann[kLhFrameLen];
+};
 
 struct FeatSmem {
-  double2 tw[kLhNfft / 2];
   union {
-    double2 buf[kFftGroup][kLhNfft];
+    FftStage fs;
     float nrm[kLhFrames * kMagStride];
   };
   float mag[kLhFrames * kMagStride];
@@ -208,19 +219,26 @@ __global__ void __launch_bounds__(kFeatThreads)
       (reinterpret_cast<uintptr_t>(smem_raw) + 15) & ~static_cast<uintptr_t>(15));
   const int e = blockIdx.x;
   const int tid = threadIdx.x;
-  for (int i = tid; i < kLhNfft / 2; i += kFeatThreads) S.tw[i] = kc.twiddle[i];
+  FftStage& F = S.fs;
+  for (int i = tid; i < kLhNfft / 2; i += kFeatThreads) F.tw[i] = kc.twiddle[i];
+  for (int j = tid; j < kLhFrameLen; j += kFeatThreads) F.hann[j] = kc.hann[j];
   pdl_wait();
   pdl_trigger();
   const LhClip cl = clips[ep_clip[e]];
   const float* audio = samples + cl.sample_off;
   const long long center = fixed[e] * 16000 / 1000;
-
-  // sample j of frame f, Hann-windowed (zero past the audio and past the
-  // 400-sample frame: the FFT input is zero-padded to 512)
+  // frame f starts at center + (f - 20) * 160 - 200 = win start + 160 f
+  const long long win0 = center - static_cast<long long>(kCtxFrames) * 160 - 200;
+  for (int i = tid; i < kWinLen; i += kFeatThreads) {
+    const long long idx = win0 + i;
+    F.win[i] = (idx >= 0 && idx < cl.n_samples) ? audio[idx] : 0.f;
+  }
+  __syncthreads();
+  // sample j of frame f, Hann-windowed (zero past the 400-sample frame: the
+  // FFT input is zero-padded to 512, and past the last frame)
   auto frame_sample = [&](int f, int j) -> float {
     if (f >= kLhFrames || j >= kLhFrameLen) return 0.f;
-    const long long idx = center + static_cast<long long>(f - kCtxFrames) * 160 - 200 + j;
-    return (idx >= 0 && idx < cl.n_samples) ? audio[idx] * kc.hann[j] : 0.f;
+    return F.win[f * 160 + j] * F.hann[j];
   };
   // frame energies: one warp per frame, lanes strided over the samples
   for (int f = tid >> 5; f < kLhFrames; f += kFeatThreads / 32) {
@@ -240,23 +258,24 @@ __global__ void __launch_bounds__(kFeatThreads)
     for (int idx = tid; idx < ng * kLhNfft; idx += kFeatThreads) {
       const int g = idx / kLhNfft, i = idx - g * kLhNfft;
       const int src = bitrev9(i), f = 2 * (p0 + g);
-      S.buf[g][i] = make_double2(static_cast<double>(frame_sample(f, src)),
+      F.buf[g][i] = make_double2(static_cast<double>(frame_sample(f, src)),
                                  static_cast<double>(frame_sample(f + 1, src)));
     }
     __syncthreads();
-    // radix-2 decimation-in-time stages, kLhNfft / 2 butterflies per transform
-    for (int len = 2; len <= kLhNfft; len <<= 1) {
-      const int half = len >> 1;
+    // radix-2 decimation-in-time stages, kLhNfft / 2 butterflies per
+    // transform; stage lh pairs elements 2^lh apart (shifts, no divisions)
+    for (int lh = 0; lh < 9; ++lh) {
+      const int half = 1 << lh;
       for (int b = tid; b < ng * (kLhNfft / 2); b += kFeatThreads) {
-        const int g = b / (kLhNfft / 2), bb = b - g * (kLhNfft / 2);
-        const int grp = bb / half, k = bb - grp * half;
-        const int i0 = grp * len + k, i1 = i0 + half;
-        const double2 w = S.tw[k * (kLhNfft / len)];
-        const double2 u = S.buf[g][i0], x = S.buf[g][i1];
+        const int g = b >> 8, bb = b & (kLhNfft / 2 - 1);
+        const int k = bb & (half - 1);
+        const int i0 = ((bb >> lh) << (lh + 1)) + k, i1 = i0 + half;
+        const double2 w = F.tw[k << (8 - lh)];
+        const double2 u = F.buf[g][i0], x = F.buf[g][i1];
         const double tr = w.x * x.x - w.y * x.y;
         const double ti = w.x * x.y + w.y * x.x;
-        S.buf[g][i0] = make_double2(u.x + tr, u.y + ti);
-        S.buf[g][i1] = make_double2(u.x - tr, u.y - ti);
+        F.buf[g][i0] = make_double2(u.x + tr, u.y + ti);
+        F.buf[g][i1] = make_double2(u.x - tr, u.y - ti);
       }
       __syncthreads();
     }
@@ -265,7 +284,7 @@ __global__ void __launch_bounds__(kFeatThreads)
     for (int idx = tid; idx < ng * kLhBins; idx += kFeatThreads) {
       const int g = idx / kLhBins, k = idx - g * kLhBins;
       const int f = 2 * (p0 + g);
-      const double2 z = S.buf[g][k], c = S.buf[g][(kLhNfft - k) & (kLhNfft - 1)];
+      const double2 z = F.buf[g][k], c = F.buf[g][(kLhNfft - k) & (kLhNfft - 1)];
       S.mag[f * kMagStride + k] = static_cast<float>(hypot(0.5 * (z.x + c.x), 0.5 * (z.y - c.y)));
       if (f + 1 < kLhFrames)
         S.mag[(f + 1) * kMagStride + k] =
@@ -769,6 +788,8 @@ __global__ void lh_repair_kernel(const long long* __restrict__ fixed, const floa
 
 }  // namespace
 
+// 228 KB of shared memory per SM, 1 KB of it reserved per resident CTA
+static_assert(2 * (sizeof(FeatSmem) + 16 + 1024) <= 228 * 1024, "two feature CTAs per SM");
 size_t lh_features_smem() { return sizeof(FeatSmem) + 16; }
 size_t lh_tail_smem() { return sizeof(TailSmem) + 16; }
 
@@ -800,6 +821,10 @@ int lh_features(const float* samples, const LhClip* clips, const int* ep_clip,
   cudaError_t e = cudaFuncSetAttribute(lh_features_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
+  if (e != cudaSuccess) return (int)e;
+  // the whole 228 KB of the SM as shared memory: two CTAs resident
+  e = cudaFuncSetAttribute(lh_features_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared);
   if (e != cudaSuccess) return (int)e;
   return (int)launch_pdl(lh_features_kernel, dim3(E), dim3(kFeatThreads), smem, s, samples, clips,
                          ep_clip, fixed, kc, x1, x2, feat_out);
