@@ -72,6 +72,27 @@ def test_library_fix_timestamps_kats():
         assert lib.fix_timestamps(data) == post.fix_timestamps(data)
 
 
+def test_library_fix_timestamps_long_streams(orc):
+    """The library's O(n log n) chain search against the oracle's O(n^2) scan
+    of the reference (src/postprocess.rs:39-48) on long streams: many equal
+    values (the tie rules pick the parent), runs that fall, constant and
+    reversed streams, and the 1,800 slots of a 300 s clip."""
+    lib = pkg()._lib
+    rng = np.random.default_rng(11)
+    cases = [list(range(2000, 0, -1)), [480] * 1500, [0, 80] * 700]
+    for n in (1, 2, 3, 17, 300, 1800, 4000):
+        cases.append((rng.integers(0, 12, n) * 80).tolist())        # heavy ties
+        cases.append(rng.integers(0, 400000, n).tolist())            # distinct-ish
+        ramp = np.sort(rng.integers(0, 5000, n)) * 80
+        flips = rng.random(n) < 0.1
+        ramp[flips] = rng.integers(0, 5000, int(flips.sum())) * 80  # anomalies
+        cases.append(ramp.tolist())
+    for data in cases:
+        got = lib.fix_timestamps(data)
+        assert got == orc.fix_timestamps(data), len(data)
+        assert all(a <= b for a, b in zip(got, got[1:]))
+
+
 def test_pairing_kat():
     post = pkg().postprocess
     k = KAT["pair_words"]
