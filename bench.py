@@ -137,6 +137,39 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def model_flops(cfg, inp, n_samples) -> float:
+    """Algorithmic FLOPs of one clip's pass (2 per multiply-add): the conv stem
+    per 100-frame chunk (a padded tail chunk counted whole), conv_out, the
+    tower layers' dense projections and windowed attention, the projector,
+    the decoder's dense projections and exact causal attention, and the
+    timestamp head on the 2W slot rows."""
+    def down(x):
+        return (x - 1) // 2 + 1  # conv 3x3, stride 2, pad 1
+    cs = 2 * cfg.n_window
+    frames = n_samples // 160
+    chunks = -(-frames // cs)
+    c, mel = cfg.downsample_hidden, cfg.num_mel_bins
+    h1, w1 = down(mel), down(cs)
+    h2, w2 = down(h1), down(w1)
+    h3, w3 = down(h2), down(w2)
+    conv = 2.0 * (9 * c * h1 * w1 + 9 * c * c * h2 * w2 + 9 * c * c * h3 * w3)
+    d, na = cfg.d_model, inp.n_audio_tokens
+    tower = chunks * conv + na * 2.0 * (c * h3 * d)                       # conv_out
+    tower += cfg.encoder_layers * na * 2.0 * d * (3 * d + d + 2 * cfg.encoder_ffn_dim)
+    win = w3 * (cfg.n_window_infer // cs)
+    ws = [win] * (na // win) + ([na % win] if na % win else [])
+    tower += cfg.encoder_layers * sum(4.0 * w * w * d for w in ws)
+    tower += na * 2.0 * d * (d + cfg.output_dim)                           # proj1, proj2
+    H, L = cfg.hidden_size, inp.seq_len()
+    qd, kvd = cfg.num_heads * cfg.head_dim, cfg.num_kv_heads * cfg.head_dim
+    dense = 2.0 * H * (qd + 2 * kvd) + 2.0 * qd * H + 2.0 * H * 2 * cfg.intermediate_size \
+        + 2.0 * cfg.intermediate_size * H
+    attn = cfg.num_heads * 4.0 * cfg.head_dim * L * (L + 1) / 2
+    dec = cfg.num_layers * (dense * L + attn)
+    head = 2.0 * H * cfg.num_labels * len(inp.timestamp_positions)
+    return tower + dec + head
+
+
 def build_inputs(qa, clips, builder):
     inps = []
     for c in clips:
@@ -246,6 +279,7 @@ def main():
     audio_s = sum(len(s) for s in samples) / 16000.0
     T_d = sum(i.seq_len() for i in inps)
     T_a = sum(i.n_audio_tokens for i in inps)
+    flops_step = sum(model_flops(cfg, i, len(s)) for i, s in zip(inps, samples))
 
     # One created stream for everything timed: the library's kernels, the L2
     # flush and the CUDA events (the legacy default stream has handle 0, which
@@ -336,7 +370,9 @@ def main():
     kernels = {k: {"launches": v["launches"], "ms_per_step": v["total_ms"] / args.steps,
                    "share": v["total_ms"] / total_prof_ms,
                    **({"tflops": v["flops"] / (v["total_ms"] / 1e3) / 1e12} if v["flops"] else {}),
-                   **({"gbs": v["bytes"] / (v["total_ms"] / 1e3) / 1e9} if v["bytes"] and not v["flops"] else {})}
+                   **({"gbs": v["bytes"] / (v["total_ms"] / 1e3) / 1e9,
+                       "hbm_frac": v["bytes"] / (v["total_ms"] / 1e3) / 1e9 / hbm}
+                      if v["bytes"] and not v["flops"] else {})}
                for k, v in sorted(prof.items(), key=lambda kv: -kv[1]["total_ms"])}
     traffic = None
     tr = os.path.join(ROOT, "profiles", "gemm_traffic.json")
@@ -357,6 +393,10 @@ def main():
                        "l2": "flushed between timed steps (256 MiB write, outside the events)",
                        "parallelism": f"clip-sharded x{world}, no collectives"},
             "realtime_factor_per_gpu": value / world,
+            "model_flops_per_gpu_step": flops_step,
+            # the whole pass's algorithmic FLOPs over its device time, against
+            # the measured sustained bf16 peak (HBM-bound kernels included)
+            "tensor_frac_whole_pass": flops_step / (ms_max / args.steps / 1e3) / (tf_sus * 1e12),
             "prefill_tok_s": T_d * world * args.steps / (ms_max / 1e3),
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(t["h2d_bytes"]) * world,
                     "d2h_bytes_per_step": int(t["d2h_bytes"]) * world,
