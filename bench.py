@@ -49,10 +49,16 @@ METRIC = "aligned audio-sec/sec per B200 at 1/2/4/8 GPUs; prefill tok/s; % TC/HB
 UNIT = "audio-s/s"
 L2_FLUSH_BYTES = 256 << 20
 WORKLOADS = {
+    0: "BASELINE config 0: one 10 s clip, 25 English words, f16",
+    1: "BASELINE config 1: one 60 s clip, 180 English words, f16",
     2: "BASELINE config 2: 64 clips/GPU, U(5,30) s, 2.5-3.5 words/s, English + CJK, f16",
     4: "BASELINE config 4 (per-GPU shard): clips U(5,60) s, English, 3 words/s, f16, "
        "Local Head on (seed-0 random-init 405k-parameter head)",
+    3: "BASELINE config 3: one 300 s clip, 900 English words, bf16 storage",
 }
+# CPU-baseline sample per workload (clips); config 3's one clip is minutes of
+# CPU work, so it has none
+CPU_SAMPLE = {0: 1, 1: 1, 2: 12, 3: 0, 4: 3}
 
 
 def parse():
@@ -62,15 +68,20 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--clips", type=int, default=64, help="clips per GPU per step")
-    ap.add_argument("--workload", type=int, default=2, choices=[2, 4],
+    ap.add_argument("--workload", type=int, default=2, choices=[0, 1, 2, 3, 4],
                     help="BASELINE config: 2 = U(5,30) s English+CJK clips (the headline); "
-                         "4 = U(5,60) s English clips at 3 words/s with the Local Head on")
-    ap.add_argument("--half", default="f16")
+                         "4 = U(5,60) s English clips at 3 words/s with the Local Head on; "
+                         "0, 1, 3 = its single clip (10 s, 60 s, 300 s) per step and GPU")
+    ap.add_argument("--half", default=None, help="f16 | bf16 (default: bf16 for config 3, "
+                                                  "else f16)")
     ap.add_argument("--cpu-sample-clips", type=int, default=None,
                     help="clips of the CPU baseline's sample (default: about 15 s of CPU "
                          "work, 12 clips of config 2 or 3 of config 4)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    return ap.parse_args()
+    args = ap.parse_args()
+    if args.half is None:
+        args.half = "bf16" if args.workload == 3 else "f16"
+    return args
 
 
 def peaks():
@@ -218,7 +229,7 @@ def run_reference(args):
     orc.set_threads(threads)
     om = orc.Model(weights, cfg)
     lh = orc.LocalHead(*qa.synth.random_local_head(0)) if args.workload == 4 else None
-    per_step = 2
+    per_step = min(2, len(clips))
     audio = 0.0
     total = 0.0
     for step in range(args.warmup + args.steps):
@@ -273,7 +284,10 @@ def main():
     lh_pkg = qa.synth.random_local_head(0) if args.workload == 4 else None
     al = qa.Aligner.load_backend_with_dtype(weights, args.half, device=local, cfg=cfg,
                                             local_head=lh_pkg)
-    clips = qa.synth.workload(args.workload, n_clips=args.clips, start=rank * args.clips)
+    if args.workload in (2, 4):
+        clips = qa.synth.workload(args.workload, n_clips=args.clips, start=rank * args.clips)
+    else:  # one clip: every rank aligns its own copy
+        clips = qa.synth.workload(args.workload)
     inps = build_inputs(qa, clips, al.input_builder)
     samples = [c.samples for c in clips]
     audio_s = sum(len(s) for s in samples) / 16000.0
@@ -388,7 +402,7 @@ def main():
             "dtype": args.half,
             "data": "synthetic (seeded audio/transcripts, random-init weights)",
             "config": {"workload": WORKLOADS[args.workload] + ", one device pass per step",
-                       "clips_per_gpu": args.clips, "audio_s_per_gpu_step": audio_s,
+                       "clips_per_gpu": len(clips), "audio_s_per_gpu_step": audio_s,
                        "decoder_tokens_per_gpu_step": T_d, "audio_tokens_per_gpu_step": T_a,
                        "l2": "flushed between timed steps (256 MiB write, outside the events)",
                        "parallelism": f"clip-sharded x{world}, no collectives"},
@@ -419,11 +433,15 @@ def main():
             "clocks": clk.summary(),
         }
     # ---- CPU baseline (rank 0 at N=1 only; after the GPU phase)
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not CPU_SAMPLE[args.workload] \
+            and not args.cpu_sample_clips:
+        out["cpu_baseline"] = None
+        out["cpu_baseline_note"] = "none for config 3: its one 300 s clip is minutes of CPU work"
+    elif rank == 0 and world == 1 and not args.no_cpu_baseline:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle as orc
         orc.build()
-        k = args.cpu_sample_clips or (12 if args.workload == 2 else 3)
+        k = args.cpu_sample_clips or CPU_SAMPLE[args.workload]
         k = min(k, len(clips))
         threads = os.cpu_count() or 1
         v, a, dt = cpu_reference(qa, orc, cfg, weights, clips[:k], inps[:k], threads, lh_pkg)
