@@ -162,11 +162,36 @@ int qa_text_hidden(qa_ctx* ctx, const uint16_t* emb, int seq, float* out);
 int qa_head(qa_ctx* ctx, const float* hidden, int seq, const int* rows, int n_rows,
             int64_t* raw_ms, float* logits, float* normed);
 
-/* Timestamp repair (src/postprocess.rs:33-113, `fix_timestamps`): longest
- * non-decreasing subsequence by O(n^2) DP with earliest-index ties; runs of
- * <= 2 outliers snap to the nearer neighbour by index distance, longer runs
- * are interpolated in f64 and truncated toward zero.  out may alias data. */
+/* Timestamp repair (src/postprocess.rs:33-113, `fix_timestamps`): the
+ * longest non-decreasing subsequence with the reference's earliest-index ties
+ * (its O(n^2) DP, :39-48, found here in O(n log n)); runs of <= 2 outliers
+ * snap to the nearer neighbour by index distance, longer runs are
+ * interpolated in f64 and truncated toward zero.  out may alias data. */
 int qa_fix_timestamps(const int64_t* data, int n, int64_t* out);
+
+/* ---------------------------------------------------------------- audio input */
+
+/* mel::load_audio_wav's decode + downmix (src/mel.rs:347-465) over a WAV
+ * file's bytes: 16-bit PCM by the reference's own reader (i16 / 32768.0f,
+ * channels summed in order and divided by their count), 8/24/32-bit PCM,
+ * 32-bit float and the extensible header as the `hound` crate decodes them.
+ * out [out_cap] receives the mono samples at the file's rate; with out NULL
+ * the call only reports n_out, sample_rate and channels (a size query).
+ * QA_ERR_SHAPE: not RIFF/WAVE, no fmt or data chunk, no samples, or a format
+ * neither reader takes; also when out_cap < n_out. */
+int qa_decode_wav(const uint8_t* bytes, int64_t n_bytes, float* out, int64_t out_cap,
+                  int64_t* n_out, int* sample_rate, int* channels);
+/* The length after resampling (librosa fix_length after soxr in
+ * src/mel.rs:537-715): ceil(n * sr_out / sr_in); -1 on bad arguments. */
+int64_t qa_resampled_length(int64_t n, int sr_in, int sr_out);
+/* Mono sample-rate conversion for sources that are not 16 kHz (the soxr HQ
+ * call of src/mel.rs:537-715): a linear-phase Kaiser-windowed sinc low-pass
+ * with soxr HQ's band edges (pass band to 0.913 of the lower Nyquist
+ * frequency, stop band from it, 125 dB), output sample k at input time
+ * k * sr_in / sr_out.  out_len must be qa_resampled_length(n, sr_in, sr_out)
+ * (QA_ERR_SHAPE otherwise).  Same band edges and length as soxr, not the same
+ * bits. */
+int qa_resample(const float* in, int64_t n, int sr_in, int sr_out, float* out, int64_t out_len);
 
 /* Timestamp head without any device allocation.  No counterpart in the
  * reference; it is the qa_head computation for callers that cannot allocate

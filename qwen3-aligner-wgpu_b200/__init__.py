@@ -7,6 +7,7 @@ reference also keeps on the CPU (word splitting, input building, timestamp
 repair) and the seeded synthetic assets the tests and benchmark run on.
 """
 from . import _lib  # noqa: F401
+from . import audio  # noqa: F401
 from . import local_head  # noqa: F401
 from . import postprocess  # noqa: F401
 from . import rope  # noqa: F401

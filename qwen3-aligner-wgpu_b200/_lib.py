@@ -57,6 +57,7 @@ EXPORTED = [
     "qa_get_timings", "qa_mel", "qa_audio_embeds", "qa_ensure_capacity", "qa_text_hidden",
     "qa_head", "qa_align_batch", "qa_batch_stage", "qa_batch_run", "qa_batch_fetch",
     "qa_set_stream", "qa_set_profile", "qa_get_profile", "qa_fix_timestamps",
+    "qa_decode_wav", "qa_resampled_length", "qa_resample",
     "qa_head_noalloc", "qa_local_head_load", "qa_set_local_head_enabled",
     "qa_local_head_enabled", "qa_local_head_refine",
     "qa_k_gemm", "qa_k_conv3x3s2", "qa_k_causal_attention", "qa_k_conv1",
@@ -206,6 +207,13 @@ def _declare(L: ctypes.CDLL) -> None:
         L.qa_align_batch.argtypes = [c_void_p, c_void_p, c_int, c_void_p]
         L.qa_batch_stage.argtypes = [c_void_p, c_void_p, c_int, c_void_p]
         L.qa_fix_timestamps.argtypes = [c_void_p, c_int, c_void_p]
+        L.qa_decode_wav.argtypes = [c_void_p, ctypes.c_int64, c_void_p, ctypes.c_int64,
+                                    ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(c_int),
+                                    ctypes.POINTER(c_int)]
+        L.qa_resampled_length.argtypes = [ctypes.c_int64, c_int, c_int]
+        L.qa_resampled_length.restype = ctypes.c_int64
+        L.qa_resample.argtypes = [c_void_p, ctypes.c_int64, c_int, c_int, c_void_p,
+                                  ctypes.c_int64]
         L.qa_head_noalloc.argtypes = [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p,
                                       c_void_p]
         L.qa_batch_run.argtypes = [c_void_p]

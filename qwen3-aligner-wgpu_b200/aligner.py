@@ -6,6 +6,8 @@ applies:
 
 * ``Aligner.load_backend_with_dtype(model, half)`` — load weights onto one
   CUDA device in the given 16-bit storage format (``"f16"`` default, ``"bf16"``);
+* ``align(path, text, language)`` -> items and ``align_with_raw(path, ...)``
+  -> ``(raw_ms, items)`` — a WAV file (src/align_inference.rs:485-511);
 * ``align_samples(samples, text, language)`` -> ``(raw_ms, items)`` — one clip
   of 16 kHz mono f32 audio (src/align_inference.rs:521-569); with a Local
   Head loaded and enabled the items are its refined word times;
@@ -29,6 +31,7 @@ import os
 import numpy as np
 
 from . import _lib
+from . import audio as _audio
 from . import local_head as _lh
 from . import postprocess
 from . import synth
@@ -162,6 +165,17 @@ class Aligner:
         self.check_language(language)
         words = synth.split_words(text, language)
         return self.input_builder.build(words, synth.valid_mel_frames(len(samples)))
+
+    def align(self, audio, text: str, language=None) -> list:
+        """Word items for a WAV file (src/align_inference.rs:485-492): the file is
+        decoded, downmixed and, if it is not 16 kHz, resampled
+        (audio.load_audio_wav), then aligned as align_samples does."""
+        return self.align_with_raw(audio, text, language)[1]
+
+    def align_with_raw(self, audio, text: str, language=None):
+        """(raw_ms, items) for a WAV file (src/align_inference.rs:501-511)."""
+        self.check_language(language)
+        return self.align_samples(_audio.load_audio_wav(audio), text, language)
 
     def align_samples(self, samples: np.ndarray, text: str, language=None):
         """(raw_ms, items) for one clip (src/align_inference.rs:521-569)."""

@@ -14,7 +14,7 @@ def _declared():
     names = []
     for h in ("qa_b200.h", "qa_b200_kernels.h"):
         src = open(os.path.join(ROOT, "include", h)).read()
-        names += re.findall(r"^\s*(?:int|const char\*)\s+(qa_\w+)\s*\(", src, re.M)
+        names += re.findall(r"^\s*(?:int|int64_t|const char\*)\s+(qa_\w+)\s*\(", src, re.M)
     return sorted(set(names))
 
 
