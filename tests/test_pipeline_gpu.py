@@ -226,3 +226,39 @@ def test_bf16_storage(env):
     assert E.rel_err(extra["logits"], ref["logits"]) <= 6e-2
     gated = ref["margin"] > 0.05
     assert np.array_equal(raw[gated], ref["raw_ms"][gated])
+
+
+def test_align_wav_file(env, tmp_path):
+    """Aligner.align / align_with_raw on WAV files (src/align_inference.rs:485-511):
+    a 16 kHz 16-bit file gives exactly what align_samples gives on the decoded
+    samples; a 44.1 kHz file is resampled to 16 kHz and aligned."""
+    import struct
+    E = env
+    al = E.gpu_aligner()
+    s, text = _clip(E, 3.0, 8, 71)
+    pcm = np.clip(np.round(s * 32767.0), -32768, 32767).astype("<i2")
+
+    def wav(rate, data):
+        fmt = struct.pack("<HHIIHH", 1, 1, rate, rate * 2, 2, 16)
+        body = b"WAVE" + b"fmt " + struct.pack("<I", 16) + fmt + b"data" + \
+            struct.pack("<I", len(data)) + data
+        return b"RIFF" + struct.pack("<I", len(body)) + body
+
+    p16 = tmp_path / "clip16.wav"
+    p16.write_bytes(wav(16000, pcm.tobytes()))
+    raw, items = al.align_with_raw(p16, text, "English")
+    raw_s, items_s = al.align_samples(pcm.astype(np.float32) / np.float32(32768.0), text, "English")
+    assert np.array_equal(raw, raw_s)
+    assert [(i.text, i.start_time, i.end_time) for i in items] == \
+        [(i.text, i.start_time, i.end_time) for i in items_s]
+    assert [i.text for i in al.align(p16, text, "English")] == text.split()
+
+    p44 = tmp_path / "clip44.wav"
+    x44 = E.qa.audio.resample(pcm.astype(np.float32) / np.float32(32768.0), 16000, 44100)
+    p44.write_bytes(wav(44100, np.clip(np.round(x44 * 32767.0), -32768, 32767)
+                        .astype("<i2").tobytes()))
+    items44 = al.align(p44, text, "English")
+    assert [i.text for i in items44] == text.split()
+    assert all(a.end_time <= b.start_time + 1e-9 for a, b in zip(items44, items44[1:]))
+    with pytest.raises(ValueError):
+        al.align(p16, text, "Klingon")
