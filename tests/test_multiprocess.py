@@ -50,6 +50,46 @@ def test_two_gloo_ranks_shard_and_reduce():
     assert all(r[3] == 10.0 for r in res)   # sum over ranks
 
 
+def _crash_main(rank, world, port, q):
+    """Step 1 on both ranks; then rank 1 dies between steps (no collective in
+    flight) and rank 0's next reduction must fail within the group's timeout."""
+    import importlib
+    import sys
+    import time
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    shard = importlib.import_module("qwen3-aligner-wgpu_b200.shard")
+    g = shard.RankGroup(backend="gloo", timeout_s=5)
+    g.barrier()
+    first = g.sum(1.0)
+    if rank == 1:
+        os._exit(3)  # a worker crash between steps
+    t0 = time.monotonic()
+    try:
+        g.max(2.0)
+        q.put((rank, first, "completed", time.monotonic() - t0))
+    except Exception as e:  # the dead peer surfaces as an error, not a hang
+        q.put((rank, first, type(e).__name__, time.monotonic() - t0))
+    os._exit(0)
+
+
+def test_worker_crash_between_steps_is_reported():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_crash_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    rank, first, outcome, waited = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+    assert rank == 0 and first == 2.0
+    assert outcome != "completed" and waited < 60.0
+    assert procs[1].exitcode == 3 and procs[0].exitcode == 0
+
+
 def test_lpt_balances_and_covers():
     shard = pkg().shard
     import random
