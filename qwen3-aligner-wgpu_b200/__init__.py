@@ -12,6 +12,7 @@ from . import local_head  # noqa: F401
 from . import postprocess  # noqa: F401
 from . import rope  # noqa: F401
 from . import shard  # noqa: F401
+from . import sweep  # noqa: F401
 from . import synth  # noqa: F401
 from .aligner import Aligner, FORCED_ALIGNER_LANGUAGES  # noqa: F401
 from ._lib import QaError  # noqa: F401

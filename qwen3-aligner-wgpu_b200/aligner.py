@@ -240,6 +240,25 @@ class Aligner:
             raws = self.fetch(staged)
             yield post(done_inputs, raws)  # overlaps the next batch's device pass
 
+    def align_inputs_stream(self, batches):
+        """align_stream for batches whose inputs are already built: an iterable
+        of (samples_list, inputs) pairs, yielding [(raw_ms, items)] per batch in
+        order, with the same two-deep overlap of host work and device passes."""
+        it = iter(batches)
+        pending = []  # (inputs, staged), oldest first
+        nxt = next(it, None)
+        if nxt is None:
+            return
+        pending.append((nxt[1], self.stage(nxt[0], nxt[1])))
+        self.run()
+        while pending:
+            nxt = next(it, None)
+            if nxt is not None:
+                pending.append((nxt[1], self.stage(nxt[0], nxt[1])))
+                self.run()
+            done_inputs, staged = pending.pop(0)
+            yield self._items(done_inputs, self.fetch(staged), False)
+
     def align_inputs(self, samples_list, inputs, want_logits=False, want_normed=False):
         """The device-resident batched call on prebuilt inputs: [(raw_ms, extra)]."""
         b = self.stage(samples_list, inputs, want_logits, want_normed)

@@ -262,3 +262,25 @@ def test_align_wav_file(env, tmp_path):
     assert all(a.end_time <= b.start_time + 1e-9 for a, b in zip(items44, items44[1:]))
     with pytest.raises(ValueError):
         al.align(p16, text, "Klingon")
+
+
+def test_sweep_matches_align_batch(env, tmp_path):
+    """sweep.py over real passes: a token budget that forces several passes
+    (two in flight) gives each clip exactly what one align_batch gives, and a
+    rerun over the journal aligns nothing."""
+    E = env
+    al = E.gpu_aligner()
+    rng = np.random.default_rng(21)
+    clips = []
+    for k in range(9):
+        s, text = _clip(E, float(rng.uniform(0.8, 6.0)), int(rng.integers(2, 12)), 900 + k)
+        clips.append((s, text, "English"))
+    path = tmp_path / "sweep.jsonl"
+    out = E.qa.sweep.sweep(al, clips, journal=path, token_budget=400, max_clips=3)
+    want = al.align_batch(clips)
+    for k, (raw, items) in enumerate(want):
+        assert out[k][0] == [int(v) for v in raw]
+        assert [(i.text, i.start_time, i.end_time) for i in out[k][1]] == \
+            [(i.text, i.start_time, i.end_time) for i in items]
+    again = E.qa.sweep.sweep(al, clips, journal=path, token_budget=400, max_clips=3)
+    assert again == out or all(again[k][0] == out[k][0] for k in out)
