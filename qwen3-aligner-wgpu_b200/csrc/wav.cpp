@@ -24,13 +24,18 @@
 // same band edges instead: a Kaiser-windowed sinc (Kaiser's window design
 // formulas for the stop-band attenuation and the transition width),
 // evaluated as a polyphase filter at output time t = k * source / target,
-// with f64 coefficients and accumulation.  Results match soxr's in band
-// edges and length, not bit for bit.
+// with f64 coefficients and accumulation.  A rate pair whose reduced ratio
+// has more than 4096 output phases interpolates the taps between 4096
+// tabulated ones.  The tables are built on the host cores and kept for the
+// last few rate pairs.  Results match soxr's in band edges and length, not
+// bit for bit.
 #include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <memory>
+#include <mutex>
 #include <thread>
 #include <vector>
 
@@ -162,6 +167,7 @@ int decode(const uint8_t* b, size_t n, std::vector<float>& mono, int* rate, int*
 constexpr double kPassEnd = 0.913;   // of the lower Nyquist frequency (soxr HQ)
 constexpr double kStopBegin = 1.0;
 constexpr double kAttenDb = 125.0;   // 20-bit quality
+constexpr int kMaxRows = 4096;        // exact polyphase rows up to this many phases
 
 double bessel_i0(double x) {  // power series, converges for every x used here
   double sum = 1.0, term = 1.0;
@@ -180,7 +186,12 @@ struct Filter {
   double cut = 1.0;            // cutoff, fraction of the input Nyquist frequency
   double beta = 0.0;
   double i0_beta = 1.0;
-  std::vector<double> table;   // [up][2 * half] when up is small enough
+  // [rows][2 * half] taps: one row per output phase p / up when up <= kMaxRows
+  // (exact), else kMaxRows + 1 rows at phases r / kMaxRows between which the
+  // taps are interpolated linearly
+  std::vector<double> table;
+  int rows = 0;
+  bool exact = true;
 
   double tap(double tau) const {  // tau: distance in input samples
     const double r = tau / half;
@@ -211,13 +222,35 @@ Filter design(int sr_in, int sr_out) {
   const double dw = M_PI * lower * (kStopBegin - kPassEnd);
   const double taps = (kAttenDb - 7.95) / (2.285 * dw) + 1.0;
   f.half = static_cast<int>(std::ceil(taps / 2.0));
-  if (f.up <= 4096) {
-    f.table.resize(static_cast<size_t>(f.up) * 2 * f.half);
-    for (long long p = 0; p < f.up; ++p)
+  f.exact = f.up <= kMaxRows;
+  f.rows = f.exact ? static_cast<int>(f.up) : kMaxRows + 1;
+  const double den = f.exact ? static_cast<double>(f.up) : static_cast<double>(kMaxRows);
+  f.table.resize(static_cast<size_t>(f.rows) * 2 * f.half);
+  std::atomic<int> next{0};
+  auto rows = [&] {
+    for (int r = next++; r < f.rows; r = next++)
       for (int j = 0; j < 2 * f.half; ++j)
-        f.table[static_cast<size_t>(p) * 2 * f.half + j] =
-            f.tap(static_cast<double>(p) / f.up + (f.half - 1 - j));
-  }
+        f.table[static_cast<size_t>(r) * 2 * f.half + j] = f.tap(r / den + (f.half - 1 - j));
+  };
+  const int nt = std::max(1, std::min<int>(f.rows / 16, static_cast<int>(std::min(16u, std::thread::hardware_concurrency()))));
+  std::vector<std::thread> th;
+  for (int t = 1; t < nt; ++t) th.emplace_back(rows);
+  rows();
+  for (auto& t : th) t.join();
+  return f;
+}
+
+// The filters of the last few rate pairs (a file set usually has one or two
+// source rates), shared by every call.
+std::shared_ptr<const Filter> filter_for(int sr_in, int sr_out) {
+  static std::mutex mu;
+  static std::vector<std::pair<std::pair<int, int>, std::shared_ptr<const Filter>>> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  for (auto& e : cache)
+    if (e.first == std::make_pair(sr_in, sr_out)) return e.second;
+  auto f = std::make_shared<const Filter>(design(sr_in, sr_out));
+  if (cache.size() >= 4) cache.erase(cache.begin());
+  cache.emplace_back(std::make_pair(sr_in, sr_out), f);
   return f;
 }
 
@@ -254,7 +287,8 @@ int qa_resample(const float* in, int64_t n, int sr_in, int sr_out, float* out, i
     std::copy(in, in + n, out);
     return QA_OK;
   }
-  const Filter f = design(sr_in, sr_out);
+  const std::shared_ptr<const Filter> fp = filter_for(sr_in, sr_out);
+  const Filter& f = *fp;
   const int width = 2 * f.half;
   auto one = [&](int64_t k) {
     // output k sits at input time t = k * down / up = n0 + p / up
@@ -262,11 +296,18 @@ int qa_resample(const float* in, int64_t n, int sr_in, int sr_out, float* out, i
     const long long n0 = num / f.up, p = num % f.up;
     const long long first = n0 - f.half + 1;
     double acc = 0.0;
-    const double* row = f.table.empty() ? nullptr : &f.table[static_cast<size_t>(p) * width];
     const long long j0 = std::max<long long>(0, -first), j1 = std::min<long long>(width, n - first);
-    for (long long j = j0; j < j1; ++j) {
-      const double h = row ? row[j] : f.tap(static_cast<double>(p) / f.up + (f.half - 1 - j));
-      acc += h * static_cast<double>(in[first + j]);
+    if (f.exact) {
+      const double* row = &f.table[static_cast<size_t>(p) * width];
+      for (long long j = j0; j < j1; ++j) acc += row[j] * static_cast<double>(in[first + j]);
+    } else {
+      const double pos = static_cast<double>(p) / f.up * kMaxRows;
+      const int r = std::min(static_cast<int>(pos), kMaxRows - 1);
+      const double w = pos - r;
+      const double* a = &f.table[static_cast<size_t>(r) * width];
+      const double* b = a + width;
+      for (long long j = j0; j < j1; ++j)
+        acc += (a[j] + w * (b[j] - a[j])) * static_cast<double>(in[first + j]);
     }
     out[k] = static_cast<float>(acc);
   };

@@ -136,7 +136,7 @@ def test_resample_length_kat(audio):
     assert np.array_equal(audio.resample(x, 16000, 16000), x)
 
 
-@pytest.mark.parametrize("sr_in", [44100, 48000, 22050, 8000])
+@pytest.mark.parametrize("sr_in", [44100, 48000, 22050, 8000, 44101])
 def test_resample_pass_band_and_dc(audio, sr_in):
     t_in = np.arange(sr_in) / sr_in  # 1 s
     lo, hi = 0.2, 0.8  # interior of the output, away from the edges' transients
