@@ -512,7 +512,6 @@ __global__ void __launch_bounds__(kTailThreads)
   const int nep = min(kTailEp, E - e0);
   pdl_wait();
   pdl_trigger();
-  const int words_total = E / 2;
   // 1. role tokens and the endpoint query (src/local_head.rs:555-568)
   for (int idx = tid; idx < kTailEp * 4 * kD; idx += kTailThreads) {
     const int i = idx / (4 * kD), r = (idx / kD) & 3, d = idx & (kD - 1);

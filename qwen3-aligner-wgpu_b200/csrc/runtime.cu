@@ -922,7 +922,6 @@ int run_decoder(qa_ctx* ctx, const Plan& P, const PlanDev& D) {
   TRY(ensure(ctx, ctx->mlp, static_cast<size_t>(T) * I * 2));
   TRY(ensure_kv(ctx, P.total_pages));
   const size_t layer_kv = static_cast<size_t>(ctx->kv_pages) * nkv * 64 * hd;  // elements
-  TokenMap tm{D.clip_of, D.pos_of, D.block_tab, P.max_pages};
   double attn_flops = 0;  // exact causal: 4 * hd * nq per (query, key <= query) pair
   for (int cl = 0; cl < P.n; ++cl) attn_flops += 4.0 * hd * nq * 0.5 * P.seq[cl] * (P.seq[cl] + 1.0);
   const float eps = static_cast<float>(c.rms_norm_eps);
@@ -1714,7 +1713,6 @@ int qa_batch_stage(qa_ctx* ctx, const qa_clip* clips, int n, const qa_result* re
   if (!slot)
     return fail(ctx, QA_ERR_STATE, "two batches are already staged or running; fetch one first");
   Staged& S = *slot;
-  cudaStream_t s = ctx->stream;
   const int cs = 2 * c.n_window;
   Plan& P = S.P;
   P = Plan();
