@@ -36,6 +36,19 @@ def test_null_and_bad_arguments():
     assert L.qa_open(0, 7, None) == lib.QA_ERR_ARG
     out = ctypes.c_void_p()
     assert L.qa_open(0, 5, ctypes.byref(out)) == lib.QA_ERR_ARG
+    # host-only entry points: argument checks, no device needed
+    n, sr, ch = ctypes.c_int64(0), ctypes.c_int(0), ctypes.c_int(0)
+    assert L.qa_decode_wav(None, 10, None, 0, ctypes.byref(n), ctypes.byref(sr),
+                           ctypes.byref(ch)) == lib.QA_ERR_ARG
+    junk = (ctypes.c_uint8 * 64)()
+    assert L.qa_decode_wav(junk, 64, None, 0, ctypes.byref(n), ctypes.byref(sr),
+                           ctypes.byref(ch)) == lib.QA_ERR_SHAPE
+    assert L.qa_resampled_length(100, 0, 16000) == -1
+    assert L.qa_resampled_length(44100, 44100, 16000) == 16000
+    buf = (ctypes.c_float * 16)()
+    assert L.qa_resample(buf, 16, 44100, 16000, buf, 5) == lib.QA_ERR_SHAPE
+    assert L.qa_resample(None, 16, 44100, 16000, buf, 6) == lib.QA_ERR_ARG
+    assert L.qa_fix_timestamps(None, 3, None) == lib.QA_ERR_ARG
 
 
 @pytest.mark.skipif(cuda_ok(), reason="checks the no-device path")
