@@ -27,6 +27,7 @@ from __future__ import annotations
 
 import ctypes
 import os
+import time
 
 import numpy as np
 
@@ -175,7 +176,12 @@ class Aligner:
     def align_with_raw(self, audio, text: str, language=None):
         """(raw_ms, items) for a WAV file (src/align_inference.rs:501-511)."""
         self.check_language(language)
-        return self.align_samples(_audio.load_audio_wav(audio), text, language)
+        t0 = time.perf_counter()
+        samples = _audio.load_audio_wav(audio)
+        wav_ms = (time.perf_counter() - t0) * 1e3
+        out = self.align_samples(samples, text, language)
+        self.timings["wav_ms"] = wav_ms
+        return out
 
     def align_samples(self, samples: np.ndarray, text: str, language=None):
         """(raw_ms, items) for one clip (src/align_inference.rs:521-569)."""
@@ -183,10 +189,28 @@ class Aligner:
 
     def align_batch(self, clips, want_logits: bool = False, want_normed: bool = False):
         """[(samples, text, language)] -> [(raw_ms, items)]; raw_ms is the
-        unrepaired argmax stream, items the repaired word times."""
-        inputs = [self.build_input(s, t, l) for s, t, l in clips]
+        unrepaired argmax stream, items the repaired word times.
+
+        Afterwards ``timings`` holds the device phases of the pass and, as the
+        reference's Timings does (src/align_inference.rs:230-251), the host
+        phases: words_ms (word split), build_ms (tokenise and assemble the
+        input ids) and post_ms (timestamp repair and pairing)."""
+        host = {"words_ms": 0.0, "build_ms": 0.0}
+        inputs = []
+        for s, t, l in clips:
+            self.check_language(l)
+            t0 = time.perf_counter()
+            words = synth.split_words(t, l)
+            t1 = time.perf_counter()
+            inputs.append(self.input_builder.build(words, synth.valid_mel_frames(len(s))))
+            host["words_ms"] += (t1 - t0) * 1e3
+            host["build_ms"] += (time.perf_counter() - t1) * 1e3
         raws = self.align_inputs([c[0] for c in clips], inputs, want_logits, want_normed)
-        return self._items(inputs, raws, want_logits or want_normed)
+        t0 = time.perf_counter()
+        out = self._items(inputs, raws, want_logits or want_normed)
+        host["post_ms"] = (time.perf_counter() - t0) * 1e3
+        self.timings = dict(self.timings or {}, **host)
+        return out
 
     @staticmethod
     def _items(inputs, raws, with_extra: bool) -> list:
