@@ -5,7 +5,9 @@
  * This is the drop-in boundary.  In the reference crate the towers sit behind
  * a private enum (src/align_inference.rs:82-181, `enum Backend { Gpu, Cpu }`)
  * with four methods; a `Backend::Cuda { ctx }` arm binds the functions below
- * one for one (see INTEGRATION.md for the Rust `extern "C"` block):
+ * one for one, through an `extern "C"` block whose Rust types follow the C
+ * types here (int -> c_int, int64_t -> i64, pointers -> *const / *mut, the
+ * structs #[repr(C)] with the same field order):
  *
  *   Backend::half()                 -> qa_half
  *   Backend::audio_embeds(mel, v)   -> qa_audio_embeds
@@ -202,7 +204,9 @@ int qa_resample(const float* in, int64_t n, int sr_in, int sr_out, float* out, i
  * DEVICE pointers the caller owns.  The scratch is one fixed array inside the
  * library (about 8.4 MB, held by every GPU that loads it until exit), so
  * n_rows <= QA_NOALLOC_HEAD_MAX_ROWS and hidden_size <= 1024, else
- * QA_ERR_CAP.  The first call on a device looks up the array's device address
+ * QA_ERR_CAP.  A row index outside [0, seq) is never read: the call returns
+ * QA_ERR_SHAPE (as qa_head does) and leaves the context usable.  The first call
+ * on a device looks up the array's device address
  * (cudaGetSymbolAddress); make that first call before any stream capture.
  * Work runs on the context's stream and the call waits (bounded) for it.
  * Every call shares the one array, so calls that overlap on the GPU (other

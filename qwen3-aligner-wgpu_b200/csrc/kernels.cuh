@@ -70,11 +70,14 @@ inline int conv_channels_padded(int c) { return (c + 63) / 64 * 64; }
 // LayerNorm (eps) over rows of f32 x [rows][d] -> 16-bit out.
 int layernorm_rows(const float* x, int rows, int d, const float* g, const float* b, float eps,
                    void* out, bool bf16, cudaStream_t s);
-// Windowed self-attention over packed audio tokens.  qkv [T][3*dm] 16-bit
-// (q | k | v, head h at columns h*hd), out [T][dm].  Windows are given as
-// (start, len) pairs, len <= 128.
-int window_attention(const void* qkv, int dm, int nh, int hd, const int2* windows, int n_windows,
-                     void* out, bool bf16, cudaStream_t s);
+// Windowed self-attention over packed audio tokens on the tcgen05 tensor
+// cores.  qkv [T][3*dm] 16-bit (q | k | v, head h at columns h*64), out
+// [T][dm].  Windows are (start, len) pairs, 1 <= len <= max_window <= 128,
+// lying inside [0, T); hd must be 64.  A pipeline wait that runs out sets
+// kStatusTimeout in *status.
+int window_attention(const void* qkv, long long T, int dm, int nh, int hd, const int2* windows,
+                     int n_windows, int max_window, void* out, bool bf16, unsigned* status,
+                     cudaStream_t s);
 
 // ---------------------------------------------------------------- decoder
 // RMSNorm over rows of 16-bit x [rows][d] -> 16-bit out, f16(x*inv*w).
@@ -96,24 +99,19 @@ struct TokenMap {
   int max_pages;
 };
 
-// (e) causal GQA flash attention.  Q rows in qkv (row stride ldq, head h at
-// column h*hd), K/V from the paged cache, out [T][nqh*hd].  Work items are
-// (clip, q0) tiles of 64 queries.
+// (e) causal GQA flash attention on the tcgen05 tensor cores.  Q rows in qkv
+// (row stride ldq, head h at column h*hd), K/V from the paged cache, out
+// [T][nqh*hd].  Work items are (clip, q0) tiles of 128 query positions (q0 a
+// multiple of 128 is not required); K/V pages are read by TMA from the
+// layer's pool of `kv_pages` pages; the qkv buffer has `q_rows` rows.
+// Persistent: one CTA per SM.  Malformed tiles and out-of-pool page ids set
+// status bit 2.
 struct AttnTile {
   int clip;
   int q0;       // first query position of the tile within the clip
   int tok0;     // packed token index of position 0 of the clip
   int len;      // clip length
 };
-int causal_attention(const void* qkv, long long ldq, int nqh, int nkvh, int hd,
-                     const AttnTile* tiles, int n_tiles, const int* block_tab, int max_pages,
-                     PagedKV kv, void* out, bool bf16, cudaStream_t s);
-
-// (e) on the tcgen05 tensor cores: the same contract as causal_attention
-// except that each tile covers 128 query positions (q0 a multiple of 128 is
-// not required); K/V pages are read by TMA from the layer's pool of
-// `kv_pages` pages; the qkv buffer has `q_rows` rows.  Persistent: one CTA per
-// SM.  Malformed tiles and out-of-pool page ids set status bit 2.
 int causal_attention_tc(const void* qkv, long long ldq, long long q_rows, int nqh, int nkvh,
                         int hd, const AttnTile* tiles, int n_tiles, const int* block_tab,
                         int max_pages, PagedKV kv, int kv_pages, void* out, bool bf16,
@@ -123,11 +121,19 @@ int causal_attention_tc(const void* qkv, long long ldq, long long q_rows, int nq
 int embed_gather(const uint32_t* ids, int T, const void* table, int vocab, int d, int audio_id,
                  void* out, int* bad, cudaStream_t s);
 
+// Bits of the device flag word `bad` that the gather kernels raise on input
+// they reject (the host turns them into QA_ERR_SHAPE).
+constexpr int kBadTokenId = 1;  // a token id outside the vocabulary
+constexpr int kBadHeadRow = 2;  // a timestamp row outside [0, n_hidden)
+
 // (f) timestamp rows: folded final RMSNorm -> [hi | lo] bf16 split (A operand
 // of the head GEMM); optional unfolded norm rows (f32).
-// hidden_kind: 0 = f16, 1 = bf16, 2 = f32 rows.
-int head_gather_norm(const void* hidden, int hidden_kind, const int* rows, int n_rows, int d,
-                     const float* w, float eps, void* a_hilo, float* unfolded, cudaStream_t s);
+// hidden_kind: 0 = f16, 1 = bf16, 2 = f32 rows.  `hidden` holds n_hidden rows;
+// a row index outside [0, n_hidden) is not read: its operand row is zeroed
+// and kBadHeadRow is or-ed into *bad.
+int head_gather_norm(const void* hidden, int hidden_kind, int n_hidden, const int* rows,
+                     int n_rows, int d, const float* w, float eps, void* a_hilo, float* unfolded,
+                     int* bad, cudaStream_t s);
 // keys -> raw_ms = (int64)(argmax * segment_ms)
 int argmax_finalize(const unsigned long long* keys, int n, double segment_ms, long long* raw_ms,
                     cudaStream_t s);

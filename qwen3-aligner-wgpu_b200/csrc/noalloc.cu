@@ -11,7 +11,6 @@
 // Its scratch (the [rows][2*hidden] bf16 hi/lo operand of the head GEMM and
 // the per-row argmax keys) lives in one file-scope __device__ array of fixed
 // size, which every GPU that loads this library holds until the process exits.
-#include <chrono>
 #include <mutex>
 #include <string>
 
@@ -86,9 +85,16 @@ extern "C" int qa_head_noalloc(qa_ctx* ctx, const float* hidden, int seq, const 
     ctx->err = "qa_head_noalloc: cudaMemsetAsync failed";
     return QA_ERR_CUDA;
   }
-  if (cudaMemsetAsync(ctx->status.p, 0, 4, s) != cudaSuccess) return QA_ERR_CUDA;
-  rc = qa::head_gather_norm(hidden, 2, rows, n_rows, H, ctx->w.final_norm,
-                            static_cast<float>(c.rms_norm_eps), a_hilo, nullptr, s);
+  if (cudaMemsetAsync(ctx->status.p, 0, 4, s) != cudaSuccess ||
+      cudaMemsetAsync(ctx->badflag.p, 0, 4, s) != cudaSuccess) {
+    ctx->err = "qa_head_noalloc: cudaMemsetAsync failed";
+    return QA_ERR_CUDA;
+  }
+  // Row indices outside [0, seq) are never read: the gather zeroes their
+  // operand rows and raises a flag, and the call returns QA_ERR_SHAPE.
+  rc = qa::head_gather_norm(hidden, 2, seq, rows, n_rows, H, ctx->w.final_norm,
+                            static_cast<float>(c.rms_norm_eps), a_hilo, nullptr,
+                            ctx->badflag.as<int>(), s);
   if (!rc) {
     qa::EpiParams ep;
     ep.status = ctx->status.as<unsigned>();
@@ -106,26 +112,10 @@ extern "C" int qa_head_noalloc(qa_ctx* ctx, const float* hidden, int seq, const 
                cudaGetErrorString(static_cast<cudaError_t>(rc));
     return QA_ERR_CUDA;
   }
-  // Bounded wait so that a device-side timeout is reported by this call.
-  if (cudaEventRecord(ctx->ev[11], s) != cudaSuccess) return QA_ERR_CUDA;
-  const auto t0 = std::chrono::steady_clock::now();
-  for (;;) {
-    const cudaError_t q = cudaEventQuery(ctx->ev[11]);
-    if (q == cudaSuccess) break;
-    if (q != cudaErrorNotReady) {
-      ctx->err = std::string("qa_head_noalloc: device error: ") + cudaGetErrorString(q);
-      return QA_ERR_CUDA;
-    }
-    if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(ctx->timeout_ms)) {
-      ctx->err = "qa_head_noalloc: device did not finish in time";
-      return QA_ERR_TIMEOUT;
-    }
-  }
-  unsigned st = 0;
-  if (cudaMemcpy(&st, ctx->status.p, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return QA_ERR_CUDA;
-  if (st & qa::kStatusTimeout) {
-    ctx->err = "qa_head_noalloc: a tensor-core pipeline wait ran out";
-    return QA_ERR_TIMEOUT;
-  }
-  return QA_OK;
+  // Bounded wait (the context's timeout), then the device status words: a
+  // tensor-core wait that ran out gives QA_ERR_TIMEOUT, a rejected row
+  // QA_ERR_SHAPE.
+  rc = qa::wait_stream(ctx);
+  if (rc) return rc;
+  return qa::check_status(ctx);
 }

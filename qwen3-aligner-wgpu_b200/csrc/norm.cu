@@ -179,7 +179,7 @@ __global__ void embed_gather_kernel(const uint32_t* __restrict__ ids, int T_,
   const uint32_t id = ids[t];
   if (static_cast<int>(id) == audio_id) return;  // filled by the projector's scatter
   if (id >= static_cast<uint32_t>(vocab)) {
-    if (v == 0) atomicExch(bad, 1);
+    if (v == 0) atomicOr(bad, kBadTokenId);
     return;
   }
   out[i] = table[static_cast<long long>(id) * dv + v];
@@ -188,13 +188,25 @@ __global__ void embed_gather_kernel(const uint32_t* __restrict__ ids, int T_,
 // ---------------------------------------------------------------- (f) head rows
 // src/align_inference.rs:766-783 (folded) and :748-765 (unfolded): one warp per row.
 template <typename T>
-__global__ void head_norm_kernel(const T* __restrict__ hidden, const int* __restrict__ rows,
-                                 int n_rows, int d, const float* __restrict__ w, float eps,
-                                 __nv_bfloat16* __restrict__ a, float* __restrict__ unfolded) {
+__global__ void head_norm_kernel(const T* __restrict__ hidden, int n_hidden,
+                                 const int* __restrict__ rows, int n_rows, int d,
+                                 const float* __restrict__ w, float eps,
+                                 __nv_bfloat16* __restrict__ a, float* __restrict__ unfolded,
+                                 int* __restrict__ bad) {
   const int r = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (r >= n_rows) return;
-  const T* x = hidden + static_cast<long long>(rows[r]) * d;
+  const int row = rows[r];
+  if (row < 0 || row >= n_hidden) {
+    // never read outside the hidden rows: zero this row's outputs and flag it
+    if (lane == 0) atomicOr(bad, kBadHeadRow);
+    __nv_bfloat16* ar = a + static_cast<long long>(r) * 2 * d;
+    for (int i = lane; i < 2 * d; i += 32) ar[i] = __float2bfloat16_rn(0.0f);
+    if (unfolded)
+      for (int i = lane; i < d; i += 32) unfolded[static_cast<long long>(r) * d + i] = 0.0f;
+    return;
+  }
+  const T* x = hidden + static_cast<long long>(row) * d;
   float v[32];
   float acc = 0.f, a2 = 0.f;
 #pragma unroll
@@ -283,21 +295,22 @@ int embed_gather(const uint32_t* ids, int T_, const void* table, int vocab, int 
   return (int)cudaGetLastError();
 }
 
-int head_gather_norm(const void* hidden, int hidden_kind, const int* rows, int n_rows, int d,
-                     const float* w, float eps, void* a_hilo, float* unfolded, cudaStream_t s) {
+int head_gather_norm(const void* hidden, int hidden_kind, int n_hidden, const int* rows,
+                     int n_rows, int d, const float* w, float eps, void* a_hilo, float* unfolded,
+                     int* bad, cudaStream_t s) {
   if (n_rows <= 0) return 0;
-  if (d > 1024) return (int)cudaErrorInvalidValue;
+  if (d > 1024 || !bad) return (int)cudaErrorInvalidValue;
   const unsigned blocks = (n_rows + 7) / 8;
   auto* a = static_cast<__nv_bfloat16*>(a_hilo);
   if (hidden_kind == 1)
-    head_norm_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(hidden), rows, n_rows,
-                                            d, w, eps, a, unfolded);
+    head_norm_kernel<<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(hidden), n_hidden,
+                                            rows, n_rows, d, w, eps, a, unfolded, bad);
   else if (hidden_kind == 2)
-    head_norm_kernel<<<blocks, 256, 0, s>>>(static_cast<const float*>(hidden), rows, n_rows, d, w,
-                                            eps, a, unfolded);
+    head_norm_kernel<<<blocks, 256, 0, s>>>(static_cast<const float*>(hidden), n_hidden, rows,
+                                            n_rows, d, w, eps, a, unfolded, bad);
   else
-    head_norm_kernel<<<blocks, 256, 0, s>>>(static_cast<const __half*>(hidden), rows, n_rows, d, w,
-                                            eps, a, unfolded);
+    head_norm_kernel<<<blocks, 256, 0, s>>>(static_cast<const __half*>(hidden), n_hidden, rows,
+                                            n_rows, d, w, eps, a, unfolded, bad);
   return (int)cudaGetLastError();
 }
 

@@ -41,6 +41,12 @@ int fail(qa_ctx* ctx, int code, const char* fmt, ...) {
                   "%s: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__, __LINE__);       \
   } while (0)
 
+// QA_ERR_SHAPE for the bits of the device flag word the gather kernels raise.
+int flag_error(qa_ctx* ctx, int bad) {
+  if (bad & kBadTokenId) return fail(ctx, QA_ERR_SHAPE, "a token id is outside the vocabulary");
+  return fail(ctx, QA_ERR_SHAPE, "a timestamp row is outside the hidden rows");
+}
+
 // Launch a kernel (expr returns a cudaError_t value), count it, and when
 // profiling is on bracket it with CUDA events tagged with its kernel class and
 // algorithmic FLOPs / HBM bytes.
@@ -236,38 +242,6 @@ int ensure_pin(qa_ctx* ctx, PinBuf& b, size_t bytes) {
   return QA_OK;
 }
 
-// Bounded wait for everything queued on the context's stream.
-int wait_stream(qa_ctx* ctx) {
-  cudaEvent_t e = ctx->ev[11];
-  CK(cudaEventRecord(e, ctx->stream));
-  const auto t0 = std::chrono::steady_clock::now();
-  for (;;) {
-    const cudaError_t q = cudaEventQuery(e);
-    if (q == cudaSuccess) break;
-    if (q != cudaErrorNotReady)
-      return fail(ctx, QA_ERR_CUDA, "device error: %s", cudaGetErrorString(q));
-    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
-                        std::chrono::steady_clock::now() - t0)
-                        .count();
-    if (ms > ctx->timeout_ms)
-      return fail(ctx, QA_ERR_TIMEOUT, "device did not finish within %d ms", ctx->timeout_ms);
-    std::this_thread::sleep_for(std::chrono::microseconds(50));
-  }
-  if (!ctx->prof_recs.empty()) prof_resolve(ctx);
-  return QA_OK;
-}
-
-int check_status(qa_ctx* ctx) {
-  unsigned st = 0;
-  int bad = 0;
-  CK(cudaMemcpy(&st, ctx->status.p, sizeof st, cudaMemcpyDeviceToHost));
-  CK(cudaMemcpy(&bad, ctx->badflag.p, sizeof bad, cudaMemcpyDeviceToHost));
-  if (st & kStatusTimeout)
-    return fail(ctx, QA_ERR_TIMEOUT, "a tensor-core pipeline wait ran out (status %u)", st);
-  if (bad) return fail(ctx, QA_ERR_SHAPE, "a token id is outside the vocabulary");
-  return QA_OK;
-}
-
 // ------------------------------------------------------------ weights
 
 struct HostT {
@@ -455,6 +429,12 @@ int load_weights(qa_ctx* ctx, const qa_tensor* tensors, int n, const qa_cfg& c) 
       c.head_dim != 128 || c.num_heads != 2 * c.num_kv_heads || c.hidden_size % 256 ||
       c.intermediate_size % 128 || c.num_mel_bins != 128 || c.n_window <= 0)
     return fail(ctx, QA_ERR_SHAPE, "unsupported model geometry");
+  {
+    // the tower's attention windows: 1..128 tokens (104 for n_window_infer 800)
+    const long long ws = feo(2LL * c.n_window) * (c.n_window_infer / (2LL * c.n_window));
+    if (ws <= 0 || ws > 128)
+      return fail(ctx, QA_ERR_SHAPE, "attention window of %lld tokens (1..128 supported)", ws);
+  }
 
   // ---- mel constants (src/mel.rs:19-27, 101-164)
   {
@@ -754,6 +734,7 @@ void plan_audio(Plan& P, const qa_cfg& c, const std::vector<int>& frames) {
   P.T_a = 0;
   P.co_map.assign(static_cast<size_t>(P.total_chunks) * tpc, -1);
   P.windows.clear();
+  P.max_window = 0;
   for (int ci = 0; ci < P.n; ++ci) {
     const int nfull = frames[ci] / cs, tail = frames[ci] % cs;
     const int nch = nfull + (tail > 0);
@@ -766,7 +747,10 @@ void plan_audio(Plan& P, const qa_cfg& c, const std::vector<int>& frames) {
       for (int t = 0; t < valid; ++t) P.co_map[static_cast<size_t>(ch) * tpc + t] = P.T_a + i * tpc + t;
     }
     const int window = (ws > 0 && ws < na) ? ws : na;
-    for (int st = 0; st < na; st += window) P.windows.push_back(make_int2(P.T_a + st, std::min(window, na - st)));
+    for (int st = 0; st < na; st += window) {
+      P.windows.push_back(make_int2(P.T_a + st, std::min(window, na - st)));
+      P.max_window = std::max(P.max_window, std::min(window, na - st));
+    }
     P.T_a += na;
   }
 }
@@ -846,8 +830,9 @@ int run_encoder(qa_ctx* ctx, const Plan& P, const PlanDev& D, void* out16, const
     KL("gemm:enc_qkv", gemm_flops(Ta, 3 * dm, dm), gemm_bytes(Ta, 3 * dm, dm, 2),
        gemm_tc(ctx->h16a.p, dm, L.qkv_w, dm, Ta, 3 * dm, dm, bf, ep, s));
     KL("window_attn", win_flops, 2.0 * Ta * 4 * dm,
-       window_attention(ctx->qkv_enc.p, dm, c.encoder_heads, 64, D.windows,
-                        static_cast<int>(P.windows.size()), ctx->attn_enc.p, bf, s));
+       window_attention(ctx->qkv_enc.p, Ta, dm, c.encoder_heads, 64, D.windows,
+                        static_cast<int>(P.windows.size()), P.max_window, ctx->attn_enc.p, bf,
+                        ctx->status.as<unsigned>(), s));
     ep.mode = EPI_RESID32;
     ep.bias = L.o_b;
     ep.out = ctx->xenc.p;
@@ -979,8 +964,8 @@ int run_decoder(qa_ctx* ctx, const Plan& P, const PlanDev& D) {
 }
 
 // Timestamp head over `rows` of a hidden buffer (kind 0 f16, 1 bf16, 2 f32).
-int run_head(qa_ctx* ctx, const void* hidden, int kind, const int* rows_dev, int R, bool want_logits,
-             bool want_normed) {
+int run_head(qa_ctx* ctx, const void* hidden, int kind, int n_hidden, const int* rows_dev, int R,
+             bool want_logits, bool want_normed) {
   const qa_cfg& c = ctx->cfg;
   cudaStream_t s = ctx->stream;
   const int H = c.hidden_size;
@@ -990,9 +975,10 @@ int run_head(qa_ctx* ctx, const void* hidden, int kind, const int* rows_dev, int
   if (want_logits) TRY(ensure(ctx, ctx->head_logits, static_cast<size_t>(R) * c.num_labels * 4));
   if (want_normed) TRY(ensure(ctx, ctx->head_normed, static_cast<size_t>(R) * H * 4));
   KL("head_norm", 0, R * (H * (kind == 2 ? 4.0 : 2.0) + 4.0 * H),
-     head_gather_norm(hidden, kind, rows_dev, R, H, ctx->w.final_norm,
+     head_gather_norm(hidden, kind, n_hidden, rows_dev, R, H, ctx->w.final_norm,
                       static_cast<float>(c.rms_norm_eps), ctx->head_a.p,
-                      want_normed ? ctx->head_normed.as<float>() : nullptr, s));
+                      want_normed ? ctx->head_normed.as<float>() : nullptr,
+                      ctx->badflag.as<int>(), s));
   CK(cudaMemsetAsync(ctx->head_keys.p, 0, static_cast<size_t>(R) * 8, s));
   EpiParams ep;
   ep.status = ctx->status.as<unsigned>();
@@ -1368,6 +1354,39 @@ int lh_valid_classes(long long n_samples, int n_labels) {
 
 }  // namespace
 
+// Bounded wait for everything queued on the context's stream.
+int qa::wait_stream(qa_ctx* ctx) {
+  cudaEvent_t e = ctx->ev[11];
+  CK(cudaEventRecord(e, ctx->stream));
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t q = cudaEventQuery(e);
+    if (q == cudaSuccess) break;
+    if (q != cudaErrorNotReady)
+      return fail(ctx, QA_ERR_CUDA, "device error: %s", cudaGetErrorString(q));
+    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                        std::chrono::steady_clock::now() - t0)
+                        .count();
+    if (ms > ctx->timeout_ms)
+      return fail(ctx, QA_ERR_TIMEOUT, "device did not finish within %d ms", ctx->timeout_ms);
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+  if (!ctx->prof_recs.empty()) prof_resolve(ctx);
+  return QA_OK;
+}
+
+int qa::check_status(qa_ctx* ctx) {
+  unsigned st = 0;
+  int bad = 0;
+  CK(cudaMemcpy(&st, ctx->status.p, sizeof st, cudaMemcpyDeviceToHost));
+  CK(cudaMemcpy(&bad, ctx->badflag.p, sizeof bad, cudaMemcpyDeviceToHost));
+  if (st & kStatusTimeout)
+    return fail(ctx, QA_ERR_TIMEOUT, "a tensor-core pipeline wait ran out (status %u)", st);
+  if (bad) return flag_error(ctx, bad);
+  return QA_OK;
+}
+
+
 // ====================================================================== C ABI
 
 extern "C" {
@@ -1607,7 +1626,8 @@ int qa_head(qa_ctx* ctx, const float* hidden, int seq, const int* rows, int n_ro
   TRY(ensure(ctx, ctx->idx_dev, static_cast<size_t>(n_rows) * 4));
   CK(cudaMemcpyAsync(ctx->hidden_f32.p, hidden, static_cast<size_t>(seq) * H * 4, cudaMemcpyHostToDevice, ctx->stream));
   CK(cudaMemcpyAsync(ctx->idx_dev.p, rows, static_cast<size_t>(n_rows) * 4, cudaMemcpyHostToDevice, ctx->stream));
-  TRY(run_head(ctx, ctx->hidden_f32.p, 2, ctx->idx_dev.as<int>(), n_rows, logits != nullptr, normed != nullptr));
+  TRY(run_head(ctx, ctx->hidden_f32.p, 2, seq, ctx->idx_dev.as<int>(), n_rows, logits != nullptr,
+               normed != nullptr));
   CK(cudaMemcpyAsync(raw_ms, ctx->head_raw.p, static_cast<size_t>(n_rows) * 8, cudaMemcpyDeviceToHost, ctx->stream));
   if (logits)
     CK(cudaMemcpyAsync(logits, ctx->head_logits.p, static_cast<size_t>(n_rows) * c.num_labels * 4, cudaMemcpyDeviceToHost, ctx->stream));
@@ -1899,8 +1919,8 @@ int qa_batch_run(qa_ctx* ctx) {
   TRY(run_decoder(ctx, P, D));
   CK(cudaEventRecord(S.ev[6], s));
   // (f) head
-  TRY(run_head(ctx, ctx->hid.p, ctx->bf16 ? 1 : 0, D.ts_rows, S.R, S.want_logits || S.want_intervals,
-               S.want_normed || S.want_intervals));
+  TRY(run_head(ctx, ctx->hid.p, ctx->bf16 ? 1 : 0, P.T_d, D.ts_rows, S.R,
+               S.want_logits || S.want_intervals, S.want_normed || S.want_intervals));
   CK(cudaEventRecord(S.ev[7], s));
   // the Local Head over every word of the batch (logits and unfolded rows
   // stay on the device)
@@ -1969,7 +1989,7 @@ int qa_batch_fetch(qa_ctx* ctx, qa_result* results) {
   std::memcpy(&bad, pr + 4, 4);
   if (st & kStatusTimeout)
     return fail(ctx, QA_ERR_TIMEOUT, "a tensor-core pipeline wait ran out (status %u)", st);
-  if (bad) return fail(ctx, QA_ERR_SHAPE, "a token id is outside the vocabulary");
+  if (bad) return flag_error(ctx, bad);
   const size_t raw_bytes = static_cast<size_t>(S.R) * 8;
   const size_t lg_bytes = S.want_logits ? static_cast<size_t>(S.R) * c.num_labels * 4 : 0;
   const size_t nm_bytes = S.want_normed ? static_cast<size_t>(S.R) * H * 4 : 0;

@@ -93,6 +93,7 @@ struct Plan {
   int T_a = 0;
   std::vector<int> co_map;     // [total_chunks*13] -> packed audio row or -1
   std::vector<int2> windows;   // encoder windows
+  int max_window = 0;          // longest window (tokens)
   // decoder
   std::vector<int> tok0, seq;
   int T_d = 0;
@@ -176,6 +177,12 @@ struct ProfRec {
   int ev0, ev1;
   double flops, bytes;
 };
+
+// Bounded wait for everything queued on the context's stream (the context's
+// timeout), then the device status words: QA_ERR_TIMEOUT for a tensor-core
+// pipeline wait that ran out, QA_ERR_SHAPE for an input a kernel rejected.
+int wait_stream(qa_ctx* ctx);
+int check_status(qa_ctx* ctx);
 
 }  // namespace qa
 

@@ -59,3 +59,29 @@ def test_head_noalloc_rejects_rows_beyond_its_scratch(env):
     with pytest.raises(E.qa.QaError) as ei:
         _noalloc(E, al, hidden, np.arange(2049), want_logits=False)
     assert ei.value.code == E.qa._lib.QA_ERR_CAP  # QA_NOALLOC_HEAD_MAX_ROWS = 2048
+
+
+def test_head_noalloc_rejects_rows_outside_hidden(env):
+    """A row index at or past `seq` (or below 0) is never read: the call
+    returns QA_ERR_SHAPE as qa_head does, and the context keeps working.
+    The hidden buffer holds more rows than the `seq` passed, so even an
+    unguarded read of the bad index would stay inside valid memory."""
+    E = env
+    al = E.gpu_aligner()
+    rng = np.random.default_rng(23)
+    seq = 64
+    hidden = (rng.standard_normal((seq + 16, al.cfg.hidden_size))).astype(np.float32)
+    import torch
+    lib = E.qa._lib
+    h = torch.from_numpy(hidden).cuda()
+    raw = torch.zeros(3, dtype=torch.int64, device="cuda")
+    for bad in ([0, seq, 5], [3, -1, 7]):
+        r = torch.tensor(bad, dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+        rc = lib.lib().qa_head_noalloc(al._ctx, h.data_ptr(), seq, r.data_ptr(), 3,
+                                       raw.data_ptr(), None)
+        assert rc == lib.QA_ERR_SHAPE, rc
+    rows = np.array([0, seq - 1, 9])
+    raw_ref, _, _ = al.head(hidden[:seq], rows)
+    raw_ok, _ = _noalloc(E, al, hidden[:seq], rows, want_logits=False)
+    assert np.array_equal(raw_ok, raw_ref)
