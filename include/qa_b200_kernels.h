@@ -83,19 +83,31 @@ int qa_k_conv1(const float* mel, int n, int h, int w, const float* wt, const flo
 /*
  * Causal GQA attention of the decoder prefill over the paged K/V cache
  * (src/cpu_decoder.rs:327-412; the reference GPU path's
- * prefill_attention_paged dispatch, src/decoder.rs:1463-1520).
+ * prefill_attention_paged dispatch, src/decoder.rs:1463-1520), on the
+ * persistent tcgen05/TMEM kernel the pipeline runs.
  * qkv [q_rows][ldq] 16-bit with query head h at column h*128; kpool/vpool
  * [kv_pages][nkvh][64][128]; tiles [n_tiles][4] = (clip, q0, tok0, len), one
- * per 64 (impl 0) or 128 (impl 1) query positions of a clip; block_tab
- * [clips][max_pages] page ids; out [q_rows][nqh*128].  impl 0 = mma.sync
- * kernel, 1 = persistent tcgen05/TMEM kernel (the one the pipeline runs).
- * Both take GQA groups of two (nqh == 2 * nkvh, the model's geometry); other
- * head counts return cudaErrorInvalidValue.
+ * per 128 query positions of a clip; block_tab [clips][max_pages] page ids;
+ * out [q_rows][nqh*128].  GQA groups of two (nqh == 2 * nkvh, the model's
+ * geometry); other head counts give QA_ERR_CUDA.
  */
 int qa_k_causal_attention(const void* qkv, long long ldq, long long q_rows, int nqh, int nkvh,
                           const int* tiles, int n_tiles, const int* block_tab, int max_pages,
                           const void* kpool, const void* vpool, int kv_pages, void* out, int bf16,
-                          int impl, unsigned* status, void* stream);
+                          unsigned* status, void* stream);
+
+/*
+ * The audio tower's windowed self-attention (src/audio_encoder.rs:574-627;
+ * the reference GPU tower's window attention, src/audio_encoder_gpu.rs:
+ * 1497-1547) on the tcgen05 tensor cores: every query of a window attends to
+ * every key of the same window.  qkv [T][3*dm] 16-bit (q | k | v, head h at
+ * columns h*64 of each), out [T][dm] with dm = 64 * nh; windows [n_windows][2]
+ * = (first token, length), 1 <= length <= max_window <= 128, inside [0, T).
+ * A pipeline wait that runs out sets bit 1 of *status (may be NULL).
+ */
+int qa_k_window_attention(const void* qkv, long long T, int dm, int nh, const int* windows,
+                          int n_windows, int max_window, void* out, int bf16, unsigned* status,
+                          void* stream);
 
 #ifdef __cplusplus
 }

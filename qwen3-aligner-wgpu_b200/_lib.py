@@ -60,8 +60,8 @@ EXPORTED = [
     "qa_decode_wav", "qa_resampled_length", "qa_resample",
     "qa_head_noalloc", "qa_local_head_load", "qa_set_local_head_enabled",
     "qa_local_head_enabled", "qa_local_head_refine",
-    "qa_k_gemm", "qa_k_conv3x3s2", "qa_k_causal_attention", "qa_k_conv1",
-    "qa_k_gemm_qkv_rope",
+    "qa_k_gemm", "qa_k_conv3x3s2", "qa_k_causal_attention", "qa_k_window_attention",
+    "qa_k_conv1", "qa_k_gemm_qkv_rope",
 ]
 
 c_void_p = ctypes.c_void_p
@@ -187,7 +187,9 @@ def _declare(L: ctypes.CDLL) -> None:
                              c_int, c_void_p]
     L.qa_k_causal_attention.argtypes = [c_void_p, c_ll, c_ll, c_int, c_int, c_void_p, c_int,
                                         c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p,
-                                        c_int, c_int, c_void_p, c_void_p]
+                                        c_int, c_void_p, c_void_p]
+    L.qa_k_window_attention.argtypes = [c_void_p, c_ll, c_int, c_int, c_void_p, c_int, c_int,
+                                        c_void_p, c_int, c_void_p, c_void_p]
     if hasattr(L, "qa_open"):
         L.qa_open.argtypes = [c_int, c_int, ctypes.POINTER(c_void_p)]
         L.qa_load.argtypes = [c_void_p, c_void_p, c_int, c_void_p]
@@ -280,7 +282,7 @@ def conv3x3s2(x, wt, out, time_major=False, mode=EPI_STORE16, act=ACT_NONE, bias
     check(rc)
 
 
-def causal_attention(qkv, nqh, nkvh, tiles, block_tab, kpool, vpool, out, impl=1, status=None,
+def causal_attention(qkv, nqh, nkvh, tiles, block_tab, kpool, vpool, out, status=None,
                      stream=None, validate=True):
     """Paged causal attention on torch CUDA tensors.
 
@@ -295,8 +297,29 @@ def causal_attention(qkv, nqh, nkvh, tiles, block_tab, kpool, vpool, out, impl=1
     rc = lib().qa_k_causal_attention(ptr(qkv), qkv.stride(0), qkv.shape[0], nqh, nkvh,
                                      ptr(tiles), tiles.shape[0], ptr(block_tab),
                                      block_tab.shape[1], ptr(kpool), ptr(vpool), kpool.shape[0],
-                                     ptr(out), bf16, impl, ptr(status), s)
+                                     ptr(out), bf16, ptr(status), s)
     check(rc)
+
+
+def window_attention(qkv, nh, windows, out, status=None, stream=None):
+    """Windowed attention on torch CUDA tensors: qkv [T, 3*64*nh] 16-bit,
+    windows int32 [n, 2] (first token, length), out [T, 64*nh]."""
+    import torch
+    T = qkv.shape[0]
+    dm = 64 * nh
+    if (qkv.dim() != 2 or qkv.shape[1] != 3 * dm or tuple(out.shape) != (T, dm)
+            or qkv.dtype != out.dtype or windows.dtype != torch.int32 or windows.dim() != 2
+            or windows.shape[1] != 2):
+        raise ValueError("qkv [T, 3*64*nh], out [T, 64*nh] of one dtype, windows int32 [n, 2]")
+    w = windows.cpu()
+    if w.numel() and (int(w[:, 0].min()) < 0 or int(w[:, 1].min()) < 1
+                      or int((w[:, 0] + w[:, 1]).max()) > T or int(w[:, 1].max()) > 128):
+        raise ValueError("window (start, len) out of range")
+    max_window = int(w[:, 1].max()) if w.numel() else 1
+    bf16 = 1 if qkv.dtype == torch.bfloat16 else 0
+    s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
+    check(lib().qa_k_window_attention(ptr(qkv), T, dm, nh, ptr(windows), windows.shape[0],
+                                      max_window, ptr(out), bf16, ptr(status), s))
 
 
 def check_attention_args(qkv, nqh, nkvh, tiles, block_tab, kpool, vpool, out) -> None:

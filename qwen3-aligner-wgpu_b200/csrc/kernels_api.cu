@@ -78,22 +78,27 @@ extern "C" int qa_k_conv3x3s2(const void* x, int n, int h, int w, int c, const v
 extern "C" int qa_k_causal_attention(const void* qkv, long long ldq, long long q_rows, int nqh,
                                      int nkvh, const int* tiles, int n_tiles, const int* block_tab,
                                      int max_pages, const void* kpool, const void* vpool,
-                                     int kv_pages, void* out, int bf16, int impl,
-                                     unsigned* status, void* stream) {
+                                     int kv_pages, void* out, int bf16, unsigned* status,
+                                     void* stream) {
   if (!qkv || !tiles || !block_tab || !kpool || !vpool || !out || n_tiles < 0 || kv_pages <= 0)
     return QA_ERR_ARG;
   PagedKV kv{const_cast<void*>(kpool), const_cast<void*>(vpool), 64};
   const AttnTile* t = reinterpret_cast<const AttnTile*>(tiles);
-  const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int rc;
-  if (impl == 0)
-    rc = causal_attention(qkv, ldq, nqh, nkvh, 128, t, n_tiles, block_tab, max_pages, kv, out,
-                          bf16 != 0, s);
-  else if (impl == 1)
-    rc = causal_attention_tc(qkv, ldq, q_rows, nqh, nkvh, 128, t, n_tiles, block_tab, max_pages,
-                             kv, kv_pages, out, bf16 != 0, status, s);
-  else
+  const int rc = causal_attention_tc(qkv, ldq, q_rows, nqh, nkvh, 128, t, n_tiles, block_tab,
+                                     max_pages, kv, kv_pages, out, bf16 != 0, status,
+                                     static_cast<cudaStream_t>(stream));
+  return rc == 0 ? QA_OK : QA_ERR_CUDA;
+}
+
+extern "C" int qa_k_window_attention(const void* qkv, long long T, int dm, int nh,
+                                     const int* windows, int n_windows, int max_window, void* out,
+                                     int bf16, unsigned* status, void* stream) {
+  if (!qkv || !out || (n_windows > 0 && !windows) || n_windows < 0 || T <= 0 || nh <= 0 ||
+      dm != 64 * nh || max_window <= 0 || max_window > 128)
     return QA_ERR_ARG;
+  const int rc = window_attention(qkv, T, dm, nh, 64, reinterpret_cast<const int2*>(windows),
+                                  n_windows, max_window, out, bf16 != 0, status,
+                                  static_cast<cudaStream_t>(stream));
   return rc == 0 ? QA_OK : QA_ERR_CUDA;
 }
 

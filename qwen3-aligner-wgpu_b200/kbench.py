@@ -2,7 +2,8 @@
 
     python qwen3-aligner-wgpu_b200/kbench.py gemm --m 16384 --n 6144 --k 1024 --mode swiglu
     python qwen3-aligner-wgpu_b200/kbench.py gemm --m 16384 --n 1024 --k 3072 --mode resid16
-    python qwen3-aligner-wgpu_b200/kbench.py attention --clips 64 --impl 1
+    python qwen3-aligner-wgpu_b200/kbench.py attention --clips 64
+    python qwen3-aligner-wgpu_b200/kbench.py window --tokens 13813
     python qwen3-aligner-wgpu_b200/kbench.py conv --n 256 --h 64 --w 50 --c 480
     python qwen3-aligner-wgpu_b200/kbench.py conv1 --n 256 --h 128 --w 100 --c 480
     python qwen3-aligner-wgpu_b200/kbench.py qkv --clips 64
@@ -29,16 +30,17 @@ sys.path.insert(0, os.path.dirname(HERE))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemm", "attention", "conv", "conv1", "qkv"])
+    ap.add_argument("kernel", choices=["gemm", "attention", "window", "conv", "conv1", "qkv"])
     ap.add_argument("--h", type=int, default=64)
     ap.add_argument("--w", type=int, default=50)
     ap.add_argument("--c", type=int, default=480)
     ap.add_argument("--cout", type=int, default=0, help="conv output channels (0 = --c)")
     ap.add_argument("--time-major", action="store_true")
     ap.add_argument("--clips", type=int, default=64)
+    ap.add_argument("--tokens", type=int, default=13813, help="window: packed audio tokens")
+    ap.add_argument("--heads", type=int, default=14, help="window: heads of 64")
     ap.add_argument("--min-len", type=int, default=130)
     ap.add_argument("--max-len", type=int, default=750)
-    ap.add_argument("--impl", type=int, default=1)
     ap.add_argument("--m", type=int, default=16384)
     ap.add_argument("--n", type=int, default=6144, help="gemm N, or images for conv")
     ap.add_argument("--k", type=int, default=1024)
@@ -58,6 +60,8 @@ def main():
     dt = torch.float16 if a.dtype == "f16" else torch.bfloat16
     if a.kernel == "attention":
         return attention(a, L, dt)
+    if a.kernel == "window":
+        return window(a, L, dt)
     if a.kernel == "conv":
         return conv(a, L, dt)
     if a.kernel == "conv1":
@@ -103,16 +107,14 @@ def attention(a, L, dt):
     perm = rng.permutation(n_pages)
     bt = np.zeros((len(lens), max(pages_per)), dtype=np.int32)
     tiles, k, tok0 = [], 0, 0
-    step = 128 if a.impl == 1 else 64
+    step = 128
     for c, n in enumerate(lens):
         bt[c, : pages_per[c]] = perm[k: k + pages_per[c]]
         k += pages_per[c]
         tiles += [(c, q0, tok0, n) for q0 in range(0, n, step)]
         tok0 += n
-    if a.impl == 1:  # the runtime's order: longest clip first, a clip's blocks adjacent
-        tiles.sort(key=lambda t: (-t[3], t[0], -t[1]))
-    else:
-        tiles.sort(key=lambda t: -t[1])
+    # the runtime's order: longest clip first, a clip's blocks adjacent
+    tiles.sort(key=lambda t: (-t[3], t[0], -t[1]))
     dev = torch.device("cuda:0")
     g = torch.Generator(device=dev).manual_seed(0)
     qkv = (torch.randn(T, (nq + 2 * nkv) * hd, device=dev, generator=g)).to(dt)
@@ -124,7 +126,7 @@ def attention(a, L, dt):
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     L.check_attention_args(qkv, nq, nkv, t, btd, kpool, vpool, out)
     run = lambda: L.causal_attention(qkv, nq, nkv, tiles=t, block_tab=btd, kpool=kpool,
-                                     vpool=vpool, out=out, impl=a.impl, status=status,
+                                     vpool=vpool, out=out, status=status,
                                      validate=False)
     for _ in range(a.warmup):
         run()
@@ -138,9 +140,52 @@ def attention(a, L, dt):
     assert int(status.item()) == 0
     ms = e0.elapsed_time(e1) / a.iters
     flops = sum(4.0 * hd * nq * 0.5 * n * (n + 1) for n in lens)
-    print(json.dumps({"kernel": "causal_attention", "impl": a.impl, "clips": a.clips,
+    print(json.dumps({"kernel": "causal_attention", "clips": a.clips,
                       "tokens": T, "items": len(tiles) * nkv, "dtype": a.dtype, "ms": ms,
                       "tflops": flops / ms / 1e9}))
+
+
+def window(a, L, dt):
+    """The tower's windowed attention over `--tokens` packed audio tokens cut
+    into clips of U(65, 390) tokens (5-30 s) and windows of 104, as the bench
+    batch is.  Algorithmic bytes: the qkv rows read once and the output written
+    once (L2 is flushed between launches by a 256 MiB write outside the timed
+    events)."""
+    import numpy as np
+    import torch
+    rng = np.random.default_rng(0)
+    wins, t0 = [], 0
+    while t0 < a.tokens:
+        n = min(int(rng.integers(65, 391)), a.tokens - t0)
+        for st in range(0, n, 104):
+            wins.append((t0 + st, min(104, n - st)))
+        t0 += n
+    T, nh = a.tokens, a.heads
+    dev = torch.device("cuda:0")
+    qkv = torch.randn(T, 3 * 64 * nh, device=dev).to(dt)
+    out = torch.empty(T, 64 * nh, device=dev, dtype=dt)
+    w = torch.tensor(wins, dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(a.warmup):
+        L.window_attention(qkv, nh, w, out, status=status)
+    torch.cuda.synchronize()
+    tot = 0.0
+    for _ in range(a.iters):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        L.window_attention(qkv, nh, w, out, status=status)
+        e1.record()
+        torch.cuda.synchronize()
+        tot += e0.elapsed_time(e1)
+    assert int(status.item()) == 0
+    ms = tot / a.iters
+    flops = sum(4.0 * n * n * 64 * nh for _, n in wins)
+    nbytes = T * 4 * 64 * nh * qkv.element_size()
+    print(json.dumps({"kernel": "window_attention", "tokens": T, "windows": len(wins),
+                      "dtype": a.dtype, "ms": ms, "tflops": flops / ms / 1e9,
+                      "gbs": nbytes / ms / 1e6}))
 
 
 def conv(a, L, dt):
