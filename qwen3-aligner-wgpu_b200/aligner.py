@@ -90,8 +90,12 @@ class Aligner:
             msg = L.qa_last_error(ctx)
             L.qa_close(ctx)
             raise _lib.QaError(rc, msg.decode() if msg else "")
-        al = cls(ctx, cfg, "bf16" if code else "f16",
-                 synth.InputBuilder(tokenizer, n_window=cfg.n_window))
+        try:
+            builder = cls._input_builder(model, tokenizer, cfg)
+        except Exception:
+            L.qa_close(ctx)
+            raise
+        al = cls(ctx, cfg, "bf16" if code else "f16", builder)
         if local_head is not None:
             try:
                 al._local_head = _lh.load_into(al, *local_head)
@@ -99,6 +103,21 @@ class Aligner:
                 al.close()
                 raise
         return al
+
+    @staticmethod
+    def _input_builder(model, tokenizer, cfg) -> synth.InputBuilder:
+        """The tokenizer as the reference loads it (src/align_inference.rs:
+        331-336 -> InputBuilder::load): a model directory's tokenizer.json +
+        tokenizer_config.json when there is one; else `tokenizer` (a
+        tokenizer.json path, a `tokenizers.Tokenizer`, or None for the
+        synthetic tokenizer)."""
+        if tokenizer is None and isinstance(model, (str, os.PathLike)) and os.path.exists(
+                os.path.join(model, "tokenizer.json")):
+            return synth.InputBuilder.load(model, cfg.timestamp_token_id, n_window=cfg.n_window)
+        if isinstance(tokenizer, (str, os.PathLike)):
+            tokenizer = synth.HFTokenizer.from_file(tokenizer)
+        return synth.InputBuilder(tokenizer, n_window=cfg.n_window,
+                                  timestamp_token_id=cfg.timestamp_token_id)
 
     @classmethod
     def load_with_dtype(cls, model, half: str = "f16", **kw) -> "Aligner":
@@ -167,6 +186,23 @@ class Aligner:
         words = synth.split_words(text, language)
         return self.input_builder.build(words, synth.valid_mel_frames(len(samples)))
 
+    def build_inputs(self, clips, host: dict = None) -> list:
+        """AlignerInputs of [(samples, text, language)]: every clip's words
+        split, then all clips tokenised in one batch call.  Adds the time of
+        each part to host["words_ms"] / host["build_ms"] when given."""
+        t0 = time.perf_counter()
+        words = []
+        for _, t, l in clips:
+            self.check_language(l)
+            words.append(synth.split_words(t, l))
+        t1 = time.perf_counter()
+        inputs = self.input_builder.build_batch(
+            words, [synth.valid_mel_frames(len(s)) for s, _, _ in clips])
+        if host is not None:
+            host["words_ms"] = host.get("words_ms", 0.0) + (t1 - t0) * 1e3
+            host["build_ms"] = host.get("build_ms", 0.0) + (time.perf_counter() - t1) * 1e3
+        return inputs
+
     def align(self, audio, text: str, language=None) -> list:
         """Word items for a WAV file (src/align_inference.rs:485-492): the file is
         decoded, downmixed and, if it is not 16 kHz, resampled
@@ -196,15 +232,7 @@ class Aligner:
         phases: words_ms (word split), build_ms (tokenise and assemble the
         input ids) and post_ms (timestamp repair and pairing)."""
         host = {"words_ms": 0.0, "build_ms": 0.0}
-        inputs = []
-        for s, t, l in clips:
-            self.check_language(l)
-            t0 = time.perf_counter()
-            words = synth.split_words(t, l)
-            t1 = time.perf_counter()
-            inputs.append(self.input_builder.build(words, synth.valid_mel_frames(len(s))))
-            host["words_ms"] += (t1 - t0) * 1e3
-            host["build_ms"] += (time.perf_counter() - t1) * 1e3
+        inputs = self.build_inputs(clips, host)
         raws = self.align_inputs([c[0] for c in clips], inputs, want_logits, want_normed)
         t0 = time.perf_counter()
         out = self._items(inputs, raws, want_logits or want_normed)
@@ -238,7 +266,8 @@ class Aligner:
         k-1's timestamps are repaired and paired with words.  Every batch's
         inputs are still copied to the device and its results read back."""
         def build(batch):
-            return batch, [self.build_input(s, t, l) for s, t, l in batch]
+            batch = list(batch)
+            return batch, self.build_inputs(batch)
 
         def post(inputs, raws):
             return self._items(inputs, raws, want_logits or want_normed)

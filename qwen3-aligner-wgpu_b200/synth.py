@@ -253,18 +253,13 @@ def load_safetensors(path: str) -> dict:
 
 def write_model_dir(path: str, cfg: ModelConfig, seed: int = 0) -> None:
     """A complete `-hf` model directory: config.json, model.safetensors and the
-    tokenizer files (tokenizer.json carries the synthetic vocabulary's markers)."""
+    tokenizer files (a real tokenizer.json for the `tokenizers` binding that
+    encodes as SyntheticTokenizer does, and tokenizer_config.json)."""
     os.makedirs(path, exist_ok=True)
     with open(os.path.join(path, "config.json"), "w") as f:
         json.dump(cfg.config_json(), f)
     save_safetensors(os.path.join(path, "model.safetensors"), random_weights(cfg, seed))
-    with open(os.path.join(path, "tokenizer_config.json"), "w") as f:
-        json.dump({"audio_token": AUDIO_PAD, "audio_bos_token": AUDIO_START,
-                   "audio_eos_token": AUDIO_END}, f)
-    with open(os.path.join(path, "tokenizer.json"), "w") as f:
-        json.dump({"synthetic": True, "added_tokens": [
-            {"id": AUDIO_START_ID, "content": AUDIO_START}, {"id": AUDIO_END_ID, "content": AUDIO_END},
-            {"id": AUDIO_PAD_ID, "content": AUDIO_PAD}, {"id": TIMESTAMP_ID, "content": TIMESTAMP}]}, f)
+    write_tokenizer_dir(path)
 
 
 # ---------------------------------------------------------------- Local Head package
@@ -422,6 +417,100 @@ class SyntheticTokenizer:
     def _word(self, w: str) -> list:
         return [self._piece_id(w[j:j + 3]) for j in range(0, len(w), 3)]
 
+    def encode_batch(self, texts: list) -> list:
+        return [self.encode(t) for t in texts]
+
+
+class HFTokenizer:
+    """A `tokenizers.Tokenizer` (the Python binding of the `tokenizers` crate
+    0.22.2 the reference links, Cargo.lock) behind the interface InputBuilder
+    uses: `token_to_id`, `encode(text) -> ids` with no special tokens added
+    (src/align_input.rs:180-186), and `encode_batch(texts)`, which the binding
+    spreads over the host cores."""
+
+    def __init__(self, tok):
+        self.tok = tok
+
+    @classmethod
+    def from_file(cls, path: str) -> "HFTokenizer":
+        import tokenizers
+        return cls(tokenizers.Tokenizer.from_file(str(path)))
+
+    def token_to_id(self, s: str):
+        return self.tok.token_to_id(s)
+
+    def encode(self, text: str) -> list:
+        return self.tok.encode(text, add_special_tokens=False).ids
+
+    def encode_batch(self, texts: list) -> list:
+        # encode_batch_fast computes no character offsets (ids are all the
+        # input builder needs); the same ids as encode_batch
+        f = getattr(self.tok, "encode_batch_fast", None) or self.tok.encode_batch
+        return [e.ids for e in f(list(texts), add_special_tokens=False)]
+
+
+def as_tokenizer(tok):
+    """SyntheticTokenizer / HFTokenizer as they are; a bare `tokenizers.Tokenizer`
+    wrapped; None -> SyntheticTokenizer."""
+    if tok is None:
+        return SyntheticTokenizer()
+    if hasattr(tok, "encode_batch") and hasattr(tok, "get_vocab_size"):
+        return HFTokenizer(tok)
+    return tok
+
+
+# Ordinary-token alphabet of the synthetic tokenizer.json: every 1-3 letter
+# lowercase piece and every CJK ideograph the workloads draw (U+4E00..U+62FF).
+_SYN_CJK = (0x4E00, 0x62FF)
+_SYN_CJK_CLASS = r"\x{3400}-\x{9FFF}\x{F900}-\x{FAFF}"  # Oniguruma syntax
+
+
+def synthetic_tokenizer_json() -> dict:
+    """A tokenizer.json (`tokenizers` 0.22.2 format) that encodes exactly as
+    SyntheticTokenizer does over the workloads' alphabet: the four markers
+    are added tokens with the checkpoint's ids; a Split pre-tokenizer cuts
+    every run of non-CJK characters into 3-character pieces and isolates each
+    CJK character; a WordLevel model maps each piece to SyntheticTokenizer's
+    id for it.  Pieces outside the alphabet map to <unk>."""
+    import itertools
+    import string
+    st = SyntheticTokenizer()
+    vocab = {}
+    for n in (1, 2, 3):
+        for p in itertools.product(string.ascii_lowercase, repeat=n):
+            piece = "".join(p)
+            vocab[piece] = st._piece_id(piece)
+    for c in range(_SYN_CJK[0], _SYN_CJK[1] + 1):
+        vocab[chr(c)] = st._piece_id(chr(c))
+    vocab["<unk>"] = SyntheticTokenizer.ORDINARY - 1
+    markers = [(AUDIO_START, AUDIO_START_ID), (AUDIO_END, AUDIO_END_ID),
+               (AUDIO_PAD, AUDIO_PAD_ID), (TIMESTAMP, TIMESTAMP_ID)]
+    for m, i in markers:
+        vocab[m] = i
+    cjk = _SYN_CJK_CLASS
+    return {
+        "version": "1.0", "truncation": None, "padding": None,
+        "added_tokens": [{"id": i, "content": m, "single_word": False, "lstrip": False,
+                          "rstrip": False, "normalized": False, "special": True}
+                         for m, i in markers],
+        "normalizer": None,
+        "pre_tokenizer": {"type": "Split", "pattern": {"Regex": f"[^{cjk}]{{1,3}}|[{cjk}]"},
+                          "behavior": "Isolated", "invert": False},
+        "post_processor": None, "decoder": None,
+        "model": {"type": "WordLevel", "vocab": vocab, "unk_token": "<unk>"},
+    }
+
+
+def write_tokenizer_dir(path: str) -> None:
+    """tokenizer.json + tokenizer_config.json (with the marker keys the
+    reference reads, src/align_input.rs:138-151) into a model directory."""
+    os.makedirs(path, exist_ok=True)
+    with open(os.path.join(path, "tokenizer.json"), "w") as f:
+        json.dump(synthetic_tokenizer_json(), f)
+    with open(os.path.join(path, "tokenizer_config.json"), "w") as f:
+        json.dump({"audio_token": AUDIO_PAD, "audio_bos_token": AUDIO_START,
+                   "audio_eos_token": AUDIO_END}, f)
+
 
 # ---------------------------------------------------------------- words / inputs
 
@@ -446,59 +535,74 @@ def is_kept_char(c: str) -> bool:
     return c == "'" or unicodedata.category(c)[0] in "LN" or is_cjk_char(c)
 
 
-_ASCII_DROP = None
+# Rust's char::is_whitespace: the Unicode White_Space property.
+_WHITE_SPACE = "\t\n\x0b\x0c\r \x85\xa0\u1680\u2000-\u200a\u2028\u2029\u202f\u205f\u3000"
+# is_cjk_char's ranges (src/words.rs:30-40).
+_CJK_RANGES = ("\u4e00-\u9fff\u3400-\u4dbf\U00020000-\U0002a6df\U0002a700-\U0002b73f"
+               "\U0002b740-\U0002b81f\U0002b820-\U0002ceaf\uf900-\ufaff\U0002f800-\U0002fa1f")
+# is_hangul_char's ranges (src/words.rs:44-51).
+_HANGUL_RANGES = "\u1100-\u11ff\u3130-\u318f\ua960-\ua97f\uac00-\ud7a3\ud7b0-\ud7ff"
+_SPLIT_RE = None
+
+
+def _split_res():
+    global _SPLIT_RE
+    if _SPLIT_RE is None:
+        import re
+        import regex  # Unicode general categories (\p{L}, \p{N})
+        _SPLIT_RE = (
+            # neither kept (apostrophe, L*, N*, CJK) nor whitespace: dropped
+            regex.compile(f"[^\\p{{L}}\\p{{N}}'{_WHITE_SPACE}{_CJK_RANGES}]+"),
+            # a CJK character alone, or a run of kept non-CJK characters
+            # (explicit ranges only: the standard engine is faster here)
+            re.compile(f"[{_CJK_RANGES}]|[^{_WHITE_SPACE}{_CJK_RANGES}]+"),
+            re.compile(f"[{_HANGUL_RANGES}]"),
+        )
+    return _SPLIT_RE
 
 
 def split_words(text: str, language=None) -> list:
     """src/words.rs:107-118 + split_default (:190-232) for every language but
-    Japanese (which needs the reference's nagisa tagger and is out of scope)."""
-    import re
-    import unicodedata
-    global _ASCII_DROP
-    text = text.strip()
+    Japanese (which needs the reference's nagisa tagger and is out of scope).
+
+    split_default walks the characters: a CJK character is a word of its own;
+    whitespace (Unicode White_Space) ends a word; apostrophes, letters (L*)
+    and numbers (N*) are kept; anything else is dropped without ending the
+    word ("50-minute" is one word); a change between Hangul and non-Hangul
+    letters inside a run ends the word, numbers and apostrophes attaching to
+    the current run.  Here the dropped characters are removed first (that
+    cannot end a word), the words are then the CJK characters and the runs
+    between whitespace and CJK characters, and only runs holding Hangul are
+    walked character by character for the script change."""
+    drop, word, hangul = _split_res()
     lang = (language or "").lower()
     if lang in ("japanese", "ja"):
         raise ValueError("Japanese word splitting requires the nagisa tagger (not available)")
-    # Whitespace ends a word and resets the Hangul/other state, so the text is
-    # split on it first.  An ASCII piece has no CJK or Hangul: its letters,
-    # digits and apostrophes are kept and every other character is dropped;
-    # other pieces go through the character-by-character rules.
-    if _ASCII_DROP is None:
-        _ASCII_DROP = re.compile(r"[^A-Za-z0-9']+")
-    tokens = []
-    for piece in text.split():
-        if piece.isascii():
-            w = _ASCII_DROP.sub("", piece)
-            if w:
-                tokens.append(w)
+    tokens = word.findall(drop.sub("", text))
+    if not hangul.search(text):
+        return tokens
+    out = []
+    for t in tokens:
+        if hangul.search(t):
+            _split_script(t, out)
         else:
-            _split_piece(piece, tokens)
-    return tokens
+            out.append(t)
+    return out
 
 
-def _split_piece(text: str, tokens: list) -> None:
-    """split_default's character rules over a run without whitespace."""
+def _split_script(run: str, tokens: list) -> None:
+    """A run of kept non-CJK characters cut where the letters change between
+    Hangul and other scripts (src/words.rs:205-224)."""
     import unicodedata
     buf, buf_hangul = "", None
-    for c in text:
-        if is_cjk_char(c):
-            if buf:
+    for c in run:
+        if c != "'" and unicodedata.category(c)[0] == "L":  # a script letter, not a number
+            h = is_hangul_char(c)
+            if buf_hangul is not None and buf_hangul != h:
                 tokens.append(buf)
-                buf, buf_hangul = "", None
-            tokens.append(c)
-        elif c.isspace():
-            if buf:
-                tokens.append(buf)
-                buf, buf_hangul = "", None
-        elif is_kept_char(c):
-            script_letter = c != "'" and unicodedata.category(c) not in ("Nd", "Nl", "No")
-            if script_letter:
-                hangul = is_hangul_char(c)
-                if buf_hangul is not None and buf_hangul != hangul:
-                    tokens.append(buf)
-                    buf = ""
-                buf_hangul = hangul
-            buf += c
+                buf = ""
+            buf_hangul = h
+        buf += c
     if buf:
         tokens.append(buf)
 
@@ -530,7 +634,8 @@ def valid_mel_frames(n_samples: int) -> int:
 
 @dataclass
 class AlignerInput:
-    """src/align_input.rs:91-111."""
+    """src/align_input.rs:91-111 (input_ids / timestamp_positions: int
+    sequences, lists or numpy arrays)."""
     input_ids: list
     words: list
     n_audio_tokens: int
@@ -543,60 +648,105 @@ class AlignerInput:
 
 
 class InputBuilder:
-    """InputBuilder::build (src/align_input.rs:190-262), same structural checks."""
+    """InputBuilder (src/align_input.rs:119-262): the checkpoint's tokenizer
+    and the marker ids, with the reference's structural checks."""
 
-    def __init__(self, tokenizer=None, n_window: int = 50):
-        self.tok = tokenizer or SyntheticTokenizer()
+    def __init__(self, tokenizer=None, n_window: int = 50, timestamp_token_id: int = TIMESTAMP_ID,
+                 markers: dict = None):
+        self.tok = as_tokenizer(tokenizer)
         self.n_window = n_window
+        m = {"audio_token": AUDIO_PAD, "audio_bos_token": AUDIO_START,
+             "audio_eos_token": AUDIO_END, **(markers or {})}
+
+        def id_of(text):
+            i = self.tok.token_to_id(text)
+            if i is None:
+                raise ValueError(f"tokenizer has no {text!r}")
+            return int(i)
+        self.audio_start_token_id = id_of(m["audio_bos_token"])
+        self.audio_end_token_id = id_of(m["audio_eos_token"])
+        self.audio_token_id = id_of(m["audio_token"])
+        self.timestamp_token_id = int(timestamp_token_id)
+
+    @classmethod
+    def load(cls, model_dir: str, timestamp_token_id: int = TIMESTAMP_ID, n_window: int = 50):
+        """InputBuilder::load (src/align_input.rs:131-171): tokenizer.json via
+        the `tokenizers` binding, the marker strings from
+        tokenizer_config.json (defaults when a key is absent)."""
+        tok = HFTokenizer.from_file(os.path.join(model_dir, "tokenizer.json"))
+        with open(os.path.join(model_dir, "tokenizer_config.json")) as f:
+            cfg = json.load(f)
+        markers = {k: cfg[k] for k in ("audio_token", "audio_bos_token", "audio_eos_token")
+                   if isinstance(cfg.get(k), str)}
+        return cls(tok, n_window=n_window, timestamp_token_id=timestamp_token_id,
+                   markers=markers)
+
+    @staticmethod
+    def _words_text(words: list) -> str:
+        # w0 <ts><ts> w1 <ts><ts> ... wn <ts><ts> (src/align_input.rs:202-210)
+        return (TIMESTAMP + TIMESTAMP).join(words) + TIMESTAMP + TIMESTAMP
 
     def build(self, words: list, valid_mel: int) -> AlignerInput:
-        n_audio = audio_token_count(valid_mel, self.n_window)
-        if n_audio <= 0:
-            raise ValueError(f"audio produced 0 tokens ({valid_mel} mel frames)")
-        # The reference tokenises "<|audio_start|>" + pads + "<|audio_end|>" +
-        # words in one string; the markers are atomic tokens (no merge crosses
-        # them), so the marker run is emitted directly and only the words part
-        # goes through the tokenizer — the same ids without scanning N pads.
-        text = ""
-        for i, w in enumerate(words):
-            if i > 0:
-                text += TIMESTAMP + TIMESTAMP
-            text += w
-        text += TIMESTAMP + TIMESTAMP
-        head = ([self.tok.token_to_id(AUDIO_START)] + [self.tok.token_to_id(AUDIO_PAD)] * n_audio
-                + [self.tok.token_to_id(AUDIO_END)])
-        enc = self.tok.encode(text)
-        ids = head + enc
-        if head.count(AUDIO_PAD_ID) + enc.count(AUDIO_PAD_ID) != n_audio:
-            raise ValueError("audio token count mismatch")
-        if ids[0] != AUDIO_START_ID or ids[n_audio + 1] != AUDIO_END_ID:
-            raise ValueError("sequence must be <|audio_start|> pads <|audio_end|> ...")
-        off = len(head)
-        ts = [off + i for i, t in enumerate(enc) if t == TIMESTAMP_ID]
-        ts = [i for i, t in enumerate(head) if t == TIMESTAMP_ID] + ts
-        if len(ts) != 2 * len(words):
-            raise ValueError(f"expected {2 * len(words)} timestamp tokens, got {len(ts)}")
-        return AlignerInput(ids, list(words), n_audio, valid_mel,
-                            padded_mel_frames(valid_mel, self.n_window), ts)
+        return self.build_batch([words], [valid_mel], as_arrays=False)[0]
+
+    def build_batch(self, word_lists: list, valid_mels: list, as_arrays: bool = True) -> list:
+        """One AlignerInput per clip, the words of all clips tokenised in one
+        encode_batch call (spread over the host cores by the `tokenizers`
+        binding).  input_ids / timestamp_positions are uint32 / int64 numpy
+        arrays (lists with as_arrays=False)."""
+        n_audio = [audio_token_count(v, self.n_window) for v in valid_mels]
+        for na, v in zip(n_audio, valid_mels):
+            if na <= 0:
+                raise ValueError(f"audio produced 0 tokens ({v} mel frames)")
+        texts = [self._words_text(w) for w in word_lists]
+        tok = self.tok
+        encs = tok.encode_batch(texts) if hasattr(tok, "encode_batch") else [tok.encode(t) for t in texts]
+        out = []
+        for words, v, na, enc in zip(word_lists, valid_mels, n_audio, encs):
+            # The reference tokenises "<|audio_start|>" + pads + "<|audio_end|>" +
+            # words as one string; the markers are atomic tokens (no merge
+            # crosses them), so the marker run is emitted directly and only the
+            # words go through the tokenizer: the same ids without scanning N pads.
+            e = np.asarray(enc, dtype=np.uint32)
+            ids = np.empty(na + 2 + len(e), np.uint32)
+            ids[0] = self.audio_start_token_id
+            ids[1:na + 1] = self.audio_token_id
+            ids[na + 1] = self.audio_end_token_id
+            ids[na + 2:] = e
+            if int(np.count_nonzero(e == self.audio_token_id)) != 0:
+                raise ValueError(f"expected {na} audio tokens, the words hold more")
+            ts = np.flatnonzero(e == self.timestamp_token_id).astype(np.int64) + (na + 2)
+            if len(ts) != 2 * len(words):
+                raise ValueError(f"expected {2 * len(words)} timestamp tokens for {len(words)} "
+                                 f"words, got {len(ts)}")
+            if as_arrays:
+                inp = AlignerInput(ids, list(words), na, v, padded_mel_frames(v, self.n_window), ts)
+            else:
+                inp = AlignerInput(ids.tolist(), list(words), na, v,
+                                   padded_mel_frames(v, self.n_window), ts.tolist())
+            out.append(inp)
+        return out
 
 
 # ---------------------------------------------------------------- audio / text
 
-def synth_audio(seconds: float, seed: int) -> np.ndarray:
-    """Syllable-like bursts of low-passed noise at RMS 0.1, 16 kHz f32."""
+def synth_audio(seconds: float, seed: int, rate: int = SAMPLE_RATE) -> np.ndarray:
+    """Syllable-like bursts of low-passed noise at RMS 0.1, f32 at `rate` Hz
+    (16 kHz by default, the model's rate; other rates stand in for files that
+    must be resampled)."""
     from scipy.signal import butter, sosfiltfilt
     rng = np.random.default_rng(seed)
-    n = int(round(seconds * SAMPLE_RATE))
+    n = int(round(seconds * rate))
     noise = rng.standard_normal(n)
-    sos = butter(4, 3400, btype="low", fs=SAMPLE_RATE, output="sos")
+    sos = butter(4, 3400, btype="low", fs=rate, output="sos")
     x = sosfiltfilt(sos, noise)
     env = np.zeros(n)
-    t = int(rng.uniform(0.04, 0.2) * SAMPLE_RATE)
+    t = int(rng.uniform(0.04, 0.2) * rate)
     while t < n:
-        d = int(rng.uniform(0.15, 0.40) * SAMPLE_RATE)
+        d = int(rng.uniform(0.15, 0.40) * rate)
         e = min(n, t + d)
         env[t:e] = np.hanning(d)[: e - t]
-        t = e + int(rng.uniform(0.04, 0.2) * SAMPLE_RATE)
+        t = e + int(rng.uniform(0.04, 0.2) * rate)
     y = x * env
     rms = np.sqrt(np.mean(y * y)) if n else 1.0
     y = y * (0.1 / max(rms, 1e-12))
