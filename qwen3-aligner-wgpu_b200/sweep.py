@@ -12,8 +12,8 @@ The reference aligns one clip per call.  Here a set of clips is
 * streamed through ``Aligner.align_inputs_stream`` (two passes in flight, the
   host building the next batch while the GPU runs the current one);
 * journaled: every finished clip is appended to a JSON-lines file as soon as
-  its pass returns, and a rerun with the same journal skips the clips already
-  there (resume after a crash or a preempted job).
+  its pass returns (one file per rank), and a rerun with the same journal
+  skips the clips already there (resume after a crash or a preempted job).
 
 Nothing here computes: the alignment is the library's, and a missing CUDA
 library fails loudly where the Aligner is created.
@@ -59,20 +59,31 @@ def clip_cost(inp, n_samples: int, n_window: int = 50) -> float:
 
 
 class Journal:
-    """JSON lines, one finished clip per line: {"id", "raw_ms", "items"}."""
+    """JSON lines, one finished clip per line: {"id", "raw_ms", "items"}.
 
-    def __init__(self, path):
-        self.path = os.fspath(path)
+    Each rank appends only to its own file: `path` for a single process,
+    `path.rank<r>` for rank r of several, so no two processes ever write one
+    file.  Every rank reads the finished clips of all of them (`path` and
+    every `path.rank*`), so a rerun skips them whatever the number of ranks
+    was before.  A record cut short by a crash (no final newline) is dropped
+    and the clip is redone; the writer trims it from its own file."""
+
+    def __init__(self, path, rank: int = 0, world: int = 1):
+        import glob
+        base = os.fspath(path)
+        self.path = base if world <= 1 else f"{base}.rank{rank}"
         self.done = {}
-        if not os.path.exists(self.path):
-            return
-        with open(self.path, "rb") as f:
+        for p in sorted({base, self.path, *glob.glob(glob.escape(base) + ".rank*")}):
+            if os.path.exists(p):
+                self._read(p, trim=p == self.path)
+
+    def _read(self, path: str, trim: bool) -> None:
+        with open(path, "rb") as f:
             data = f.read()
-        # a record cut short by a crash has no newline: drop it (the clip is
-        # redone) so that new records start on a line of their own
         keep = data.rfind(b"\n") + 1
-        if keep < len(data):
-            with open(self.path, "r+b") as f:
+        if trim and keep < len(data):
+            # new records must start on a line of their own
+            with open(path, "r+b") as f:
                 f.truncate(keep)
         for line in data[:keep].decode().splitlines():
             line = line.strip()
@@ -96,6 +107,19 @@ class Journal:
             os.fsync(f.fileno())
 
 
+def estimate_cost(samples_len: int, words: list, n_window: int = 50) -> float:
+    """clip_cost from the sample count and the words alone, before any
+    tokenisation: the audio tokens are exact; the text tokens are taken as
+    one per three characters of each word (exact for the synthetic
+    tokenizer, an estimate for a BPE)."""
+    from . import synth
+    valid = synth.valid_mel_frames(samples_len)
+    na = synth.audio_token_count(valid, n_window)
+    seq = na + 2 + 2 * len(words) + sum(-(-len(w) // 3) for w in words)
+    chunks = -(-valid // (2 * n_window))
+    return shard.clip_flops(na, seq, 2 * len(words), chunks)
+
+
 def rank_share(costs, rank: int, world: int) -> list:
     """The clip indices rank `rank` of `world` aligns (LPT over the costs)."""
     if not 0 <= rank < world:
@@ -108,16 +132,20 @@ def sweep(aligner, clips, ids=None, journal=None, token_budget: int = DEFAULT_TO
     """Align `clips` ([(samples, text, language)]) on this rank's share.
 
     ids: one JSON-serialisable id per clip (default: the index).  journal: a
-    path; clips already in it are skipped, new ones are appended.  Returns
-    {id: (raw_ms, items)} for this rank's share, journaled clips included."""
+    path; clips already in it (or in another rank's `path.rank*`) are
+    skipped, this rank's new ones are appended to its own file.  The share
+    is chosen from estimated costs (estimate_cost: word split only), and only
+    this rank's clips are tokenised.  Returns {id: (raw_ms, items)} for this
+    rank's share, journaled clips included."""
+    from . import synth
     ids = list(range(len(clips))) if ids is None else list(ids)
     if len(ids) != len(clips) or len(set(ids)) != len(ids):
         raise ValueError("one distinct id per clip")
-    j = Journal(journal) if journal is not None else None
-    inputs = [aligner.build_input(s, t, l) for s, t, l in clips]
+    j = Journal(journal, rank, world) if journal is not None else None
     mine = list(range(len(clips)))
     if world > 1:
-        costs = [clip_cost(inp, len(c[0])) for inp, c in zip(inputs, clips)]
+        n_window = aligner.cfg.n_window
+        costs = [estimate_cost(len(c[0]), synth.split_words(c[1], c[2]), n_window) for c in clips]
         mine = rank_share(costs, rank, world)
     out = {}
     todo = []
@@ -126,6 +154,8 @@ def sweep(aligner, clips, ids=None, journal=None, token_budget: int = DEFAULT_TO
             out[ids[i]] = j.done[ids[i]]
         else:
             todo.append(i)
+    built = aligner.build_inputs([clips[i] for i in todo]) if todo else []
+    inputs = dict(zip(todo, built))
     batches = [[todo[k] for k in b] for b in
                pack_batches([inputs[i].seq_len() for i in todo], token_budget, max_clips)]
     stream = aligner.align_inputs_stream(([clips[i][0] for i in b], [inputs[i] for i in b])

@@ -27,10 +27,16 @@ class FakeAligner:
 
     def __init__(self, crash_after=None):
         self.passes = []
+        self.built = 0
         self.crash_after = crash_after
+        self.cfg = pkg().synth.ModelConfig()
 
     def build_input(self, samples, text, language):
         return _Input(text.split(), len(samples))
+
+    def build_inputs(self, clips):
+        self.built += len(clips)
+        return [self.build_input(*c) for c in clips]
 
     def align_inputs_stream(self, batches):
         post = pkg().postprocess
@@ -114,12 +120,35 @@ def test_rank_shares_cover_once_and_balance():
     shares = [sw.sweep(FakeAligner(), clips, rank=r, world=4, token_budget=200) for r in range(4)]
     got = sorted(k for s in shares for k in s)
     assert got == list(range(64))
-    fa = FakeAligner()
-    inputs = [fa.build_input(*c) for c in clips]
-    costs = [sw.clip_cost(inp, len(c[0])) for inp, c in zip(inputs, clips)]
+    S = pkg().synth
+    costs = [sw.estimate_cost(len(c[0]), S.split_words(c[1], c[2])) for c in clips]
     loads = [sum(costs[k] for k in s) for s in shares]
     assert max(loads) <= sum(costs) / 4 + max(costs)
+    # a rank tokenises its own share only
+    fa = FakeAligner()
+    sw.sweep(fa, clips, rank=1, world=4, token_budget=200)
+    assert fa.built == len(shares[1])
     with pytest.raises(ValueError):
         sw.rank_share(costs, 4, 4)
     with pytest.raises(ValueError):
         sw.sweep(FakeAligner(), clips[:2], ids=["a", "a"])
+
+
+def test_rank_journals_are_separate_and_shared_on_resume(tmp_path):
+    """Each rank writes its own journal file; a rerun with another number of
+    ranks skips every clip any rank finished."""
+    sw = pkg().sweep
+    clips = _clips(48, seed=4)
+    path = tmp_path / "j.jsonl"
+    for r in range(3):
+        sw.sweep(FakeAligner(), clips, journal=path, rank=r, world=3, token_budget=150)
+    files = sorted(p.name for p in tmp_path.iterdir())
+    assert files == ["j.jsonl.rank0", "j.jsonl.rank1", "j.jsonl.rank2"]
+    assert sum(len((tmp_path / f).read_text().splitlines()) for f in files) == 48
+    for r in range(2):  # resumed on two ranks: nothing left to align
+        fa = FakeAligner()
+        out = sw.sweep(fa, clips, journal=path, rank=r, world=2, token_budget=150)
+        assert fa.passes == [] and fa.built == 0 and len(out) > 0
+    fa = FakeAligner()
+    assert len(sw.sweep(fa, clips, journal=path, token_budget=150)) == 48
+    assert fa.passes == []
