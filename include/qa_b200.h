@@ -195,6 +195,16 @@ int64_t qa_resampled_length(int64_t n, int sr_in, int sr_out);
  * bits. */
 int qa_resample(const float* in, int64_t n, int sr_in, int sr_out, float* out, int64_t out_len);
 
+/* The failure path of a bounded device wait, on purpose (no counterpart in
+ * the reference, which reports a lost device after each submit,
+ * src/decoder.rs:1670-1672).  Launches one CTA that waits, for at most
+ * limit_ms (1..10000), on a pipeline barrier that nothing completes -- the
+ * state a lost TMA copy or MMA commit leaves a tensor-core kernel in.  The
+ * wait runs out, the kernel sets the timeout bit of the context's status
+ * word and returns, and the call returns QA_ERR_TIMEOUT; the context stays
+ * usable (nothing is left in flight).  QA_ERR_ARG for a limit out of range. */
+int qa_probe_timeout(qa_ctx* ctx, int limit_ms);
+
 /* Timestamp head without any device allocation.  No counterpart in the
  * reference; it is the qa_head computation for callers that cannot allocate
  * device memory: a host that has given the whole GPU to its own memory pool,

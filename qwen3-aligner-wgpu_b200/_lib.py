@@ -58,7 +58,7 @@ EXPORTED = [
     "qa_head", "qa_align_batch", "qa_batch_stage", "qa_batch_run", "qa_batch_fetch",
     "qa_set_stream", "qa_set_profile", "qa_get_profile", "qa_fix_timestamps",
     "qa_decode_wav", "qa_resampled_length", "qa_resample",
-    "qa_head_noalloc", "qa_local_head_load", "qa_set_local_head_enabled",
+    "qa_head_noalloc", "qa_probe_timeout", "qa_local_head_load", "qa_set_local_head_enabled",
     "qa_local_head_enabled", "qa_local_head_refine",
     "qa_k_gemm", "qa_k_conv3x3s2", "qa_k_causal_attention", "qa_k_window_attention",
     "qa_k_conv1", "qa_k_gemm_qkv_rope",
@@ -218,6 +218,7 @@ def _declare(L: ctypes.CDLL) -> None:
                                   ctypes.c_int64]
         L.qa_head_noalloc.argtypes = [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p,
                                       c_void_p]
+        L.qa_probe_timeout.argtypes = [c_void_p, c_int]
         L.qa_batch_run.argtypes = [c_void_p]
         L.qa_batch_fetch.argtypes = [c_void_p, c_void_p]
         L.qa_set_stream.argtypes = [c_void_p, c_void_p]
@@ -301,9 +302,11 @@ def causal_attention(qkv, nqh, nkvh, tiles, block_tab, kpool, vpool, out, status
     check(rc)
 
 
-def window_attention(qkv, nh, windows, out, status=None, stream=None):
+def window_attention(qkv, nh, windows, out, status=None, stream=None, max_window=None):
     """Windowed attention on torch CUDA tensors: qkv [T, 3*64*nh] 16-bit,
-    windows int32 [n, 2] (first token, length), out [T, 64*nh]."""
+    windows int32 [n, 2] (first token, length), out [T, 64*nh].  The windows
+    are range-checked on the host (a copy to the host) unless `max_window`
+    (the longest window) is given, which a caller that checked them passes."""
     import torch
     T = qkv.shape[0]
     dm = 64 * nh
@@ -311,11 +314,12 @@ def window_attention(qkv, nh, windows, out, status=None, stream=None):
             or qkv.dtype != out.dtype or windows.dtype != torch.int32 or windows.dim() != 2
             or windows.shape[1] != 2):
         raise ValueError("qkv [T, 3*64*nh], out [T, 64*nh] of one dtype, windows int32 [n, 2]")
-    w = windows.cpu()
-    if w.numel() and (int(w[:, 0].min()) < 0 or int(w[:, 1].min()) < 1
-                      or int((w[:, 0] + w[:, 1]).max()) > T or int(w[:, 1].max()) > 128):
-        raise ValueError("window (start, len) out of range")
-    max_window = int(w[:, 1].max()) if w.numel() else 1
+    if max_window is None:
+        w = windows.cpu()
+        if w.numel() and (int(w[:, 0].min()) < 0 or int(w[:, 1].min()) < 1
+                          or int((w[:, 0] + w[:, 1]).max()) > T or int(w[:, 1].max()) > 128):
+            raise ValueError("window (start, len) out of range")
+        max_window = int(w[:, 1].max()) if w.numel() else 1
     bf16 = 1 if qkv.dtype == torch.bfloat16 else 0
     s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
     check(lib().qa_k_window_attention(ptr(qkv), T, dm, nh, ptr(windows), windows.shape[0],

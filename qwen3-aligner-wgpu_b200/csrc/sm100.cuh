@@ -61,16 +61,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
   return ok != 0;
 }
 
-// Wait until the barrier's phase with the given parity has completed.
-// Returns false when the wall-clock limit ran out first.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Wait until the barrier's phase with the given parity has completed, for at
+// most limit_ns of wall-clock time.  Returns false when the limit ran out.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity,
+                                              unsigned long long limit_ns) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const unsigned long long t0 = global_ns();
   for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait(addr, parity)) return true;
-    if ((it & 255u) == 255u && global_ns() - t0 > kSpinLimitNs) return false;
+    if ((it & 255u) == 255u && global_ns() - t0 > limit_ns) return false;
   }
+}
+
+// mbar_wait_for with the library's limit (kSpinLimitNs).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  return mbar_wait_for(bar, parity, kSpinLimitNs);
 }
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
