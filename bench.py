@@ -78,6 +78,11 @@ def parse():
                     help="clips of the CPU baseline's sample (default: about 15 s of CPU "
                          "work, 12 clips of config 2 or 3 of config 4)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", action="store_true",
+                    help="BASELINE config 4 as a whole set: --sweep-clips clips split across the "
+                         "ranks by LPT and aligned through sweep.py (strong scaling)")
+    ap.add_argument("--sweep-clips", type=int, default=4096)
+    ap.add_argument("--token-budget", type=int, default=65536)
     args = ap.parse_args()
     if args.half is None:
         args.half = "bf16" if args.workload == 3 else "f16"
@@ -266,10 +271,122 @@ def run_reference(args):
     return 0
 
 
+class _Length:
+    """Stands in for the samples of a clip another rank aligns: sweep.py reads
+    only their count."""
+
+    def __init__(self, n):
+        self.n = n
+
+    def __len__(self):
+        return self.n
+
+
+def _gen_config4_audio(i):
+    qa = importlib.import_module("qwen3-aligner-wgpu_b200")
+    return qa.synth.workload_clip(4, i).samples
+
+
+def run_sweep(args):
+    """BASELINE config 4 as a whole set through sweep.py: every rank computes
+    the same LPT shares from the clips' durations and words, synthesises the
+    audio of its own share only (a process pool, before the GPU work), warms
+    up on a few of its clips, then aligns its share (Local Head on) between a
+    barrier and a device synchronisation.  Reported: the whole set's audio
+    seconds over the slowest rank's time, and every rank's time."""
+    import concurrent.futures as cf
+    import multiprocessing as mp
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    qa = importlib.import_module("qwen3-aligner-wgpu_b200")
+    texts = qa.synth.workload_texts(4, args.sweep_clips)
+    n_samples = [int(round(sec * 16000)) for sec, _, _ in texts]
+    words = [qa.synth.split_words(t, l) for _, t, l in texts]
+    costs = [qa.sweep.estimate_cost(n, w) for n, w in zip(n_samples, words)]
+    mine = qa.sweep.rank_share(costs, rank, world)
+    t0 = time.perf_counter()
+    workers = max(1, (os.cpu_count() or 2) // world - 1)
+    with cf.ProcessPoolExecutor(workers, mp_context=mp.get_context("spawn")) as ex:
+        audio = dict(zip(mine, ex.map(_gen_config4_audio, mine, chunksize=4)))
+    gen_s = time.perf_counter() - t0
+    clips = [(audio[i] if i in audio else _Length(n), t, l)
+             for i, (n, (_, t, l)) in enumerate(zip(n_samples, texts))]
+
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    cfg = qa.synth.ModelConfig()
+    al = qa.Aligner.load_backend_with_dtype(qa.synth.random_weights(cfg), "f16", device=local,
+                                            cfg=cfg, local_head=qa.synth.random_local_head(0))
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    al.set_stream(stream.cuda_stream)
+    # warm-up: the grow-only workspaces of a full pass
+    warm = sorted(mine, key=lambda i: -n_samples[i])[:48]
+    qa.sweep.sweep(al, [clips[i] for i in warm], token_budget=args.token_budget)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    out = qa.sweep.sweep(al, clips, token_budget=args.token_budget, rank=rank, world=world)
+    e1.record(stream)
+    barrier()
+    ms = e0.elapsed_time(e1)
+    assert sorted(out) == sorted(mine)
+    per_rank = torch.zeros(world, dtype=torch.float64, device=dev)
+    per_rank[rank] = ms
+    mine_audio = torch.zeros(world, dtype=torch.float64, device=dev)
+    mine_audio[rank] = sum(n_samples[i] for i in mine) / 16000.0
+    if world > 1:
+        dist.all_reduce(per_rank)
+        dist.all_reduce(mine_audio)
+    per_rank, mine_audio = per_rank.cpu().tolist(), mine_audio.cpu().tolist()
+    total_audio = sum(n_samples) / 16000.0
+    value = total_audio / (max(per_rank) / 1e3)
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": 1,
+            "warmup": 1, "ms_per_step": max(per_rank), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded audio/transcripts, random-init weights)",
+            "config": {"workload": f"BASELINE config 4 whole set: {args.sweep_clips} clips "
+                                   "U(5,60) s, English, 3 words/s, Local Head on, through "
+                                   "sweep.py (LPT shares, token-budget passes, two in flight)",
+                       "clips": args.sweep_clips, "audio_s": total_audio,
+                       "token_budget": args.token_budget,
+                       "parallelism": f"clip-sharded x{world} by LPT, no collectives"},
+            "rank_ms": per_rank, "rank_audio_s": mine_audio,
+            "imbalance_max_over_mean": max(per_rank) / (sum(per_rank) / world),
+            "e2e": {"value": value, "unit": UNIT,
+                    "h2d_bytes_per_step": int(sum(n_samples) * 4),
+                    # raw_ms (8 B per slot) and the refined intervals (2 x 8 B per word)
+                    "d2h_bytes_per_step": int(sum(32 * len(w) for w in words)),
+                    "includes": "word split + tokenisation + staging + H2D + device passes + "
+                                "Local Head + D2H + repair, for the whole set"},
+            "audio_synthesis_s_rank0": gen_s,
+        }), flush=True)
+    al.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.sweep:
+        return run_sweep(args)
 
     import numpy as np
     import torch

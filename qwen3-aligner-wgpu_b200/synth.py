@@ -770,6 +770,51 @@ class Clip:
     seconds: float
 
 
+def _clip_text(config: int, i: int, n_words: int, mix_cjk: bool, seed_base=None):
+    seed = 1000 * config + i if seed_base is None else seed_base + i
+    rng = np.random.default_rng(seed + 7)
+    if mix_cjk:
+        words, left, en = [], n_words, True
+        while left > 0:
+            run = min(left, int(rng.integers(2, 7)))
+            words += english_words(run, rng) if en else chinese_words(run, rng)
+            left -= run
+            en = not en
+        text, lang = "".join(w if is_cjk_char(w[0]) else f" {w} " for w in words), "Chinese"
+    else:
+        words = english_words(n_words, rng)
+        text, lang = " ".join(words), "English"
+    return " ".join(text.split()), lang, seed
+
+
+def _spec(config: int, n: int) -> list:
+    """(seconds, n_words, mix_cjk) of clips 0 .. n-1 of configuration 2 or 4."""
+    if config == 2:
+        rng = np.random.default_rng(2000)
+        spec = [(float(rng.uniform(5, 30)), float(rng.uniform(2.5, 3.5))) for _ in range(n)]
+        return [(sec, max(1, int(round(sec * rate))), True) for sec, rate in spec]
+    if config == 4:
+        rng = np.random.default_rng(4000)
+        spec = [float(rng.uniform(5, 60)) for _ in range(n)]
+        return [(sec, max(1, int(round(sec * 3.0))), False) for sec in spec]
+    raise ValueError(config)
+
+
+def workload_texts(config: int, n_clips: int) -> list:
+    """(seconds, text, language) of clips 0 .. n_clips-1 of configuration 2 or
+    4, without synthesising any audio (the text and duration of clip i are
+    those workload() gives it)."""
+    return [(sec, *_clip_text(config, i, nw, cjk)[:2])
+            for i, (sec, nw, cjk) in enumerate(_spec(config, n_clips))]
+
+
+def workload_clip(config: int, i: int) -> Clip:
+    """Clip i of configuration 2 or 4 alone (the same clip workload() gives)."""
+    sec, nw, cjk = _spec(config, i + 1)[i]
+    text, lang, seed = _clip_text(config, i, nw, cjk)
+    return Clip(synth_audio(sec, seed), text, lang, sec)
+
+
 def workload(config: int, seed_base: int = None, n_clips: int = None, start: int = 0) -> list:
     """The clips of a BASELINE configuration (0-4), clip i seeded 1000 * config + i.
 
@@ -779,40 +824,20 @@ def workload(config: int, seed_base: int = None, n_clips: int = None, start: int
     clips = []
 
     def one(i, seconds, n_words, mix_cjk=False):
-        seed = 1000 * config + i if seed_base is None else seed_base + i
-        rng = np.random.default_rng(seed + 7)
-        if mix_cjk:
-            words, left, en = [], n_words, True
-            while left > 0:
-                run = min(left, int(rng.integers(2, 7)))
-                words += english_words(run, rng) if en else chinese_words(run, rng)
-                left -= run
-                en = not en
-            text, lang = "".join(w if is_cjk_char(w[0]) else f" {w} " for w in words), "Chinese"
-        else:
-            words = english_words(n_words, rng)
-            text, lang = " ".join(words), "English"
-        return Clip(synth_audio(seconds, seed), " ".join(text.split()), lang, seconds)
+        text, lang, seed = _clip_text(config, i, n_words, mix_cjk, seed_base)
+        return Clip(synth_audio(seconds, seed), text, lang, seconds)
 
     if config == 0:
         clips.append(one(0, 10.0, 25))
     elif config == 1:
         clips.append(one(0, 60.0, 180))
-    elif config == 2:
-        n = 64 if n_clips is None else n_clips
-        rng = np.random.default_rng(2000)
-        spec = [(float(rng.uniform(5, 30)), float(rng.uniform(2.5, 3.5))) for _ in range(start + n)]
-        for i in range(start, start + n):
-            sec, rate = spec[i]
-            clips.append(one(i, sec, max(1, int(round(sec * rate))), mix_cjk=True))
+    elif config in (2, 4):
+        n = (64 if config == 2 else 4096) if n_clips is None else n_clips
+        for i, (sec, nw, cjk) in enumerate(_spec(config, start + n)):
+            if i >= start:
+                clips.append(one(i, sec, nw, mix_cjk=cjk))
     elif config == 3:
         clips.append(one(0, 300.0, 900))
-    elif config == 4:
-        n = 4096 if n_clips is None else n_clips
-        rng = np.random.default_rng(4000)
-        spec = [float(rng.uniform(5, 60)) for _ in range(start + n)]
-        for i in range(start, start + n):
-            clips.append(one(i, spec[i], max(1, int(round(spec[i] * 3.0)))))
     else:
         raise ValueError(config)
     return clips
