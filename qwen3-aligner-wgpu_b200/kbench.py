@@ -7,6 +7,7 @@
     python qwen3-aligner-wgpu_b200/kbench.py conv --n 256 --h 64 --w 50 --c 480
     python qwen3-aligner-wgpu_b200/kbench.py conv1 --n 256 --h 128 --w 100 --c 480
     python qwen3-aligner-wgpu_b200/kbench.py qkv --clips 64
+    python qwen3-aligner-wgpu_b200/kbench.py pass --clips 16 --iters 2
 
 Each run times `--iters` launches with CUDA events on the launching stream
 (after `--warmup` launches) and prints one JSON line with the mean launch time
@@ -30,7 +31,7 @@ sys.path.insert(0, os.path.dirname(HERE))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemm", "attention", "window", "conv", "conv1", "qkv"])
+    ap.add_argument("kernel", choices=["gemm", "attention", "window", "conv", "conv1", "qkv", "pass"])
     ap.add_argument("--h", type=int, default=64)
     ap.add_argument("--w", type=int, default=50)
     ap.add_argument("--c", type=int, default=480)
@@ -62,6 +63,8 @@ def main():
         return attention(a, L, dt)
     if a.kernel == "window":
         return window(a, L, dt)
+    if a.kernel == "pass":
+        return whole_pass(a, qa)
     if a.kernel == "conv":
         return conv(a, L, dt)
     if a.kernel == "conv1":
@@ -143,6 +146,25 @@ def attention(a, L, dt):
     print(json.dumps({"kernel": "causal_attention", "clips": a.clips,
                       "tokens": T, "items": len(tiles) * nkv, "dtype": a.dtype, "ms": ms,
                       "tflops": flops / ms / 1e9}))
+
+
+def whole_pass(a, qa):
+    """--iters batched passes (qa_batch_run) over the first --clips clips of
+    BASELINE config 2 on the seeded model, staged once (for profiling the
+    pass's kernels: the launches of pass k follow those of pass k-1)."""
+    cfg = qa.synth.ModelConfig()
+    al = qa.Aligner.load_backend_with_dtype(qa.synth.random_weights(cfg), a.dtype, cfg=cfg)
+    clips = qa.synth.workload(2, n_clips=a.clips)
+    inps = al.build_inputs([(c.samples, c.text, c.language) for c in clips])
+    st = al.stage([c.samples for c in clips], inps)
+    for _ in range(a.iters):
+        al.run()
+    al.fetch(st)
+    print(json.dumps({"kernel": "pass", "clips": a.clips, "passes": a.iters,
+                      "decoder_tokens": sum(i.seq_len() for i in inps),
+                      "audio_tokens": sum(i.n_audio_tokens for i in inps),
+                      "launches_per_pass": al.timings["gpu_launches"]}))
+    al.close()
 
 
 def window(a, L, dt):
