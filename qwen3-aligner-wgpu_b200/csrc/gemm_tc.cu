@@ -155,9 +155,11 @@ __device__ __forceinline__ QkvRow qkv_row_meta(const EpiParams& ep, int row, int
 // product and sum rounded as in the reference's loop (norm_rope_head,
 // src/cpu_decoder.rs:305-321), two lanes per f32x2 instruction.  The head is
 // read from TMEM twice (sums, then the 32-column chunks d and d + 64 together)
-// instead of being held in registers.  `gain` is the q_norm | k_norm gains
-// staged in shared memory; each chunk's cos / sin are loaded (read-only path)
-// before its TMEM reads so that their latency overlaps.
+// instead of being held in registers (the 10-warp GEMM kernels have 168
+// registers a thread; holding the head spills).  `gain` is the q_norm |
+// k_norm gains staged in shared memory; each chunk's four cos and four sin
+// 16-byte loads (read-only path) are issued before its TMEM read so that
+// their latencies overlap.
 template <typename T>
 __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem_col0, int row,
                                               int M, int head, const QkvRow& meta,
@@ -220,17 +222,25 @@ __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem
   const float* nw = is_q ? gain : gain + HD;
   const uint4* ct = reinterpret_cast<const uint4*>(static_cast<const T*>(rk.cos_t) + meta.pos * (HD / 2));
   const uint4* st = reinterpret_cast<const uint4*>(static_cast<const T*>(rk.sin_t) + meta.pos * (HD / 2));
-  // pass 2: elements d in [32c, 32c + 32) with their partners d + 64
+  // pass 2: elements d in [32c, 32c + 32) with their partners d + 64; the
+  // chunk's cos / sin lines are requested before its TMEM read, so the two
+  // latencies overlap
 #pragma unroll 1
   for (int c = 0; c < 2; ++c) {
+    uint4 cu[4], su[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      cu[q] = ok ? __ldg(ct + c * 4 + q) : make_uint4(0, 0, 0, 0);
+      su[q] = ok ? __ldg(st + c * 4 + q) : make_uint4(0, 0, 0, 0);
+    }
     float va[32], vb[32];
     tmem_ld2x32(tmem_col0 + c * 32, tmem_col0 + 64 + c * 32, va, vb);
     if (!ok) continue;
 #pragma unroll
     for (int j0 = 0; j0 < 32; j0 += 8) {
       const int d0 = c * 32 + j0;
-      const uint4 cu = __ldg(ct + d0 / 8), su = __ldg(st + d0 / 8);
-      const uint32_t cw[4] = {cu.x, cu.y, cu.z, cu.w}, sw[4] = {su.x, su.y, su.z, su.w};
+      const uint32_t cw[4] = {cu[j0 / 8].x, cu[j0 / 8].y, cu[j0 / 8].z, cu[j0 / 8].w};
+      const uint32_t sw[4] = {su[j0 / 8].x, su[j0 / 8].y, su[j0 / 8].z, su[j0 / 8].w};
       const float4 na0 = *reinterpret_cast<const float4*>(nw + d0);
       const float4 na1 = *reinterpret_cast<const float4*>(nw + d0 + 4);
       const float4 nb0 = *reinterpret_cast<const float4*>(nw + d0 + 64);
@@ -809,7 +819,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       epilogue<BN, T>(ep, trow, row, M, n0, N, cb, ce, meta, gain);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_remote(tempty_lead + buf * 8);
+      if (lane == 0) mbar_arrive_remote_relaxed(tempty_lead + buf * 8);
     }
   }
 
@@ -1174,7 +1184,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       epilogue<BN, T>(ep, trow, valid ? orow : M, M, n0, N, cb, ce);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_remote(tempty_lead + buf * 8);
+      if (lane == 0) mbar_arrive_remote_relaxed(tempty_lead + buf * 8);
     }
   }
 

@@ -423,6 +423,18 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
                : "memory");
 }
 
+// Arrive on an mbarrier of the cluster without release ordering of this
+// thread's earlier memory writes.  For a barrier that only hands tensor
+// memory back: the arriving thread's tcgen05.ld reads are complete
+// (tcgen05.wait::ld, then tcgen05.fence::before_thread_sync) before it
+// arrives, and its global stores need no ordering with the waiter, so the
+// release (which holds the thread until those stores are performed at
+// cluster scope) is not needed.
+__device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
 // Bounded wait with cluster-scope acquire (for barriers other CTAs arrive on).
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t addr, uint32_t parity) {
   uint32_t ok;
