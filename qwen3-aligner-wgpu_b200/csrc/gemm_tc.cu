@@ -131,7 +131,33 @@ __device__ __forceinline__ uint32_t pack2_rn(float2 v) {
 struct QkvRow {
   int pos = 0;
   long long kv_off = 0;
+  float inv = 1.0f;  // the row's folded RMSNorm factor (ssq_in), else 1
 };
+
+// Folded RMSNorm statistics: sums of squares per 128-column block of a row.
+constexpr int kSsqCols = 128;
+constexpr int kSsqMax = 8;  // blocks per row read by the consumer (rows up to 1024 wide)
+
+// The row's block sums (EpiParams::ssq_in), loaded ahead of their use: the
+// epilogue loops issue them for the next tile while they process this one.
+struct SsqRow {
+  float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f), b = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+};
+__device__ __forceinline__ SsqRow ssq_load(const EpiParams& ep, int row, int M) {
+  SsqRow r;
+  if (!ep.ssq_in || row >= M) return r;
+  const float4* p = reinterpret_cast<const float4*>(ep.ssq_in + static_cast<long long>(row) * ep.ssq_n);
+  r.a = __ldg(p);
+  if (ep.ssq_n > 4) r.b = __ldg(p + 1);
+  return r;
+}
+// 1 / rms of the row from its block sums, summed in block order.
+__device__ __forceinline__ float row_rms_inv(const EpiParams& ep, const SsqRow& q) {
+  if (!ep.ssq_in) return 1.0f;
+  float s = __fadd_rn(__fadd_rn(__fadd_rn(q.a.x, q.a.y), q.a.z), q.a.w);
+  if (ep.ssq_n > 4) s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, q.b.x), q.b.y), q.b.z), q.b.w);
+  return 1.0f / sqrtf(s / ep.rms_d + ep.rms_eps);
+}
 
 template <typename T>
 __device__ __forceinline__ QkvRow qkv_row_meta(const EpiParams& ep, int row, int M) {
@@ -186,7 +212,8 @@ __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem
       for (int h = 0; h < 2; ++h) {
         uint32_t w[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) w[i] = pack2_rn<T>(make_float2(v[h][2 * i], v[h][2 * i + 1]));
+        for (int i = 0; i < 16; ++i)
+          w[i] = pack2_rn<T>(make_float2(v[h][2 * i] * meta.inv, v[h][2 * i + 1] * meta.inv));
 #pragma unroll
         for (int j = 0; j < 4; ++j)
           reinterpret_cast<uint4*>(dst + (c + h) * 32)[j] =
@@ -201,17 +228,18 @@ __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem
   for (int c = 0; c < HD / 32; c += 2) {
     float v[32], w[32];
     tmem_ld2x32(tmem_col0 + c * 32, tmem_col0 + (c + 1) * 32, v, w);
+    const float r = meta.inv;
 #pragma unroll
     for (int i = 0; i < 32; i += 4) {
-      const float2 x0 = make_float2(round16<T>(v[i]), round16<T>(v[i + 1]));
-      const float2 x1 = make_float2(round16<T>(v[i + 2]), round16<T>(v[i + 3]));
+      const float2 x0 = make_float2(round16<T>(v[i] * r), round16<T>(v[i + 1] * r));
+      const float2 x1 = make_float2(round16<T>(v[i + 2] * r), round16<T>(v[i + 3] * r));
       s2a = add2_rn(s2a, mul2_rn(x0, x0));
       s2b = add2_rn(s2b, mul2_rn(x1, x1));
     }
 #pragma unroll
     for (int i = 0; i < 32; i += 4) {
-      const float2 x0 = make_float2(round16<T>(w[i]), round16<T>(w[i + 1]));
-      const float2 x1 = make_float2(round16<T>(w[i + 2]), round16<T>(w[i + 3]));
+      const float2 x0 = make_float2(round16<T>(w[i] * r), round16<T>(w[i + 1] * r));
+      const float2 x1 = make_float2(round16<T>(w[i + 2] * r), round16<T>(w[i + 3] * r));
       s2a = add2_rn(s2a, mul2_rn(x0, x0));
       s2b = add2_rn(s2b, mul2_rn(x1, x1));
     }
@@ -253,8 +281,9 @@ __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem
 #pragma unroll
       for (int p = 0; p < 4; ++p) {
         const int i = j0 + 2 * p;
-        const float2 xa = mul2_rn(mul2_rn(make_float2(round16<T>(va[i]), round16<T>(va[i + 1])), inv2), ga[p]);
-        const float2 xb = mul2_rn(mul2_rn(make_float2(round16<T>(vb[i]), round16<T>(vb[i + 1])), inv2), gb[p]);
+        const float r = meta.inv;
+        const float2 xa = mul2_rn(mul2_rn(make_float2(round16<T>(va[i] * r), round16<T>(va[i + 1] * r)), inv2), ga[p]);
+        const float2 xb = mul2_rn(mul2_rn(make_float2(round16<T>(vb[i] * r), round16<T>(vb[i + 1] * r)), inv2), gb[p]);
         const float2 cc = unpack2<T>(cw[p]), sn = unpack2<T>(sw[p]);
         const float2 nxb = make_float2(-xb.x, -xb.y);
         lo[p] = pack2_rn<T>(add2_rn(mul2_rn(xa, cc), mul2_rn(nxb, sn)));
@@ -303,8 +332,8 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
       if (row < M) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float gh = round16<T>(g[i]);
-          const float uh = round16<T>(u[i]);
+          const float gh = round16<T>(g[i] * meta.inv);
+          const float uh = round16<T>(u[i] * meta.inv);
           const float silu = __fdividef(gh, 1.0f + __expf(-gh));
           g[i] = silu * uh;
         }
@@ -349,6 +378,7 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
     return;
   }
 
+  float ssq_acc = 0.0f;  // EPI_RESID16 with ssq_out: the current 128-column block
   // one 32-column chunk: bias, then the mode's operation
   auto chunk = [&](int c0, float (&v)[32]) {
     if (row >= M) return;
@@ -391,6 +421,17 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] += h[i];
         store16_row<T>(dst, v, nc);
+        if (ep.ssq_out) {  // the 128-column block's sum of squares of the stored values
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float x = i < nc ? round16<T>(v[i]) : 0.0f;
+            ssq_acc = fmaf(x, x, ssq_acc);
+          }
+          if ((col + 32) % kSsqCols == 0 || col + 32 >= N) {
+            ep.ssq_out[static_cast<long long>(row) * ep.ssq_n + col / kSsqCols] = ssq_acc;
+            ssq_acc = 0.0f;
+          }
+        }
         break;
       }
       case EPI_RESID32: {
@@ -631,16 +672,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __shared__ float gain[256];  // EPI_QKV_ROPE: q_norm | k_norm gains
     if (ep.mode == EPI_QKV_ROPE) stage_qkv_gains(ep, gain);
     int lt = 0;
+    // the row's folded-norm statistics are loaded one tile ahead
+    auto tile_row = [&](int t) { return (t / n_tiles_n) * kBM + q * 32 + lane; };
+    SsqRow ssq = ssq_load(ep, tile_row(blockIdx.x), M);
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++lt) {
       const int buf = lt & 1;
       const int m0 = (t / n_tiles_n) * kBM, n0 = (t % n_tiles_n) * BN;
       const int row = m0 + q * 32 + lane;
       QkvRow meta;
       if (ep.mode == EPI_QKV_ROPE) meta = qkv_row_meta<T>(ep, row, M);  // before the wait
+      meta.inv = row_rms_inv(ep, ssq);
       if (*abort_flag || !mbar_wait(&tfull[buf], (lt >> 1) & 1)) {
         if (lane == 0) timed_out();
         break;
       }
+      ssq = ssq_load(ep, tile_row(t + gridDim.x), M);  // arrives during this epilogue
       tc_fence_after();
       const uint32_t trow = tbase + buf * kAccCols + (static_cast<uint32_t>(q * 32) << 16);
       epilogue<BN, T>(ep, trow, row, M, n0, N, cb, ce, meta, gain);
@@ -804,16 +850,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __shared__ float gain[256];  // EPI_QKV_ROPE: q_norm | k_norm gains
     if (ep.mode == EPI_QKV_ROPE) stage_qkv_gains(ep, gain);
     int lt = 0;
+    // the row's folded-norm statistics are loaded one tile ahead
+    auto tile_row = [&](int t) { return (t / n_tiles_n) * 2 * kBM + rank * kBM + q * 32 + lane; };
+    SsqRow ssq = ssq_load(ep, tile_row(pair), M);
     for (int t = pair; t < n_tiles; t += n_pairs, ++lt) {
       const int buf = lt & 1;
       const int m0 = (t / n_tiles_n) * 2 * kBM, n0 = (t % n_tiles_n) * BN;
       const int row = m0 + rank * kBM + q * 32 + lane;
       QkvRow meta;
       if (ep.mode == EPI_QKV_ROPE) meta = qkv_row_meta<T>(ep, row, M);  // before the wait
+      meta.inv = row_rms_inv(ep, ssq);
       if (*abort_flag || !mbar_wait(&tfull[buf], (lt >> 1) & 1)) {
         if (lane == 0) timed_out();
         break;
       }
+      ssq = ssq_load(ep, tile_row(t + n_pairs), M);  // arrives during this epilogue
       tc_fence_after();
       const uint32_t trow = tbase + buf * kAccCols + (static_cast<uint32_t>(q * 32) << 16);
       epilogue<BN, T>(ep, trow, row, M, n0, N, cb, ce, meta, gain);
@@ -1637,6 +1688,13 @@ int gemm_tc(const void* A, long long lda, const void* B, long long ldb, int M, i
   }
   // 256 x 256 (or 256 x 224) tiles on CTA pairs whenever N allows (force_bn 0
   // = choose, -1 = require the pair kernel, > 0 = one CTA per tile, that width)
+  // folded RMSNorm: whole rows of 128-column blocks, read as float4, one
+  // block per epilogue thread (256-wide tiles)
+  if ((ep.ssq_in || ep.ssq_out) &&
+      (ep.ssq_n % 4 || ep.ssq_n > kSsqMax || (ep.ssq_out && ep.ssq_n * kSsqCols != N) ||
+       (ep.ssq_out && force_bn > 0 && force_bn != 256) ||
+       ((reinterpret_cast<uintptr_t>(ep.ssq_in) | reinterpret_cast<uintptr_t>(ep.ssq_out)) & 15u)))
+    return (int)cudaErrorInvalidValue;
   const bool pair224 = N % 224 == 0 && ep.mode != EPI_SWIGLU16 && ep.mode != EPI_QKV_ROPE;
   if (force_bn == -1 || (force_bn == 0 && M > 128 && (N % 256 == 0 || pair224))) {
     if (N % 256 == 0)

@@ -77,6 +77,18 @@ struct EpiParams {
   // with r % row_period >= row_valid is skipped, the others go to output row
   // (r / row_period) * row_out_period + row_out_off + r % row_period.
   int row_period = 0, row_valid = 0, row_out_period = 0, row_out_off = 0;
+  // RMSNorm folded into the decoder GEMMs (rms_norm_row, src/cpu_decoder.rs:
+  // 289-300).  EPI_RESID16 with ssq_out: for every 128-column block of a row
+  // it also writes the sum of squares of the row's new 16-bit values, in
+  // column order, ssq_out[r * ssq_n + col / 128] (ssq_n = N / 128, 4 or 8).
+  // EPI_QKV_ROPE / EPI_SWIGLU16 with ssq_in: the accumulator of row r is
+  // multiplied by 1 / sqrt(sum_j ssq_in[r * ssq_n + j] / rms_d + rms_eps)
+  // (sum in j order) before its 16-bit rounding; the norm gain is folded
+  // into the B operand's columns.
+  float* ssq_out = nullptr;
+  const float* ssq_in = nullptr;
+  int ssq_n = 0;
+  float rms_d = 1.0f, rms_eps = 0.0f;
   // Implicit 1-D convolution along the rows of A (0 = plain GEMM): A is
   // [M, conv_kb * 64] and k-block kb reads the 64 columns (kb % conv_kb) * 64
   // of rows shifted down by kb / conv_kb, so K = taps * conv_kb * 64 covers

@@ -117,6 +117,11 @@ int causal_attention_tc(const void* qkv, long long ldq, long long q_rows, int nq
                         int max_pages, PagedKV kv, int kv_pages, void* out, bool bf16,
                         unsigned* status, cudaStream_t s);
 
+// Block sums of squares of 16-bit rows [rows][d] (d % 512 == 0):
+// out[r * (d/128) + j] = sum of the squares of block j's 128 values, in order
+// (the first decoder RMSNorm's statistics, EpiParams::ssq_in).
+int row_ssq(const void* x, int rows, int d, float* out, bool bf16, cudaStream_t s);
+
 // Embedding gather: rows of the device table for every non-audio token.
 int embed_gather(const uint32_t* ids, int T, const void* table, int vocab, int d, int audio_id,
                  void* out, int* bad, cudaStream_t s);

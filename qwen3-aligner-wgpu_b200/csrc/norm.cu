@@ -167,6 +167,36 @@ __global__ void rmsnorm_kernel(const T* __restrict__ x, int rows, int d,
   }
 }
 
+// ---------------------------------------------------------------- row sums of squares
+// The decoder's first RMSNorm input (embedding rows + projected audio rows):
+// out[r * (d / 128) + j] = sum of squares of the 128 16-bit values of block j
+// of row r, in column order -- the form the residual GEMM epilogues write for
+// the later norms (EpiParams::ssq_out).  One warp per row, one block per lane.
+template <typename T>
+__global__ void row_ssq_kernel(const T* __restrict__ x, int rows, int d, float* __restrict__ out) {
+  pdl_wait();  // the previous kernel's results are visible from here
+  pdl_trigger();
+  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int nblk = d / 128;
+  for (int j = lane; j < nblk; j += 32) {
+    const uint4* p = reinterpret_cast<const uint4*>(x + static_cast<long long>(row) * d + j * 128);
+    float s2 = 0.0f;
+#pragma unroll 4
+    for (int q = 0; q < 16; ++q) {
+      const uint4 u = p[q];
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float f = h2f<T>(e[k]);
+        s2 = fmaf(f, f, s2);
+      }
+    }
+    out[static_cast<long long>(row) * nblk + j] = s2;
+  }
+}
+
 // ---------------------------------------------------------------- embedding gather
 // src/align_inference.rs:690-715, on the device: one thread per 16 bytes.
 __global__ void embed_gather_kernel(const uint32_t* __restrict__ ids, int T_,
@@ -282,6 +312,17 @@ int rmsnorm_rows(const void* x, int rows, int d, const float* w, float eps, void
                            static_cast<__nv_bfloat16*>(out));
   return (int)launch_pdl(rmsnorm_kernel<__half>, dim3(blocks), dim3(256), 0, s,
                          static_cast<const __half*>(x), rows, d, w, eps, static_cast<__half*>(out));
+}
+
+int row_ssq(const void* x, int rows, int d, float* out, bool bf16, cudaStream_t s) {
+  if (rows <= 0) return 0;
+  if (d % 512) return (int)cudaErrorInvalidValue;
+  const unsigned blocks = (rows + 7) / 8;
+  if (bf16)
+    return (int)launch_pdl(row_ssq_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, s,
+                           static_cast<const __nv_bfloat16*>(x), rows, d, out);
+  return (int)launch_pdl(row_ssq_kernel<__half>, dim3(blocks), dim3(256), 0, s,
+                         static_cast<const __half*>(x), rows, d, out);
 }
 
 int embed_gather(const uint32_t* ids, int T_, const void* table, int vocab, int d, int audio_id,

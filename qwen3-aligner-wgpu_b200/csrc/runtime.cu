@@ -426,7 +426,8 @@ int load_weights(qa_ctx* ctx, const qa_tensor* tensors, int n, const qa_cfg& c) 
   for (int i = 0; i < 3; ++i) f3 = (f3 - 1) / 2 + 1;
   ctx->f3 = f3;
   if (dm % 64 || dm != c.encoder_heads * 64 || ds % 8 || c.hidden_size != c.output_dim ||
-      c.head_dim != 128 || c.num_heads != 2 * c.num_kv_heads || c.hidden_size % 256 ||
+      c.head_dim != 128 || c.num_heads != 2 * c.num_kv_heads || c.hidden_size % 512 ||
+      c.hidden_size > 1024 ||
       c.intermediate_size % 128 || c.num_mel_bins != 128 || c.n_window <= 0)
     return fail(ctx, QA_ERR_SHAPE, "unsupported model geometry");
   {
@@ -591,6 +592,20 @@ int load_weights(qa_ctx* ctx, const qa_tensor* tensors, int n, const qa_cfg& c) 
     std::vector<float> qkv(q);
     qkv.insert(qkv.end(), k.begin(), k.end());
     qkv.insert(qkv.end(), v.begin(), v.end());
+    // RMSNorm folded into the projections that follow it: column k of the
+    // QKV (gate/up) weights carries input_layernorm (post_attention_layernorm)
+    // gain k, rounded to the run's format as the reference rounds the gains;
+    // the GEMM epilogue applies the row's 1 / rms.
+    {
+      const std::vector<float> gi = rounded(iln, bf), gp = rounded(pln, bf);
+      for (size_t r = 0; r < qkv.size() / H; ++r)
+        for (int j = 0; j < H; ++j) qkv[r * H + j] *= gi[j];
+      for (size_t r = 0; r < gt.size() / H; ++r)
+        for (int j = 0; j < H; ++j) {
+          gt[r * H + j] *= gp[j];
+          up[r * H + j] *= gp[j];
+        }
+    }
     // gate/up interleaved in blocks of 128 rows: a 256-wide GEMM tile holds
     // the gate and up rows of the same 128 outputs (SwiGLU epilogue).
     std::vector<float> gu(static_cast<size_t>(2) * I * H);
@@ -901,7 +916,9 @@ int run_decoder(qa_ctx* ctx, const Plan& P, const PlanDev& D) {
   cudaStream_t s = ctx->stream;
   const int T = P.T_d, H = c.hidden_size, hd = c.head_dim, nq = c.num_heads, nkv = c.num_kv_heads;
   const int I = c.intermediate_size, qd = nq * hd, ldq = (nq + 2 * nkv) * hd;
-  TRY(ensure(ctx, ctx->xn, static_cast<size_t>(T) * H * 2));
+  const int nch = H / 128;  // 128-column blocks per row (folded RMSNorm statistics)
+  TRY(ensure(ctx, ctx->ssq_attn, static_cast<size_t>(T) * nch * 4));
+  TRY(ensure(ctx, ctx->ssq_mlp, static_cast<size_t>(T) * nch * 4));
   TRY(ensure(ctx, ctx->qkv, static_cast<size_t>(T) * ldq * 2));
   TRY(ensure(ctx, ctx->attn, static_cast<size_t>(T) * qd * 2));
   TRY(ensure(ctx, ctx->mlp, static_cast<size_t>(T) * I * 2));
@@ -912,13 +929,25 @@ int run_decoder(qa_ctx* ctx, const Plan& P, const PlanDev& D) {
   const float eps = static_cast<float>(c.rms_norm_eps);
   EpiParams ep;
   ep.status = ctx->status.as<unsigned>();
+  ep.ssq_n = nch;
+  ep.rms_d = static_cast<float>(H);
+  ep.rms_eps = eps;
+  // Each RMSNorm (rms_norm_row, src/cpu_decoder.rs:289-300) is folded into
+  // the projection after it: its gain sits in the weights' columns, and the
+  // GEMM epilogue scales row r by 1 / rms(r), computed from the block sums of
+  // squares that the residual epilogue before it wrote (the first layer's
+  // from row_ssq over the embedded input).
+  KL("row_ssq", 0, 2.0 * T * H + 4.0 * T * nch,
+     row_ssq(ctx->hid.p, T, H, ctx->ssq_mlp.as<float>(), bf, s));
   for (int l = 0; l < c.num_layers; ++l) {
     const DecLayerW& L = ctx->w.dec[l];
     PagedKV kv{ctx->kcache.as<uint16_t>() + l * layer_kv, ctx->vcache.as<uint16_t>() + l * layer_kv, 64};
-    KL("rmsnorm", 0, 4.0 * T * H, rmsnorm_rows(ctx->hid.p, T, H, L.iln, eps, ctx->xn.p, bf, s));
-    // QKV projection with (d) fused into its epilogue: Q (normed + roped)
-    // lands in the q columns of ctx->qkv, K and V in this layer's pages.
+    // QKV projection of the normed rows with (d) fused into its epilogue: Q
+    // (normed + roped) lands in the q columns of ctx->qkv, K and V in this
+    // layer's pages.
     ep.mode = EPI_QKV_ROPE;
+    ep.ssq_in = ctx->ssq_mlp.as<float>();
+    ep.ssq_out = nullptr;
     ep.act = ACT_NONE;
     ep.bias = nullptr;
     ep.out = ctx->qkv.p;
@@ -938,7 +967,7 @@ int run_decoder(qa_ctx* ctx, const Plan& P, const PlanDev& D) {
     ep.rk.nq = nq;
     ep.rk.nkv = nkv;
     KL("gemm:dec_qkv", gemm_flops(T, ldq, H), gemm_bytes(T, ldq, H, 2),
-       gemm_tc(ctx->xn.p, H, L.qkv_w, H, T, ldq, H, bf, ep, s, 0));
+       gemm_tc(ctx->hid.p, H, L.qkv_w, H, T, ldq, H, bf, ep, s, 0));
     KL("causal_attn", attn_flops, T * (2.0 * qd * 2 + 2.0 * nkv * hd * 2),
        causal_attention_tc(ctx->qkv.p, ldq, T, nq, nkv, hd, D.tiles,
                            static_cast<int>(P.tiles.size()), D.block_tab, P.max_pages, kv,
@@ -946,18 +975,23 @@ int run_decoder(qa_ctx* ctx, const Plan& P, const PlanDev& D) {
     ep.mode = EPI_RESID16;
     ep.out = ctx->hid.p;
     ep.ldo = H;
-    KL("gemm:dec_o", gemm_flops(T, H, qd), gemm_bytes(T, H, qd, 4),
+    ep.ssq_in = nullptr;
+    ep.ssq_out = ctx->ssq_attn.as<float>();  // statistics of the post-attention norm
+    KL("gemm:dec_o", gemm_flops(T, H, qd), gemm_bytes(T, H, qd, 4) + 4.0 * T * nch,
        gemm_tc(ctx->attn.p, qd, L.o_w, qd, T, H, qd, bf, ep, s));
-    KL("rmsnorm", 0, 4.0 * T * H, rmsnorm_rows(ctx->hid.p, T, H, L.pln, eps, ctx->xn.p, bf, s));
     ep.mode = EPI_SWIGLU16;
     ep.out = ctx->mlp.p;
     ep.ldo = I;
+    ep.ssq_in = ctx->ssq_attn.as<float>();
+    ep.ssq_out = nullptr;
     KL("gemm:dec_gate_up", gemm_flops(T, 2 * I, H), gemm_bytes(T, I, H, 2) + 2.0 * I * H,
-       gemm_tc(ctx->xn.p, H, L.gu_w, H, T, 2 * I, H, bf, ep, s, 0));
+       gemm_tc(ctx->hid.p, H, L.gu_w, H, T, 2 * I, H, bf, ep, s, 0));
     ep.mode = EPI_RESID16;
     ep.out = ctx->hid.p;
     ep.ldo = H;
-    KL("gemm:dec_down", gemm_flops(T, H, I), gemm_bytes(T, H, I, 4),
+    ep.ssq_in = nullptr;
+    ep.ssq_out = ctx->ssq_mlp.as<float>();  // statistics of the next layer's input norm
+    KL("gemm:dec_down", gemm_flops(T, H, I), gemm_bytes(T, H, I, 4) + 4.0 * T * nch,
        gemm_tc(ctx->mlp.p, I, L.down_w, I, T, H, I, bf, ep, s));
   }
   return QA_OK;
@@ -1447,7 +1481,8 @@ int qa_close(qa_ctx* ctx) {
                     &ctx->mel_frames, &ctx->mel_spec,
                     &ctx->clips_dev, &ctx->idx_dev, &ctx->act1, &ctx->cols, &ctx->act2,
                     &ctx->act3, &ctx->xenc, &ctx->h16a, &ctx->qkv_enc, &ctx->attn_enc,
-                    &ctx->ffn_enc, &ctx->proj1, &ctx->emb_out, &ctx->hid, &ctx->xn, &ctx->qkv,
+                    &ctx->ffn_enc, &ctx->proj1, &ctx->emb_out, &ctx->hid, &ctx->ssq_attn,
+                    &ctx->ssq_mlp, &ctx->qkv,
                     &ctx->attn, &ctx->mlp, &ctx->kcache, &ctx->vcache, &ctx->head_a,
                     &ctx->head_keys, &ctx->head_raw, &ctx->head_logits, &ctx->head_normed,
                     &ctx->hidden_f32, &ctx->status, &ctx->badflag};

@@ -202,7 +202,8 @@ struct qa_ctx {
   qa::DevBuf samples, mel_scratch, mel_chunked, maxkey, clips_dev, idx_dev;
   qa::DevBuf mel_frames, mel_spec;  // tensor-core mel: A rows, re / im
   qa::DevBuf act1, cols, act2, act3, xenc, h16a, qkv_enc, attn_enc, ffn_enc, proj1;
-  qa::DevBuf emb_out, hid, xn, qkv, attn, mlp, kcache, vcache;
+  qa::DevBuf emb_out, hid, qkv, attn, mlp, kcache, vcache;
+  qa::DevBuf ssq_attn, ssq_mlp;  // folded RMSNorm: block sums of squares [T][H/128]
   qa::DevBuf head_a, head_keys, head_raw, head_logits, head_normed, hidden_f32, status, badflag;
   qa::PinBuf pin_in, pin_out, pin_res;  // plan staging, sample staging, results
   int kv_pages = 0;     // pages per layer the cache holds
