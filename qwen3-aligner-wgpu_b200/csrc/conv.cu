@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(256) conv1_kernel(const float* __restrict__ me
       // erf by A&S 7.1.26 (erf_as), as the reference's GPU tower computes it
       const float2 x = add2_rn(a[c], b[c]);
       const float2 z = mul2_rn(x, kRsqrt2);
-      const float2 g = mul2_rn(mul2_rn(kHalf, x), add2_rn(kOne, make_float2(erf_as(z.x), erf_as(z.y))));
+      const float2 g = mul2_rn(mul2_rn(kHalf, x), add2_rn(kOne, erf_as2(z)));
       const T lo = f2h<T>(g.x), hi = f2h<T>(g.y);
       pr[c] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&lo)) |
               (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&hi)) << 16);

@@ -407,7 +407,11 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
       case EPI_STORE16: {
         if (ep.act == ACT_GELU) {  // the tower's GELU (conv2/conv3, fc1, proj1)
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = gelu_as(v[i]);
+          for (int i = 0; i < 32; i += 2) {
+            const float2 g = gelu_as2(make_float2(v[i], v[i + 1]));
+            v[i] = g.x;
+            v[i + 1] = g.y;
+          }
         }
         int orow = row;
         if (ep.row_map) orow = ep.row_map[row];

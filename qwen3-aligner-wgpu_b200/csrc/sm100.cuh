@@ -622,6 +622,32 @@ __device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
   return *reinterpret_cast<const float2*>(&r);
 }
 
+// erf_as / gelu_as on two lanes: the same operations in the same order with
+// f32x2 FMA / mul / add (each lane rounded as the scalar instruction would
+// be), so the results are bit-identical to two scalar calls with half the
+// FMA-pipe instructions; the reciprocal and the exponential stay MUFU ops.
+__device__ __forceinline__ float2 erf_as2(float2 x) {
+  const float2 a = make_float2(fabsf(x.x), fabsf(x.y));
+  const float2 d = fma2_rn(make_float2(0.3275911f, 0.3275911f), a, make_float2(1.0f, 1.0f));
+  const float2 t = make_float2(rcp_approx(d.x), rcp_approx(d.y));
+  float2 p = fma2_rn(make_float2(1.061405429f, 1.061405429f), t,
+                     make_float2(-1.453152027f, -1.453152027f));
+  p = fma2_rn(p, t, make_float2(1.421413741f, 1.421413741f));
+  p = fma2_rn(p, t, make_float2(-0.284496736f, -0.284496736f));
+  p = fma2_rn(p, t, make_float2(0.254829592f, 0.254829592f));
+  const float2 q = mul2_rn(mul2_rn(make_float2(-a.x, -a.y), a),
+                           make_float2(1.4426950408889634f, 1.4426950408889634f));
+  const float2 e = make_float2(ex2_approx(q.x), ex2_approx(q.y));
+  const float2 pt = mul2_rn(p, t);
+  const float2 r = fma2_rn(make_float2(-pt.x, -pt.y), e, make_float2(1.0f, 1.0f));
+  return make_float2(copysignf(r.x, x.x), copysignf(r.y, x.y));
+}
+
+__device__ __forceinline__ float2 gelu_as2(float2 x) {
+  const float2 z = mul2_rn(x, make_float2(0.70710678118654752f, 0.70710678118654752f));
+  return mul2_rn(mul2_rn(make_float2(0.5f, 0.5f), x), add2_rn(make_float2(1.0f, 1.0f), erf_as2(z)));
+}
+
 // ---------------------------------------------------------------- 16-bit helpers
 
 template <typename T>
