@@ -62,7 +62,8 @@ constexpr uint32_t kHalf = kTile / 2;        // 16 KB: one 64-column block of a 
 constexpr uint32_t kPageBytes = kHalf / 2;   // 8 KB: 64 rows of one block
 constexpr int kStages = 2;                   // K and V ring depth
 constexpr uint32_t kSumBytes = 2 * 2 * kRows * 4;  // row sums [item parity][head][row]
-constexpr size_t kSmem = 1024 + (2 + 2 * kStages) * kTile + kSumBytes + 256;
+constexpr int kMaxStaged = 128;  // work items of one CTA whose descriptors sit in shared memory
+constexpr size_t kSmem = 1024 + (2 + 2 * kStages) * kTile + kSumBytes + 256 + kMaxStaged * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.0f;  // rescale O when the row max grows by > 2^8
 
@@ -155,13 +156,17 @@ __device__ __forceinline__ void exp_pack64(const uint32_t (&u)[64], float scale,
   sum += (s4[0] + s4[1]) + (s4[2] + s4[3]);
 }
 
-// First valid item at or after i in this CTA's sequence.  Warp 0 walks every
-// index of the sequence once and reports the invalid ones.
-__device__ __forceinline__ int next_valid(const AttnParams& ap, int i, bool report) {
-  for (; i < ap.n_items; i += gridDim.x) {
-    if (get_item(ap, i).valid) break;
-    if (report && ap.status) atomicOr(ap.status, kStatusBadShape);
-  }
+// The CTA's items i = blockIdx.x + k * gridDim.x are derived once, at the
+// start, into shared memory (`staged`, index k), so no role waits on a global
+// load at an item boundary.
+__device__ __forceinline__ const Item& staged_item(const Item* staged, int i) {
+  return staged[(i - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x)];
+}
+
+// First valid item at or after i in this CTA's sequence.
+__device__ __forceinline__ int next_valid(const AttnParams& ap, const Item* staged, int i) {
+  for (; i < ap.n_items; i += gridDim.x)
+    if (staged_item(staged, i).valid) break;
   return i;
 }
 
@@ -191,6 +196,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* l_full = bars + 22;   // [item & 1][head] row sums in xsum
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 26);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+  Item* staged = reinterpret_cast<Item*>(bars + 32);  // [kMaxStaged]
+  static_assert(sizeof(Item) <= 32, "staged item size");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int kSmHead = 32 * kSoftmaxWarps / 2;
@@ -224,6 +231,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tbase = *tslot;
   pdl_wait();  // the previous kernel's results are visible from here
   pdl_trigger();
+  {  // this CTA's item descriptors (at most kMaxStaged: the launcher sizes the grid)
+    const int n_seq = static_cast<int>(blockIdx.x) < ap.n_items
+                          ? (ap.n_items - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                          : 0;
+    for (int k = threadIdx.x; k < n_seq; k += blockDim.x) {
+      const Item it = get_item(ap, static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x));
+      staged[k] = it;
+      if (!it.valid && ap.status) atomicOr(ap.status, kStatusBadShape);
+    }
+    __syncthreads();
+  }
   const uint32_t tS0 = tbase, tO0 = tbase + 256;  // S_h at tS0 + 128 h, O_h at tO0 + 128 h
   auto fail = [&]() {
     *abort_flag = 1;
@@ -240,9 +258,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool is_k = warp == 0;
       bool ok = true;
       uint32_t n_it = 0, g = 0;
-      for (int ci = next_valid(ap, blockIdx.x, is_k); ok && ci < ap.n_items;
-           ci = next_valid(ap, ci + gridDim.x, is_k), ++n_it) {
-        const Item it = get_item(ap, ci);
+      for (int ci = next_valid(ap, staged, blockIdx.x); ok && ci < ap.n_items;
+           ci = next_valid(ap, staged, ci + gridDim.x), ++n_it) {
+        const Item it = staged_item(staged, ci);
         if (is_k) {
           // Q_h of this item once the previous item's last S_h is done
           for (int h = 0; h < 2 && ok; ++h) {
@@ -262,12 +280,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint64_t* empty = is_k ? k_empty : v_empty;
         uint8_t* ring = is_k ? sK : sV;
         const CUtensorMap* tm = is_k ? &tmK : &tmV;
+        // page ids are read one tile ahead: the next tile's load is in flight
+        // while this one waits for its ring slot
+        int nxt[2] = {bt[0], tile_keys(it, 0) > kPage ? bt[1] : 0};
         for (int j = 0; j < it.n_tiles; ++j, ++g) {
           const int st = g & 1;
           const int npg = tile_keys(it, j) / kPage;
+          const int cur[2] = {nxt[0], nxt[1]};
+          if (j + 1 < it.n_tiles) {
+            nxt[0] = bt[2 * (j + 1)];
+            nxt[1] = tile_keys(it, j + 1) > kPage ? bt[2 * (j + 1) + 1] : 0;
+          }
           int rows[2] = {0, 0};
           for (int pg = 0; pg < npg; ++pg) {
-            int page = bt[2 * j + pg];
+            int page = cur[pg];
             if (page < 0 || page >= ap.kv_pages) {
               if (ap.status) atomicOr(ap.status, kStatusBadShape);
               page = 0;
@@ -308,10 +334,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     bool ok = true;
     uint32_t n_it = 0, g = 0;
-    int ci = next_valid(ap, blockIdx.x, false);
+    int ci = next_valid(ap, staged, blockIdx.x);
     Item cur{};
     if (ci < ap.n_items) {
-      cur = get_item(ap, ci);
+      cur = staged_item(staged, ci);
       ok = wait(&q_full[0], 0) && wait(&q_full[1], 0) && wait(&k_full[0], 0);
       if (ok) {
         tc_fence_after();
@@ -328,8 +354,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int ni = ci;
       Item nxt{};
       if (last) {
-        ni = next_valid(ap, ci + gridDim.x, false);
-        if (ni < ap.n_items) nxt = get_item(ap, ni);
+        ni = next_valid(ap, staged, ci + gridDim.x);
+        if (ni < ap.n_items) nxt = staged_item(staged, ni);
       }
       const bool has_next = !last || ni < ap.n_items;
       const Item& sit = last ? nxt : cur;  // owner of the next S
@@ -393,9 +419,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float scale = ap.scale_log2;
     uint32_t n_it = 0, g = 0;
     bool ok = true;
-    for (int i = next_valid(ap, blockIdx.x, false); ok && i < ap.n_items;
-         i = next_valid(ap, i + gridDim.x, false), ++n_it) {
-      const Item it = get_item(ap, i);
+    for (int i = next_valid(ap, staged, blockIdx.x); ok && i < ap.n_items;
+         i = next_valid(ap, staged, i + gridDim.x), ++n_it) {
+      const Item it = staged_item(staged, i);
       const int pos = it.t.q0 + r;
       const int len = it.t.len;
       float m_used = -INFINITY, l = 0.0f;
@@ -467,9 +493,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     uint32_t n_it = 0;
     bool ok = true;
-    for (int i = next_valid(ap, blockIdx.x, false); ok && i < ap.n_items;
-         i = next_valid(ap, i + gridDim.x, false), ++n_it) {
-      const Item it = get_item(ap, i);
+    for (int i = next_valid(ap, staged, blockIdx.x); ok && i < ap.n_items;
+         i = next_valid(ap, staged, i + gridDim.x), ++n_it) {
+      const Item it = staged_item(staged, i);
       const int pos = it.t.q0 + r;
       for (int h = 0; h < 2; ++h) {
         if (!wait(&o_done[h], n_it & 1) || !wait(&l_full[(n_it & 1) * 2 + h], (n_it >> 1) & 1)) {
@@ -537,7 +563,10 @@ int causal_attention_tc(const void* qkv, long long ldq, long long q_rows, int nq
   ap.q_rows = q_rows;
   ap.kv_pages = kv_pages;
   ap.status = status;
-  const int grid = std::min(ap.n_items, device_sm_count());
+  // persistent, one CTA per SM; more CTAs (queued) only when an SM's share of
+  // items would exceed what its shared memory stages
+  const int grid = std::max(std::min(ap.n_items, device_sm_count()),
+                            (ap.n_items + kMaxStaged - 1) / kMaxStaged);
   if (bf16) {
     auto k = attn_tc_kernel<__nv_bfloat16>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
