@@ -62,13 +62,12 @@ __device__ __forceinline__ int out_row(const EpiParams& ep, int row) {
 template <typename T>
 __device__ __forceinline__ void store16_row(T* dst, const float (&v)[32], int ncols) {
   if (ncols == 32 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
-    alignas(16) T tmp[32];
+    uint32_t w[16];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) tmp[i] = f2h<T>(v[i]);
-    const uint4* s = reinterpret_cast<const uint4*>(tmp);
+    for (int i = 0; i < 16; ++i) w[i] = cvt2_rn<T>(make_float2(v[2 * i], v[2 * i + 1]));
     uint4* d = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) d[i] = s[i];
+    for (int i = 0; i < 4; ++i) d[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
   } else {
 #pragma unroll
     for (int i = 0; i < 32; ++i)
@@ -121,7 +120,12 @@ __device__ __forceinline__ float2 unpack2(uint32_t w) {
 }
 template <typename T>
 __device__ __forceinline__ uint32_t pack2_rn(float2 v) {
-  return pack_bits(bits_of(f2h<T>(v.x)), bits_of(f2h<T>(v.y)));
+  return cvt2_rn<T>(v);
+}
+// round16 on two lanes: one packed conversion there and two widenings back.
+template <typename T>
+__device__ __forceinline__ float2 round16x2(float2 v) {
+  return unpack2<T>(pack2_rn<T>(v));
 }
 
 // Per-row inputs of EPI_QKV_ROPE, loaded before the tile's accumulator is
@@ -213,7 +217,7 @@ __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem
         uint32_t w[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i)
-          w[i] = pack2_rn<T>(make_float2(v[h][2 * i] * meta.inv, v[h][2 * i + 1] * meta.inv));
+          w[i] = pack2_rn<T>(mul2_rn(make_float2(v[h][2 * i], v[h][2 * i + 1]), make_float2(meta.inv, meta.inv)));
 #pragma unroll
         for (int j = 0; j < 4; ++j)
           reinterpret_cast<uint4*>(dst + (c + h) * 32)[j] =
@@ -228,18 +232,18 @@ __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem
   for (int c = 0; c < HD / 32; c += 2) {
     float v[32], w[32];
     tmem_ld2x32(tmem_col0 + c * 32, tmem_col0 + (c + 1) * 32, v, w);
-    const float r = meta.inv;
+    const float2 r = make_float2(meta.inv, meta.inv);
 #pragma unroll
     for (int i = 0; i < 32; i += 4) {
-      const float2 x0 = make_float2(round16<T>(v[i] * r), round16<T>(v[i + 1] * r));
-      const float2 x1 = make_float2(round16<T>(v[i + 2] * r), round16<T>(v[i + 3] * r));
+      const float2 x0 = round16x2<T>(mul2_rn(make_float2(v[i], v[i + 1]), r));
+      const float2 x1 = round16x2<T>(mul2_rn(make_float2(v[i + 2], v[i + 3]), r));
       s2a = add2_rn(s2a, mul2_rn(x0, x0));
       s2b = add2_rn(s2b, mul2_rn(x1, x1));
     }
 #pragma unroll
     for (int i = 0; i < 32; i += 4) {
-      const float2 x0 = make_float2(round16<T>(w[i] * r), round16<T>(w[i + 1] * r));
-      const float2 x1 = make_float2(round16<T>(w[i + 2] * r), round16<T>(w[i + 3] * r));
+      const float2 x0 = round16x2<T>(mul2_rn(make_float2(w[i], w[i + 1]), r));
+      const float2 x1 = round16x2<T>(mul2_rn(make_float2(w[i + 2], w[i + 3]), r));
       s2a = add2_rn(s2a, mul2_rn(x0, x0));
       s2b = add2_rn(s2b, mul2_rn(x1, x1));
     }
@@ -281,9 +285,9 @@ __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem
 #pragma unroll
       for (int p = 0; p < 4; ++p) {
         const int i = j0 + 2 * p;
-        const float r = meta.inv;
-        const float2 xa = mul2_rn(mul2_rn(make_float2(round16<T>(va[i] * r), round16<T>(va[i + 1] * r)), inv2), ga[p]);
-        const float2 xb = mul2_rn(mul2_rn(make_float2(round16<T>(vb[i] * r), round16<T>(vb[i + 1] * r)), inv2), gb[p]);
+        const float2 r = make_float2(meta.inv, meta.inv);
+        const float2 xa = mul2_rn(mul2_rn(round16x2<T>(mul2_rn(make_float2(va[i], va[i + 1]), r)), inv2), ga[p]);
+        const float2 xb = mul2_rn(mul2_rn(round16x2<T>(mul2_rn(make_float2(vb[i], vb[i + 1]), r)), inv2), gb[p]);
         const float2 cc = unpack2<T>(cw[p]), sn = unpack2<T>(sw[p]);
         const float2 nxb = make_float2(-xb.x, -xb.y);
         lo[p] = pack2_rn<T>(add2_rn(mul2_rn(xa, cc), mul2_rn(nxb, sn)));

@@ -674,6 +674,19 @@ __device__ __forceinline__ T f2h(float x) {
   return H16Traits<T>::from(x);
 }
 
+// Two f32 rounded to the 16-bit type by one packed conversion (x in the low
+// half), each lane rounded to nearest-even as the scalar conversion rounds it.
+template <typename T>
+__device__ __forceinline__ uint32_t cvt2_rn(float2 v) {
+  if constexpr (H16Traits<T>::kBf16) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(v.x, v.y);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  } else {
+    const __half2 h = __floats2half2_rn(v.x, v.y);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+}
+
 // Round an f32 through the 16-bit format and back.
 template <typename T>
 __device__ __forceinline__ float round16(float x) {

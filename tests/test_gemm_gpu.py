@@ -87,13 +87,16 @@ def test_resid16(dtype):
     assert _rel(h, ref) < TOL16[dtype]
 
 
-def test_resid32_bias():
+@pytest.mark.parametrize("m,k,bn", [(250, 3584, 0), (1000, 896, 0), (1000, 896, 128), (700, 896, 224)])
+def test_resid32_bias(m, k, bn):
+    """The f32 residual epilogue: 64-column blocks with the residual read ahead
+    of the accumulator, and the 32-column tail of a 224-wide tile."""
     L = _lib()
-    A, B = _mk(250, 896, 3584, torch.float16, seed=5)
+    A, B = _mk(m, 896, k, torch.float16, seed=5)
     bias = torch.randn(896, device="cuda") * 0.1
-    h = torch.randn(250, 896, device="cuda")
+    h = torch.randn(m, 896, device="cuda")
     ref = h + A.float() @ B.float().t() + bias
-    L.gemm(A, B, h, mode=L.EPI_RESID32, bias=bias)
+    L.gemm(A, B, h, mode=L.EPI_RESID32, bias=bias, force_bn=bn)
     torch.cuda.synchronize()
     assert _rel(h, ref) < 1e-4
 
