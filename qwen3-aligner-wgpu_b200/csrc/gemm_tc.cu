@@ -534,6 +534,158 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
   }
 }
 
+// ---------------------------------------------------------------------------
+// EPI_RESID32 / EPI_RESID16 with the residual staged in shared memory.  An
+// epilogue thread owns one row, so reading the residual straight from global
+// memory puts 32 rows (32 lines) behind every warp load and leaves the
+// epilogue waiting on memory latency for each 32-column chunk.  Here each
+// epilogue warp has a 4 KB buffer: the 32 rows x 32 columns of residual for
+// its next chunk are copied in by coalesced 16-byte cp.async (four or eight
+// whole rows per instruction) while the current chunk is processed, and the
+// tile's first chunk is requested before the tile's accumulator wait.  The
+// buffer is XOR-swizzled in 16-byte units so that both the copies and the
+// row-per-thread reads are free of bank conflicts.
+constexpr int kEpiStageBytes = 4096;  // per epilogue warp
+
+// Whether the staged path applies (warp-uniform): a residual mode with 16-byte
+// aligned rows and whole 16-byte units at the row ends.
+template <typename T>
+__device__ __forceinline__ bool resid_stageable(const EpiParams& ep, int N) {
+  if (ep.mode != EPI_RESID32 && ep.mode != EPI_RESID16) return false;
+  const int per16 = ep.mode == EPI_RESID32 ? 4 : 16 / static_cast<int>(sizeof(T));
+  return (reinterpret_cast<uintptr_t>(ep.out) & 15u) == 0 && ep.ldo % per16 == 0 && N % per16 == 0;
+}
+
+// Request the residual of rows row0 .. row0 + 31, columns col .. col + 31,
+// into the warp's buffer (rows past M and columns past N arrive as zeros).
+template <typename T>
+__device__ __forceinline__ void resid_issue(const EpiParams& ep, uint8_t* buf, int row0, int col,
+                                            int M, int N) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t sb = smem_u32(buf);
+  if (ep.mode == EPI_RESID32) {
+    const float* src0 = static_cast<const float*>(ep.out);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = 4 * i + (lane >> 3), q = lane & 7;  // 128-byte rows, 8 units
+      const int grow = row0 + r, gcol = col + 4 * q;
+      const bool ok = grow < M && gcol < N;
+      const float* src = src0 + (ok ? static_cast<long long>(grow) * ep.ldo + gcol : 0);
+      cp_async16(sb + r * 128 + 16 * (q ^ (r & 7)), src, ok ? 16u : 0u);
+    }
+  } else {
+    const T* src0 = static_cast<const T*>(ep.out);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = 8 * i + (lane >> 2), q = lane & 3;  // 64-byte rows, 4 units
+      const int grow = row0 + r, gcol = col + 8 * q;
+      const bool ok = grow < M && gcol < N;
+      const T* src = src0 + (ok ? static_cast<long long>(grow) * ep.ldo + gcol : 0);
+      cp_async16(sb + r * 64 + 16 * (q ^ ((r >> 1) & 3)), src, ok ? 16u : 0u);
+    }
+  }
+  cp_async_commit();
+}
+
+// The staged epilogue over columns [cb, ce) of the warp's 32 tile rows from
+// row0.  The chunk at cb must already be requested; the last chunk requests
+// the first chunk of the warp's next tile (rows nxt_row0, columns from
+// nxt_n0 + cb) when nxt_n0 >= 0.  Same arithmetic as the direct path: bias,
+// then the residual, rounded once at the store.
+template <int BN, typename T>
+__device__ __forceinline__ void epilogue_resid_staged(const EpiParams& ep, uint32_t tmem_row,
+                                                      int row0, int M, int n0, int N, int cb,
+                                                      int ce, uint8_t* buf, int nxt_row0,
+                                                      int nxt_n0) {
+  const int lane = threadIdx.x & 31;
+  const int row = row0 + lane;
+  float ssq_acc = 0.0f;
+#pragma unroll 1
+  for (int c0 = cb; c0 < ce; c0 += 32) {
+    cp_async_wait_all();
+    __syncwarp();
+    float h[32];
+    if (ep.mode == EPI_RESID32) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 t = *reinterpret_cast<const float4*>(buf + lane * 128 + 16 * (j ^ (lane & 7)));
+        h[4 * j] = t.x;
+        h[4 * j + 1] = t.y;
+        h[4 * j + 2] = t.z;
+        h[4 * j + 3] = t.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 t = *reinterpret_cast<const uint4*>(buf + lane * 64 + 16 * (j ^ ((lane >> 1) & 3)));
+        const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = unpack2<T>(w[k]);
+          h[8 * j + 2 * k] = f.x;
+          h[8 * j + 2 * k + 1] = f.y;
+        }
+      }
+    }
+    __syncwarp();  // every lane has read the buffer before it is refilled
+    const bool more = c0 + 32 < ce;
+    if (more || nxt_n0 >= 0)
+      resid_issue<T>(ep, buf, more ? row0 : nxt_row0, more ? n0 + c0 + 32 : nxt_n0 + cb, M, N);
+    float v[32];
+    tmem_ld32(tmem_row + c0, v);  // warp-collective: every lane, every chunk
+    const int col = n0 + c0;
+    const int nc = min(min(32, BN - c0), N - col);
+    if (row >= M || nc <= 0) continue;
+    if (ep.bias) {
+      const float* bp = ep.bias + col;
+      if (vec_ok(bp, nc)) {
+        const float4* b4 = reinterpret_cast<const float4*>(bp);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 t = __ldg(b4 + i);
+          v[4 * i] += t.x;
+          v[4 * i + 1] += t.y;
+          v[4 * i + 2] += t.z;
+          v[4 * i + 3] += t.w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < nc) v[i] += bp[i];
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] += h[i];
+    if (ep.mode == EPI_RESID32) {
+      float* dst = static_cast<float*>(ep.out) + static_cast<long long>(row) * ep.ldo + col;
+      if (vec_ok(dst, nc)) {
+        float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < nc) dst[i] = v[i];
+      }
+    } else {
+      T* dst = static_cast<T*>(ep.out) + static_cast<long long>(row) * ep.ldo + col;
+      store16_row<T>(dst, v, nc);
+      if (ep.ssq_out) {  // the 128-column block's sum of squares of the stored values
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float x = i < nc ? round16<T>(v[i]) : 0.0f;
+          ssq_acc = fmaf(x, x, ssq_acc);
+        }
+        if ((col + 32) % kSsqCols == 0 || col + 32 >= N) {
+          ep.ssq_out[static_cast<long long>(row) * ep.ssq_n + col / kSsqCols] = ssq_acc;
+          ssq_acc = 0.0f;
+        }
+      }
+    }
+  }
+}
+
 // Column range of epilogue warpgroup `wg` out of `nwg` for a BN-wide tile.
 template <int BN>
 __device__ __forceinline__ void epi_range(int mode, int wg, int nwg, int& cb, int& ce) {
@@ -683,6 +835,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // the row's folded-norm statistics are loaded one tile ahead
     auto tile_row = [&](int t) { return (t / n_tiles_n) * kBM + q * 32 + lane; };
     SsqRow ssq = ssq_load(ep, tile_row(blockIdx.x), M);
+    if (resid_stageable<T>(ep, N)) {
+      // residual modes: the warp's staging buffer, the first tile's first
+      // chunk requested before the first accumulator wait
+      uint8_t* stage = smem + S * (Cfg::kABytes + Cfg::kBBytes) + 256 + (warp - 2) * kEpiStageBytes;
+      auto warp_row0 = [&](int t) { return (t / n_tiles_n) * kBM + q * 32; };
+      if (static_cast<int>(blockIdx.x) < n_tiles)
+        resid_issue<T>(ep, stage, warp_row0(blockIdx.x), (blockIdx.x % n_tiles_n) * BN + cb, M, N);
+      for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++lt) {
+        const int buf = lt & 1;
+        if (*abort_flag || !mbar_wait(&tfull[buf], (lt >> 1) & 1)) {
+          if (lane == 0) timed_out();
+          break;
+        }
+        tc_fence_after();
+        const uint32_t trow = tbase + buf * kAccCols + (static_cast<uint32_t>(q * 32) << 16);
+        const int tn = t + gridDim.x;
+        epilogue_resid_staged<BN, T>(ep, trow, warp_row0(t), M, (t % n_tiles_n) * BN, N, cb, ce,
+                                     stage, tn < n_tiles ? warp_row0(tn) : 0,
+                                     tn < n_tiles ? (tn % n_tiles_n) * BN : -1);
+        tc_fence_before();
+        mbar_arrive(&tempty[buf]);
+      }
+      cp_async_wait_all();  // nothing in flight into shared memory at exit
+    } else {
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++lt) {
       const int buf = lt & 1;
       const int m0 = (t / n_tiles_n) * kBM, n0 = (t % n_tiles_n) * BN;
@@ -700,6 +876,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       epilogue<BN, T>(ep, trow, row, M, n0, N, cb, ce, meta, gain);
       tc_fence_before();
       mbar_arrive(&tempty[buf]);
+    }
     }
   }
 
@@ -861,6 +1038,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // the row's folded-norm statistics are loaded one tile ahead
     auto tile_row = [&](int t) { return (t / n_tiles_n) * 2 * kBM + rank * kBM + q * 32 + lane; };
     SsqRow ssq = ssq_load(ep, tile_row(pair), M);
+    if (resid_stageable<T>(ep, N)) {
+      // residual modes: the warp's staging buffer, the first tile's first
+      // chunk requested before the first accumulator wait
+      uint8_t* stage = smem + S * (kPairHalf + kBHalf) + 256 + (warp - 2) * kEpiStageBytes;
+      auto warp_row0 = [&](int t) { return (t / n_tiles_n) * 2 * kBM + rank * kBM + q * 32; };
+      if (pair < n_tiles)
+        resid_issue<T>(ep, stage, warp_row0(pair), (pair % n_tiles_n) * BN + cb, M, N);
+      for (int t = pair; t < n_tiles; t += n_pairs, ++lt) {
+        const int buf = lt & 1;
+        if (*abort_flag || !mbar_wait(&tfull[buf], (lt >> 1) & 1)) {
+          if (lane == 0) timed_out();
+          break;
+        }
+        tc_fence_after();
+        const uint32_t trow = tbase + buf * kAccCols + (static_cast<uint32_t>(q * 32) << 16);
+        const int tn = t + n_pairs;
+        epilogue_resid_staged<BN, T>(ep, trow, warp_row0(t), M, (t % n_tiles_n) * BN, N, cb, ce,
+                                     stage, tn < n_tiles ? warp_row0(tn) : 0,
+                                     tn < n_tiles ? (tn % n_tiles_n) * BN : -1);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote_relaxed(tempty_lead + buf * 8);
+      }
+      cp_async_wait_all();  // nothing in flight into shared memory at exit
+    } else {
     for (int t = pair; t < n_tiles; t += n_pairs, ++lt) {
       const int buf = lt & 1;
       const int m0 = (t / n_tiles_n) * 2 * kBM, n0 = (t % n_tiles_n) * BN;
@@ -879,6 +1081,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote_relaxed(tempty_lead + buf * 8);
+    }
     }
   }
 
@@ -1604,7 +1807,9 @@ int launch_conv_tma(const void* x, int n, int h, int w, int c, const void* wt, i
 template <int BN, typename T>
 int launch_pair(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
                 const EpiParams& ep, cudaStream_t stream) {
-  constexpr size_t kPairSmem = PairCfg<BN>::kSmem;
+  // the residual modes add the epilogue warps' staging buffers
+  const bool resid = ep.mode == EPI_RESID32 || ep.mode == EPI_RESID16;
+  const size_t kPairSmem = PairCfg<BN>::kSmem + (resid ? kGemmEpiWarps * kEpiStageBytes : 0);
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, A, H16Traits<T>::kBf16, K, M, lda, kBK, kBM);
   if (rc) return rc;
@@ -1659,12 +1864,14 @@ int launch(const void* A, long long lda, const void* B, long long ldb, int M, in
   rc = make_tmap_2d(&tb, B, H16Traits<T>::kBf16, K, N, ldb, kBK, BN);
   if (rc) return rc;
   auto kern = gemm_tc_kernel<BN, T>;
-  cudaError_t e =
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmem);
+  // the residual modes add the epilogue warps' staging buffers
+  const bool resid = ep.mode == EPI_RESID32 || ep.mode == EPI_RESID16;
+  const size_t smem = Cfg::kSmem + (resid ? kGemmEpiWarps * kEpiStageBytes : 0);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return (int)e;
   const int tiles = ((N + BN - 1) / BN) * ((M + kBM - 1) / kBM);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  e = launch_pdl(kern, dim3(grid), dim3(kGemmThreads), Cfg::kSmem, stream, ta, tb, M, N, K, ep);
+  e = launch_pdl(kern, dim3(grid), dim3(kGemmThreads), smem, stream, ta, tb, M, N, K, ep);
   if (e != cudaSuccess) return (int)e;
   return (int)cudaGetLastError();
 }

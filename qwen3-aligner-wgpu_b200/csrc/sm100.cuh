@@ -95,6 +95,23 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// ---------------------------------------------------------------- cp.async
+// 16 bytes global -> shared through the L2 only; src_bytes < 16 fills the rest
+// with zeros (0 reads nothing).  Completion: cp_async_commit groups the
+// thread's copies, cp_async_wait_all waits for all of them (visible to the
+// issuing thread; a warp or CTA barrier then publishes them).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
 // 2-D tiled load global -> shared, completion signalled on `bar` (tx bytes).
 // x is the innermost (contiguous) coordinate in elements, y the row.
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst,

@@ -77,12 +77,15 @@ def test_bias_gelu():
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-def test_resid16(dtype):
+@pytest.mark.parametrize("m,n,k,bn", [(300, 1024, 2048, 0), (77, 640, 1024, 0), (200, 1024, 1024, 128)])
+def test_resid16(dtype, m, n, k, bn):
+    """The 16-bit residual epilogue (residual staged through shared memory):
+    CTA pairs, a last column tile past N, ragged rows, one-CTA tiles."""
     L = _lib()
-    A, B = _mk(300, 1024, 2048, dtype, seed=4)
-    h = (torch.randn(300, 1024, device="cuda") * 2).to(dtype)
+    A, B = _mk(m, n, k, dtype, seed=4)
+    h = (torch.randn(m, n, device="cuda") * 2).to(dtype)
     ref = (h.float() + A.float() @ B.float().t())
-    L.gemm(A, B, h, mode=L.EPI_RESID16)
+    L.gemm(A, B, h, mode=L.EPI_RESID16, force_bn=bn)
     torch.cuda.synchronize()
     assert _rel(h, ref) < TOL16[dtype]
 
