@@ -177,6 +177,31 @@ __device__ __forceinline__ QkvRow qkv_row_meta(const EpiParams& ep, int row, int
   return r;
 }
 
+// Writes the warp's staged 32 rows x 128 bytes (eight 16-byte units a row,
+// XOR-swizzled by row) to global memory, four whole rows per instruction:
+// units 0-3 of row r go to base_r + off0, units 4-7 to base_r + off1
+// (elements), where base_r is lane r's `base` (nullptr: row not stored).
+// Warp-collective; the buffer may be refilled once it returns.
+template <typename T>
+__device__ __forceinline__ void flush_rows(const uint8_t* st, T* base, int off0, int off1) {
+  const int lane = threadIdx.x & 31;
+  __syncwarp();
+  const unsigned long long b = reinterpret_cast<unsigned long long>(base);
+#pragma unroll 1
+  for (int i = 0; i < 8; ++i) {
+    const int r = 4 * i + (lane >> 3), u = lane & 7;
+    const unsigned long long rb = __shfl_sync(0xFFFFFFFFu, b, r);
+    const uint4 d = *reinterpret_cast<const uint4*>(st + r * 128 + 16 * (u ^ (r & 7)));
+    if (rb) *reinterpret_cast<uint4*>(reinterpret_cast<T*>(rb) + (u < 4 ? off0 + 8 * u : off1 + 8 * (u - 4))) = d;
+  }
+  __syncwarp();
+}
+// This lane's row, 16-byte unit u, into the staging buffer (row = lane).
+__device__ __forceinline__ void stage_unit(uint8_t* st, int u, uint4 d) {
+  const int lane = threadIdx.x & 31;
+  *reinterpret_cast<uint4*>(st + lane * 128 + 16 * (u ^ (lane & 7))) = d;
+}
+
 // EPI_QKV_ROPE for one 128-column head of this thread's row.  The head's
 // values are rounded to the storage type (the GEMM output's rounding point).
 // A v head is appended to the cache as rounded.  A q or k head takes RMSNorm
@@ -190,10 +215,10 @@ __device__ __forceinline__ QkvRow qkv_row_meta(const EpiParams& ep, int row, int
 // k_norm gains staged in shared memory; each chunk's four cos and four sin
 // 16-byte loads (read-only path) are issued before its TMEM read so that
 // their latencies overlap.
-template <typename T>
+template <typename T, bool kStaged>
 __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem_col0, int row,
                                               int M, int head, const QkvRow& meta,
-                                              const float* gain) {
+                                              const float* gain, uint8_t* ost) {
   constexpr int HD = 128;
   const RopeKV& rk = ep.rk;
   const bool ok = row < M;
@@ -206,7 +231,7 @@ __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem
     dst = static_cast<T*>(is_v ? rk.vc : rk.kc) + meta.kv_off +
           static_cast<long long>(kvh) * rk.page_size * HD;
   }
-  if (is_v) {
+  if (is_v) {  // stored directly: staging these too would make the kernel spill
 #pragma unroll 1
     for (int c = 0; c < HD / 32; c += 2) {
       float v[2][32];
@@ -267,7 +292,9 @@ __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem
     }
     float va[32], vb[32];
     tmem_ld2x32(tmem_col0 + c * 32, tmem_col0 + 64 + c * 32, va, vb);
-    if (!ok) continue;
+    if constexpr (!kStaged) {
+      if (!ok) continue;
+    }  // staged: rows past M are computed (from zeros) and not stored
 #pragma unroll
     for (int j0 = 0; j0 < 32; j0 += 8) {
       const int d0 = c * 32 + j0;
@@ -293,9 +320,15 @@ __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem
         lo[p] = pack2_rn<T>(add2_rn(mul2_rn(xa, cc), mul2_rn(nxb, sn)));
         hi[p] = pack2_rn<T>(add2_rn(mul2_rn(xb, cc), mul2_rn(xa, sn)));
       }
-      *reinterpret_cast<uint4*>(dst + d0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-      *reinterpret_cast<uint4*>(dst + d0 + 64) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      if constexpr (kStaged) {
+        stage_unit(ost, j0 / 8, make_uint4(lo[0], lo[1], lo[2], lo[3]));
+        stage_unit(ost, 4 + j0 / 8, make_uint4(hi[0], hi[1], hi[2], hi[3]));
+      } else {
+        *reinterpret_cast<uint4*>(dst + d0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        *reinterpret_cast<uint4*>(dst + d0 + 64) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      }
     }
+    if constexpr (kStaged) flush_rows<T>(ost, ok ? dst : nullptr, c * 32, 64 + c * 32);
   }
 }
 
@@ -312,16 +345,17 @@ __device__ __forceinline__ void stage_qkv_gains(const EpiParams& ep, float* gain
 // The fused epilogue over columns [cb, ce) of this thread's tile row (cb, ce
 // multiples of 32; two epilogue warpgroups split a tile between them).  For
 // SwiGLU the range is over the output columns [0, BN/2).
-template <int BN, typename T>
+template <int BN, typename T, bool kStagedQkv = false>
 __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row, int row, int M,
                                          int n0, int N, int cb, int ce, const QkvRow& meta = {},
-                                         const float* gain = nullptr) {
+                                         const float* gain = nullptr, uint8_t* stage = nullptr) {
   if constexpr (BN % 128 == 0) {
     if (ep.mode == EPI_QKV_ROPE) {
 #pragma unroll 1
       for (int hb = cb / 128; hb < ce / 128; ++hb)
         if (n0 + hb * 128 < N)
-          qkv_rope_head<T>(ep, tmem_row + hb * 128, row, M, (n0 + hb * 128) / 128, meta, gain);
+          qkv_rope_head<T, kStagedQkv>(ep, tmem_row + hb * 128, row, M, (n0 + hb * 128) / 128,
+                                       meta, gain, stage);
       return;
     }
   }
@@ -1063,6 +1097,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       cp_async_wait_all();  // nothing in flight into shared memory at exit
     } else {
+    // EPI_QKV_ROPE: the warp's buffer stages each head's rows for coalesced stores
+    uint8_t* qstage = ep.mode == EPI_QKV_ROPE
+                          ? smem + S * (kPairHalf + kBHalf) + 256 + (warp - 2) * kEpiStageBytes
+                          : nullptr;
     for (int t = pair; t < n_tiles; t += n_pairs, ++lt) {
       const int buf = lt & 1;
       const int m0 = (t / n_tiles_n) * 2 * kBM, n0 = (t % n_tiles_n) * BN;
@@ -1077,7 +1115,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       ssq = ssq_load(ep, tile_row(t + n_pairs), M);  // arrives during this epilogue
       tc_fence_after();
       const uint32_t trow = tbase + buf * kAccCols + (static_cast<uint32_t>(q * 32) << 16);
-      epilogue<BN, T>(ep, trow, row, M, n0, N, cb, ce, meta, gain);
+      epilogue<BN, T, true>(ep, trow, row, M, n0, N, cb, ce, meta, gain, qstage);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote_relaxed(tempty_lead + buf * 8);
@@ -1807,9 +1845,10 @@ int launch_conv_tma(const void* x, int n, int h, int w, int c, const void* wt, i
 template <int BN, typename T>
 int launch_pair(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
                 const EpiParams& ep, cudaStream_t stream) {
-  // the residual modes add the epilogue warps' staging buffers
-  const bool resid = ep.mode == EPI_RESID32 || ep.mode == EPI_RESID16;
-  const size_t kPairSmem = PairCfg<BN>::kSmem + (resid ? kGemmEpiWarps * kEpiStageBytes : 0);
+  // the residual and QKV modes add the epilogue warps' staging buffers
+  const bool staged =
+      ep.mode == EPI_RESID32 || ep.mode == EPI_RESID16 || ep.mode == EPI_QKV_ROPE;
+  const size_t kPairSmem = PairCfg<BN>::kSmem + (staged ? kGemmEpiWarps * kEpiStageBytes : 0);
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, A, H16Traits<T>::kBf16, K, M, lda, kBK, kBM);
   if (rc) return rc;
