@@ -163,7 +163,7 @@ __device__ __forceinline__ float row_rms_inv(const EpiParams& ep, const SsqRow& 
   return 1.0f / sqrtf(s / ep.rms_d + ep.rms_eps);
 }
 
-template <typename T>
+template <typename T, bool kPrefetch = true>
 __device__ __forceinline__ QkvRow qkv_row_meta(const EpiParams& ep, int row, int M) {
   QkvRow r;
   if (row >= M) return r;
@@ -172,9 +172,30 @@ __device__ __forceinline__ QkvRow qkv_row_meta(const EpiParams& ep, int row, int
   const int clip = rk.clip_of[row];
   const int page = rk.block_tab[clip * rk.max_pages + r.pos / rk.page_size];
   r.kv_off = (static_cast<long long>(page) * rk.nkv * rk.page_size + r.pos % rk.page_size) * 128;
-  asm volatile("prefetch.global.L1 [%0];" ::"l"(static_cast<const T*>(rk.cos_t) + r.pos * 64));
-  asm volatile("prefetch.global.L1 [%0];" ::"l"(static_cast<const T*>(rk.sin_t) + r.pos * 64));
+  if constexpr (kPrefetch) {
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(static_cast<const T*>(rk.cos_t) + r.pos * 64));
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(static_cast<const T*>(rk.sin_t) + r.pos * 64));
+  }
   return r;
+}
+
+// Request the cos (table 0) or sin (table 1) lines of the warp's 32 rows at
+// their positions (lane r's `pos`; rows with !ok arrive as zeros) into a 4 KB
+// buffer: 128 bytes a row, 16-byte units XOR-swizzled by row, four whole rows
+// per cp.async instruction.
+template <typename T>
+__device__ __forceinline__ void qkv_cs_issue(const EpiParams& ep, uint8_t* buf, int table, int pos,
+                                             bool ok) {
+  const int lane = threadIdx.x & 31;
+  const T* tab = static_cast<const T*>(table ? ep.rk.sin_t : ep.rk.cos_t);
+  const uint32_t sb = smem_u32(buf);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = 4 * i + (lane >> 3), u = lane & 7;
+    const int p = __shfl_sync(0xFFFFFFFFu, pos, r);
+    const bool rok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, r) != 0;
+    cp_async16(sb + r * 128 + 16 * (u ^ (r & 7)), rok ? tab + p * 64 + 8 * u : tab, rok ? 16u : 0u);
+  }
 }
 
 // Writes the warp's staged 32 rows x 128 bytes (eight 16-byte units a row,
@@ -216,9 +237,10 @@ __device__ __forceinline__ void stage_unit(uint8_t* st, int u, uint4 d) {
 // 16-byte loads (read-only path) are issued before its TMEM read so that
 // their latencies overlap.
 template <typename T, bool kStaged>
-__device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem_col0, int row,
+__device__ __forceinline__ bool qkv_rope_head(const EpiParams& ep, uint32_t tmem_col0, int row,
                                               int M, int head, const QkvRow& meta,
-                                              const float* gain, uint8_t* ost) {
+                                              const float* gain, uint8_t* ost, const uint8_t* cs,
+                                              uint64_t* csfull, uint32_t cs_parity) {
   constexpr int HD = 128;
   const RopeKV& rk = ep.rk;
   const bool ok = row < M;
@@ -249,7 +271,7 @@ __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem
               make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
       }
     }
-    return;
+    return true;
   }
   // pass 1: sum of squares of the rounded values (two 32-column chunks per wait)
   float2 s2a = make_float2(0.0f, 0.0f), s2b = make_float2(0.0f, 0.0f);
@@ -279,6 +301,9 @@ __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem
   const float* nw = is_q ? gain : gain + HD;
   const uint4* ct = reinterpret_cast<const uint4*>(static_cast<const T*>(rk.cos_t) + meta.pos * (HD / 2));
   const uint4* st = reinterpret_cast<const uint4*>(static_cast<const T*>(rk.sin_t) + meta.pos * (HD / 2));
+  if constexpr (kStaged) {  // the rows' cos | sin lines, requested at the top of the tile
+    if (!mbar_wait_warp(csfull, cs_parity)) return false;
+  }
   // pass 2: elements d in [32c, 32c + 32) with their partners d + 64; the
   // chunk's cos / sin lines are requested before its TMEM read, so the two
   // latencies overlap
@@ -287,8 +312,14 @@ __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem
     uint4 cu[4], su[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      cu[q] = ok ? __ldg(ct + c * 4 + q) : make_uint4(0, 0, 0, 0);
-      su[q] = ok ? __ldg(st + c * 4 + q) : make_uint4(0, 0, 0, 0);
+      if constexpr (kStaged) {
+        const int o = (threadIdx.x & 31) * 128 + 16 * ((4 * c + q) ^ (threadIdx.x & 7));
+        cu[q] = *reinterpret_cast<const uint4*>(cs + o);
+        su[q] = *reinterpret_cast<const uint4*>(cs + 4096 + o);
+      } else {
+        cu[q] = ok ? __ldg(ct + c * 4 + q) : make_uint4(0, 0, 0, 0);
+        su[q] = ok ? __ldg(st + c * 4 + q) : make_uint4(0, 0, 0, 0);
+      }
     }
     float va[32], vb[32];
     tmem_ld2x32(tmem_col0 + c * 32, tmem_col0 + 64 + c * 32, va, vb);
@@ -330,6 +361,7 @@ __device__ __forceinline__ void qkv_rope_head(const EpiParams& ep, uint32_t tmem
     }
     if constexpr (kStaged) flush_rows<T>(ost, ok ? dst : nullptr, c * 32, 64 + c * 32);
   }
+  return true;
 }
 
 // The epilogue warps (threads 64 .. 64 + 32 * 8 - 1 of the two GEMM kernels)
@@ -345,18 +377,23 @@ __device__ __forceinline__ void stage_qkv_gains(const EpiParams& ep, float* gain
 // The fused epilogue over columns [cb, ce) of this thread's tile row (cb, ce
 // multiples of 32; two epilogue warpgroups split a tile between them).  For
 // SwiGLU the range is over the output columns [0, BN/2).
+// Returns false only when a staged QKV epilogue's wait for its cos | sin
+// lines ran out.
 template <int BN, typename T, bool kStagedQkv = false>
-__device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row, int row, int M,
+__device__ __forceinline__ bool epilogue(const EpiParams& ep, uint32_t tmem_row, int row, int M,
                                          int n0, int N, int cb, int ce, const QkvRow& meta = {},
-                                         const float* gain = nullptr, uint8_t* stage = nullptr) {
+                                         const float* gain = nullptr, uint8_t* stage = nullptr,
+                                         const uint8_t* cs = nullptr, uint64_t* csfull = nullptr,
+                                         uint32_t cs_parity = 0) {
   if constexpr (BN % 128 == 0) {
     if (ep.mode == EPI_QKV_ROPE) {
 #pragma unroll 1
       for (int hb = cb / 128; hb < ce / 128; ++hb)
-        if (n0 + hb * 128 < N)
-          qkv_rope_head<T, kStagedQkv>(ep, tmem_row + hb * 128, row, M, (n0 + hb * 128) / 128,
-                                       meta, gain, stage);
-      return;
+        if (n0 + hb * 128 < N &&
+            !qkv_rope_head<T, kStagedQkv>(ep, tmem_row + hb * 128, row, M, (n0 + hb * 128) / 128,
+                                          meta, gain, stage, cs, csfull, cs_parity))
+          return false;
+      return true;
     }
   }
   if (ep.mode == EPI_SWIGLU16) {
@@ -380,7 +417,7 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
         if (nc > 0) store16_row<T>(out + (long long)row * ep.ldo + oc, g, nc);
       }
     }
-    return;
+    return true;
   }
 
   if (ep.mode == EPI_ARGMAX) {
@@ -413,7 +450,7 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
       }
     }
     if (row < M && best != 0ull) atomicMax(ep.keys + row, best);
-    return;
+    return true;
   }
 
   float ssq_acc = 0.0f;  // EPI_RESID16 with ssq_out: the current 128-column block
@@ -566,6 +603,7 @@ __device__ __forceinline__ void epilogue(const EpiParams& ep, uint32_t tmem_row,
       chunk(c0, v);
     }
   }
+  return true;
 }
 
 // ---------------------------------------------------------------------------
@@ -949,7 +987,8 @@ template <int BN, typename T>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      int M, int N, int K, EpiParams ep) {
-  constexpr int S = kPairStages;
+  // EPI_QKV_ROPE gives one ring stage to the epilogue's cos | sin staging
+  const int S = ep.mode == EPI_QKV_ROPE ? kPairStages - 1 : kPairStages;
   constexpr uint32_t kBHalf = PairCfg<BN>::kBHalf;
   constexpr uint32_t kAccCols = 256;
   constexpr uint32_t kAllocCols = 512;
@@ -962,8 +1001,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* csfull = tempty + 2;   // [4] EPI_QKV_ROPE: a lane quarter's cos | sin lines landed
+  uint64_t* csempty = csfull + 4;  // [4] ... and were read by both of its warps
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(csempty + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+  uint8_t* epi_smem = smem + S * (kPairHalf + kBHalf) + 256;  // epilogue staging buffers
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -981,6 +1023,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
       mbar_init(&tempty[i], 2 * kGemmEpiWarps);
+    }
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&csfull[i], 64);  // both warps' lanes, as their copies land
+      mbar_init(&csempty[i], 2);  // one arrival per warp
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -1005,13 +1051,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       const uint32_t full_lead = mapa_shared(smem_u32(full), 0);
-      uint32_t c = 0;
+      int s = 0;        // ring slot and its phase, advanced per k-block
+      uint32_t ph = 0;  // (S is a runtime value here: no division per k-block)
       for (int t = pair; t < n_tiles && !*abort_flag; t += n_pairs) {
         const int m0 = (t / n_tiles_n) * 2 * kBM, n0 = (t % n_tiles_n) * BN;
         bool ok = true;
-        for (int kb = 0; kb < nkb; ++kb, ++c) {
-          const int s = c % S;
-          const uint32_t ph = (c / S) & 1;
+        for (int kb = 0; kb < nkb; ++kb, s = (s + 1 == S) ? 0 : s + 1, ph ^= (s == 0)) {
           if (!mbar_wait(&empty[s], ph ^ 1u)) {
             timed_out();
             ok = false;
@@ -1028,7 +1073,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     if (rank == 0) {  // the whole warp; one elected lane issues
       constexpr uint32_t idesc = f16_instr_desc(2 * kBM, BN, H16Traits<T>::kBf16);
-      uint32_t c = 0;
+      int s = 0;        // ring slot and its phase, advanced per k-block
+      uint32_t ph = 0;
       int lt = 0;
       for (int t = pair; t < n_tiles && !__any_sync(0xFFFFFFFFu, *abort_flag != 0); t += n_pairs, ++lt) {
         const int buf = lt & 1;
@@ -1039,9 +1085,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_fence_after();
         const uint32_t acc = tbase + buf * kAccCols;
         bool ok = true;
-        for (int kb = 0; kb < nkb; ++kb, ++c) {
-          const int s = c % S;
-          const uint32_t ph = (c / S) & 1;
+        for (int kb = 0; kb < nkb; ++kb, s = (s + 1 == S) ? 0 : s + 1, ph ^= (s == 0)) {
           if (!mbar_wait_warp(&full[s], ph)) {
             timed_out();
             ok = false;
@@ -1075,7 +1119,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (resid_stageable<T>(ep, N)) {
       // residual modes: the warp's staging buffer, the first tile's first
       // chunk requested before the first accumulator wait
-      uint8_t* stage = smem + S * (kPairHalf + kBHalf) + 256 + (warp - 2) * kEpiStageBytes;
+      uint8_t* stage = epi_smem + (warp - 2) * kEpiStageBytes;
       auto warp_row0 = [&](int t) { return (t / n_tiles_n) * 2 * kBM + rank * kBM + q * 32; };
       if (pair < n_tiles)
         resid_issue<T>(ep, stage, warp_row0(pair), (pair % n_tiles_n) * BN + cb, M, N);
@@ -1097,16 +1141,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       cp_async_wait_all();  // nothing in flight into shared memory at exit
     } else {
-    // EPI_QKV_ROPE: the warp's buffer stages each head's rows for coalesced stores
-    uint8_t* qstage = ep.mode == EPI_QKV_ROPE
-                          ? smem + S * (kPairHalf + kBHalf) + 256 + (warp - 2) * kEpiStageBytes
-                          : nullptr;
+    // EPI_QKV_ROPE: the warp's buffer stages each head's rows for coalesced
+    // stores; the two warps of a TMEM lane quarter (one per column half)
+    // share the cos | sin lines of their 32 rows, each warp copying one table
+    const bool qkv = ep.mode == EPI_QKV_ROPE;
+    uint8_t* qstage = qkv ? epi_smem + (warp - 2) * kEpiStageBytes : nullptr;
+    uint8_t* cs = qkv ? epi_smem + kGemmEpiWarps * kEpiStageBytes + q * 8192 : nullptr;
     for (int t = pair; t < n_tiles; t += n_pairs, ++lt) {
       const int buf = lt & 1;
       const int m0 = (t / n_tiles_n) * 2 * kBM, n0 = (t % n_tiles_n) * BN;
       const int row = m0 + rank * kBM + q * 32 + lane;
       QkvRow meta;
-      if (ep.mode == EPI_QKV_ROPE) meta = qkv_row_meta<T>(ep, row, M);  // before the wait
+      if (qkv) {
+        meta = qkv_row_meta<T, false>(ep, row, M);  // before the wait
+        // both warps have read the previous tile's lines; request this tile's
+        if (lt > 0 && !mbar_wait_warp(&csempty[q], (lt - 1) & 1)) {
+          if (lane == 0) timed_out();
+          break;
+        }
+        qkv_cs_issue<T>(ep, cs + wg * 4096, wg, meta.pos, row < M);
+        cp_async_mbar_arrive_noinc(&csfull[q]);
+      }
       meta.inv = row_rms_inv(ep, ssq);
       if (*abort_flag || !mbar_wait(&tfull[buf], (lt >> 1) & 1)) {
         if (lane == 0) timed_out();
@@ -1115,11 +1170,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       ssq = ssq_load(ep, tile_row(t + n_pairs), M);  // arrives during this epilogue
       tc_fence_after();
       const uint32_t trow = tbase + buf * kAccCols + (static_cast<uint32_t>(q * 32) << 16);
-      epilogue<BN, T, true>(ep, trow, row, M, n0, N, cb, ce, meta, gain, qstage);
+      const bool ep_ok =
+          epilogue<BN, T, true>(ep, trow, row, M, n0, N, cb, ce, meta, gain, qstage, cs, &csfull[q], lt & 1);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_remote_relaxed(tempty_lead + buf * 8);
+      if (!ep_ok) {
+        if (lane == 0) timed_out();
+        break;
+      }
+      if (lane == 0) {
+        mbar_arrive_remote_relaxed(tempty_lead + buf * 8);
+        if (qkv) mbar_arrive(&csempty[q]);
+      }
     }
+    if (qkv) cp_async_wait_all();  // nothing in flight into shared memory at exit
     }
   }
 

@@ -111,6 +111,12 @@ __device__ __forceinline__ void cp_async_commit() {
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
+// bar's pending count drops by one once all of this thread's earlier
+// cp.async copies have landed (noinc: the arrival is part of the barrier's
+// initial count).
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 
 // 2-D tiled load global -> shared, completion signalled on `bar` (tx bytes).
 // x is the innermost (contiguous) coordinate in elements, y the row.
