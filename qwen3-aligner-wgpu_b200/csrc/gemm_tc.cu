@@ -201,8 +201,9 @@ __device__ __forceinline__ void qkv_cs_issue(const EpiParams& ep, uint8_t* buf, 
 // Writes the warp's staged 32 rows x 128 bytes (eight 16-byte units a row,
 // XOR-swizzled by row) to global memory, four whole rows per instruction:
 // units 0-3 of row r go to base_r + off0, units 4-7 to base_r + off1
-// (elements), where base_r is lane r's `base` (nullptr: row not stored).
-// Warp-collective; the buffer may be refilled once it returns.
+// (elements; off1 < 0: units 4-7 are not stored), where base_r is lane r's
+// `base` (nullptr: row not stored).  Warp-collective; the buffer may be
+// refilled once it returns.
 template <typename T>
 __device__ __forceinline__ void flush_rows(const uint8_t* st, T* base, int off0, int off1) {
   const int lane = threadIdx.x & 31;
@@ -213,7 +214,8 @@ __device__ __forceinline__ void flush_rows(const uint8_t* st, T* base, int off0,
     const int r = 4 * i + (lane >> 3), u = lane & 7;
     const unsigned long long rb = __shfl_sync(0xFFFFFFFFu, b, r);
     const uint4 d = *reinterpret_cast<const uint4*>(st + r * 128 + 16 * (u ^ (r & 7)));
-    if (rb) *reinterpret_cast<uint4*>(reinterpret_cast<T*>(rb) + (u < 4 ? off0 + 8 * u : off1 + 8 * (u - 4))) = d;
+    if (rb && (u < 4 || off1 >= 0))
+      *reinterpret_cast<uint4*>(reinterpret_cast<T*>(rb) + (u < 4 ? off0 + 8 * u : off1 + 8 * (u - 4))) = d;
   }
   __syncwarp();
 }
@@ -379,13 +381,14 @@ __device__ __forceinline__ void stage_qkv_gains(const EpiParams& ep, float* gain
 // SwiGLU the range is over the output columns [0, BN/2).
 // Returns false only when a staged QKV epilogue's wait for its cos | sin
 // lines ran out.
-template <int BN, typename T, bool kStagedQkv = false>
+// kOnly: 0 = every mode, 1 = EPI_QKV_ROPE only, 2 = every mode but EPI_QKV_ROPE.
+template <int BN, typename T, bool kStagedQkv = false, int kOnly = 0>
 __device__ __forceinline__ bool epilogue(const EpiParams& ep, uint32_t tmem_row, int row, int M,
                                          int n0, int N, int cb, int ce, const QkvRow& meta = {},
                                          const float* gain = nullptr, uint8_t* stage = nullptr,
                                          const uint8_t* cs = nullptr, uint64_t* csfull = nullptr,
                                          uint32_t cs_parity = 0) {
-  if constexpr (BN % 128 == 0) {
+  if constexpr (BN % 128 == 0 && kOnly != 2) {
     if (ep.mode == EPI_QKV_ROPE) {
 #pragma unroll 1
       for (int hb = cb / 128; hb < ce / 128; ++hb)
@@ -396,6 +399,7 @@ __device__ __forceinline__ bool epilogue(const EpiParams& ep, uint32_t tmem_row,
       return true;
     }
   }
+  if constexpr (kOnly == 1) return true;
   if (ep.mode == EPI_SWIGLU16) {
     // gate in columns [0, BN/2), up in [BN/2, BN) of this tile
     constexpr int H = BN / 2;
@@ -590,6 +594,51 @@ __device__ __forceinline__ bool epilogue(const EpiParams& ep, uint32_t tmem_row,
         break;
     }
   };
+  if constexpr (kStagedQkv) {
+    // EPI_STORE16 on CTA pairs (N a multiple of BN): each 64-column block of
+    // the warp's 32 rows is staged in the warp's buffer and stored four whole
+    // rows per instruction, instead of 16 bytes from each of 32 rows
+    if (ep.mode == EPI_STORE16 && stage && (reinterpret_cast<uintptr_t>(ep.out) & 15u) == 0 &&
+        ep.ldo % 8 == 0 && (reinterpret_cast<uintptr_t>(ep.bias) & 15u) == 0) {
+      int orow = row;
+      if (ep.row_map && row < M) orow = ep.row_map[row];
+      T* base = (row < M && orow >= 0) ? static_cast<T*>(ep.out) + (long long)orow * ep.ldo + n0
+                                       : nullptr;
+#pragma unroll 1
+      for (int c0 = cb; c0 < ce; c0 += 64) {
+        const bool two = c0 + 32 < ce;
+#pragma unroll 1
+        for (int h = 0; h < (two ? 2 : 1); ++h) {
+          float x[32];
+          tmem_ld32(tmem_row + c0 + 32 * h, x);  // warp-collective (h's bound is warp-uniform)
+          if (ep.bias) {
+            const float4* b4 = reinterpret_cast<const float4*>(ep.bias + n0 + c0 + 32 * h);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 t = __ldg(b4 + i);
+              x[4 * i] += t.x;
+              x[4 * i + 1] += t.y;
+              x[4 * i + 2] += t.z;
+              x[4 * i + 3] += t.w;
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t u[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              float2 g = make_float2(x[8 * j + 2 * k], x[8 * j + 2 * k + 1]);
+              if (ep.act == ACT_GELU) g = gelu_as2(g);
+              u[k] = cvt2_rn<T>(g);
+            }
+            stage_unit(stage, 4 * h + j, make_uint4(u[0], u[1], u[2], u[3]));
+          }
+        }
+        flush_rows<T>(stage, base, c0, two ? c0 + 32 : -1);
+      }
+      return true;
+    }
+  }
   // chunks are read from TMEM two at a time behind one wait
 #pragma unroll 1
   for (int c0 = cb; c0 < ce; c0 += 64) {
@@ -983,12 +1032,14 @@ struct PairCfg {
   static constexpr size_t kSmem = 1024 + kPairStages * (kPairHalf + kBHalf) + 256;
 };
 
-template <int BN, typename T>
+// kQkv: the EPI_QKV_ROPE instantiation (its epilogue only); otherwise every
+// other mode.  Separate instantiations keep each epilogue's registers apart.
+template <int BN, typename T, bool kQkv>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      int M, int N, int K, EpiParams ep) {
   // EPI_QKV_ROPE gives one ring stage to the epilogue's cos | sin staging
-  const int S = ep.mode == EPI_QKV_ROPE ? kPairStages - 1 : kPairStages;
+  constexpr int S = kQkv ? kPairStages - 1 : kPairStages;
   constexpr uint32_t kBHalf = PairCfg<BN>::kBHalf;
   constexpr uint32_t kAccCols = 256;
   constexpr uint32_t kAllocCols = 512;
@@ -1116,7 +1167,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // the row's folded-norm statistics are loaded one tile ahead
     auto tile_row = [&](int t) { return (t / n_tiles_n) * 2 * kBM + rank * kBM + q * 32 + lane; };
     SsqRow ssq = ssq_load(ep, tile_row(pair), M);
-    if (resid_stageable<T>(ep, N)) {
+    if (!kQkv && resid_stageable<T>(ep, N)) {
       // residual modes: the warp's staging buffer, the first tile's first
       // chunk requested before the first accumulator wait
       uint8_t* stage = epi_smem + (warp - 2) * kEpiStageBytes;
@@ -1144,8 +1195,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // EPI_QKV_ROPE: the warp's buffer stages each head's rows for coalesced
     // stores; the two warps of a TMEM lane quarter (one per column half)
     // share the cos | sin lines of their 32 rows, each warp copying one table
-    const bool qkv = ep.mode == EPI_QKV_ROPE;
-    uint8_t* qstage = qkv ? epi_smem + (warp - 2) * kEpiStageBytes : nullptr;
+    constexpr bool qkv = kQkv;
+    uint8_t* qstage =
+        (qkv || ep.mode == EPI_STORE16) ? epi_smem + (warp - 2) * kEpiStageBytes : nullptr;
     uint8_t* cs = qkv ? epi_smem + kGemmEpiWarps * kEpiStageBytes + q * 8192 : nullptr;
     for (int t = pair; t < n_tiles; t += n_pairs, ++lt) {
       const int buf = lt & 1;
@@ -1170,8 +1222,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       ssq = ssq_load(ep, tile_row(t + n_pairs), M);  // arrives during this epilogue
       tc_fence_after();
       const uint32_t trow = tbase + buf * kAccCols + (static_cast<uint32_t>(q * 32) << 16);
-      const bool ep_ok =
-          epilogue<BN, T, true>(ep, trow, row, M, n0, N, cb, ce, meta, gain, qstage, cs, &csfull[q], lt & 1);
+      const bool ep_ok = epilogue<BN, T, true, kQkv ? 1 : 2>(ep, trow, row, M, n0, N, cb, ce, meta, gain,
+                                                            qstage, cs, &csfull[q], lt & 1);
       tc_fence_before();
       __syncwarp();
       if (!ep_ok) {
@@ -1910,15 +1962,17 @@ template <int BN, typename T>
 int launch_pair(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
                 const EpiParams& ep, cudaStream_t stream) {
   // the residual and QKV modes add the epilogue warps' staging buffers
-  const bool staged =
-      ep.mode == EPI_RESID32 || ep.mode == EPI_RESID16 || ep.mode == EPI_QKV_ROPE;
+  const bool staged = ep.mode == EPI_RESID32 || ep.mode == EPI_RESID16 ||
+                      ep.mode == EPI_QKV_ROPE || ep.mode == EPI_STORE16;
   const size_t kPairSmem = PairCfg<BN>::kSmem + (staged ? kGemmEpiWarps * kEpiStageBytes : 0);
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, A, H16Traits<T>::kBf16, K, M, lda, kBK, kBM);
   if (rc) return rc;
   rc = make_tmap_2d(&tb, B, H16Traits<T>::kBf16, K, N, ldb, kBK, BN / 2);
   if (rc) return rc;
-  auto kern = gemm_pair_kernel<BN, T>;
+  auto kern = gemm_pair_kernel<BN, T, false>;
+  if constexpr (BN % 128 == 0)
+    if (ep.mode == EPI_QKV_ROPE) kern = gemm_pair_kernel<BN, T, true>;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairSmem);
   if (e != cudaSuccess) return (int)e;
