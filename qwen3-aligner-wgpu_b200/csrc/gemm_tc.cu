@@ -201,11 +201,12 @@ __device__ __forceinline__ void qkv_cs_issue(const EpiParams& ep, uint8_t* buf, 
 // Writes the warp's staged 32 rows x 128 bytes (eight 16-byte units a row,
 // XOR-swizzled by row) to global memory, four whole rows per instruction:
 // units 0-3 of row r go to base_r + off0, units 4-7 to base_r + off1
-// (elements; off1 < 0: units 4-7 are not stored), where base_r is lane r's
-// `base` (nullptr: row not stored).  Warp-collective; the buffer may be
-// refilled once it returns.
+// (elements; only units [0, nv) are stored), where base_r is lane r's `base`
+// (nullptr: row not stored).  Warp-collective; the buffer may be refilled
+// once it returns.
 template <typename T>
-__device__ __forceinline__ void flush_rows(const uint8_t* st, T* base, int off0, int off1) {
+__device__ __forceinline__ void flush_rows(const uint8_t* st, T* base, int off0, int off1,
+                                           int nv = 8) {
   const int lane = threadIdx.x & 31;
   __syncwarp();
   const unsigned long long b = reinterpret_cast<unsigned long long>(base);
@@ -214,7 +215,7 @@ __device__ __forceinline__ void flush_rows(const uint8_t* st, T* base, int off0,
     const int r = 4 * i + (lane >> 3), u = lane & 7;
     const unsigned long long rb = __shfl_sync(0xFFFFFFFFu, b, r);
     const uint4 d = *reinterpret_cast<const uint4*>(st + r * 128 + 16 * (u ^ (r & 7)));
-    if (rb && (u < 4 || off1 >= 0))
+    if (rb && u < nv)
       *reinterpret_cast<uint4*>(reinterpret_cast<T*>(rb) + (u < 4 ? off0 + 8 * u : off1 + 8 * (u - 4))) = d;
   }
   __syncwarp();
@@ -404,6 +405,38 @@ __device__ __forceinline__ bool epilogue(const EpiParams& ep, uint32_t tmem_row,
     // gate in columns [0, BN/2), up in [BN/2, BN) of this tile
     constexpr int H = BN / 2;
     T* out = static_cast<T*>(ep.out);
+    if constexpr (kStagedQkv) {
+      // CTA pairs: the thread's 64 output columns (one 128-byte row segment)
+      // go through the warp's buffer and leave four whole segments per store
+      if (stage && ce - cb == 64 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0 &&
+          ep.ldo % 8 == 0) {
+        T* base = row < M ? out + (long long)row * ep.ldo + n0 / 2 : nullptr;
+#pragma unroll 1
+        for (int k = 0; k < 2; ++k) {
+          float g[32], u[32];
+          tmem_ld2x32(tmem_row + cb + 32 * k, tmem_row + H + cb + 32 * k, g, u);  // warp-collective
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float h2[2];
+#pragma unroll
+              for (int l = 0; l < 2; ++l) {
+                const int i = 8 * j + 2 * e + l;
+                const float gh = round16<T>(g[i] * meta.inv);
+                const float uh = round16<T>(u[i] * meta.inv);
+                h2[l] = __fdividef(gh, 1.0f + __expf(-gh)) * uh;
+              }
+              w[e] = cvt2_rn<T>(make_float2(h2[0], h2[1]));
+            }
+            stage_unit(stage, 4 * k + j, make_uint4(w[0], w[1], w[2], w[3]));
+          }
+        }
+        flush_rows<T>(stage, base, cb, cb + 32);
+        return true;
+      }
+    }
 #pragma unroll 1
     for (int c0 = cb; c0 < ce; c0 += 32) {
       float g[32], u[32];
@@ -599,7 +632,7 @@ __device__ __forceinline__ bool epilogue(const EpiParams& ep, uint32_t tmem_row,
     // the warp's 32 rows is staged in the warp's buffer and stored four whole
     // rows per instruction, instead of 16 bytes from each of 32 rows
     if (ep.mode == EPI_STORE16 && stage && (reinterpret_cast<uintptr_t>(ep.out) & 15u) == 0 &&
-        ep.ldo % 8 == 0 && (reinterpret_cast<uintptr_t>(ep.bias) & 15u) == 0) {
+        ep.ldo % 8 == 0 && (reinterpret_cast<uintptr_t>(ep.bias) & 15u) == 0 && N % BN == 0) {
       int orow = row;
       if (ep.row_map && row < M) orow = ep.row_map[row];
       T* base = (row < M && orow >= 0) ? static_cast<T*>(ep.out) + (long long)orow * ep.ldo + n0
@@ -607,15 +640,18 @@ __device__ __forceinline__ bool epilogue(const EpiParams& ep, uint32_t tmem_row,
 #pragma unroll 1
       for (int c0 = cb; c0 < ce; c0 += 64) {
         const bool two = c0 + 32 < ce;
+        // whole 16-byte units inside the tile (BN = 240: the last chunk has 2)
+        const int nv = two ? 4 + min(32, BN - c0 - 32) / 8 : min(32, BN - c0) / 8;
 #pragma unroll 1
         for (int h = 0; h < (two ? 2 : 1); ++h) {
           float x[32];
           tmem_ld32(tmem_row + c0 + 32 * h, x);  // warp-collective (h's bound is warp-uniform)
           if (ep.bias) {
             const float4* b4 = reinterpret_cast<const float4*>(ep.bias + n0 + c0 + 32 * h);
+            const int nb = min(32, BN - c0 - 32 * h) / 4;  // bias entries inside the tile
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-              const float4 t = __ldg(b4 + i);
+              const float4 t = i < nb ? __ldg(b4 + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
               x[4 * i] += t.x;
               x[4 * i + 1] += t.y;
               x[4 * i + 2] += t.z;
@@ -634,7 +670,7 @@ __device__ __forceinline__ bool epilogue(const EpiParams& ep, uint32_t tmem_row,
             stage_unit(stage, 4 * h + j, make_uint4(u[0], u[1], u[2], u[3]));
           }
         }
-        flush_rows<T>(stage, base, c0, two ? c0 + 32 : -1);
+        flush_rows<T>(stage, base, c0, c0 + 32, nv);
       }
       return true;
     }
@@ -1196,8 +1232,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // stores; the two warps of a TMEM lane quarter (one per column half)
     // share the cos | sin lines of their 32 rows, each warp copying one table
     constexpr bool qkv = kQkv;
-    uint8_t* qstage =
-        (qkv || ep.mode == EPI_STORE16) ? epi_smem + (warp - 2) * kEpiStageBytes : nullptr;
+    uint8_t* qstage = (qkv || ep.mode == EPI_STORE16 || ep.mode == EPI_SWIGLU16)
+                          ? epi_smem + (warp - 2) * kEpiStageBytes
+                          : nullptr;
     uint8_t* cs = qkv ? epi_smem + kGemmEpiWarps * kEpiStageBytes + q * 8192 : nullptr;
     for (int t = pair; t < n_tiles; t += n_pairs, ++lt) {
       const int buf = lt & 1;
@@ -1580,6 +1617,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int cb, ce;
     epi_range<BN>(ep.mode, wg, kGemmEpiWarps / 4, cb, ce);
     const uint32_t tempty_lead = mapa_shared(smem_u32(tempty), 0);
+    // EPI_STORE16: the warp's buffer stages its rows for coalesced stores
+    uint8_t* stage = ep.mode == EPI_STORE16
+                         ? smem + S * (Cfg::kABytes + Cfg::kBHalf) + 256 + (warp - 2) * kEpiStageBytes
+                         : nullptr;
     int lt = 0;
     for (int t = pair; t < n_tiles; t += n_pairs, ++lt) {
       const int buf = lt & 1;
@@ -1597,7 +1638,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const bool valid = mt < g.n_mtiles && m < g.rows * g.wo && oh < g.ho;
       const int orow = img * g.ho * g.wo + (g.time_major ? ow * g.ho + oh : oh * g.wo + ow);
       const uint32_t trow = tbase + buf * kAccCols + (static_cast<uint32_t>(q * 32) << 16);
-      epilogue<BN, T>(ep, trow, valid ? orow : M, M, n0, N, cb, ce);
+      epilogue<BN, T, true, 2>(ep, trow, valid ? orow : M, M, n0, N, cb, ce, {}, nullptr, stage);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote_relaxed(tempty_lead + buf * 8);
@@ -1883,8 +1924,9 @@ int launch_conv_pair(const void* x, int n, int h, int w, int c, const void* wt, 
   rc = make_tmap_nd(&tb, wt, H16Traits<T>::kBf16, 2, bdims, bstr, bbox, bestr, 2 * BK);
   if (rc) return rc;
   auto kern = conv_pair_kernel<BN, BK, T>;
-  cudaError_t e =
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmem);
+  // the 16-bit store epilogue adds the epilogue warps' staging buffers
+  const size_t smem = Cfg::kSmem + (ep.mode == EPI_STORE16 ? kGemmEpiWarps * kEpiStageBytes : 0);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return (int)e;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
@@ -1895,7 +1937,7 @@ int launch_conv_pair(const void* x, int n, int h, int w, int c, const void* wt, 
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // added for the launch
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.blockDim = dim3(kGemmThreads, 1, 1);
-  cfg.dynamicSmemBytes = Cfg::kSmem;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
@@ -1963,7 +2005,8 @@ int launch_pair(const void* A, long long lda, const void* B, long long ldb, int 
                 const EpiParams& ep, cudaStream_t stream) {
   // the residual and QKV modes add the epilogue warps' staging buffers
   const bool staged = ep.mode == EPI_RESID32 || ep.mode == EPI_RESID16 ||
-                      ep.mode == EPI_QKV_ROPE || ep.mode == EPI_STORE16;
+                      ep.mode == EPI_QKV_ROPE || ep.mode == EPI_STORE16 ||
+                      ep.mode == EPI_SWIGLU16;
   const size_t kPairSmem = PairCfg<BN>::kSmem + (staged ? kGemmEpiWarps * kEpiStageBytes : 0);
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, A, H16Traits<T>::kBf16, K, M, lda, kBK, kBM);
