@@ -215,8 +215,9 @@ __device__ __forceinline__ void flush_rows(const uint8_t* st, T* base, int off0,
     const int r = 4 * i + (lane >> 3), u = lane & 7;
     const unsigned long long rb = __shfl_sync(0xFFFFFFFFu, b, r);
     const uint4 d = *reinterpret_cast<const uint4*>(st + r * 128 + 16 * (u ^ (r & 7)));
+    constexpr int kPer = 16 / static_cast<int>(sizeof(T));  // elements per unit
     if (rb && u < nv)
-      *reinterpret_cast<uint4*>(reinterpret_cast<T*>(rb) + (u < 4 ? off0 + 8 * u : off1 + 8 * (u - 4))) = d;
+      *reinterpret_cast<uint4*>(reinterpret_cast<T*>(rb) + (u < 4 ? off0 + kPer * u : off1 + kPer * (u - 4))) = d;
   }
   __syncwarp();
 }
@@ -749,11 +750,14 @@ __device__ __forceinline__ void resid_issue(const EpiParams& ep, uint8_t* buf, i
 // the first chunk of the warp's next tile (rows nxt_row0, columns from
 // nxt_n0 + cb) when nxt_n0 >= 0.  Same arithmetic as the direct path: bias,
 // then the residual, rounded once at the store.
-template <int BN, typename T>
+// kOut (CTA pairs: N a multiple of BN, whole 32-column chunks, 16-byte
+// aligned bias): the results also leave through a second 4 KB buffer, four
+// whole row segments per store instruction.
+template <int BN, typename T, bool kOut = false>
 __device__ __forceinline__ void epilogue_resid_staged(const EpiParams& ep, uint32_t tmem_row,
                                                       int row0, int M, int n0, int N, int cb,
                                                       int ce, uint8_t* buf, int nxt_row0,
-                                                      int nxt_n0) {
+                                                      int nxt_n0, uint8_t* obuf = nullptr) {
   const int lane = threadIdx.x & 31;
   const int row = row0 + lane;
   float ssq_acc = 0.0f;
@@ -791,6 +795,54 @@ __device__ __forceinline__ void epilogue_resid_staged(const EpiParams& ep, uint3
     float v[32];
     tmem_ld32(tmem_row + c0, v);  // warp-collective: every lane, every chunk
     const int col = n0 + c0;
+    if constexpr (kOut) {
+      // every lane computes (rows past M from their zero rows); only live
+      // rows are stored
+      const bool live = row < M;
+      if (ep.bias) {
+        const float4* b4 = reinterpret_cast<const float4*>(ep.bias + col);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 t = __ldg(b4 + i);
+          v[4 * i] += t.x;
+          v[4 * i + 1] += t.y;
+          v[4 * i + 2] += t.z;
+          v[4 * i + 3] += t.w;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] += h[i];
+      if (ep.mode == EPI_RESID32) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          stage_unit(obuf, j, make_uint4(__float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]),
+                                         __float_as_uint(v[4 * j + 2]), __float_as_uint(v[4 * j + 3])));
+        flush_rows<float>(obuf, live ? static_cast<float*>(ep.out) + static_cast<long long>(row) * ep.ldo : nullptr,
+                          col, col + 16, 8);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t w[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) w[k] = cvt2_rn<T>(make_float2(v[8 * j + 2 * k], v[8 * j + 2 * k + 1]));
+          stage_unit(obuf, j, make_uint4(w[0], w[1], w[2], w[3]));
+        }
+        flush_rows<T>(obuf, live ? static_cast<T*>(ep.out) + static_cast<long long>(row) * ep.ldo : nullptr,
+                      col, col, 4);
+        if (ep.ssq_out && live) {  // the 128-column block's sum of squares of the stored values
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float x = round16<T>(v[i]);
+            ssq_acc = fmaf(x, x, ssq_acc);
+          }
+          if ((col + 32) % kSsqCols == 0 || col + 32 >= N) {
+            ep.ssq_out[static_cast<long long>(row) * ep.ssq_n + col / kSsqCols] = ssq_acc;
+            ssq_acc = 0.0f;
+          }
+        }
+      }
+      continue;
+    }
     const int nc = min(min(32, BN - c0), N - col);
     if (row >= M || nc <= 0) continue;
     if (ep.bias) {
@@ -1068,14 +1120,17 @@ struct PairCfg {
   static constexpr size_t kSmem = 1024 + kPairStages * (kPairHalf + kBHalf) + 256;
 };
 
-// kQkv: the EPI_QKV_ROPE instantiation (its epilogue only); otherwise every
-// other mode.  Separate instantiations keep each epilogue's registers apart.
-template <int BN, typename T, bool kQkv>
+// kVar: 1 = the EPI_QKV_ROPE instantiation (its epilogue only), 2 = the
+// residual modes' (EPI_RESID16 / EPI_RESID32), 0 = every other mode.  Separate
+// instantiations keep each epilogue's registers apart; 1 and 2 run one ring
+// stage fewer and stage 64 KB of epilogue data instead of 32 KB.
+template <int BN, typename T, int kVar>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      int M, int N, int K, EpiParams ep) {
   // EPI_QKV_ROPE gives one ring stage to the epilogue's cos | sin staging
-  constexpr int S = kQkv ? kPairStages - 1 : kPairStages;
+  constexpr bool kQkv = kVar == 1;
+  constexpr int S = kVar ? kPairStages - 1 : kPairStages;
   constexpr uint32_t kBHalf = PairCfg<BN>::kBHalf;
   constexpr uint32_t kAccCols = 256;
   constexpr uint32_t kAllocCols = 512;
@@ -1203,10 +1258,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // the row's folded-norm statistics are loaded one tile ahead
     auto tile_row = [&](int t) { return (t / n_tiles_n) * 2 * kBM + rank * kBM + q * 32 + lane; };
     SsqRow ssq = ssq_load(ep, tile_row(pair), M);
-    if (!kQkv && resid_stageable<T>(ep, N)) {
+    if (kVar == 2 && resid_stageable<T>(ep, N) &&
+        (reinterpret_cast<uintptr_t>(ep.bias) & 15u) == 0) {
       // residual modes: the warp's staging buffer, the first tile's first
       // chunk requested before the first accumulator wait
       uint8_t* stage = epi_smem + (warp - 2) * kEpiStageBytes;
+      uint8_t* ostage = stage + kGemmEpiWarps * kEpiStageBytes;  // the results
       auto warp_row0 = [&](int t) { return (t / n_tiles_n) * 2 * kBM + rank * kBM + q * 32; };
       if (pair < n_tiles)
         resid_issue<T>(ep, stage, warp_row0(pair), (pair % n_tiles_n) * BN + cb, M, N);
@@ -1219,9 +1276,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_fence_after();
         const uint32_t trow = tbase + buf * kAccCols + (static_cast<uint32_t>(q * 32) << 16);
         const int tn = t + n_pairs;
-        epilogue_resid_staged<BN, T>(ep, trow, warp_row0(t), M, (t % n_tiles_n) * BN, N, cb, ce,
-                                     stage, tn < n_tiles ? warp_row0(tn) : 0,
-                                     tn < n_tiles ? (tn % n_tiles_n) * BN : -1);
+        epilogue_resid_staged<BN, T, true>(ep, trow, warp_row0(t), M, (t % n_tiles_n) * BN, N, cb,
+                                           ce, stage, tn < n_tiles ? warp_row0(tn) : 0,
+                                           tn < n_tiles ? (tn % n_tiles_n) * BN : -1, ostage);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_remote_relaxed(tempty_lead + buf * 8);
@@ -2003,19 +2060,22 @@ int launch_conv_tma(const void* x, int n, int h, int w, int c, const void* wt, i
 template <int BN, typename T>
 int launch_pair(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
                 const EpiParams& ep, cudaStream_t stream) {
-  // the residual and QKV modes add the epilogue warps' staging buffers
-  const bool staged = ep.mode == EPI_RESID32 || ep.mode == EPI_RESID16 ||
-                      ep.mode == EPI_QKV_ROPE || ep.mode == EPI_STORE16 ||
-                      ep.mode == EPI_SWIGLU16;
-  const size_t kPairSmem = PairCfg<BN>::kSmem + (staged ? kGemmEpiWarps * kEpiStageBytes : 0);
+  // the instantiation (QKV, residual, other) and its shared memory: the
+  // ring, the barriers and the epilogue warps' staging buffers
+  const bool resid = ep.mode == EPI_RESID32 || ep.mode == EPI_RESID16;
+  const bool qkv = BN % 128 == 0 && ep.mode == EPI_QKV_ROPE;
+  const bool staged = ep.mode == EPI_STORE16 || ep.mode == EPI_SWIGLU16;
+  const int stages = (qkv || resid) ? kPairStages - 1 : kPairStages;
+  const size_t kPairSmem = 1024 + stages * (kPairHalf + PairCfg<BN>::kBHalf) + 256 +
+                           ((qkv || resid) ? 2 : staged ? 1 : 0) * kGemmEpiWarps * kEpiStageBytes;
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, A, H16Traits<T>::kBf16, K, M, lda, kBK, kBM);
   if (rc) return rc;
   rc = make_tmap_2d(&tb, B, H16Traits<T>::kBf16, K, N, ldb, kBK, BN / 2);
   if (rc) return rc;
-  auto kern = gemm_pair_kernel<BN, T, false>;
+  auto kern = resid ? gemm_pair_kernel<BN, T, 2> : gemm_pair_kernel<BN, T, 0>;
   if constexpr (BN % 128 == 0)
-    if (ep.mode == EPI_QKV_ROPE) kern = gemm_pair_kernel<BN, T, true>;
+    if (qkv) kern = gemm_pair_kernel<BN, T, 1>;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairSmem);
   if (e != cudaSuccess) return (int)e;
