@@ -63,7 +63,9 @@ constexpr uint32_t kPageBytes = kHalf / 2;   // 8 KB: 64 rows of one block
 constexpr int kStages = 2;                   // K and V ring depth
 constexpr uint32_t kSumBytes = 2 * 2 * kRows * 4;  // row sums [item parity][head][row]
 constexpr int kMaxStaged = 128;  // work items of one CTA whose descriptors sit in shared memory
-constexpr size_t kSmem = 1024 + (2 + 2 * kStages) * kTile + kSumBytes + 256 + kMaxStaged * 32;
+constexpr uint32_t kOutStage = 4096;  // per epilogue warp: 32 rows x 64 output columns
+constexpr size_t kSmem =
+    1024 + (2 + 2 * kStages) * kTile + kSumBytes + 256 + kMaxStaged * 32 + kEpiWarps * kOutStage;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.0f;  // rescale O when the row max grows by > 2^8
 
@@ -198,6 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
   Item* staged = reinterpret_cast<Item*>(bars + 32);  // [kMaxStaged]
   static_assert(sizeof(Item) <= 32, "staged item size");
+  uint8_t* ostage = reinterpret_cast<uint8_t*>(bars + 32) + kMaxStaged * 32;  // [kEpiWarps]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int kSmHead = 32 * kSoftmaxWarps / 2;
@@ -507,21 +510,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         T* dst = static_cast<T*>(ap.out) + (static_cast<long long>(it.t.tok0) + pos) * ap.ldo +
                  static_cast<long long>(2 * it.kvh + h) * kHD;
         const uint32_t tO = tO0 + h * 128 + lane_off;
-#pragma unroll 1
+        // the row's 128 values, scaled and packed, then O_h goes back to the
+        // MMA warp before any of them is stored
+        uint32_t w[kHD / 2];
+#pragma unroll
         for (int c = 0; c < kHD / 32; ++c) {
           float o[32];
           tmem_ld32(tO + c * 32, o);
-          if (pos < it.t.len) {
-            alignas(16) T ov[32];
 #pragma unroll
-            for (int e = 0; e < 32; ++e) ov[e] = f2h<T>(o[e] * inv);
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              reinterpret_cast<uint4*>(dst + c * 32)[e] = reinterpret_cast<const uint4*>(ov)[e];
-          }
+          for (int e = 0; e < 16; ++e) w[c * 16 + e] = cvt2_rn<T>(make_float2(o[2 * e] * inv, o[2 * e + 1] * inv));
         }
         tc_fence_before();
         mbar_arrive(&o_free[h]);
+        // 64 columns per staged block, stored four whole row segments at a time
+        uint8_t* st = ostage + quarter * kOutStage;
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            stage_unit(st, u, make_uint4(w[b * 32 + 4 * u], w[b * 32 + 4 * u + 1], w[b * 32 + 4 * u + 2],
+                                         w[b * 32 + 4 * u + 3]));
+          flush_rows<T>(st, pos < it.t.len ? dst : nullptr, b * 64, b * 64 + 32);
+        }
       }
     }
     if (!ok && lane == 0) fail();

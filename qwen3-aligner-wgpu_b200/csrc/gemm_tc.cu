@@ -198,35 +198,6 @@ __device__ __forceinline__ void qkv_cs_issue(const EpiParams& ep, uint8_t* buf, 
   }
 }
 
-// Writes the warp's staged 32 rows x 128 bytes (eight 16-byte units a row,
-// XOR-swizzled by row) to global memory, four whole rows per instruction:
-// units 0-3 of row r go to base_r + off0, units 4-7 to base_r + off1
-// (elements; only units [0, nv) are stored), where base_r is lane r's `base`
-// (nullptr: row not stored).  Warp-collective; the buffer may be refilled
-// once it returns.
-template <typename T>
-__device__ __forceinline__ void flush_rows(const uint8_t* st, T* base, int off0, int off1,
-                                           int nv = 8) {
-  const int lane = threadIdx.x & 31;
-  __syncwarp();
-  const unsigned long long b = reinterpret_cast<unsigned long long>(base);
-#pragma unroll 1
-  for (int i = 0; i < 8; ++i) {
-    const int r = 4 * i + (lane >> 3), u = lane & 7;
-    const unsigned long long rb = __shfl_sync(0xFFFFFFFFu, b, r);
-    const uint4 d = *reinterpret_cast<const uint4*>(st + r * 128 + 16 * (u ^ (r & 7)));
-    constexpr int kPer = 16 / static_cast<int>(sizeof(T));  // elements per unit
-    if (rb && u < nv)
-      *reinterpret_cast<uint4*>(reinterpret_cast<T*>(rb) + (u < 4 ? off0 + kPer * u : off1 + kPer * (u - 4))) = d;
-  }
-  __syncwarp();
-}
-// This lane's row, 16-byte unit u, into the staging buffer (row = lane).
-__device__ __forceinline__ void stage_unit(uint8_t* st, int u, uint4 d) {
-  const int lane = threadIdx.x & 31;
-  *reinterpret_cast<uint4*>(st + lane * 128 + 16 * (u ^ (lane & 7))) = d;
-}
-
 // EPI_QKV_ROPE for one 128-column head of this thread's row.  The head's
 // values are rounded to the storage type (the GEMM output's rounding point).
 // A v head is appended to the cache as rounded.  A q or k head takes RMSNorm
