@@ -228,12 +228,14 @@ __device__ __forceinline__ bool qkv_rope_head(const EpiParams& ep, uint32_t tmem
     dst = static_cast<T*>(is_v ? rk.vc : rk.kc) + meta.kv_off +
           static_cast<long long>(kvh) * rk.page_size * HD;
   }
-  if (is_v) {  // stored directly: staging these too would make the kernel spill
+  if (is_v) {
 #pragma unroll 1
     for (int c = 0; c < HD / 32; c += 2) {
       float v[2][32];
       tmem_ld2x32(tmem_col0 + c * 32, tmem_col0 + (c + 1) * 32, v[0], v[1]);  // warp-collective
-      if (!ok) continue;
+      if constexpr (!kStaged) {
+        if (!ok) continue;
+      }
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t w[16];
@@ -241,10 +243,15 @@ __device__ __forceinline__ bool qkv_rope_head(const EpiParams& ep, uint32_t tmem
         for (int i = 0; i < 16; ++i)
           w[i] = pack2_rn<T>(mul2_rn(make_float2(v[h][2 * i], v[h][2 * i + 1]), make_float2(meta.inv, meta.inv)));
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          reinterpret_cast<uint4*>(dst + (c + h) * 32)[j] =
-              make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+        for (int j = 0; j < 4; ++j) {
+          const uint4 d = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+          if constexpr (kStaged)
+            stage_unit(ost, 4 * h + j, d);
+          else
+            reinterpret_cast<uint4*>(dst + (c + h) * 32)[j] = d;
+        }
       }
+      if constexpr (kStaged) flush_rows<T>(ost, ok ? dst : nullptr, c * 32, c * 32 + 32);
     }
     return true;
   }
