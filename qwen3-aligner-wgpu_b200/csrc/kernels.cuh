@@ -59,9 +59,12 @@ int mel_finalize_rows(const float* scratch, int n_frames, const unsigned* maxkey
 
 // ---------------------------------------------------------------- (b) audio tower
 // conv1: chunked mel [n][h][w] f32 (c_in = 1) -> NHWC [n][ho][wo][c_out] 16-bit,
-// gelu(w·x + b).  w [c_out][9] f32 (k = kh*3 + kw).
+// gelu(w·x + b).  w [c_out][9] f32 (k = kh*3 + kw).  On the tensor cores (split
+// f16 operands, f32-grade products) when c_out is a multiple of 32 up to 512
+// and the output rows are 16-byte aligned; a bounded wait that runs out sets
+// kStatusTimeout in *status.
 int conv1_direct(const float* mel, int n, int h, int w, const float* wt, const float* bias,
-                 int c_out, int ldc, void* out, bool bf16, cudaStream_t s);
+                 int c_out, int ldc, void* out, bool bf16, unsigned* status, cudaStream_t s);
 
 // Channels per pixel of the conv activations that feed the implicit GEMMs:
 // c rounded up to 64 (the pad channels hold zeros), so that a 64-channel

@@ -105,7 +105,7 @@ extern "C" int qa_k_window_attention(const void* qkv, long long T, int dm, int n
 extern "C" int qa_k_conv1(const float* mel, int n, int h, int w, const float* wt,
                           const float* bias, int c_out, void* out, int bf16, void* stream) {
   if (!mel || !wt || !bias || !out || n < 0 || h <= 0 || w <= 0) return QA_ERR_ARG;
-  const int rc = conv1_direct(mel, n, h, w, wt, bias, c_out, c_out, out, bf16 != 0,
+  const int rc = conv1_direct(mel, n, h, w, wt, bias, c_out, c_out, out, bf16 != 0, nullptr,
                               static_cast<cudaStream_t>(stream));
   return rc == 0 ? QA_OK : QA_ERR_CUDA;
 }

@@ -797,7 +797,8 @@ int run_encoder(qa_ctx* ctx, const Plan& P, const PlanDev& D, void* out16, const
     const int g = std::min(G, P.total_chunks - g0);
     const float* mel = ctx->mel_chunked.as<float>() + static_cast<size_t>(g0) * c.num_mel_bins * cs;
     KL("conv1", 18.0 * g * h1 * w1 * ds, 4.0 * g * c.num_mel_bins * cs + 2.0 * g * h1 * w1 * ds,
-       conv1_direct(mel, g, c.num_mel_bins, cs, W.c1_w, W.c1_b, ds, cp, ctx->act1.p, bf, s));
+       conv1_direct(mel, g, c.num_mel_bins, cs, W.c1_w, W.c1_b, ds, cp, ctx->act1.p, bf,
+                    ctx->status.as<unsigned>(), s));
     // conv2 / conv3: implicit GEMM on the tensor cores, A gathered from NHWC
     ep.mode = EPI_STORE16;
     ep.act = ACT_GELU;

@@ -251,3 +251,29 @@ def test_qkv_rope_epilogue(dtype):
         assert (kg - kw).abs().max().item() <= tol * kw.abs().max().item()
         # v is the rounded GEMM output; torch's fp32 matmul sums in another order
         assert (vg - vw).abs().max().item() <= tol * vw.abs().max().item()
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("n,h,w,co", [(3, 128, 100, 480), (1, 9, 7, 480), (2, 16, 13, 64), (2, 9, 7, 40)])
+def test_conv1(dtype, n, h, w, co):
+    """conv1 (one input channel, 3x3 / stride 2 / pad 1, bias, erf GELU) on the
+    tensor cores with split f16 operands (channel counts that are multiples of
+    32; 40 takes the CUDA-core kernel), against a float64 torch reference:
+    every output within one unit of the 16-bit format's precision."""
+    L = _lib()
+    g = torch.Generator(device="cuda").manual_seed(11)
+    mel = torch.randn(n, h, w, device="cuda", generator=g) * 1.5
+    wt = torch.randn(co, 9, device="cuda", generator=g) * 0.3
+    bias = torch.randn(co, device="cuda", generator=g) * 0.1
+    ho, wo = (h - 1) // 2 + 1, (w - 1) // 2 + 1
+    out = torch.full((n * ho * wo, co), float("nan"), device="cuda", dtype=dtype)
+    L.conv1(mel, wt, bias, out)
+    torch.cuda.synchronize()
+    # float64 reference (a float32 cuDNN convolution may run in TF32)
+    ref = torch.nn.functional.conv2d(mel[:, None].double(), wt.view(co, 1, 3, 3).double(), bias.double(),
+                                     stride=2, padding=1)
+    ref = torch.nn.functional.gelu(ref).permute(0, 2, 3, 1).reshape(n * ho * wo, co).float()
+    assert torch.isfinite(out.float()).all()
+    ulp = 2.0 ** -10 if dtype == torch.float16 else 2.0 ** -7
+    err = (out.float() - ref).abs() - ulp * ref.abs()
+    assert err.max().item() <= 1e-5
