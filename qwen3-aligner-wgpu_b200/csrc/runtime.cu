@@ -789,7 +789,9 @@ int run_encoder(qa_ctx* ctx, const Plan& P, const PlanDev& D, void* out16, const
   const int cp = conv_channels_padded(ds);  // channels per pixel of act1 / act2 (pads zero)
   TRY(ensure_zeroed(ctx, ctx->act1, static_cast<size_t>(G) * h1 * w1 * cp * 2));
   TRY(ensure_zeroed(ctx, ctx->act2, static_cast<size_t>(G) * h2 * w2 * cp * 2));
-  TRY(ensure(ctx, ctx->act3, static_cast<size_t>(G) * h3 * w3 * ds * 2));
+  // conv3's output is kept for every chunk of the pass (≈ 200 KB a chunk), so
+  // that conv_out runs as one GEMM over all of them instead of one per group
+  TRY(ensure(ctx, ctx->act3, static_cast<size_t>(P.total_chunks) * h3 * w3 * ds * 2));
   TRY(ensure(ctx, ctx->xenc, static_cast<size_t>(std::max(P.T_a, 1)) * dm * 4));
   EpiParams ep;
   ep.status = ctx->status.as<unsigned>();
@@ -810,12 +812,13 @@ int run_encoder(qa_ctx* ctx, const Plan& P, const PlanDev& D, void* out16, const
        2.0 * g * (h1 * w1 * ds + h2 * w2 * ds) + 2.0 * ds * 9 * ds,
        conv3x3s2_tc(ctx->act1.p, g, h1, w1, cp, W.c2_w, ds, false, bf, ep, s));
     ep.bias = W.c3_b;
-    ep.out = ctx->act3.p;
+    ep.out = static_cast<uint8_t*>(ctx->act3.p) + static_cast<size_t>(g0) * h3 * w3 * ds * 2;
     ep.ldo = ds;
     KL("conv_gemm", gemm_flops(g * h3 * w3, ds, 9 * ds),
        2.0 * g * (h2 * w2 * ds + h3 * w3 * ds) + 2.0 * ds * 9 * ds,
        conv3x3s2_tc(ctx->act2.p, g, h2, w2, cp, W.c3_w, ds, true, bf, ep, s));
-    // conv_out + bias + PE[t], scattered into the packed token rows
+  }
+  {  // conv_out + bias + PE[t] over every chunk, scattered into the packed token rows
     EpiParams eo;
     eo.status = ep.status;
     eo.mode = EPI_STORE32;
@@ -824,9 +827,10 @@ int run_encoder(qa_ctx* ctx, const Plan& P, const PlanDev& D, void* out16, const
     eo.pe_period = tpc;
     eo.out = ctx->xenc.p;
     eo.ldo = dm;
-    eo.row_map = D.co_map + static_cast<size_t>(g0) * tpc;
-    KL("gemm:conv_out", gemm_flops(g * tpc, dm, h3 * ds), gemm_bytes(g * tpc, dm, h3 * ds, 4),
-       gemm_tc(ctx->act3.p, (long long)h3 * ds, W.co_w, (long long)h3 * ds, g * tpc, dm, h3 * ds,
+    eo.row_map = D.co_map;
+    const int rows = P.total_chunks * tpc;
+    KL("gemm:conv_out", gemm_flops(rows, dm, h3 * ds), gemm_bytes(rows, dm, h3 * ds, 4),
+       gemm_tc(ctx->act3.p, (long long)h3 * ds, W.co_w, (long long)h3 * ds, rows, dm, h3 * ds,
                bf, eo, s));
   }
   const int Ta = P.T_a;
@@ -1904,6 +1908,11 @@ int qa_batch_stage(qa_ctx* ctx, const qa_clip* clips, int n, const qa_result* re
   TRY(ensure(ctx, ctx->mel_spec, static_cast<size_t>(P.total_frames) * kMelDftRows * 4));
   TRY(ensure(ctx, ctx->maxkey, static_cast<size_t>(n) * 4));
   TRY(ensure(ctx, ctx->hid, static_cast<size_t>(P.T_d) * H * 2));
+  {  // conv3's output for every chunk of the pass (the tower's conv_out input)
+    const int ds = c.downsample_hidden;
+    const int h3 = ((c.num_mel_bins - 1) / 2 / 2) / 2 + 1, w3 = ((cs - 1) / 2 / 2) / 2 + 1;
+    TRY(ensure(ctx, ctx->act3, static_cast<size_t>(P.total_chunks) * h3 * w3 * ds * 2));
+  }
   S.seq = ++ctx->batch_seq;
   S.state = Staged::kStaged;
   return QA_OK;
