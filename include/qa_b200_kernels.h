@@ -76,6 +76,8 @@ int qa_k_conv3x3s2(const void* x, int n, int h, int w, int c, const void* wt, in
  * pad 1) + bias + erf-GELU over mel chunks [n][h][w] (f32), output NHWC
  * [n][ho][wo][c_out] 16-bit (CpuConvStem::conv_block_stages level 1,
  * src/audio_encoder.rs:361-447).  wt [c_out][9] f32, bias [c_out] f32.
+ * c_out a multiple of 32 (up to 512) runs on the tensor cores with split f16
+ * operands (f32-grade products); other channel counts on CUDA cores.
  */
 int qa_k_conv1(const float* mel, int n, int h, int w, const float* wt, const float* bias,
                int c_out, void* out, int bf16, void* stream);
