@@ -72,26 +72,36 @@ __global__ void layernorm_kernel(const float* __restrict__ x, int rows, int d,
 
 // The same row arithmetic with 16-byte loads: rows of d % 4 == 0 f32 elements,
 // 16-byte aligned x / g / b, 8-byte aligned output rows.  Lane l holds float4
-// vectors l, l + 32, ... of its row.
+// vectors l, l + 32, ... of its row.  The block copies the gain and bias into
+// shared memory while its rows' loads are in flight, so that the output loop
+// after the two reductions does not wait on them.
 template <typename T>
 __global__ void layernorm_vec_kernel(const float* __restrict__ x, int rows, int d,
                                      const float* __restrict__ g, const float* __restrict__ b,
                                      float eps, T* __restrict__ out) {
+  __shared__ float4 sg[256], sb[256];  // d <= 1024
   pdl_wait();  // the previous kernel's results are visible from here
   pdl_trigger();
   const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
   const int nv = d / 4;
-  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<long long>(row) * d);
+  const bool live = row < rows;
+  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<long long>(live ? row : 0) * d);
   float4 v[8];
-  float s = 0.f;
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     const int i = lane + 32 * k;
-    v[k] = i < nv ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-    s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+    v[k] = (live && i < nv) ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
   }
+  for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+    sg[i] = __ldg(reinterpret_cast<const float4*>(g) + i);
+    sb[i] = __ldg(reinterpret_cast<const float4*>(b) + i);
+  }
+  __syncthreads();
+  if (!live) return;
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
   const float mean = warp_sum(s) / static_cast<float>(d);
   float q = 0.f;
 #pragma unroll
@@ -107,13 +117,11 @@ __global__ void layernorm_vec_kernel(const float* __restrict__ x, int rows, int 
   const float var = warp_sum(q) / static_cast<float>(d);
   const float inv = 1.0f / sqrtf(var + eps);
   uint2* o = reinterpret_cast<uint2*>(out + static_cast<long long>(row) * d);
-  const float4* g4 = reinterpret_cast<const float4*>(g);
-  const float4* b4 = reinterpret_cast<const float4*>(b);
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     const int i = lane + 32 * k;
     if (i < nv) {
-      const float4 gg = __ldg(g4 + i), bb = __ldg(b4 + i);
+      const float4 gg = sg[i], bb = sb[i];
       const float e0 = __fadd_rn(__fmul_rn(__fmul_rn(v[k].x - mean, inv), gg.x), bb.x);
       const float e1 = __fadd_rn(__fmul_rn(__fmul_rn(v[k].y - mean, inv), gg.y), bb.y);
       const float e2 = __fadd_rn(__fmul_rn(__fmul_rn(v[k].z - mean, inv), gg.z), bb.z);
